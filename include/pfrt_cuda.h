@@ -1,0 +1,192 @@
+/*
+ * pfrt_cuda.h -- C ABI of the B200 (sm_100a) backend for PyFlameRT's
+ * MatMul / Gemm / QuantizedMatMul / sparse-weight MatMul hot path.
+ *
+ * Plain C: pointers, sizes and status codes, no C++ or torch types, so the
+ * library can be bound from C++ (the PyFlameRT CudaBackend), ctypes, cgo or
+ * JNI alike.  Device pointers are CUDA device addresses of the context's
+ * device; "host" pointers are ordinary host memory.  Every function returns
+ * PFRT_OK (0) or an error code; pfrt_last_error() gives the message of the
+ * last failure on the calling thread.  There is no CPU fallback: on a machine
+ * without a usable sm_100 GPU, pfrt_ctx_create fails with PFRT_ERR_NO_DEVICE.
+ *
+ * Layouts are dense row-major, as in the reference Tensor
+ * (include/pyflame_rt/tensor.hpp:12-90).  Each entry point names the
+ * reference routine whose result it reproduces.
+ *
+ * Kernels are enqueued asynchronously on the given stream (NULL = the
+ * context's own stream, (pfrt_stream)1 = CUDA's legacy default stream).  Device-side failures (a bounded wait that gave up,
+ * an out-of-range CSR index) are recorded in the context and reported by
+ * pfrt_ctx_check().  A context and its scratch memory serve one stream at a
+ * time; use one context per thread for concurrent calls.
+ */
+#ifndef PFRT_CUDA_H
+#define PFRT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PFRT_API __attribute__((visibility("default")))
+#else
+#define PFRT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum pfrt_status {
+    PFRT_OK = 0,
+    PFRT_ERR_INVALID_ARGUMENT = 1, /* shape / dtype / attribute error (the reference throws std::invalid_argument) */
+    PFRT_ERR_BAD_CSR = 2,          /* malformed CSR structure or index out of range */
+    PFRT_ERR_CUDA = 3,             /* CUDA runtime or launch failure */
+    PFRT_ERR_OUT_OF_MEMORY = 4,
+    PFRT_ERR_UNSUPPORTED = 5,      /* a size or mode this backend does not implement */
+    PFRT_ERR_DEVICE_TIMEOUT = 6,   /* a bounded device-side wait gave up */
+    PFRT_ERR_NO_DEVICE = 7         /* no usable sm_100 device */
+} pfrt_status;
+
+/* Output element types of the quantized path. */
+typedef enum pfrt_out_mode {
+    PFRT_OUT_F32 = 0, /* dequantized fp32 (quant_ops.cpp:464) */
+    PFRT_OUT_S8 = 1,  /* requantized int8 (quantize_tensor, quant_ops.cpp:42-47) */
+    PFRT_OUT_U8 = 2   /* requantized uint8 (quant_ops.cpp:49-54) */
+} pfrt_out_mode;
+
+typedef struct pfrt_ctx pfrt_ctx;
+typedef struct pfrt_qweight pfrt_qweight;
+typedef struct pfrt_fweight pfrt_fweight;
+typedef struct pfrt_csr pfrt_csr;
+/* A cudaStream_t.  NULL selects the context's own stream; CUDA's legacy
+ * default stream is (pfrt_stream)1 (cudaStreamLegacy). */
+typedef void* pfrt_stream;
+
+/* ------------------------------------------------------------ context
+ * Replaces the CPUExecutor construction in InferenceSession::select_backend
+ * (src/session.cpp:90-94): one context per device. */
+PFRT_API const char* pfrt_version(void);
+PFRT_API const char* pfrt_last_error(void);
+PFRT_API pfrt_status pfrt_device_count(int* count);
+PFRT_API pfrt_status pfrt_ctx_create(int device, pfrt_ctx** out);
+PFRT_API pfrt_status pfrt_ctx_destroy(pfrt_ctx* ctx);
+PFRT_API pfrt_status pfrt_ctx_stream(pfrt_ctx* ctx, pfrt_stream* out);
+PFRT_API pfrt_status pfrt_ctx_num_sms(pfrt_ctx* ctx, int* out);
+/* Synchronizes `stream` and reports device-side failures recorded since the
+ * last check (PFRT_ERR_DEVICE_TIMEOUT, PFRT_ERR_BAD_CSR); clears them. */
+PFRT_API pfrt_status pfrt_ctx_check(pfrt_ctx* ctx, pfrt_stream stream);
+
+/* ------------------------------------------------------------ memory
+ * Device and pinned host buffers, so that C callers need no CUDA headers.
+ * Copies are asynchronous on `stream` (pinned host memory for overlap). */
+PFRT_API pfrt_status pfrt_malloc(pfrt_ctx* ctx, size_t bytes, void** dptr);
+PFRT_API pfrt_status pfrt_free(pfrt_ctx* ctx, void* dptr);
+PFRT_API pfrt_status pfrt_host_alloc(pfrt_ctx* ctx, size_t bytes, void** hptr);
+PFRT_API pfrt_status pfrt_host_free(pfrt_ctx* ctx, void* hptr);
+PFRT_API pfrt_status pfrt_memcpy_h2d(pfrt_ctx* ctx, void* dst, const void* src, size_t bytes, pfrt_stream stream);
+PFRT_API pfrt_status pfrt_memcpy_d2h(pfrt_ctx* ctx, void* dst, const void* src, size_t bytes, pfrt_stream stream);
+PFRT_API pfrt_status pfrt_memcpy_d2d(pfrt_ctx* ctx, void* dst, const void* src, size_t bytes, pfrt_stream stream);
+PFRT_API pfrt_status pfrt_memset(pfrt_ctx* ctx, void* dst, int value, size_t bytes, pfrt_stream stream);
+
+/* ------------------------------------------------------------ fp32 Gemm / MatMul
+ * Replaces cpu_gemm (src/backends/cpu/ops/math.cpp:377-438) and the 2-D path
+ * of cpu_matmul (math.cpp:326-336):
+ *     Y[M,N] = alpha * op(A) * op(B) + beta * C[(m*N + n) % c_len]
+ * computed on tcgen05 tensor cores with the 3xTF32 split (hi*hi + hi*lo +
+ * lo*hi), which keeps the result within ~1e-6 relative of fp32.
+ *
+ * pfrt_fweight_create uploads and prepares a constant B operand (a graph
+ * initializer) once: B is [K,N] (trans_b = 0) or [N,K] (trans_b = 1) in HOST
+ * memory.  pfrt_gemm_f32 then takes device A ([M,K], or [K,M] if trans_a),
+ * optional device C of c_len elements (c_len = 0 or C = NULL: no bias), and
+ * writes device Y [M,N]. */
+PFRT_API pfrt_status pfrt_fweight_create(pfrt_ctx* ctx, int64_t K, int64_t N, int trans_b,
+                                const float* b_host, pfrt_fweight** out);
+PFRT_API pfrt_status pfrt_fweight_destroy(pfrt_fweight* w);
+PFRT_API pfrt_status pfrt_gemm_f32(pfrt_ctx* ctx, int64_t M, int trans_a, float alpha, const float* a,
+                          const pfrt_fweight* b, float beta, const float* c, int64_t c_len,
+                          float* y, pfrt_stream stream);
+/* Same with B a device matrix given per call (a graph input rather than an
+ * initializer); B is prepared into the context's scratch memory each call. */
+PFRT_API pfrt_status pfrt_gemm_f32_dense(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, int trans_a,
+                                int trans_b, float alpha, const float* a, const float* b,
+                                float beta, const float* c, int64_t c_len, float* y,
+                                pfrt_stream stream);
+
+/* ------------------------------------------------------------ quantized MatMul
+ * Replaces quantization::quantized_matmul + quantize_tensor
+ * (src/quantization/quant_ops.cpp:387-506, 15-127) and, fused, the Add (bias)
+ * and Relu that follow it (math.cpp:222-226, activation.cpp:45-60), with
+ * per-output-channel weight scales:
+ *     acc[m,n] = sum_k (a[m,k] - a_zp) * (w[k,n] - w_zp)       (exact int)
+ *     y        = (float)acc * (a_scale * w_scale[n])  [+ bias[n]]  [max(0,.)]
+ *     out      = y (PFRT_OUT_F32) or clamp(round(y / y_scale) + y_zp)
+ * Results are bit-identical to the reference CPU arithmetic.
+ *
+ * pfrt_qweight_create uploads int8 weights w [K,N] (the reference's B
+ * layout, HOST memory) once, with w_zp and n_scales = N per-channel scales
+ * (or 1 per-tensor scale).  K must be <= 65536 (the s32 tensor-core
+ * accumulator is exact up to there).
+ *
+ * pfrt_qlinear: a is device [M,K] uint8 (a_is_u8 = 1) or int8 with row
+ * stride lda elements (lda >= K); bias is device fp32 [N] or NULL; y is device
+ * [M,N] with row stride ldy elements, fp32 or int8/uint8 per out_mode;
+ * acc_out (device int32 [M,N], nullable) receives the exact accumulators. */
+PFRT_API pfrt_status pfrt_qweight_create(pfrt_ctx* ctx, int64_t K, int64_t N, const int8_t* w_host,
+                                int32_t w_zp, const float* w_scale_host, int64_t n_scales,
+                                pfrt_qweight** out);
+PFRT_API pfrt_status pfrt_qweight_destroy(pfrt_qweight* w);
+PFRT_API pfrt_status pfrt_qlinear(pfrt_ctx* ctx, const pfrt_qweight* w, int64_t M, const void* a,
+                         int64_t lda, int a_is_u8, float a_scale, int32_t a_zp,
+                         const float* bias, int relu, int out_mode, float y_scale, int32_t y_zp,
+                         void* y, int64_t ldy, int32_t* acc_out, pfrt_stream stream);
+
+/* ------------------------------------------------------------ CSR SpMM
+ * Replaces pruning::sparse_matmul (src/pruning/sparse_tensor.cpp:473-519) in
+ * the pruned-Linear orientation used by the SparseMatMul graph op:
+ *     Y[M,N] = X[M,K] * W^T,   W [N,K] in CSR (one CSR row per output channel)
+ * i.e. Y = transpose(sparse_matmul(W, X^T)).
+ *
+ * pfrt_csr_create validates and uploads a HOST CSR once: indptr [N+1] and
+ * indices [nnz] of int32 (index_bits = 32) or int64 (index_bits = 64), values
+ * fp32 [nnz].  It checks what SparseTensor::from_csr (:170-197) does not:
+ * indptr[0] = 0, indptr non-decreasing, indptr[N] = nnz, 0 <= index < K
+ * (PFRT_ERR_BAD_CSR otherwise).  The device copy uses int32 indices.
+ *
+ * pfrt_spmm: X device [M,K] (row stride ldx), Y device [M,N] (row stride ldy).
+ * pfrt_spmm_csr_f32: same on a caller-owned device CSR (int32); the kernel
+ * bounds-checks every index, skips out-of-range entries and reports
+ * PFRT_ERR_BAD_CSR through pfrt_ctx_check(). */
+PFRT_API pfrt_status pfrt_csr_create(pfrt_ctx* ctx, int64_t N, int64_t K, int64_t nnz,
+                            const void* indptr_host, const void* indices_host, int index_bits,
+                            const float* values_host, pfrt_csr** out);
+PFRT_API pfrt_status pfrt_csr_destroy(pfrt_csr* w);
+/* The host-side structure check of pfrt_csr_create on its own (no device
+ * needed): returns PFRT_OK or PFRT_ERR_BAD_CSR / PFRT_ERR_INVALID_ARGUMENT. */
+PFRT_API pfrt_status pfrt_csr_validate_host(int64_t N, int64_t K, int64_t nnz,
+                                            const void* indptr_host, const void* indices_host,
+                                            int index_bits);
+PFRT_API pfrt_status pfrt_csr_info(const pfrt_csr* w, int64_t* n, int64_t* k, int64_t* nnz);
+PFRT_API pfrt_status pfrt_spmm(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* x, int64_t ldx,
+                      float* y, int64_t ldy, pfrt_stream stream);
+PFRT_API pfrt_status pfrt_spmm_csr_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, int64_t nnz,
+                              const int32_t* indptr, const int32_t* indices,
+                              const float* values, const float* x, int64_t ldx, float* y,
+                              int64_t ldy, pfrt_stream stream);
+
+/* ------------------------------------------------------------ elementwise
+ * Standalone forms of the ops the backend normally fuses into epilogues:
+ * quantize_tensor per-tensor (quant_ops.cpp:33-55), bias Add broadcast over
+ * rows (math.cpp:222-226 for a [N] operand) and Relu (activation.cpp:45-60). */
+PFRT_API pfrt_status pfrt_quantize_f32(pfrt_ctx* ctx, int64_t n, const float* x, float scale, int32_t zp,
+                              int out_is_u8, void* q, pfrt_stream stream);
+PFRT_API pfrt_status pfrt_add_rowvec_f32(pfrt_ctx* ctx, int64_t rows, int64_t cols, const float* x,
+                                const float* b, float* y, pfrt_stream stream);
+PFRT_API pfrt_status pfrt_relu_f32(pfrt_ctx* ctx, int64_t n, const float* x, float* y,
+                          pfrt_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PFRT_CUDA_H */

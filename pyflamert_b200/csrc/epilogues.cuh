@@ -1,0 +1,216 @@
+// epilogues.cuh -- fused epilogues of the tcgen05 GEMM (umma_gemm.cuh) and
+// the matching split-K reductions.
+//
+// QEpi (int8 path) turns the raw s32 accumulator sum_k a*w into the
+// reference's quantized linear result (src/quantization/quant_ops.cpp):
+//   acc  = sum_k (a - a_zp)(w - w_zp)
+//        = raw - a_zp*colsum[n] - w_zp*rowsum[m] + K*a_zp*w_zp   (exact, int64)
+//   y    = (float)acc * (a_scale * w_scale[n])          quant_ops.cpp:435,464
+//   y    = y + bias[n]                                  math.cpp:225 (fused Add)
+//   y    = max(0, y)                                    activation.cpp:56 (fused Relu)
+//   q    = clamp((int)round(y * (1/y_scale)) + y_zp)    quant_ops.cpp:42-55
+// Every product and sum is rounded separately (__fmul_rn/__fadd_rn): no FMA
+// contraction, so the result is bit-identical to the reference CPU code.
+//
+// FEpi (fp32 path) applies cpu_gemm's tail (src/backends/cpu/ops/math.cpp:
+// 427-435): y = alpha*acc + beta*C[(m*N + n) % c_len].
+#pragma once
+
+#include "common.cuh"
+
+namespace pfrt {
+
+enum OutMode : int {
+    kOutF32 = 0,      // fp32 (dequantized) output
+    kOutS8 = 1,       // requantized int8
+    kOutU8 = 2,       // requantized uint8
+    kOutPartial = 3,  // raw split-K partial accumulators
+};
+
+// static_cast<int32_t>(float) as the reference's x86-64 build executes it
+// (cvttss2si): a value outside the int32 range, or NaN, becomes INT32_MIN.
+// The GPU's own conversion saturates instead, so the range test is explicit.
+__device__ __forceinline__ int32_t f2i_like_x86(float r) {
+    return (r >= -2147483648.0f && r < 2147483648.0f) ? static_cast<int32_t>(r) : INT32_MIN;
+}
+
+// quant_ops.cpp:44-46: clamp((int32)std::round(y * inv_scale) + zp, qmin, qmax),
+// with the int32 addition wrapping as it does on the reference's target.
+__device__ __forceinline__ int32_t requant_rn(float y, float inv_scale, int32_t zp, bool u8) {
+    const int32_t r = f2i_like_x86(roundf(__fmul_rn(y, inv_scale)));
+    const int32_t q = static_cast<int32_t>(static_cast<uint32_t>(r) + static_cast<uint32_t>(zp));
+    return u8 ? min(max(q, 0), 255) : min(max(q, -128), 127);
+}
+
+struct QEpi {
+    uint32_t idesc;
+    int M, N, K;
+    int a_zp, w_zp;
+    float a_scale;
+    const int32_t* colsum;  // [Npad] sum_k W[n,k]
+    const int32_t* rowsum;  // [M] sum_k A[m,k]; only read when w_zp != 0
+    const float* w_scale;   // [Npad]
+    const float* bias;      // [N] or null
+    int relu;
+    int out_mode;
+    float inv_y_scale;
+    int y_zp;
+    void* out;
+    int64_t ldo;            // output row stride, elements
+    int32_t* acc_out;       // [M, N] exact accumulators, or null
+    int32_t* partial;       // [splits][M][N] when out_mode == kOutPartial
+    int vec_ok;             // output rows 16-byte aligned for vector stores
+    int acc_vec_ok;         // acc_out 16-byte aligned and N % 4 == 0
+
+    // Exact accumulator and dequantized/biased/activated value of one element.
+    __device__ __forceinline__ float finalize(int row, int n, int64_t raw, int32_t rs,
+                                              int32_t& acc_true) const {
+        int64_t a = raw - static_cast<int64_t>(a_zp) * colsum[n];
+        if (w_zp != 0)
+            a += static_cast<int64_t>(K) * a_zp * w_zp - static_cast<int64_t>(w_zp) * rs;
+        acc_true = static_cast<int32_t>(a);
+        float y = __fmul_rn(__ll2float_rn(a), __fmul_rn(a_scale, w_scale[n]));
+        if (bias != nullptr && n < N) y = __fadd_rn(y, bias[n]);
+        if (relu) y = (0.0f < y) ? y : 0.0f;
+        return y;
+    }
+
+    __device__ __forceinline__ void emit(int row, int col0, const int32_t (&at)[32],
+                                         const float (&y)[32]) const {
+        const bool full = (col0 + 32 <= N);
+        if (acc_out != nullptr) {
+            int32_t* d = acc_out + static_cast<int64_t>(row) * N + col0;
+            if (full && acc_vec_ok) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<int4*>(d + j) = make_int4(at[j], at[j + 1], at[j + 2], at[j + 3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (col0 + j < N) d[j] = at[j];
+            }
+        }
+        if (out_mode == kOutF32) {
+            float* d = static_cast<float*>(out) + static_cast<int64_t>(row) * ldo + col0;
+            if (full && vec_ok) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4*>(d + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (col0 + j < N) d[j] = y[j];
+            }
+        } else {
+            const bool u8 = (out_mode == kOutU8);
+            uint8_t* d = static_cast<uint8_t*>(out) + static_cast<int64_t>(row) * ldo + col0;
+            uint32_t packed[8];
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+                uint32_t v = 0;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const uint32_t q = static_cast<uint32_t>(requant_rn(y[4 * w + b], inv_y_scale, y_zp, u8)) & 0xFFu;
+                    v |= q << (8 * b);
+                }
+                packed[w] = v;
+            }
+            if (full && vec_ok) {
+                *reinterpret_cast<uint4*>(d) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                *reinterpret_cast<uint4*>(d + 16) = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (col0 + j < N) d[j] = static_cast<uint8_t>((packed[j >> 2] >> (8 * (j & 3))) & 0xFFu);
+            }
+        }
+    }
+
+    __device__ __forceinline__ void store(int row, int col0, int ks, const uint32_t (&acc)[32]) const {
+        if (row >= M) return;
+        if (out_mode == kOutPartial) {
+            int32_t* d = partial + (static_cast<int64_t>(ks) * M + row) * N + col0;
+            if (col0 + 32 <= N && (N % 4) == 0) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<int4*>(d + j) =
+                        make_int4(static_cast<int>(acc[j]), static_cast<int>(acc[j + 1]),
+                                  static_cast<int>(acc[j + 2]), static_cast<int>(acc[j + 3]));
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (col0 + j < N) d[j] = static_cast<int32_t>(acc[j]);
+            }
+            return;
+        }
+        const int32_t rs = (w_zp != 0) ? rowsum[row] : 0;
+        int32_t at[32];
+        float y[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            y[j] = finalize(row, col0 + j, static_cast<int64_t>(static_cast<int32_t>(acc[j])), rs, at[j]);
+        emit(row, col0, at, y);
+    }
+};
+
+struct FEpi {
+    int M, N;
+    float alpha, beta;
+    const float* C;   // bias operand, flat length c_len, or null
+    int64_t c_len;
+    float* out;
+    int64_t ldo;
+    int out_mode;     // kOutF32 or kOutPartial
+    float* partial;   // [splits][M][N]
+    int vec_ok;
+
+    __device__ __forceinline__ float finalize(int row, int n, float acc) const {
+        float y = __fmul_rn(alpha, acc);
+        if (C != nullptr && n < N) {
+            const int64_t flat = static_cast<int64_t>(row) * N + n;
+            const int64_t ci = (c_len == N) ? n : (c_len == 1 ? 0 : flat % c_len);
+            y = __fadd_rn(y, __fmul_rn(beta, C[ci]));
+        }
+        return y;
+    }
+
+    __device__ __forceinline__ void store(int row, int col0, int ks, const uint32_t (&acc)[32]) const {
+        if (row >= M) return;
+        const bool full = (col0 + 32 <= N);
+        if (out_mode == kOutPartial) {
+            float* d = partial + (static_cast<int64_t>(ks) * M + row) * N + col0;
+            if (full && (N % 4) == 0) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4*>(d + j) =
+                        make_float4(__uint_as_float(acc[j]), __uint_as_float(acc[j + 1]),
+                                    __uint_as_float(acc[j + 2]), __uint_as_float(acc[j + 3]));
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (col0 + j < N) d[j] = __uint_as_float(acc[j]);
+            }
+            return;
+        }
+        float y[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) y[j] = finalize(row, col0 + j, __uint_as_float(acc[j]));
+        float* d = out + static_cast<int64_t>(row) * ldo + col0;
+        if (full && vec_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(d + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < N) d[j] = y[j];
+        }
+    }
+};
+
+// Split-K reductions: thread per output element, partial sums added in split
+// order, then the same finalisation as the single-pass epilogue.
+__global__ void q_splitk_reduce_kernel(const QEpi e, int splits);
+__global__ void f_splitk_reduce_kernel(const FEpi e, int splits);
+
+}  // namespace pfrt

@@ -1,0 +1,339 @@
+// gemm_f32.cu -- fp32 Gemm / MatMul on tcgen05 kind::tf32 with the 3xTF32
+// split.
+//
+// Replaces cpu_gemm (src/backends/cpu/ops/math.cpp:377-438) and the 2-D path
+// of cpu_matmul (:326-336).  Each fp32 operand x is split once into
+// hi = tf32(x) (round to nearest) and lo = x - hi (exact in fp32); the tensor
+// cores accumulate lo_a*hi_b + hi_a*lo_b + hi_a*hi_b in fp32, which recovers
+// close to fp32 accuracy (the dropped lo*lo term is ~2^-22 relative).
+//
+// The split writes both parts K-major ([rows, Kpad], Kpad = K rounded up to
+// 32 and zero padded), whatever the transA/transB of the input, so one GEMM
+// kernel serves all four transpose combinations.  A constant B (a graph
+// initializer) is split once by pfrt_fweight_create.
+#include <algorithm>
+#include <cstdlib>
+#include <string>
+
+#include "epilogues.cuh"
+#include "internal.hpp"
+#include "umma_gemm.cuh"
+
+struct pfrt_fweight {
+    pfrt_ctx* ctx = nullptr;
+    int64_t K = 0, N = 0, Kpad = 0;
+    float* hi = nullptr;  // [N, Kpad]
+    float* lo = nullptr;  // [N, Kpad]
+    CUtensorMap tm_hi{}, tm_lo{};
+};
+
+namespace pfrt {
+
+constexpr int kF32BN = 128;
+constexpr int kF32Stages = 3;
+
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+    uint32_t h;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+    hi = __uint_as_float(h);
+    lo = __fsub_rn(x, hi);
+}
+
+// out_{hi,lo}[r, k] = split(src(r, k)) for k < K, 0 for K <= k < Kpad, where
+// src(r, k) = src[r*ld + k] (trans = 0) or src[k*ld + r] (trans = 1).
+// 32x32 tiles through shared memory keep both sides coalesced for trans = 1.
+__global__ void split_kmajor_kernel(const float* __restrict__ src, int64_t rows, int64_t K,
+                                    int64_t ld, int trans, float* __restrict__ hi,
+                                    float* __restrict__ lo, int64_t Kpad) {
+    __shared__ float tile[32][33];
+    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32;
+    const int64_t k0 = static_cast<int64_t>(blockIdx.x) * 32;
+    if (trans) {
+        for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+            const int64_t k = k0 + i, r = r0 + threadIdx.x;
+            tile[i][threadIdx.x] = (k < K && r < rows) ? src[k * ld + r] : 0.0f;
+        }
+        __syncthreads();
+        for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+            const int64_t r = r0 + i, k = k0 + threadIdx.x;
+            if (r < rows && k < Kpad) {
+                float h, l;
+                split_tf32(tile[threadIdx.x][i], h, l);
+                hi[r * Kpad + k] = h;
+                lo[r * Kpad + k] = l;
+            }
+        }
+    } else {
+        for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+            const int64_t r = r0 + i, k = k0 + threadIdx.x;
+            if (r < rows && k < Kpad) {
+                const float x = (k < K) ? src[r * ld + k] : 0.0f;
+                float h, l;
+                split_tf32(x, h, l);
+                hi[r * Kpad + k] = h;
+                lo[r * Kpad + k] = l;
+            }
+        }
+    }
+}
+
+__global__ void f_splitk_reduce_kernel(const FEpi e, int splits) {
+    const int chunks = (e.N + 31) / 32;
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<int64_t>(e.M) * chunks) return;
+    const int row = static_cast<int>(idx / chunks);
+    const int col0 = static_cast<int>(idx % chunks) * 32;
+    uint32_t acc[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        float s = 0.0f;
+        if (col0 + j < e.N)
+            for (int k = 0; k < splits; ++k)
+                s = __fadd_rn(s, e.partial[(static_cast<int64_t>(k) * e.M + row) * e.N + col0 + j]);
+        acc[j] = __float_as_uint(s);
+    }
+    FEpi fin = e;
+    fin.out_mode = kOutF32;
+    fin.store(row, col0, 0, acc);
+}
+
+namespace {
+
+int env_int(const char* name, int dflt) {
+    const char* v = std::getenv(name);
+    return (v && *v) ? std::atoi(v) : dflt;
+}
+
+pfrt_status launch_split(const float* src, int64_t rows, int64_t K, int64_t ld, int trans,
+                         float* hi, float* lo, int64_t Kpad, cudaStream_t s) {
+    dim3 tb(32, 8);
+    dim3 tg(static_cast<unsigned>(ceil_div(Kpad, 32)), static_cast<unsigned>(ceil_div(rows, 32)));
+    split_kmajor_kernel<<<tg, tb, 0, s>>>(src, rows, K, ld, trans, hi, lo, Kpad);
+    PFRT_CHECK_LAUNCH("split_kmajor_kernel");
+    return PFRT_OK;
+}
+
+// Runs the GEMM on prepared K-major hi/lo operands.
+pfrt_status run_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad, const CUtensorMap& tmAh,
+                    const CUtensorMap& tmAl, const CUtensorMap& tmBh, const CUtensorMap& tmBl,
+                    float alpha, float beta, const float* c, int64_t c_len, float* y,
+                    void* scratch_tail, size_t tail_bytes, cudaStream_t s) {
+    using Cfg = GemmCfg<KIND_TF32X3, kF32BN, kF32Stages>;
+    const int64_t mblk = ceil_div(M, 128), nblk = ceil_div(N, kF32BN);
+    const int64_t tiles = mblk * nblk;
+    const int kb_total = static_cast<int>(ceil_div(Kpad, Cfg::BK));
+    int splits = 1;
+    if (tiles * 2 <= ctx->num_sms) splits = static_cast<int>(std::min<int64_t>(ctx->num_sms / tiles, kb_total / 4));
+    splits = env_int("PFRT_GEMM_SPLITS", splits);
+    splits = std::max(1, std::min(splits, kb_total));
+    const int kb_per = static_cast<int>(ceil_div(kb_total, splits));
+    splits = static_cast<int>(ceil_div(kb_total, kb_per));
+    if (splits > 1 && sizeof(float) * splits * M * N > tail_bytes)
+        return fail(PFRT_ERR_INVALID_ARGUMENT, "internal: split-K scratch too small");
+
+    FEpi e{};
+    e.M = static_cast<int>(M);
+    e.N = static_cast<int>(N);
+    e.alpha = alpha;
+    e.beta = beta;
+    e.C = (c != nullptr && c_len > 0) ? c : nullptr;
+    e.c_len = c_len;
+    e.out = y;
+    e.ldo = N;
+    e.out_mode = kOutF32;
+    e.vec_ok = ((reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (N % 4) == 0) ? 1 : 0;
+    FEpi eg = e;
+    if (splits > 1) {
+        eg.out_mode = kOutPartial;
+        eg.partial = static_cast<float*>(scratch_tail);
+        e.partial = eg.partial;
+    }
+    GemmSched sched{};
+    sched.num_m_blk = static_cast<int>(mblk);
+    sched.num_n_blk = static_cast<int>(nblk);
+    sched.splits = splits;
+    sched.kb_total = kb_total;
+    sched.kb_per_split = kb_per;
+    sched.num_units = static_cast<int>(mblk * nblk * splits);
+
+    auto kern = umma_gemm_kernel<KIND_TF32X3, kF32BN, kF32Stages, FEpi>;
+    PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Cfg::SMEM_BYTES));
+    const int grid = std::min(sched.num_units, ctx->num_sms);
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(tmAh, tmBh, tmAl, tmBl, sched, eg, ctx->d_err);
+    PFRT_CHECK_LAUNCH("umma_gemm_kernel<tf32x3>");
+    if (splits > 1) {
+        const int64_t threads = M * ceil_div(N, 32);
+        f_splitk_reduce_kernel<<<static_cast<unsigned>(ceil_div(threads, 128)), 128, 0, s>>>(e, splits);
+        PFRT_CHECK_LAUNCH("f_splitk_reduce_kernel");
+    }
+    return PFRT_OK;
+}
+
+size_t splitk_bytes(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad) {
+    // Upper bound of the split-K partial buffer run_f32 may ask for.
+    const int64_t tiles = ceil_div(M, 128) * ceil_div(N, kF32BN);
+    const int64_t kb_total = ceil_div(Kpad, 32);
+    int64_t splits = 1;
+    if (tiles * 2 <= ctx->num_sms) splits = std::min<int64_t>(ctx->num_sms / tiles, kb_total / 4);
+    splits = std::max<int64_t>(1, env_int("PFRT_GEMM_SPLITS", static_cast<int>(splits)));
+    splits = std::min<int64_t>(splits, kb_total);
+    return splits > 1 ? align_up(sizeof(float) * splits * M * N, 256) : 0;
+}
+
+pfrt_status check_common(int64_t M, int64_t N, int64_t K, const float* a, float* y) {
+    if (M < 0 || N < 0 || K < 0) return fail(PFRT_ERR_INVALID_ARGUMENT, "Gemm: negative dimension");
+    if (M > (int64_t{1} << 31) - 256 || N > (int64_t{1} << 31) - 256)
+        return fail(PFRT_ERR_UNSUPPORTED, "Gemm: dimension too large");
+    if ((M > 0 && N > 0) && (!y || (K > 0 && !a)))
+        return fail(PFRT_ERR_INVALID_ARGUMENT, "Gemm: null input or output");
+    return PFRT_OK;
+}
+
+// K == 0: the product is empty and Y = beta*C (or 0).  Reuses the reduction
+// kernel with zero splits.
+pfrt_status run_empty_k(int64_t M, int64_t N, float alpha, float beta, const float* c,
+                        int64_t c_len, float* y, cudaStream_t s) {
+    FEpi e{};
+    e.M = static_cast<int>(M);
+    e.N = static_cast<int>(N);
+    e.alpha = alpha;
+    e.beta = beta;
+    e.C = (c != nullptr && c_len > 0) ? c : nullptr;
+    e.c_len = c_len;
+    e.out = y;
+    e.ldo = N;
+    e.out_mode = kOutF32;
+    e.vec_ok = 0;
+    const int64_t threads = M * ceil_div(N, 32);
+    f_splitk_reduce_kernel<<<static_cast<unsigned>(ceil_div(threads, 128)), 128, 0, s>>>(e, 0);
+    PFRT_CHECK_LAUNCH("f_splitk_reduce_kernel");
+    return PFRT_OK;
+}
+
+}  // namespace
+}  // namespace pfrt
+
+using namespace pfrt;
+
+extern "C" {
+
+pfrt_status pfrt_fweight_create(pfrt_ctx* ctx, int64_t K, int64_t N, int trans_b,
+                                const float* b_host, pfrt_fweight** out) {
+    pfrt_status st = enter(ctx);
+    if (st) return st;
+    if (!out || !b_host) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_fweight_create: null argument");
+    *out = nullptr;
+    if (K <= 0 || N <= 0)
+        return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_fweight_create: K and N must be positive");
+    auto* w = new pfrt_fweight();
+    w->ctx = ctx;
+    w->K = K;
+    w->N = N;
+    w->Kpad = static_cast<int64_t>(align_up(K, 32));
+    float* staging = nullptr;
+    auto cleanup = [&](pfrt_status s) {
+        if (staging) cudaFree(staging);
+        if (s != PFRT_OK) pfrt_fweight_destroy(w);
+        return s;
+    };
+    const size_t n_el = static_cast<size_t>(N * w->Kpad);
+    cudaError_t e = cudaMalloc(&w->hi, sizeof(float) * n_el);
+    if (e == cudaSuccess) e = cudaMalloc(&w->lo, sizeof(float) * n_el);
+    if (e == cudaSuccess) e = cudaMalloc(&staging, sizeof(float) * K * N);
+    if (e == cudaSuccess) e = cudaMemcpy(staging, b_host, sizeof(float) * K * N, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "pfrt_fweight_create"));
+    // B [K,N] (trans_b = 0) is the transposed view of the K-major [N,K] we want.
+    st = launch_split(staging, N, K, trans_b ? K : N, trans_b ? 0 : 1, w->hi, w->lo, w->Kpad,
+                      ctx->stream);
+    if (st) return cleanup(st);
+    e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "pfrt_fweight_create split"));
+    st = make_tmap_2d(&w->tm_hi, w->hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, w->Kpad, N,
+                      w->Kpad * 4, 32, kF32BN);
+    if (st == PFRT_OK)
+        st = make_tmap_2d(&w->tm_lo, w->lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, w->Kpad, N,
+                          w->Kpad * 4, 32, kF32BN);
+    if (st) return cleanup(st);
+    *out = w;
+    return cleanup(PFRT_OK);
+}
+
+pfrt_status pfrt_fweight_destroy(pfrt_fweight* w) {
+    if (!w) return PFRT_OK;
+    if (w->ctx) cudaSetDevice(w->ctx->device);
+    if (w->hi) cudaFree(w->hi);
+    if (w->lo) cudaFree(w->lo);
+    delete w;
+    return PFRT_OK;
+}
+
+pfrt_status pfrt_gemm_f32(pfrt_ctx* ctx, int64_t M, int trans_a, float alpha, const float* a,
+                          const pfrt_fweight* b, float beta, const float* c, int64_t c_len,
+                          float* y, pfrt_stream stream) {
+    pfrt_status st = enter(ctx);
+    if (st) return st;
+    if (!b) return fail(PFRT_ERR_INVALID_ARGUMENT, "Gemm: null weight");
+    if (b->ctx != ctx) return fail(PFRT_ERR_INVALID_ARGUMENT, "Gemm: weight belongs to another context");
+    const int64_t N = b->N, K = b->K;
+    st = check_common(M, N, K, a, y);
+    if (st) return st;
+    if (M == 0) return PFRT_OK;
+    cudaStream_t s = pick_stream(ctx, stream);
+    const size_t part_bytes = align_up(sizeof(float) * M * b->Kpad, 256);
+    const size_t tail = splitk_bytes(ctx, M, N, b->Kpad);
+    void* scr = nullptr;
+    st = scratch(ctx, 2 * part_bytes + tail, &scr);
+    if (st) return st;
+    float* ahi = static_cast<float*>(scr);
+    float* alo = reinterpret_cast<float*>(static_cast<uint8_t*>(scr) + part_bytes);
+    st = launch_split(a, M, K, trans_a ? M : K, trans_a, ahi, alo, b->Kpad, s);
+    if (st) return st;
+    CUtensorMap tah, tal;
+    st = make_tmap_2d(&tah, ahi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, b->Kpad, M, b->Kpad * 4, 32, 128);
+    if (st == PFRT_OK)
+        st = make_tmap_2d(&tal, alo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, b->Kpad, M, b->Kpad * 4, 32, 128);
+    if (st) return st;
+    return run_f32(ctx, M, N, b->Kpad, tah, tal, b->tm_hi, b->tm_lo, alpha, beta, c, c_len, y,
+                   static_cast<uint8_t*>(scr) + 2 * part_bytes, tail, s);
+}
+
+pfrt_status pfrt_gemm_f32_dense(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, int trans_a,
+                                int trans_b, float alpha, const float* a, const float* b,
+                                float beta, const float* c, int64_t c_len, float* y,
+                                pfrt_stream stream) {
+    pfrt_status st = enter(ctx);
+    if (st) return st;
+    st = check_common(M, N, K, a, y);
+    if (st) return st;
+    if (M == 0 || N == 0) return PFRT_OK;
+    cudaStream_t s = pick_stream(ctx, stream);
+    if (K == 0) return run_empty_k(M, N, alpha, beta, c, c_len, y, s);
+    if (!b) return fail(PFRT_ERR_INVALID_ARGUMENT, "Gemm: null B");
+    const int64_t Kpad = static_cast<int64_t>(align_up(K, 32));
+    const size_t pa = align_up(sizeof(float) * M * Kpad, 256);
+    const size_t pb = align_up(sizeof(float) * N * Kpad, 256);
+    const size_t tail = splitk_bytes(ctx, M, N, Kpad);
+    void* scr = nullptr;
+    st = scratch(ctx, 2 * pa + 2 * pb + tail, &scr);
+    if (st) return st;
+    uint8_t* base = static_cast<uint8_t*>(scr);
+    float* ahi = reinterpret_cast<float*>(base);
+    float* alo = reinterpret_cast<float*>(base + pa);
+    float* bhi = reinterpret_cast<float*>(base + 2 * pa);
+    float* blo = reinterpret_cast<float*>(base + 2 * pa + pb);
+    st = launch_split(a, M, K, trans_a ? M : K, trans_a, ahi, alo, Kpad, s);
+    if (st) return st;
+    st = launch_split(b, N, K, trans_b ? K : N, trans_b ? 0 : 1, bhi, blo, Kpad, s);
+    if (st) return st;
+    CUtensorMap tah, tal, tbh, tbl;
+    st = make_tmap_2d(&tah, ahi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Kpad, M, Kpad * 4, 32, 128);
+    if (!st) st = make_tmap_2d(&tal, alo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Kpad, M, Kpad * 4, 32, 128);
+    if (!st) st = make_tmap_2d(&tbh, bhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Kpad, N, Kpad * 4, 32, kF32BN);
+    if (!st) st = make_tmap_2d(&tbl, blo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Kpad, N, Kpad * 4, 32, kF32BN);
+    if (st) return st;
+    return run_f32(ctx, M, N, Kpad, tah, tal, tbh, tbl, alpha, beta, c, c_len, y,
+                   base + 2 * pa + 2 * pb, tail, s);
+}
+
+}  // extern "C"

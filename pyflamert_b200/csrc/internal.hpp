@@ -1,0 +1,60 @@
+// internal.hpp -- host-side plumbing shared by the C-ABI translation units:
+// the context object, error reporting, scratch memory and TMA descriptors.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "pfrt_cuda.h"
+
+struct pfrt_ctx {
+    int device = 0;
+    int num_sms = 0;
+    int cc_major = 0, cc_minor = 0;
+    cudaStream_t stream = nullptr;
+    int* d_err = nullptr;       // device error word (pfrt::DeviceError)
+    void* scratch = nullptr;    // grow-only scratch arena
+    size_t scratch_cap = 0;
+};
+
+namespace pfrt {
+
+// Records `msg` as this thread's last error and returns `st`.
+pfrt_status fail(pfrt_status st, const std::string& msg);
+// Maps a CUDA error to PFRT_ERR_CUDA / PFRT_ERR_OUT_OF_MEMORY with context.
+pfrt_status cuda_fail(cudaError_t e, const char* what);
+
+#define PFRT_CUDA_TRY(expr)                                 \
+    do {                                                    \
+        cudaError_t e__ = (expr);                           \
+        if (e__ != cudaSuccess) return ::pfrt::cuda_fail(e__, #expr); \
+    } while (0)
+
+#define PFRT_CHECK_LAUNCH(what)                             \
+    do {                                                    \
+        cudaError_t e__ = cudaGetLastError();               \
+        if (e__ != cudaSuccess) return ::pfrt::cuda_fail(e__, what); \
+    } while (0)
+
+// Makes the context's device current for the calling thread.
+pfrt_status enter(pfrt_ctx* ctx);
+cudaStream_t pick_stream(pfrt_ctx* ctx, pfrt_stream s);
+
+// Returns a pointer to at least `bytes` of scratch device memory owned by the
+// context.  Growing it synchronizes the device.  The memory is shared by all
+// calls on the context.
+pfrt_status scratch(pfrt_ctx* ctx, size_t bytes, void** out);
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// 2-D K-major tensor map with 128-byte swizzle:
+// global [rows, cols] with row stride `ld_bytes`, box [box_rows, 128 bytes].
+pfrt_status make_tmap_2d(CUtensorMap* tm, const void* base, CUtensorMapDataType dt, int elem_bytes,
+                         uint64_t cols, uint64_t rows, uint64_t ld_bytes, uint32_t box_cols,
+                         uint32_t box_rows);
+
+}  // namespace pfrt

@@ -1,0 +1,276 @@
+// umma_gemm.cuh -- persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   D[M,N] = A[M,K] * B[N,K]^T      (both operands K-major in global memory)
+//
+// One CTA per SM, 192 threads:
+//   warp 0      TMA producer   (one lane)  -- global -> shared, STAGES-deep ring
+//   warp 1      MMA issuer     (one lane)  -- tcgen05.mma into TMEM; also owns
+//                                             the TMEM allocation
+//   warps 2..5  epilogue       (128 threads) -- tcgen05.ld TMEM -> registers,
+//                                             fused epilogue, global stores
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
+// of one tile overlaps the MMAs of the next.
+//
+// Two element kinds share the pipeline:
+//   KIND_I8    A uint8/int8, B int8, s32 accumulate; BK = 128 bytes = 128 elems,
+//              UMMA K = 32, one A and one B tile per stage.
+//   KIND_TF32X3  fp32 operands pre-split into hi/lo tf32 parts; per UMMA K-step
+//              three MMAs lo*hi + hi*lo + hi*hi (the "3xTF32" scheme) so the
+//              product keeps ~fp32 accuracy; BK = 32 elems, UMMA K = 8, two A
+//              and two B tiles per stage.
+//
+// Work unit = (m block, n block, k split).  With k_splits > 1 the epilogue
+// writes raw partial accumulators and a separate reduction applies the final
+// epilogue.  No cluster launch and no TMA multicast: each CTA loads its own
+// tiles, so the same binary is safe in multi-GPU jobs.
+#pragma once
+
+#include "common.cuh"
+
+namespace pfrt {
+
+constexpr int KIND_I8 = 0;
+constexpr int KIND_TF32X3 = 1;
+
+struct GemmSched {
+    int num_m_blk;
+    int num_n_blk;
+    int splits;        // k splits per (m,n) tile
+    int kb_total;      // number of BK blocks covering K
+    int kb_per_split;  // BK blocks per split (the last split may have fewer)
+    int num_units;     // num_m_blk * num_n_blk * splits
+};
+
+template <int KIND, int BN, int STAGES>
+struct GemmCfg {
+    static constexpr int BM = 128;
+    static constexpr int BK_BYTES = 128;
+    static constexpr int ELEM = (KIND == KIND_I8) ? 1 : 4;
+    static constexpr int BK = BK_BYTES / ELEM;
+    static constexpr int UMMA_K = (KIND == KIND_I8) ? 32 : 8;
+    static constexpr int NPARTS = (KIND == KIND_I8) ? 1 : 2;
+    static constexpr int A_TILE = BM * BK_BYTES;
+    static constexpr int B_TILE = BN * BK_BYTES;
+    static constexpr int STAGE_BYTES = NPARTS * (A_TILE + B_TILE);
+    static constexpr uint32_t TMEM_COLS = 2 * BN;
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    static constexpr int THREADS = 192;
+    static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns must be a power of two");
+    static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+    static_assert(STAGES <= 8, "stages");
+};
+
+__device__ __forceinline__ void decode_unit(const GemmSched& s, int unit, int& mb, int& nb, int& ks) {
+    ks = unit % s.splits;
+    const int t = unit / s.splits;
+    mb = t % s.num_m_blk;
+    nb = t / s.num_m_blk;
+}
+
+// Epi must provide:
+//   __device__ void store(int row, int col0, int ks, const uint32_t (&acc)[32]) const;
+// row is the global row of this thread; col0 the first of 32 consecutive
+// global columns held in acc (raw 32-bit accumulator bits).
+template <int KIND, int BN, int STAGES, class Epi>
+__global__ void __launch_bounds__(192, 1)
+    umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA0,
+                     const __grid_constant__ CUtensorMap tmB0,
+                     const __grid_constant__ CUtensorMap tmA1,
+                     const __grid_constant__ CUtensorMap tmB1, const GemmSched sched,
+                     const Epi epi, int* err) {
+    using Cfg = GemmCfg<KIND, BN, STAGES>;
+    constexpr int BM = Cfg::BM;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* tiles = smem;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], 128);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tmA0);
+            tma_prefetch_desc(&tmB0);
+            if (Cfg::NPARTS == 2) {
+                tma_prefetch_desc(&tmA1);
+                tma_prefetch_desc(&tmB1);
+            }
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued = 0;          // stages with a load issued
+            uint32_t last_par[STAGES];    // parity of the last load issued per stage
+            bool ok = true;
+            for (int unit = blockIdx.x; ok && unit < sched.num_units; unit += gridDim.x) {
+                int mb, nb, ks;
+                decode_unit(sched, unit, mb, nb, ks);
+                const int kb0 = ks * sched.kb_per_split;
+                const int kb1 = min(kb0 + sched.kb_per_split, sched.kb_total);
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+                    uint8_t* st = tiles + stage * Cfg::STAGE_BYTES;
+                    const int kx = kb * Cfg::BK;
+                    tma_load_2d(st, &tmA0, &full[stage], kx, mb * BM);
+                    tma_load_2d(st + Cfg::NPARTS * Cfg::A_TILE, &tmB0, &full[stage], kx, nb * BN);
+                    if constexpr (Cfg::NPARTS == 2) {
+                        tma_load_2d(st + Cfg::A_TILE, &tmA1, &full[stage], kx, mb * BM);
+                        tma_load_2d(st + 2 * Cfg::A_TILE + Cfg::B_TILE, &tmB1, &full[stage], kx,
+                                    nb * BN);
+                    }
+                    issued |= 1u << stage;
+                    last_par[stage] = phase;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                report_error(err, kDevWaitTimeout);
+                // Let every copy already issued land before the CTA can exit.
+                const int zero = 0;
+                for (int s = 0; s < STAGES; ++s)
+                    if (issued & (1u << s)) mbar_wait(&full[s], last_par[s], &zero);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            uint32_t idesc;
+            if constexpr (KIND == KIND_I8) idesc = epi.idesc;
+            else idesc = idesc_make(1, 2, 2, BM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int t = 0;
+            for (int unit = blockIdx.x; ok && unit < sched.num_units; unit += gridDim.x, ++t) {
+                int mb, nb, ks;
+                decode_unit(sched, unit, mb, nb, ks);
+                const int kb0 = ks * sched.kb_per_split;
+                const int kb1 = min(kb0 + sched.kb_per_split, sched.kb_total);
+                const int slot = t & 1;
+                const uint32_t ap = static_cast<uint32_t>(t >> 1) & 1u;
+                if (!mbar_wait(&tempty[slot], ap ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot * BN);
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t st = smem_u32(tiles + stage * Cfg::STAGE_BYTES);
+                    if constexpr (KIND == KIND_I8) {
+                        const uint64_t da = sdesc_kmajor_sw128(st);
+                        const uint64_t db = sdesc_kmajor_sw128(st + Cfg::A_TILE);
+#pragma unroll
+                        for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
+                            const uint64_t koff = static_cast<uint64_t>((k * Cfg::UMMA_K * Cfg::ELEM) >> 4);
+                            umma_i8(d_tmem, da + koff, db + koff, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+                        }
+                    } else {
+                        const uint64_t dah = sdesc_kmajor_sw128(st);
+                        const uint64_t dal = sdesc_kmajor_sw128(st + Cfg::A_TILE);
+                        const uint64_t dbh = sdesc_kmajor_sw128(st + 2 * Cfg::A_TILE);
+                        const uint64_t dbl = sdesc_kmajor_sw128(st + 2 * Cfg::A_TILE + Cfg::B_TILE);
+#pragma unroll
+                        for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
+                            const uint64_t koff = static_cast<uint64_t>((k * Cfg::UMMA_K * Cfg::ELEM) >> 4);
+                            const uint32_t acc0 = (kb > kb0 || k > 0) ? 1u : 0u;
+                            umma_tf32(d_tmem, dal + koff, dbh + koff, idesc, acc0);
+                            umma_tf32(d_tmem, dah + koff, dbl + koff, idesc, 1u);
+                            umma_tf32(d_tmem, dah + koff, dbh + koff, idesc, 1u);
+                        }
+                    }
+                    umma_commit(&empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(&tfull[slot]);
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                report_error(err, kDevWaitTimeout);
+            }
+            // Every MMA issued so far must finish before TMEM is released.
+            umma_commit(drain);
+            const int zero = 0;
+            mbar_wait(drain, 0, &zero);
+        }
+    } else {
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        int t = 0;
+        for (int unit = blockIdx.x; unit < sched.num_units; unit += gridDim.x, ++t) {
+            int mb, nb, ks;
+            decode_unit(sched, unit, mb, nb, ks);
+            const int slot = t & 1;
+            const uint32_t ap = static_cast<uint32_t>(t >> 1) & 1u;
+            // Warp-uniform decision: tcgen05.ld below needs the whole warp.
+            const bool got = __all_sync(0xffffffffu, mbar_wait(&tfull[slot], ap, abort_flag));
+            if (!got) {
+                *abort_flag = 1;
+                report_error(err, kDevWaitTimeout);
+                break;
+            }
+            tc_fence_after();
+            const int row = mb * BM + q * 32 + lane;
+            const uint32_t taddr =
+                tmem_base + static_cast<uint32_t>(slot * BN) + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t acc[32];
+                tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), acc);
+                tmem_ld_wait();
+                epi.store(row, nb * BN + c * 32, ks, acc);
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[slot]);
+        }
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    }
+}
+
+}  // namespace pfrt

@@ -1,0 +1,109 @@
+"""CSR SpMM on the GPU vs pruning::sparse_matmul
+(src/pruning/sparse_tensor.cpp:473-519) in the pruned-Linear orientation
+Y = X W^T.  Summation order differs, so parity is normwise <= 1e-5."""
+import numpy as np
+import pytest
+import torch
+
+import pyflamert_b200 as pf
+from oracle import pyoracle as po
+from pyflamert_b200 import workloads as wl
+from tests.golden import cases as gcases
+from tests.helpers import FP32_TOL, normwise_rel
+
+pytestmark = pytest.mark.gpu
+
+
+def gpu(ctx, c: wl.CsrCase, X=None):
+    X = c.X if X is None else X
+    w = pf.CSR(ctx, c.N, c.K, c.indptr, c.indices, c.values)
+    y = w(torch.from_numpy(np.ascontiguousarray(X)).cuda())
+    ctx.check()
+    return y.cpu().numpy()
+
+
+def oracle(c: wl.CsrCase, X=None):
+    X = c.X if X is None else X
+    return po.spmm_linear(c.indptr, c.indices, c.values, X, c.N)
+
+
+@pytest.mark.parametrize("name", [n for n, c in gcases.all_cases().items() if c["kind"] == "spmm"])
+def test_golden(ctx, golden, name):
+    case = gcases.all_cases()[name]
+    c = case["case"]
+    rows = case.get("rows", c.X.shape[0])
+    y = gpu(ctx, c, c.X[:rows])
+    assert normwise_rel(y, golden[0][name]) <= FP32_TOL
+
+
+def test_config3_full(ctx):
+    c = wl.spmm_case()
+    y = gpu(ctx, c)
+    ref = oracle(c)
+    assert normwise_rel(y, ref) <= FP32_TOL
+    f64 = po.spmm_linear_f64(c.indptr, c.indices, c.values, c.X, c.N)
+    assert normwise_rel(y, f64) <= 2 * normwise_rel(ref, f64) + 1e-6
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 9, 31, 64, 130])
+def test_batch_sizes(ctx, M):
+    c = wl.spmm_case(M, 300, 700, sparsity=0.9, seed=M)
+    assert normwise_rel(gpu(ctx, c), oracle(c)) <= FP32_TOL
+
+
+@pytest.mark.parametrize("sparsity", [0.5, 0.7, 0.9, 0.95])
+@pytest.mark.parametrize("M", [1, 64, 1024])
+def test_config5_sweep(ctx, sparsity, M):
+    """Config 5 weights (8192 x 8192); the oracle checks 8 rows of the output."""
+    c = wl.spmm_case(M, 8192, 8192, sparsity=sparsity, seed=50 + int(sparsity * 100))
+    y = gpu(ctx, c)
+    rows = np.unique(np.r_[0:4, M - 4:M].clip(0, M - 1))
+    ref = oracle(c, c.X[rows])
+    assert normwise_rel(y[rows], ref) <= FP32_TOL
+    assert np.isfinite(y).all()
+
+
+def test_empty_rows_and_unaligned_starts(ctx):
+    rng = np.random.default_rng(5)
+    N, K, M = 97, 211, 6
+    counts = rng.integers(0, 9, N)
+    counts[::7] = 0
+    indptr = np.zeros(N + 1, np.int64)
+    indptr[1:] = np.cumsum(counts)
+    indices = np.concatenate([np.sort(rng.choice(K, k, replace=False)) for k in counts]).astype(np.int64)
+    values = rng.standard_normal(indices.size).astype(np.float32)
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    c = wl.CsrCase(N, K, indptr.astype(np.int32), indices.astype(np.int32), values, X)
+    y = gpu(ctx, c)
+    assert normwise_rel(y, oracle(c)) <= FP32_TOL
+    np.testing.assert_array_equal(y[:, counts == 0], 0.0)
+
+
+def test_no_nonzeros(ctx):
+    c = wl.CsrCase(5, 8, np.zeros(6, np.int32), np.zeros(0, np.int32), np.zeros(0, np.float32),
+                   np.ones((3, 8), np.float32))
+    np.testing.assert_array_equal(gpu(ctx, c), np.zeros((3, 5), np.float32))
+
+
+def test_bad_csr_rejected_on_upload(ctx):
+    with pytest.raises(pf.PfrtError, match="out of range"):
+        pf.CSR(ctx, 2, 4, np.array([0, 1, 2], np.int32), np.array([0, 4], np.int32), np.ones(2, np.float32))
+    with pytest.raises(pf.PfrtError, match="indptr"):
+        pf.CSR(ctx, 2, 4, np.array([0, 2, 1], np.int32), np.array([0, 1], np.int32), np.ones(2, np.float32))
+
+
+def test_raw_api_bad_index_is_skipped_and_reported(ctx):
+    """A caller-owned device CSR with an index >= K: the kernel skips it (no
+    out-of-bounds read) and pfrt_ctx_check reports PFRT_ERR_BAD_CSR."""
+    indptr = torch.tensor([0, 2, 4], dtype=torch.int32, device="cuda")
+    indices = torch.tensor([0, 3, 1, 99], dtype=torch.int32, device="cuda")
+    values = torch.tensor([1.0, 2.0, 3.0, 4.0], dtype=torch.float32, device="cuda")
+    x = torch.arange(8, dtype=torch.float32, device="cuda").reshape(2, 4)
+    y = ctx.spmm_csr_raw(2, 2, 4, 4, indptr, indices, values, x)
+    with pytest.raises(pf.PfrtError) as ei:
+        ctx.check()
+    assert ei.value.status == 2
+    yy = y.cpu().numpy()
+    np.testing.assert_array_equal(yy[:, 0], x.cpu().numpy() @ np.array([1, 0, 0, 2], np.float32))
+    np.testing.assert_array_equal(yy[:, 1], x.cpu().numpy()[:, 1] * 3.0)
+    ctx.check()  # the error was cleared
