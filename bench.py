@@ -1,0 +1,466 @@
+"""Benchmark of the PyFlameRT MatMul/Gemm hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload (the configuration the metric is
+quoted on): the quantized int8 linear layer, uint8 activations [512, 4096] x
+int8 weights [4096, 4096], int32 accumulation, per-output-channel scales,
+requantized to int8.  One step = one pass over one batch.  At N GPUs each rank
+processes its own 512-row batch (batch sharding, no collective: weak scaling)
+and `value` is the whole-job TOPS: N * 2*M*N*K ops / max-over-ranks time.
+
+Timing: W warm-up steps, then K steps captured in a CUDA graph and replayed
+between barriers + synchronizes, timed with CUDA events on the launching
+stream; the max over ranks is taken.  The step inputs rotate over enough
+copies of (activations, weights, output) that each step's working set has
+left L2 (the copies total more than twice the 126 MB L2), so every step reads
+its operands from HBM.  `e2e` is the same metric through the public API
+with host buffers: pinned-host -> device copy of the activations, the layer,
+device -> pinned-host copy of the output, every step.
+
+The secondary objects report the CSR SpMM (config 5, M=1, 90% sparse,
+8192 x 8192: the HBM-bound point) and the fp32 Gemm (config 1) measured the
+same way.  `--impl reference` times the reference's own CPU implementation
+(its sources compiled into oracle/_ref) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 1024 * 1024
+M, N, K = 512, 4096, 4096                         # config 2
+SPMM_N, SPMM_K, SPMM_S = 8192, 8192, 0.90         # config 5 HBM-bound point (M = 1)
+GEMM_M, GEMM_N, GEMM_K = 256, 1024, 1024          # config 1
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def profile_traffic(name):
+    """dram bytes per launch recorded in profiles/<name>.md by an ncu capture."""
+    p = os.path.join(ROOT, "profiles", name + ".md")
+    if not os.path.exists(p):
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons in the background."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.samples = []
+        self.proc = None
+        self.error = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception as e:  # no nvidia-smi
+            self.error = str(e)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append((time.time(), parts))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self, t0, t1):
+        sel = [p for (t, p) in self.samples if t0 - 0.15 <= t <= t1 + 0.15] or [p for (_, p) in self.samples]
+        if not sel:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [],
+                    "note": self.error or "no nvidia-smi samples"}
+        mhz = [float(p[1]) for p in sel if p[1].replace(".", "").isdigit()]
+        mx = [float(p[2]) for p in sel if p[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for p in sel for i in range(4) if p[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(sel),
+                "power_w_max": max(float(p[3]) for p in sel if re.match(r"^[0-9.]+$", p[3])) if sel else None}
+
+
+# --------------------------------------------------------------------------- dist
+def dist_init(n_gpus):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        import datetime
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    elif n_gpus > 1:
+        raise SystemExit("--gpus N > 1 must be launched with torch.distributed.run (one process per GPU)")
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------- timing
+EAGER = False  # --eager: plain launches, no graph and no soak (for profiler runs)
+
+
+def graph_time(step_fns, K, W, world, sampler=None):
+    """W eager warm-up steps; K steps captured in one CUDA graph; a soak replay
+    for the clock sampler; then one timed replay between barriers.  Returns
+    (ms per step, t_start, t_end) with the max over ranks."""
+    import torch
+    n = len(step_fns)
+    for i in range(W):
+        step_fns[i % n]()
+    torch.cuda.synchronize()
+    if EAGER:
+        barrier(world)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.time()
+        ev0.record()
+        for i in range(K):
+            step_fns[i % n]()
+        ev1.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        return max_over_ranks(ev0.elapsed_time(ev1) / K, world), t0, time.time()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for i in range(K):
+                step_fns[i % n]()
+    torch.cuda.synchronize()
+    # soak: replay until ~1 s has passed so the clock samples see the load
+    t_soak = time.time()
+    while time.time() - t_soak < 1.0:
+        g.replay()
+        torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    ev0.record()
+    g.replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    t1 = time.time()
+    barrier(world)
+    ms = ev0.elapsed_time(ev1) / K
+    del g
+    return max_over_ranks(ms, world), t_soak, t1
+
+
+# --------------------------------------------------------------------------- workloads
+def qlinear_setup(ctx, n_copies):
+    import numpy as np
+    import torch
+
+    import pyflamert_b200 as pf
+    from pyflamert_b200 import workloads as wl
+    q = wl.qlinear_case(M, N, K, seed=2)
+    copies = []
+    for i in range(n_copies):
+        w = pf.QWeight(ctx, q.w, q.w_scale)
+        a = torch.from_numpy(q.a).cuda()
+        y = torch.empty((M, N), dtype=torch.int8, device="cuda")
+        copies.append((w, a, y))
+    fns = [(lambda w=w, a=a, y=y: w(a, q.a_scale, q.a_zp, out="int8", y_scale=q.y_scale, y=y))
+           for (w, a, y) in copies]
+    return q, copies, fns
+
+
+def qlinear_e2e(ctx, q, w, steps):
+    """Public API with host buffers: H2D activations, the layer, D2H output."""
+    import numpy as np
+    import torch
+    a_host = torch.from_numpy(q.a).pin_memory()
+    y_host = torch.empty((M, N), dtype=torch.int8).pin_memory()
+    a_dev = torch.empty((M, K), dtype=torch.uint8, device="cuda")
+    y_dev = torch.empty((M, N), dtype=torch.int8, device="cuda")
+
+    def step():
+        a_dev.copy_(a_host, non_blocking=True)
+        w(a_dev, q.a_scale, q.a_zp, out="int8", y_scale=q.y_scale, y=y_dev)
+        y_host.copy_(y_dev, non_blocking=True)
+
+    for _ in range(5):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    # the result read back must be the layer's output
+    ref_dev = w(a_dev, q.a_scale, q.a_zp, out="int8", y_scale=q.y_scale)
+    torch.cuda.synchronize()
+    assert torch.equal(ref_dev.cpu(), y_host)
+    return ms, M * K, M * N
+
+
+def spmm_setup(ctx, n_copies):
+    import torch
+
+    import pyflamert_b200 as pf
+    from pyflamert_b200 import workloads as wl
+    c = wl.spmm_case(1, SPMM_N, SPMM_K, sparsity=SPMM_S, seed=3)
+    copies = []
+    for i in range(n_copies):
+        w = pf.CSR(ctx, c.N, c.K, c.indptr, c.indices, c.values)
+        x = torch.from_numpy(c.X).cuda()
+        y = torch.empty((1, c.N), dtype=torch.float32, device="cuda")
+        copies.append((w, x, y))
+    fns = [(lambda w=w, x=x, y=y: w(x, y=y)) for (w, x, y) in copies]
+    nnz = c.values.size
+    alg_bytes = 8 * nnz + 4 * (c.N + 1) + 4 * c.K + 4 * c.N
+    return c, copies, fns, alg_bytes
+
+
+def gemm_setup(ctx, n_copies):
+    import torch
+
+    import pyflamert_b200 as pf
+    from pyflamert_b200 import workloads as wl
+    g = wl.gemm_case(GEMM_M, GEMM_N, GEMM_K, seed=1)
+    copies = []
+    for i in range(n_copies):
+        fw = pf.FWeight(ctx, g.B)
+        a = torch.from_numpy(g.A).cuda()
+        c = torch.from_numpy(g.C).cuda()
+        y = torch.empty((GEMM_M, GEMM_N), dtype=torch.float32, device="cuda")
+        copies.append((fw, a, c, y))
+    fns = [(lambda fw=fw, a=a, c=c, y=y: fw(a, c, y=y)) for (fw, a, c, y) in copies]
+    return g, copies, fns
+
+
+# --------------------------------------------------------------------------- CPU reference
+def cpu_reference_rate(budget_s=12.0, threads=None):
+    """The reference's own quantized_matmul + quantize_tensor (compiled from its
+    sources into oracle/_ref) on a row sample of config 2, all host threads."""
+    import numpy as np
+
+    from oracle import pyoracle as po
+    from pyflamert_b200 import workloads as wl
+    threads = threads or os.cpu_count() or 1
+    q = wl.qlinear_case(M, N, K, seed=2)
+    # calibrate rows per thread from a 1-row single-thread run
+    t = time.time()
+    po.ref_quantized_matmul(q.a[:1], q.a_scale, q.a_zp, q.w, 0.0125, 0, out="int8", y_scale=q.y_scale)
+    per_row = time.time() - t
+    rows = int(max(threads, min(M, threads * max(1, budget_s / per_row // 1))))
+    rows = min(rows, M)
+    t = time.time()
+    po.ref_quantized_matmul(q.a[:rows], q.a_scale, q.a_zp, q.w, 0.0125, 0, out="int8",
+                            y_scale=q.y_scale, nthreads=threads)
+    dt = time.time() - t
+    tops = 2.0 * rows * N * K / dt / 1e12
+    return {"value": tops, "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+            "sample": f"{rows} of config 2's 512 rows (x 4096 x 4096), reference quantized_matmul "
+                      f"+ quantize_tensor, {threads} threads over row slices, {dt:.1f} s"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    steps = args.steps + args.warmup
+    # each step: a row sample sized so that all steps end within ~3 minutes
+    budget = max(0.05, 180.0 / max(1, steps))
+    from oracle import pyoracle as po
+    from pyflamert_b200 import workloads as wl
+    q = wl.qlinear_case(M, N, K, seed=2)
+    t = time.time()
+    po.ref_quantized_matmul(q.a[:1], q.a_scale, q.a_zp, q.w, 0.0125, 0, out="int8", y_scale=q.y_scale)
+    per_row = time.time() - t
+    rows = max(1, min(M, int(threads * budget / per_row)))
+    times = []
+    for i in range(steps):
+        r0 = (i * rows) % (M - rows + 1)
+        t = time.time()
+        po.ref_quantized_matmul(q.a[r0:r0 + rows], q.a_scale, q.a_zp, q.w, 0.0125, 0, out="int8",
+                                y_scale=q.y_scale, nthreads=threads)
+        times.append(time.time() - t)
+    timed = times[args.warmup:]
+    sec = sum(timed) / len(timed)
+    tops = 2.0 * rows * N * K / sec / 1e12
+    sample = (f"{rows} rows of config 2 (512 x 4096 x 4096) per step, reference quantized_matmul + "
+              f"quantize_tensor (its sources compiled into oracle/_ref), {threads} host threads over "
+              f"row slices")
+    line = {
+        "impl": "reference", "metric": "int8 GEMM TOPS (config 2: u8[512,4096] x s8[4096,4096] -> s8, per-channel)",
+        "value": tops, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic (seeded, config 2 shapes and distributions)",
+        "config": {"workload": "config2_qlinear_int8", "M": M, "N": N, "K": K, "sample_rows": rows},
+        "cpu_baseline": {"value": tops, "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": tops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--eager", action="store_true",
+                    help="plain launches without CUDA graph or soak (profiler runs; not a bench value)")
+    args = ap.parse_args()
+    global EAGER
+    EAGER = args.eager
+    args.warmup = max(3, args.warmup)
+
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)
+        return
+
+    import torch
+
+    import pyflamert_b200 as pf
+    world, rank, local = dist_init(args.gpus)
+    torch.cuda.set_device(local)
+    ctx = pf.Context(local)
+    peaks, peak_src = measured_peaks()
+    sampler = ClockSampler(local)
+    sampler.start()
+
+    # ---- headline: config 2 quantized int8 linear layer
+    per_copy = M * K + N * K + M * N
+    n_copies = max(2, math.ceil(2 * L2_BYTES / per_copy))
+    q, copies, fns = qlinear_setup(ctx, n_copies)
+    ms, t_soak, t_end = graph_time(fns, args.steps, args.warmup, world)
+    ctx.check()
+    ops = 2.0 * M * N * K
+    value = world * ops / (ms * 1e-3) / 1e12
+    achieved = ops / (ms * 1e-3) / 1e12
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    clocks = sampler.summary(t_soak, t_end)
+
+    e2e_ms, h2d, d2h = qlinear_e2e(ctx, q, copies[0][0], max(20, args.steps // 4))
+    e2e_ms = max_over_ranks(e2e_ms, world)
+
+    line = {
+        "metric": "int8 GEMM TOPS (config 2: u8[512,4096] x s8[4096,4096] -> s8, per-channel)",
+        "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic (seeded, config 2 shapes and distributions)",
+        "config": {"workload": "config2_qlinear_int8", "M_per_rank": M, "N": N, "K": K,
+                   "global_batch": M * world, "parallelism": f"batch-shard x{world}",
+                   "l2": f"inputs rotate over {n_copies} copies ({n_copies * per_copy / 2**20:.0f} MiB > 2x L2)",
+                   "timing": "K steps in one CUDA graph, CUDA events, max over ranks"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
+                     "frac": achieved / int8_peak, "traffic": profile_traffic("qlinear_config2"),
+                     "peak_source": f"int8 dense = 2 x bf16_tflops ({peak_src} MEASURED_PEAKS.json); "
+                                    f"counts a multiply-add as 2 ops",
+                     "kernel": "umma_gemm_kernel<i8> (1 launch per step)"},
+        "e2e": {"value": world * ops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms, "path": "pinned host -> device, pfrt_qlinear, device -> pinned host"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+
+    # ---- secondary: SpMM (HBM-bound point) and fp32 Gemm
+    if not args.no_secondary:
+        for obj in copies:
+            obj[0].close()
+        del copies, fns
+        c, sc, sfns, alg_bytes = spmm_setup(ctx, max(2, math.ceil(2 * L2_BYTES / (8 * 6.7e6))))
+        sms, _, _ = graph_time(sfns, args.steps, args.warmup, world)
+        ctx.check()
+        gbs = alg_bytes / (sms * 1e-3) / 1e9
+        line["spmm"] = {
+            "metric": "CSR SpMM HBM GB/s (config 5: M=1, W 8192x8192 90% sparse)",
+            "value": world * gbs, "unit": "GB/s", "ms_per_step": sms,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "traffic": profile_traffic("spmm_config5_m1"),
+                         "algorithmic_bytes": alg_bytes,
+                         "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)"},
+            "gpu_launches": args.steps,
+        }
+        for obj in sc:
+            obj[0].close()
+        g, gc, gfns = gemm_setup(ctx, 2)
+        gms, _, _ = graph_time(gfns, args.steps, args.warmup, world)
+        ctx.check()
+        flops = 2.0 * GEMM_M * GEMM_N * GEMM_K
+        line["gemm_f32"] = {
+            "metric": "fp32 Gemm TFLOP/s (config 1: [256,1024] x [1024,1024] + bias, 3xTF32)",
+            "value": world * flops / (gms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": gms,
+            "note": "working set fits L2; launch-bound at this size",
+        }
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            line["cpu_baseline"] = cpu_reference_rate()
+        except Exception as e:  # the compiled reference is missing
+            line["cpu_baseline"] = {"value": None, "unit": "TFLOP/s", "cores": 0, "kind": "reference",
+                                    "sample": f"unavailable: {e}"}
+    sampler.stop()
+    ctx.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

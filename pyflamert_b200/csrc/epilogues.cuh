@@ -61,6 +61,7 @@ struct QEpi {
     int32_t* partial;       // [splits][M][N] when out_mode == kOutPartial
     int vec_ok;             // output rows 16-byte aligned for vector stores
     int acc_vec_ok;         // acc_out 16-byte aligned and N % 4 == 0
+    int fast32;             // every intermediate of the zero-point correction fits in int32
 
     // Exact accumulator and dequantized/biased/activated value of one element.
     __device__ __forceinline__ float finalize(int row, int n, int64_t raw, int32_t rs,
@@ -126,29 +127,79 @@ struct QEpi {
         }
     }
 
-    __device__ __forceinline__ void store(int row, int col0, int ks, const uint32_t (&acc)[32]) const {
+    // Per-column parameters of one tile, in shared memory (4*bn bytes each):
+    // zc[i] = a_zp * colsum[n] (valid when fast32), os[i] = a_scale * w_scale[n],
+    // b[i] = bias[n] (0 past N or without bias).
+    __device__ __forceinline__ void prepare(uint8_t* p, int n0, int bn, int tid, int nthreads) const {
+        int32_t* zc = reinterpret_cast<int32_t*>(p);
+        float* os = reinterpret_cast<float*>(p + 4 * bn);
+        float* b = reinterpret_cast<float*>(p + 8 * bn);
+        for (int i = tid; i < bn; i += nthreads) {
+            const int n = n0 + i;
+            zc[i] = a_zp * colsum[n];
+            os[i] = __fmul_rn(a_scale, w_scale[n]);
+            b[i] = (bias != nullptr && n < N) ? bias[n] : 0.0f;
+        }
+    }
+
+    __device__ __forceinline__ void store_partial(int row, int col0, int ks, const uint32_t (&acc)[32]) const {
+        int32_t* d = partial + (static_cast<int64_t>(ks) * M + row) * N + col0;
+        if (col0 + 32 <= N && (N % 4) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<int4*>(d + j) =
+                    make_int4(static_cast<int>(acc[j]), static_cast<int>(acc[j + 1]),
+                              static_cast<int>(acc[j + 2]), static_cast<int>(acc[j + 3]));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < N) d[j] = static_cast<int32_t>(acc[j]);
+        }
+    }
+
+    __device__ __forceinline__ void store(const uint8_t* p, int bn, int row, int col0, int cl, int ks,
+                                          const uint32_t (&acc)[32]) const {
         if (row >= M) return;
         if (out_mode == kOutPartial) {
-            int32_t* d = partial + (static_cast<int64_t>(ks) * M + row) * N + col0;
-            if (col0 + 32 <= N && (N % 4) == 0) {
-#pragma unroll
-                for (int j = 0; j < 32; j += 4)
-                    *reinterpret_cast<int4*>(d + j) =
-                        make_int4(static_cast<int>(acc[j]), static_cast<int>(acc[j + 1]),
-                                  static_cast<int>(acc[j + 2]), static_cast<int>(acc[j + 3]));
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (col0 + j < N) d[j] = static_cast<int32_t>(acc[j]);
-            }
+            store_partial(row, col0, ks, acc);
             return;
         }
-        const int32_t rs = (w_zp != 0) ? rowsum[row] : 0;
         int32_t at[32];
         float y[32];
+        const int32_t rs = (w_zp != 0) ? rowsum[row] : 0;
+        if (fast32) {
+            // Exact in int32: the host checked that no intermediate can overflow.
+            const int32_t rterm = (w_zp != 0) ? w_zp * rs - K * a_zp * w_zp : 0;
+            const int4* zc4 = reinterpret_cast<const int4*>(p) + cl / 4;
+            const float4* os4 = reinterpret_cast<const float4*>(p + 4 * bn) + cl / 4;
+            const float4* b4 = reinterpret_cast<const float4*>(p + 8 * bn) + cl / 4;
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-            y[j] = finalize(row, col0 + j, static_cast<int64_t>(static_cast<int32_t>(acc[j])), rs, at[j]);
+            for (int v = 0; v < 8; ++v) {
+                const int4 z = zc4[v];
+                const float4 o = os4[v];
+                const int zz[4] = {z.x, z.y, z.z, z.w};
+                const float oo[4] = {o.x, o.y, o.z, o.w};
+                float bb[4] = {0.f, 0.f, 0.f, 0.f};
+                if (bias != nullptr) {
+                    const float4 b = b4[v];
+                    bb[0] = b.x; bb[1] = b.y; bb[2] = b.z; bb[3] = b.w;
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int j = 4 * v + u;
+                    const int32_t a = static_cast<int32_t>(acc[j]) - zz[u] - rterm;
+                    at[j] = a;
+                    float t = __fmul_rn(__int2float_rn(a), oo[u]);
+                    if (bias != nullptr) t = __fadd_rn(t, bb[u]);
+                    if (relu) t = (0.0f < t) ? t : 0.0f;
+                    y[j] = t;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                y[j] = finalize(row, col0 + j, static_cast<int64_t>(static_cast<int32_t>(acc[j])), rs, at[j]);
+        }
         emit(row, col0, at, y);
     }
 };
@@ -174,12 +225,44 @@ struct FEpi {
         return y;
     }
 
-    __device__ __forceinline__ void store(int row, int col0, int ks, const uint32_t (&acc)[32]) const {
+    // cb[i] = beta * C[n] when the bias operand is a row vector (c_len == N).
+    __device__ __forceinline__ void prepare(uint8_t* p, int n0, int bn, int tid, int nthreads) const {
+        if (C == nullptr || c_len != N) return;
+        float* cb = reinterpret_cast<float*>(p);
+        for (int i = tid; i < bn; i += nthreads) {
+            const int n = n0 + i;
+            cb[i] = (n < N) ? __fmul_rn(beta, C[n]) : 0.0f;
+        }
+    }
+
+    __device__ __forceinline__ void write(int row, int col0, const float (&y)[32]) const {
+        float* d = out + static_cast<int64_t>(row) * ldo + col0;
+        if (col0 + 32 <= N && vec_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(d + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < N) d[j] = y[j];
+        }
+    }
+
+    // Final epilogue from global parameters (split-K reduction, empty K).
+    __device__ __forceinline__ void store_direct(int row, int col0, const uint32_t (&acc)[32]) const {
         if (row >= M) return;
-        const bool full = (col0 + 32 <= N);
+        float y[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) y[j] = finalize(row, col0 + j, __uint_as_float(acc[j]));
+        write(row, col0, y);
+    }
+
+    __device__ __forceinline__ void store(const uint8_t* p, int bn, int row, int col0, int cl, int ks,
+                                          const uint32_t (&acc)[32]) const {
+        if (row >= M) return;
         if (out_mode == kOutPartial) {
             float* d = partial + (static_cast<int64_t>(ks) * M + row) * N + col0;
-            if (full && (N % 4) == 0) {
+            if (col0 + 32 <= N && (N % 4) == 0) {
 #pragma unroll
                 for (int j = 0; j < 32; j += 4)
                     *reinterpret_cast<float4*>(d + j) =
@@ -193,18 +276,21 @@ struct FEpi {
             return;
         }
         float y[32];
+        if (C != nullptr && c_len == N) {
+            const float4* cb4 = reinterpret_cast<const float4*>(p) + cl / 4;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) y[j] = finalize(row, col0 + j, __uint_as_float(acc[j]));
-        float* d = out + static_cast<int64_t>(row) * ldo + col0;
-        if (full && vec_ok) {
+            for (int v = 0; v < 8; ++v) {
+                const float4 c = cb4[v];
+                const float cc[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(d + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
+                for (int u = 0; u < 4; ++u)
+                    y[4 * v + u] = __fadd_rn(__fmul_rn(alpha, __uint_as_float(acc[4 * v + u])), cc[u]);
+            }
         } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (col0 + j < N) d[j] = y[j];
+            for (int j = 0; j < 32; ++j) y[j] = finalize(row, col0 + j, __uint_as_float(acc[j]));
         }
+        write(row, col0, y);
     }
 };
 

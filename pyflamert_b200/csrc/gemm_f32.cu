@@ -92,9 +92,7 @@ __global__ void f_splitk_reduce_kernel(const FEpi e, int splits) {
                 s = __fadd_rn(s, e.partial[(static_cast<int64_t>(k) * e.M + row) * e.N + col0 + j]);
         acc[j] = __float_as_uint(s);
     }
-    FEpi fin = e;
-    fin.out_mode = kOutF32;
-    fin.store(row, col0, 0, acc);
+    e.store_direct(row, col0, acc);
 }
 
 namespace {
@@ -122,9 +120,10 @@ pfrt_status run_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad, const CUt
     const int64_t mblk = ceil_div(M, 128), nblk = ceil_div(N, kF32BN);
     const int64_t tiles = mblk * nblk;
     const int kb_total = static_cast<int>(ceil_div(Kpad, Cfg::BK));
-    int splits = 1;
-    if (tiles * 2 <= ctx->num_sms) splits = static_cast<int>(std::min<int64_t>(ctx->num_sms / tiles, kb_total / 4));
-    splits = env_int("PFRT_GEMM_SPLITS", splits);
+    (void)tiles;
+    // Split-K is opt-in (PFRT_GEMM_SPLITS): one pass measured faster at the
+    // benchmark shapes.
+    int splits = env_int("PFRT_GEMM_SPLITS", 1);
     splits = std::max(1, std::min(splits, kb_total));
     const int kb_per = static_cast<int>(ceil_div(kb_total, splits));
     splits = static_cast<int>(ceil_div(kb_total, kb_per));
@@ -172,11 +171,9 @@ pfrt_status run_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad, const CUt
 
 size_t splitk_bytes(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad) {
     // Upper bound of the split-K partial buffer run_f32 may ask for.
-    const int64_t tiles = ceil_div(M, 128) * ceil_div(N, kF32BN);
+    (void)ctx;
     const int64_t kb_total = ceil_div(Kpad, 32);
-    int64_t splits = 1;
-    if (tiles * 2 <= ctx->num_sms) splits = std::min<int64_t>(ctx->num_sms / tiles, kb_total / 4);
-    splits = std::max<int64_t>(1, env_int("PFRT_GEMM_SPLITS", static_cast<int>(splits)));
+    int64_t splits = std::max<int64_t>(1, env_int("PFRT_GEMM_SPLITS", 1));
     splits = std::min<int64_t>(splits, kb_total);
     return splits > 1 ? align_up(sizeof(float) * splits * M * N, 256) : 0;
 }

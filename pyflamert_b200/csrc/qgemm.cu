@@ -250,9 +250,10 @@ pfrt_status pfrt_qlinear(pfrt_ctx* ctx, const pfrt_qweight* w, int64_t M, const 
     if (bn != 128 && bn != 256) bn = 128;
     const int64_t tiles = (bn == 256) ? t256 : t128;
     const int kb_total = static_cast<int>(ceil_div(w->Kpad, 128));
-    int splits = 1;
-    if (tiles * 2 <= ctx->num_sms) splits = static_cast<int>(std::min<int64_t>(ctx->num_sms / tiles, kb_total / 4));
-    splits = env_int("PFRT_QGEMM_SPLITS", splits);
+    (void)tiles;
+    // Split-K (partial accumulators + a reduction pass) is available but off
+    // by default: measured slower than one pass at every benchmark shape.
+    int splits = env_int("PFRT_QGEMM_SPLITS", 1);
     splits = std::max(1, std::min(splits, kb_total));
     const int kb_per = static_cast<int>(ceil_div(kb_total, splits));
     splits = static_cast<int>(ceil_div(kb_total, kb_per));
@@ -308,6 +309,15 @@ pfrt_status pfrt_qlinear(pfrt_ctx* ctx, const pfrt_qweight* w, int64_t M, const 
     const int esz = (out_mode == PFRT_OUT_F32) ? 4 : 1;
     e.vec_ok = ((reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (ldy * esz) % 16 == 0) ? 1 : 0;
     e.acc_vec_ok = ((reinterpret_cast<uintptr_t>(acc_out) & 15u) == 0 && (N % 4) == 0) ? 1 : 0;
+    {
+        // Largest magnitude any intermediate of raw - a_zp*colsum - w_zp*rowsum
+        // + K*a_zp*w_zp can reach; below 2^31 the epilogue runs in int32.
+        const double k = static_cast<double>(K);
+        const double bound = k * 255.0 * 128.0 + std::fabs(static_cast<double>(a_zp)) * k * 128.0 +
+                             std::fabs(static_cast<double>(w->w_zp)) * k * 255.0 +
+                             k * std::fabs(static_cast<double>(a_zp) * w->w_zp);
+        e.fast32 = (bound < 2147483647.0) ? 1 : 0;
+    }
 
     GemmSched sched{};
     sched.num_m_blk = static_cast<int>(mblk);

@@ -2,12 +2,17 @@
 //
 //   D[M,N] = A[M,K] * B[N,K]^T      (both operands K-major in global memory)
 //
-// One CTA per SM, 192 threads:
+// One CTA per SM, 320 threads:
 //   warp 0      TMA producer   (one lane)  -- global -> shared, STAGES-deep ring
 //   warp 1      MMA issuer     (one lane)  -- tcgen05.mma into TMEM; also owns
 //                                             the TMEM allocation
-//   warps 2..5  epilogue       (128 threads) -- tcgen05.ld TMEM -> registers,
-//                                             fused epilogue, global stores
+//   warps 2..9  epilogue       (256 threads) -- tcgen05.ld TMEM -> registers,
+//                                             fused epilogue, global stores.
+//               Two warps per TMEM lane quarter (a warp may only read the
+//               32 TMEM lanes of its warp-id % 4), each taking half of the
+//               tile's columns, so every SM sub-partition runs two epilogue
+//               warps.  Per-column epilogue parameters are staged in shared
+//               memory once per tile.
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
 // of one tile overlaps the MMAs of the next.
 //
@@ -54,8 +59,11 @@ struct GemmCfg {
     static constexpr int STAGE_BYTES = NPARTS * (A_TILE + B_TILE);
     static constexpr uint32_t TMEM_COLS = 2 * BN;
     static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
-    static constexpr int THREADS = 192;
+    static constexpr int EPI_WARPS = 8;
+    static constexpr int EPI_THREADS = 32 * EPI_WARPS;
+    static constexpr int PARAM_BYTES = 16 * BN;  // up to 4 words of per-column parameters
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + PARAM_BYTES + 1024;
+    static constexpr int THREADS = 64 + EPI_THREADS;
     static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns must be a power of two");
     static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
     static_assert(STAGES <= 8, "stages");
@@ -69,11 +77,35 @@ __device__ __forceinline__ void decode_unit(const GemmSched& s, int unit, int& m
 }
 
 // Epi must provide:
-//   __device__ void store(int row, int col0, int ks, const uint32_t (&acc)[32]) const;
-// row is the global row of this thread; col0 the first of 32 consecutive
-// global columns held in acc (raw 32-bit accumulator bits).
+//   __device__ void prepare(uint8_t* params, int n0, int bn, int tid, int nthreads) const;
+//       stage the per-column parameters of columns [n0, n0 + bn) (called by
+//       all epilogue threads before a tile's stores; params holds 16*bn bytes)
+//   __device__ void store(const uint8_t* params, int bn, int row, int col0, int c_local,
+//                         int ks, const uint32_t (&acc)[32]) const;
+//       row is the global row of this thread; col0 (= n0 + c_local) the first
+//       of 32 consecutive global columns held in acc (raw 32-bit accumulator bits).
+
+// Named barrier over the epilogue warps that also ORs a predicate across
+// them, so a stop decision is the same in every epilogue warp.
+__device__ __forceinline__ bool epi_barrier_or(bool pred, int nthreads) {
+    uint32_t out;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(out)
+        : "r"(pred ? 1u : 0u), "r"(nthreads)
+        : "memory");
+    return out != 0;
+}
+
+__device__ __forceinline__ void epi_barrier(int nthreads) {
+    asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
 template <int KIND, int BN, int STAGES, class Epi>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA0,
                      const __grid_constant__ CUtensorMap tmB0,
                      const __grid_constant__ CUtensorMap tmA1,
@@ -93,6 +125,7 @@ __global__ void __launch_bounds__(192, 1)
     uint64_t* drain = tempty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    uint8_t* params = smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -104,7 +137,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], 128);
+            mbar_init(&tempty[i], Cfg::EPI_THREADS);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -236,30 +269,36 @@ __global__ void __launch_bounds__(192, 1)
             mbar_wait(drain, 0, &zero);
         }
     } else {
-        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int q = warp & 3;                    // TMEM lane quarter this warp may access
+        const int etid = threadIdx.x - 64;         // 0 .. EPI_THREADS-1
+        const int half = (warp - 2) >> 2;          // which half of the tile's columns
+        constexpr int CHUNKS = BN / 32 / 2;        // 32-column chunks per warp
         int t = 0;
         for (int unit = blockIdx.x; unit < sched.num_units; unit += gridDim.x, ++t) {
             int mb, nb, ks;
             decode_unit(sched, unit, mb, nb, ks);
             const int slot = t & 1;
             const uint32_t ap = static_cast<uint32_t>(t >> 1) & 1u;
-            // Warp-uniform decision: tcgen05.ld below needs the whole warp.
-            const bool got = __all_sync(0xffffffffu, mbar_wait(&tfull[slot], ap, abort_flag));
-            if (!got) {
+            const bool got = mbar_wait(&tfull[slot], ap, abort_flag);
+            // Uniform stop decision across the epilogue warps; this barrier also
+            // ensures the previous tile's parameters are no longer being read.
+            if (epi_barrier_or(!got || *abort_flag != 0, Cfg::EPI_THREADS)) {
                 *abort_flag = 1;
                 report_error(err, kDevWaitTimeout);
                 break;
             }
             tc_fence_after();
+            epi.prepare(params, nb * BN, BN, etid, Cfg::EPI_THREADS);
+            epi_barrier(Cfg::EPI_THREADS);
             const int row = mb * BM + q * 32 + lane;
             const uint32_t taddr =
                 tmem_base + static_cast<uint32_t>(slot * BN) + (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
+            for (int c = half * CHUNKS; c < (half + 1) * CHUNKS; ++c) {
                 uint32_t acc[32];
                 tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), acc);
                 tmem_ld_wait();
-                epi.store(row, nb * BN + c * 32, ks, acc);
+                epi.store(params, BN, row, nb * BN + c * 32, c * 32, ks, acc);
             }
             tc_fence_before();
             mbar_arrive(&tempty[slot]);
