@@ -76,18 +76,21 @@ struct QEpi {
         return y;
     }
 
-    __device__ __forceinline__ void emit(int row, int col0, const int32_t (&at)[32],
-                                         const float (&y)[32]) const {
-        const bool full = (col0 + 32 <= N);
+    // Writes W consecutive outputs (and accumulators) of one row; W is 32 in
+    // the GEMM epilogue and 4 in the split-K reduction.
+    template <int W>
+    __device__ __forceinline__ void emit(int row, int col0, const int32_t (&at)[W],
+                                         const float (&y)[W]) const {
+        const bool full = (col0 + W <= N);
         if (acc_out != nullptr) {
             int32_t* d = acc_out + static_cast<int64_t>(row) * N + col0;
             if (full && acc_vec_ok) {
 #pragma unroll
-                for (int j = 0; j < 32; j += 4)
+                for (int j = 0; j < W; j += 4)
                     *reinterpret_cast<int4*>(d + j) = make_int4(at[j], at[j + 1], at[j + 2], at[j + 3]);
             } else {
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
+                for (int j = 0; j < W; ++j)
                     if (col0 + j < N) d[j] = at[j];
             }
         }
@@ -95,19 +98,19 @@ struct QEpi {
             float* d = static_cast<float*>(out) + static_cast<int64_t>(row) * ldo + col0;
             if (full && vec_ok) {
 #pragma unroll
-                for (int j = 0; j < 32; j += 4)
+                for (int j = 0; j < W; j += 4)
                     *reinterpret_cast<float4*>(d + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
             } else {
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
+                for (int j = 0; j < W; ++j)
                     if (col0 + j < N) d[j] = y[j];
             }
         } else {
             const bool u8 = (out_mode == kOutU8);
             uint8_t* d = static_cast<uint8_t*>(out) + static_cast<int64_t>(row) * ldo + col0;
-            uint32_t packed[8];
+            uint32_t packed[W / 4];
 #pragma unroll
-            for (int w = 0; w < 8; ++w) {
+            for (int w = 0; w < W / 4; ++w) {
                 uint32_t v = 0;
 #pragma unroll
                 for (int b = 0; b < 4; ++b) {
@@ -116,14 +119,16 @@ struct QEpi {
                 }
                 packed[w] = v;
             }
-            if (full && vec_ok) {
-                *reinterpret_cast<uint4*>(d) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                *reinterpret_cast<uint4*>(d + 16) = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (col0 + j < N) d[j] = static_cast<uint8_t>((packed[j >> 2] >> (8 * (j & 3))) & 0xFFu);
+            if constexpr (W == 32) {
+                if (full && vec_ok) {
+                    *reinterpret_cast<uint4*>(d) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                    *reinterpret_cast<uint4*>(d + 16) = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                    return;
+                }
             }
+#pragma unroll
+            for (int j = 0; j < W; ++j)
+                if (col0 + j < N) d[j] = static_cast<uint8_t>((packed[j >> 2] >> (8 * (j & 3))) & 0xFFu);
         }
     }
 
@@ -200,7 +205,7 @@ struct QEpi {
             for (int j = 0; j < 32; ++j)
                 y[j] = finalize(row, col0 + j, static_cast<int64_t>(static_cast<int32_t>(acc[j])), rs, at[j]);
         }
-        emit(row, col0, at, y);
+        emit<32>(row, col0, at, y);
     }
 };
 
@@ -235,26 +240,28 @@ struct FEpi {
         }
     }
 
-    __device__ __forceinline__ void write(int row, int col0, const float (&y)[32]) const {
+    template <int W>
+    __device__ __forceinline__ void write(int row, int col0, const float (&y)[W]) const {
         float* d = out + static_cast<int64_t>(row) * ldo + col0;
-        if (col0 + 32 <= N && vec_ok) {
+        if (col0 + W <= N && vec_ok) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
+            for (int j = 0; j < W; j += 4)
                 *reinterpret_cast<float4*>(d + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
         } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
+            for (int j = 0; j < W; ++j)
                 if (col0 + j < N) d[j] = y[j];
         }
     }
 
     // Final epilogue from global parameters (split-K reduction, empty K).
-    __device__ __forceinline__ void store_direct(int row, int col0, const uint32_t (&acc)[32]) const {
+    template <int W>
+    __device__ __forceinline__ void store_direct(int row, int col0, const float (&acc)[W]) const {
         if (row >= M) return;
-        float y[32];
+        float y[W];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) y[j] = finalize(row, col0 + j, __uint_as_float(acc[j]));
-        write(row, col0, y);
+        for (int j = 0; j < W; ++j) y[j] = finalize(row, col0 + j, acc[j]);
+        write<W>(row, col0, y);
     }
 
     __device__ __forceinline__ void store(const uint8_t* p, int bn, int row, int col0, int cl, int ks,
@@ -290,7 +297,7 @@ struct FEpi {
 #pragma unroll
             for (int j = 0; j < 32; ++j) y[j] = finalize(row, col0 + j, __uint_as_float(acc[j]));
         }
-        write(row, col0, y);
+        write<32>(row, col0, y);
     }
 };
 

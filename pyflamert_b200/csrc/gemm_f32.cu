@@ -77,22 +77,32 @@ __global__ void split_kmajor_kernel(const float* __restrict__ src, int64_t rows,
     }
 }
 
+// Thread per (row, 4 columns): partials added in split order (IEEE fp32),
+// then alpha/beta/C as in the single-pass epilogue.  splits = 0 gives the
+// empty-K result beta*C.
 __global__ void f_splitk_reduce_kernel(const FEpi e, int splits) {
-    const int chunks = (e.N + 31) / 32;
+    const int quads = (e.N + 3) / 4;
     const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (idx >= static_cast<int64_t>(e.M) * chunks) return;
-    const int row = static_cast<int>(idx / chunks);
-    const int col0 = static_cast<int>(idx % chunks) * 32;
-    uint32_t acc[32];
+    if (idx >= static_cast<int64_t>(e.M) * quads) return;
+    const int row = static_cast<int>(idx / quads);
+    const int col0 = static_cast<int>(idx % quads) * 4;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const bool vec = (e.N % 4) == 0;
+    for (int k = 0; k < splits; ++k) {
+        const float* p = e.partial + (static_cast<int64_t>(k) * e.M + row) * e.N + col0;
+        if (vec) {
+            const float4 v = *reinterpret_cast<const float4*>(p);
+            acc[0] = __fadd_rn(acc[0], v.x);
+            acc[1] = __fadd_rn(acc[1], v.y);
+            acc[2] = __fadd_rn(acc[2], v.z);
+            acc[3] = __fadd_rn(acc[3], v.w);
+        } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        float s = 0.0f;
-        if (col0 + j < e.N)
-            for (int k = 0; k < splits; ++k)
-                s = __fadd_rn(s, e.partial[(static_cast<int64_t>(k) * e.M + row) * e.N + col0 + j]);
-        acc[j] = __float_as_uint(s);
+            for (int j = 0; j < 4; ++j)
+                if (col0 + j < e.N) acc[j] = __fadd_rn(acc[j], p[j]);
+        }
     }
-    e.store_direct(row, col0, acc);
+    e.store_direct<4>(row, col0, acc);
 }
 
 namespace {
@@ -162,8 +172,8 @@ pfrt_status run_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad, const CUt
     kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(tmAh, tmBh, tmAl, tmBl, sched, eg, ctx->d_err);
     PFRT_CHECK_LAUNCH("umma_gemm_kernel<tf32x3>");
     if (splits > 1) {
-        const int64_t threads = M * ceil_div(N, 32);
-        f_splitk_reduce_kernel<<<static_cast<unsigned>(ceil_div(threads, 128)), 128, 0, s>>>(e, splits);
+        const int64_t threads = M * ceil_div(N, 4);
+        f_splitk_reduce_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, s>>>(e, splits);
         PFRT_CHECK_LAUNCH("f_splitk_reduce_kernel");
     }
     return PFRT_OK;
@@ -202,8 +212,8 @@ pfrt_status run_empty_k(int64_t M, int64_t N, float alpha, float beta, const flo
     e.ldo = N;
     e.out_mode = kOutF32;
     e.vec_ok = 0;
-    const int64_t threads = M * ceil_div(N, 32);
-    f_splitk_reduce_kernel<<<static_cast<unsigned>(ceil_div(threads, 128)), 128, 0, s>>>(e, 0);
+    const int64_t threads = M * ceil_div(N, 4);
+    f_splitk_reduce_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, s>>>(e, 0);
     PFRT_CHECK_LAUNCH("f_splitk_reduce_kernel");
     return PFRT_OK;
 }

@@ -90,24 +90,33 @@ __global__ void q_pad_rows_kernel(const uint8_t* __restrict__ a, int64_t M, int6
     }
 }
 
+// Thread per (row, 4 columns): partial sums added in split order (exact in
+// int64), then the single-pass epilogue's finalisation.
 __global__ void q_splitk_reduce_kernel(const QEpi e, int splits) {
-    const int chunks = (e.N + 31) / 32;
+    const int quads = (e.N + 3) / 4;
     const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (idx >= static_cast<int64_t>(e.M) * chunks) return;
-    const int row = static_cast<int>(idx / chunks);
-    const int col0 = static_cast<int>(idx % chunks) * 32;
+    if (idx >= static_cast<int64_t>(e.M) * quads) return;
+    const int row = static_cast<int>(idx / quads);
+    const int col0 = static_cast<int>(idx % quads) * 4;
     const int32_t rs = (e.w_zp != 0) ? e.rowsum[row] : 0;
-    int32_t at[32];
-    float y[32];
+    int64_t raw[4] = {0, 0, 0, 0};
+    const bool vec = (e.N % 4) == 0;
+    for (int s = 0; s < splits; ++s) {
+        const int32_t* p = e.partial + (static_cast<int64_t>(s) * e.M + row) * e.N + col0;
+        if (vec) {
+            const int4 v = *reinterpret_cast<const int4*>(p);
+            raw[0] += v.x; raw[1] += v.y; raw[2] += v.z; raw[3] += v.w;
+        } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        int64_t raw = 0;
-        if (col0 + j < e.N)
-            for (int s = 0; s < splits; ++s)
-                raw += e.partial[(static_cast<int64_t>(s) * e.M + row) * e.N + col0 + j];
-        y[j] = e.finalize(row, col0 + j, raw, rs, at[j]);
+            for (int j = 0; j < 4; ++j)
+                if (col0 + j < e.N) raw[j] += p[j];
+        }
     }
-    e.emit(row, col0, at, y);
+    int32_t at[4];
+    float y[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) y[j] = e.finalize(row, col0 + j, raw[j], rs, at[j]);
+    e.emit<4>(row, col0, at, y);
 }
 
 namespace {
@@ -338,8 +347,8 @@ pfrt_status pfrt_qlinear(pfrt_ctx* ctx, const pfrt_qweight* w, int64_t M, const 
                      : launch_q<128, 6>(ctx, tmA, w->tm_b128, sched, eg, s);
     if (st) return st;
     if (splits > 1) {
-        const int64_t threads = M * ceil_div(N, 32);
-        q_splitk_reduce_kernel<<<static_cast<unsigned>(ceil_div(threads, 128)), 128, 0, s>>>(e, splits);
+        const int64_t threads = M * ceil_div(N, 4);
+        q_splitk_reduce_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, s>>>(e, splits);
         PFRT_CHECK_LAUNCH("q_splitk_reduce_kernel");
     }
     return PFRT_OK;

@@ -64,6 +64,15 @@ struct GemmCfg {
     static constexpr int PARAM_BYTES = 16 * BN;  // up to 4 words of per-column parameters
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + PARAM_BYTES + 1024;
     static constexpr int THREADS = 64 + EPI_THREADS;
+    // fp32 (3xTF32) accumulation: the tensor core's fp32 accumulator is not
+    // an IEEE round-to-nearest sum, and its error grows with the number of
+    // K steps it adds up.  So the MMAs accumulate PROMOTE_KB k-blocks
+    // (PROMOTE_KB * BK = 128 K elements) into TMEM, and the epilogue adds each
+    // such partial into fp32 registers with IEEE adds.  int8 accumulation is
+    // exact, so one TMEM accumulation covers the whole K range.
+    static constexpr bool PROMOTE = (KIND == KIND_TF32X3);
+    static constexpr int PROMOTE_KB = 4;
+    static constexpr int CHUNK_KB = PROMOTE ? PROMOTE_KB : (1 << 30);
     static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns must be a power of two");
     static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
     static_assert(STAGES <= 8, "stages");
@@ -207,57 +216,60 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            int t = 0;
-            for (int unit = blockIdx.x; ok && unit < sched.num_units; unit += gridDim.x, ++t) {
+            int t = 0;  // accumulation chunks issued so far (selects the TMEM slot)
+            for (int unit = blockIdx.x; ok && unit < sched.num_units; unit += gridDim.x) {
                 int mb, nb, ks;
                 decode_unit(sched, unit, mb, nb, ks);
                 const int kb0 = ks * sched.kb_per_split;
                 const int kb1 = min(kb0 + sched.kb_per_split, sched.kb_total);
-                const int slot = t & 1;
-                const uint32_t ap = static_cast<uint32_t>(t >> 1) & 1u;
-                if (!mbar_wait(&tempty[slot], ap ^ 1u, abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot * BN);
-                for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!mbar_wait(&full[stage], phase, abort_flag)) {
+                for (int kc = kb0; ok && kc < kb1; kc += Cfg::CHUNK_KB, ++t) {
+                    const int kce = min(kc + Cfg::CHUNK_KB, kb1);
+                    const int slot = t & 1;
+                    const uint32_t ap = static_cast<uint32_t>(t >> 1) & 1u;
+                    if (!mbar_wait(&tempty[slot], ap ^ 1u, abort_flag)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t st = smem_u32(tiles + stage * Cfg::STAGE_BYTES);
-                    if constexpr (KIND == KIND_I8) {
-                        const uint64_t da = sdesc_kmajor_sw128(st);
-                        const uint64_t db = sdesc_kmajor_sw128(st + Cfg::A_TILE);
-#pragma unroll
-                        for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
-                            const uint64_t koff = static_cast<uint64_t>((k * Cfg::UMMA_K * Cfg::ELEM) >> 4);
-                            umma_i8(d_tmem, da + koff, db + koff, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+                    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot * BN);
+                    for (int kb = kc; kb < kce; ++kb) {
+                        if (!mbar_wait(&full[stage], phase, abort_flag)) {
+                            ok = false;
+                            break;
                         }
-                    } else {
-                        const uint64_t dah = sdesc_kmajor_sw128(st);
-                        const uint64_t dal = sdesc_kmajor_sw128(st + Cfg::A_TILE);
-                        const uint64_t dbh = sdesc_kmajor_sw128(st + 2 * Cfg::A_TILE);
-                        const uint64_t dbl = sdesc_kmajor_sw128(st + 2 * Cfg::A_TILE + Cfg::B_TILE);
+                        tc_fence_after();
+                        const uint32_t st = smem_u32(tiles + stage * Cfg::STAGE_BYTES);
+                        if constexpr (KIND == KIND_I8) {
+                            const uint64_t da = sdesc_kmajor_sw128(st);
+                            const uint64_t db = sdesc_kmajor_sw128(st + Cfg::A_TILE);
 #pragma unroll
-                        for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
-                            const uint64_t koff = static_cast<uint64_t>((k * Cfg::UMMA_K * Cfg::ELEM) >> 4);
-                            const uint32_t acc0 = (kb > kb0 || k > 0) ? 1u : 0u;
-                            umma_tf32(d_tmem, dal + koff, dbh + koff, idesc, acc0);
-                            umma_tf32(d_tmem, dah + koff, dbl + koff, idesc, 1u);
-                            umma_tf32(d_tmem, dah + koff, dbh + koff, idesc, 1u);
+                            for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
+                                const uint64_t koff = static_cast<uint64_t>((k * Cfg::UMMA_K * Cfg::ELEM) >> 4);
+                                umma_i8(d_tmem, da + koff, db + koff, idesc, (kb > kc || k > 0) ? 1u : 0u);
+                            }
+                        } else {
+                            const uint64_t dah = sdesc_kmajor_sw128(st);
+                            const uint64_t dal = sdesc_kmajor_sw128(st + Cfg::A_TILE);
+                            const uint64_t dbh = sdesc_kmajor_sw128(st + 2 * Cfg::A_TILE);
+                            const uint64_t dbl = sdesc_kmajor_sw128(st + 2 * Cfg::A_TILE + Cfg::B_TILE);
+#pragma unroll
+                            for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
+                                const uint64_t koff = static_cast<uint64_t>((k * Cfg::UMMA_K * Cfg::ELEM) >> 4);
+                                const uint32_t acc0 = (kb > kc || k > 0) ? 1u : 0u;
+                                umma_tf32(d_tmem, dal + koff, dbh + koff, idesc, acc0);
+                                umma_tf32(d_tmem, dah + koff, dbl + koff, idesc, 1u);
+                                umma_tf32(d_tmem, dah + koff, dbh + koff, idesc, 1u);
+                            }
+                        }
+                        umma_commit(&empty[stage]);
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1u;
                         }
                     }
-                    umma_commit(&empty[stage]);
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
+                    if (!ok) break;
+                    umma_commit(&tfull[slot]);
                 }
-                if (!ok) break;
-                umma_commit(&tfull[slot]);
             }
             if (!ok) {
                 *abort_flag = 1;
@@ -273,35 +285,87 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
         const int etid = threadIdx.x - 64;         // 0 .. EPI_THREADS-1
         const int half = (warp - 2) >> 2;          // which half of the tile's columns
         constexpr int CHUNKS = BN / 32 / 2;        // 32-column chunks per warp
-        int t = 0;
-        for (int unit = blockIdx.x; unit < sched.num_units; unit += gridDim.x, ++t) {
+        int t = 0;                                 // accumulation chunks consumed so far
+        for (int unit = blockIdx.x; unit < sched.num_units; unit += gridDim.x) {
             int mb, nb, ks;
             decode_unit(sched, unit, mb, nb, ks);
-            const int slot = t & 1;
-            const uint32_t ap = static_cast<uint32_t>(t >> 1) & 1u;
-            const bool got = mbar_wait(&tfull[slot], ap, abort_flag);
-            // Uniform stop decision across the epilogue warps; this barrier also
-            // ensures the previous tile's parameters are no longer being read.
-            if (epi_barrier_or(!got || *abort_flag != 0, Cfg::EPI_THREADS)) {
-                *abort_flag = 1;
-                report_error(err, kDevWaitTimeout);
-                break;
-            }
-            tc_fence_after();
-            epi.prepare(params, nb * BN, BN, etid, Cfg::EPI_THREADS);
-            epi_barrier(Cfg::EPI_THREADS);
+            const int kb0 = ks * sched.kb_per_split;
+            const int kb1 = min(kb0 + sched.kb_per_split, sched.kb_total);
             const int row = mb * BM + q * 32 + lane;
-            const uint32_t taddr =
-                tmem_base + static_cast<uint32_t>(slot * BN) + (static_cast<uint32_t>(q * 32) << 16);
+            const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+            if constexpr (Cfg::PROMOTE) {
+                // Sum the TMEM partials of every chunk into registers (IEEE fp32).
+                float racc[CHUNKS][32];
+#pragma unroll
+                for (int c = 0; c < CHUNKS; ++c)
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) racc[c][j] = 0.0f;
+                bool stop = false;
+                for (int kc = kb0; kc < kb1; kc += Cfg::CHUNK_KB, ++t) {
+                    const int slot = t & 1;
+                    const uint32_t ap = static_cast<uint32_t>(t >> 1) & 1u;
+                    const bool got = mbar_wait(&tfull[slot], ap, abort_flag);
+                    if (epi_barrier_or(!got || *abort_flag != 0, Cfg::EPI_THREADS)) {
+                        stop = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t taddr = tmem_base + static_cast<uint32_t>(slot * BN) + lane_off;
+#pragma unroll
+                    for (int c = 0; c < CHUNKS; ++c) {
+                        uint32_t v[32];
+                        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>((half * CHUNKS + c) * 32), v);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) racc[c][j] = __fadd_rn(racc[c][j], __uint_as_float(v[j]));
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&tempty[slot]);
+                }
+                if (stop) {
+                    *abort_flag = 1;
+                    report_error(err, kDevWaitTimeout);
+                    break;
+                }
+                // The barrier of the last chunk also ensures the previous tile's
+                // parameters are no longer being read.
+                epi.prepare(params, nb * BN, BN, etid, Cfg::EPI_THREADS);
+                epi_barrier(Cfg::EPI_THREADS);
+#pragma unroll
+                for (int c = 0; c < CHUNKS; ++c) {
+                    uint32_t bits[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) bits[j] = __float_as_uint(racc[c][j]);
+                    const int cl = (half * CHUNKS + c) * 32;
+                    epi.store(params, BN, row, nb * BN + cl, cl, ks, bits);
+                }
+                epi_barrier(Cfg::EPI_THREADS);  // parameters stay valid until every warp stored
+            } else {
+                const int slot = t & 1;
+                const uint32_t ap = static_cast<uint32_t>(t >> 1) & 1u;
+                ++t;
+                const bool got = mbar_wait(&tfull[slot], ap, abort_flag);
+                // Uniform stop decision across the epilogue warps; this barrier also
+                // ensures the previous tile's parameters are no longer being read.
+                if (epi_barrier_or(!got || *abort_flag != 0, Cfg::EPI_THREADS)) {
+                    *abort_flag = 1;
+                    report_error(err, kDevWaitTimeout);
+                    break;
+                }
+                tc_fence_after();
+                epi.prepare(params, nb * BN, BN, etid, Cfg::EPI_THREADS);
+                epi_barrier(Cfg::EPI_THREADS);
+                const uint32_t taddr = tmem_base + static_cast<uint32_t>(slot * BN) + lane_off;
 #pragma unroll 1
-            for (int c = half * CHUNKS; c < (half + 1) * CHUNKS; ++c) {
-                uint32_t acc[32];
-                tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), acc);
-                tmem_ld_wait();
-                epi.store(params, BN, row, nb * BN + c * 32, c * 32, ks, acc);
+                for (int c = half * CHUNKS; c < (half + 1) * CHUNKS; ++c) {
+                    uint32_t acc[32];
+                    tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), acc);
+                    tmem_ld_wait();
+                    epi.store(params, BN, row, nb * BN + c * 32, c * 32, ks, acc);
+                }
+                tc_fence_before();
+                mbar_arrive(&tempty[slot]);
             }
-            tc_fence_before();
-            mbar_arrive(&tempty[slot]);
         }
     }
 
