@@ -106,6 +106,21 @@ PFRT_API pfrt_status pfrt_fweight_destroy(pfrt_fweight* w);
 PFRT_API pfrt_status pfrt_gemm_f32(pfrt_ctx* ctx, int64_t M, int trans_a, float alpha, const float* a,
                           const pfrt_fweight* b, float beta, const float* c, int64_t c_len,
                           float* y, pfrt_stream stream);
+/* No counterpart in the reference: an allocation-free form of pfrt_gemm_f32
+ * for callers that cannot allocate device memory while they run (for example
+ * a host program whose device memory is all handed out by its own pool, or a
+ * latency-bound loop that must not pay cudaMalloc's device synchronization).
+ * Same arguments and result as pfrt_gemm_f32; the per-call split of A uses a
+ * fixed 16 MiB device array built into the library instead of the context's
+ * scratch memory.  Limit: M * Kpad <= 2097152 (Kpad = K rounded up to 32),
+ * else PFRT_ERR_UNSUPPORTED.  The first call on each device does a one-time
+ * set-up (it looks up the array's device address), so make that first call
+ * before any stream capture.  All calls share the array and it keeps the last
+ * call's contents: calls that overlap on the GPU race on it. */
+PFRT_API pfrt_status pfrt_gemm_f32_noalloc(pfrt_ctx* ctx, int64_t M, int trans_a, float alpha,
+                                           const float* a, const pfrt_fweight* b, float beta,
+                                           const float* c, int64_t c_len, float* y,
+                                           pfrt_stream stream);
 /* Same with B a device matrix given per call (a graph input rather than an
  * initializer); B is prepared into the context's scratch memory each call. */
 PFRT_API pfrt_status pfrt_gemm_f32_dense(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, int trans_a,

@@ -36,6 +36,7 @@ PROTOTYPES = {
     "pfrt_fweight_create": [_P, _I64, _I64, _INT, _P, _P],
     "pfrt_fweight_destroy": [_P],
     "pfrt_gemm_f32": [_P, _I64, _INT, _F32, _P, _P, _F32, _P, _I64, _P, _P],
+    "pfrt_gemm_f32_noalloc": [_P, _I64, _INT, _F32, _P, _P, _F32, _P, _I64, _P, _P],
     "pfrt_gemm_f32_dense": [_P, _I64, _I64, _I64, _INT, _INT, _F32, _P, _P, _F32, _P, _I64, _P, _P],
     "pfrt_qweight_create": [_P, _I64, _I64, _P, _I32, _P, _I64, _P],
     "pfrt_qweight_destroy": [_P],

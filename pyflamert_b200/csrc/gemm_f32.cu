@@ -13,6 +13,7 @@
 // initializer) is split once by pfrt_fweight_create.
 #include <algorithm>
 #include <cstdlib>
+#include <mutex>
 #include <string>
 
 #include "epilogues.cuh"
@@ -219,6 +220,39 @@ pfrt_status run_empty_k(int64_t M, int64_t N, float alpha, float beta, const flo
 }
 
 }  // namespace
+
+// Fixed scratch for pfrt_gemm_f32_noalloc: the hi/lo split of A lives here
+// instead of in memory allocated at call time.  Every device that loads this
+// library holds these 16 MiB until the process exits.  Host code must not use
+// the array's name as a device address (on the host it only stands for the
+// symbol); noalloc_scratch() looks up the real device address.
+constexpr size_t kNoAllocScratchBytes = size_t{16} << 20;
+constexpr int64_t kNoAllocMaxElems = static_cast<int64_t>(kNoAllocScratchBytes / (2 * sizeof(float)));
+static __device__ __align__(256) unsigned char g_gemm_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+
+// Device address of g_gemm_noalloc_scratch on `device`, looked up once per
+// device with that device current (the caller has made it current).
+pfrt_status noalloc_scratch(int device, void** out) {
+    if (device < 0 || device >= kNoAllocMaxDevices)
+        return fail(PFRT_ERR_UNSUPPORTED, "pfrt_gemm_f32_noalloc: device ordinal too large");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_addr[device] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_gemm_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+        g_noalloc_addr[device] = p;
+    }
+    *out = g_noalloc_addr[device];
+    return PFRT_OK;
+}
+
+}  // namespace
 }  // namespace pfrt
 
 using namespace pfrt;
@@ -341,6 +375,53 @@ pfrt_status pfrt_gemm_f32_dense(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, 
     if (st) return st;
     return run_f32(ctx, M, N, Kpad, tah, tal, tbh, tbl, alpha, beta, c, c_len, y,
                    base + 2 * pa + 2 * pb, tail, s);
+}
+
+// Same result as pfrt_gemm_f32, for callers that must not allocate device
+// memory during a call.  The per-call split of A goes to the fixed 16 MiB
+// array above instead of the context's scratch arena, so the call makes no
+// cudaMalloc/cudaFree and no other allocation.  Limit: M * Kpad <= 2^21
+// elements (Kpad = K rounded up to 32); larger calls are rejected.  The first
+// call on a device does a one-time set-up (the lookup of the array's device
+// address), so that first call should come before any stream capture.  All
+// calls share the array, so calls that overlap on the GPU (other streams,
+// other threads) race on it; split-K is not available here.
+pfrt_status pfrt_gemm_f32_noalloc(pfrt_ctx* ctx, int64_t M, int trans_a, float alpha, const float* a,
+                                  const pfrt_fweight* b, float beta, const float* c, int64_t c_len,
+                                  float* y, pfrt_stream stream) {
+    pfrt_status st = enter(ctx);
+    if (st) return st;
+    if (!b) return fail(PFRT_ERR_INVALID_ARGUMENT, "Gemm: null weight");
+    if (b->ctx != ctx) return fail(PFRT_ERR_INVALID_ARGUMENT, "Gemm: weight belongs to another context");
+    const int64_t N = b->N, K = b->K;
+    st = check_common(M, N, K, a, y);
+    if (st) return st;
+    if (M == 0) return PFRT_OK;
+    if (M > kNoAllocMaxElems / b->Kpad)
+        return fail(PFRT_ERR_UNSUPPORTED,
+                    "pfrt_gemm_f32_noalloc: M * Kpad = " + std::to_string(M) + " * " +
+                        std::to_string(b->Kpad) + " exceeds the fixed scratch limit of " +
+                        std::to_string(kNoAllocMaxElems) + " elements; use pfrt_gemm_f32");
+    if (env_int("PFRT_GEMM_SPLITS", 1) > 1)
+        return fail(PFRT_ERR_UNSUPPORTED, "pfrt_gemm_f32_noalloc: split-K (PFRT_GEMM_SPLITS) needs extra scratch");
+    void* base = nullptr;
+    st = noalloc_scratch(ctx->device, &base);
+    if (st) return st;
+    cudaStream_t s = pick_stream(ctx, stream);
+    const size_t part_bytes = align_up(sizeof(float) * M * b->Kpad, 256);
+    float* ahi = static_cast<float*>(base);
+    float* alo = reinterpret_cast<float*>(static_cast<uint8_t*>(base) + part_bytes);
+    // The split writes every element of [M, Kpad] (zero padding included), so
+    // nothing left in the array by an earlier call is read.
+    st = launch_split(a, M, K, trans_a ? M : K, trans_a, ahi, alo, b->Kpad, s);
+    if (st) return st;
+    CUtensorMap tah, tal;
+    st = make_tmap_2d(&tah, ahi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, b->Kpad, M, b->Kpad * 4, 32, 128);
+    if (st == PFRT_OK)
+        st = make_tmap_2d(&tal, alo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, b->Kpad, M, b->Kpad * 4, 32, 128);
+    if (st) return st;
+    return run_f32(ctx, M, N, b->Kpad, tah, tal, b->tm_hi, b->tm_lo, alpha, beta, c, c_len, y,
+                   nullptr, 0, s);
 }
 
 }  // extern "C"
