@@ -13,11 +13,19 @@
 // and grid-stride row assignment over a persistent grid.  Two kernels:
 //   skinny (M <= 8):  lanes split the row's nonzeros; each lane keeps M
 //                     partial sums; X (a few KB to 256 KB) is read through L1.
-//   wide   (M > 8):   X is transposed once to X^T [K, Mpad]; lanes split M
-//                     (4 consecutive rows of X per lane, float4), and each
-//                     nonzero's (index, value) is broadcast with a shuffle.
+//   tiled  (M > 8, CSR uploaded with pfrt_csr_create): the weight is
+//                     re-blocked once into 256-column chunks; a block stages a
+//                     64-row x 256-column tile of X in shared memory and its
+//                     warps walk their CSR rows' nonzeros in that chunk, each
+//                     lane owning 2 rows of X; every X operand comes from
+//                     shared memory instead of an L2 gather.
+//   wide   (M > 8, caller-owned device CSR): X is transposed once to
+//                     X^T [K, Mpad]; lanes split M (4 rows of X per lane,
+//                     float4) and each nonzero's (index, value) is broadcast
+//                     with a shuffle; the X^T rows are gathered from L2.
 // Every index is bounds-checked; a bad one is skipped and recorded.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -31,6 +39,12 @@ struct pfrt_csr {
     int32_t* indptr = nullptr;   // [N+1]
     int32_t* indices = nullptr;  // [nnz]
     float* values = nullptr;     // [nnz]
+    // Column-blocked copy for the tiled kernel: the nonzeros of column chunk
+    // c (columns [c*KT, (c+1)*KT)) of every row, chunk-major, as packed
+    // (local column, value bits) pairs, with row pointers cptr[c][N+1].
+    int nchunks = 0;
+    int32_t* cptr = nullptr;     // [nchunks][N+1]
+    uint2* cent = nullptr;       // [nnz]
 };
 
 namespace pfrt {
@@ -80,15 +94,30 @@ __global__ void __launch_bounds__(kSpmmThreads)
         const int64_t ja = min((j0 + 3) & ~int64_t{3}, j1);
         if (j0 + lane < ja)
             skinny_accum<MV>(acc, M, __ldg(indices + j0 + lane), __ldg(values + j0 + lane), x, ldx, K, bad);
-        // Body: 4 nonzeros per lane per step, 128-bit loads.
+        // Body: 128-bit loads, 4 nonzeros each, four loads per lane issued
+        // back to back before any use, so each lane keeps 8 independent
+        // 16-byte loads in flight instead of one dependent load per step.
         const int64_t jb = ja + ((j1 - ja) & ~int64_t{3});
-        for (int64_t j = ja + 4 * lane; j < jb; j += 128) {
-            const int4 c4 = __ldg(reinterpret_cast<const int4*>(indices + j));
-            const float4 v4 = __ldg(reinterpret_cast<const float4*>(values + j));
-            skinny_accum<MV>(acc, M, c4.x, v4.x, x, ldx, K, bad);
-            skinny_accum<MV>(acc, M, c4.y, v4.y, x, ldx, K, bad);
-            skinny_accum<MV>(acc, M, c4.z, v4.z, x, ldx, K, bad);
-            skinny_accum<MV>(acc, M, c4.w, v4.w, x, ldx, K, bad);
+        for (int64_t j = ja + 4 * lane; j < jb; j += 512) {
+            int4 c4[4];
+            float4 v4[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t jj = j + 128 * u;
+                if (jj < jb) {
+                    c4[u] = __ldg(reinterpret_cast<const int4*>(indices + jj));
+                    v4[u] = __ldg(reinterpret_cast<const float4*>(values + jj));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (j + 128 * u < jb) {
+                    skinny_accum<MV>(acc, M, c4[u].x, v4[u].x, x, ldx, K, bad);
+                    skinny_accum<MV>(acc, M, c4[u].y, v4[u].y, x, ldx, K, bad);
+                    skinny_accum<MV>(acc, M, c4[u].z, v4[u].z, x, ldx, K, bad);
+                    skinny_accum<MV>(acc, M, c4[u].w, v4[u].w, x, ldx, K, bad);
+                }
+            }
         }
         // Tail: fewer than 4 nonzeros.
         if (jb + lane < j1)
@@ -164,6 +193,97 @@ __global__ void __launch_bounds__(kSpmmThreads)
             if (mm + 2 < M) yp[2 * ldy] = acc.z;
             if (mm + 3 < M) yp[3 * ldy] = acc.w;
         }
+    }
+    if (bad) report_error(err, kDevBadIndex);
+}
+
+constexpr int kTileKT = 256;  // columns of X per staged chunk
+constexpr int kTileMT = 64;   // rows of X per block (2 per lane)
+
+// Dynamic shared memory of spmm_tiled_kernel: the X tile, then one 32-entry
+// nonzero buffer per warp.  The output staging reuses the X tile.
+constexpr size_t kTileSmem = sizeof(float2) * kTileKT * 32 + sizeof(uint2) * 8 * 32;
+
+// Block = (64 rows of X, 8*RPW CSR rows).  For each 256-column chunk the block
+// stages X[m0:m0+64, chunk] transposed into xs[k][pair] (pair p holds rows
+// m0+2p and m0+2p+1, stored at position p ^ (k & 31) so that staging writes
+// spread over the banks and the reads of one k stay a permutation), then
+// each warp walks the chunk's nonzeros of its RPW rows: 32 (index, value)
+// pairs are loaded coalesced into a per-warp buffer and broadcast to all
+// lanes, and lane l accumulates rows m0+2l and m0+2l+1.
+template <int RPW>
+__global__ void __launch_bounds__(256)
+    spmm_tiled_kernel(int M, int64_t N, int64_t K, int nchunks, const int32_t* __restrict__ cptr,
+                      const uint2* __restrict__ cent, const float* __restrict__ x, int64_t ldx,
+                      float* __restrict__ y, int64_t ldy, int64_t mtiles, int* err) {
+    extern __shared__ __align__(16) uint8_t tsm[];
+    float2* xs = reinterpret_cast<float2*>(tsm);
+    uint2* ent = reinterpret_cast<uint2*>(tsm + sizeof(float2) * kTileKT * 32);
+    constexpr int R = 8 * RPW;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t mt = blockIdx.x % mtiles, nt = blockIdx.x / mtiles;
+    const int m0 = static_cast<int>(mt) * kTileMT;
+    const int64_t n0 = nt * R;
+    uint2* wbuf = ent + warp * 32;
+    float2 acc[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) acc[r] = make_float2(0.f, 0.f);
+    bool bad = false;
+    for (int c = 0; c < nchunks; ++c) {
+        const int64_t k0 = static_cast<int64_t>(c) * kTileKT;
+        const int kt = static_cast<int>((K - k0) < kTileKT ? (K - k0) : kTileKT);
+        // Stage: thread i handles column k = i % 256 of pair p (rows m0+2p, +1).
+        for (int e = threadIdx.x; e < kTileKT * 32; e += 256) {
+            const int k = e % kTileKT, p = e / kTileKT;
+            const int m = m0 + 2 * p;
+            float2 v = make_float2(0.f, 0.f);
+            if (k < kt) {
+                if (m < M) v.x = __ldg(x + static_cast<int64_t>(m) * ldx + k0 + k);
+                if (m + 1 < M) v.y = __ldg(x + static_cast<int64_t>(m + 1) * ldx + k0 + k);
+            }
+            xs[k * 32 + (p ^ (k & 31))] = v;
+        }
+        __syncthreads();
+        const int32_t* cp = cptr + static_cast<int64_t>(c) * (N + 1);
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+            const int64_t n = n0 + warp * RPW + r;
+            if (n < N) {
+                const int64_t j0 = __ldg(cp + n), j1 = __ldg(cp + n + 1);
+                for (int64_t jc = j0; jc < j1; jc += 32) {
+                    if (jc + lane < j1) wbuf[lane] = __ldg(cent + jc + lane);
+                    __syncwarp();
+                    const int cnt = static_cast<int>((j1 - jc) < 32 ? (j1 - jc) : 32);
+                    for (int t = 0; t < cnt; ++t) {
+                        const uint2 en = wbuf[t];
+                        const int k = static_cast<int>(en.x);
+                        if (k >= kt) {  // outside this chunk: skip and record
+                            bad = true;
+                            continue;
+                        }
+                        const float v = __uint_as_float(en.y);
+                        const float2 xv = xs[k * 32 + (lane ^ (k & 31))];
+                        acc[r].x = __fmaf_rn(v, xv.x, acc[r].x);
+                        acc[r].y = __fmaf_rn(v, xv.y, acc[r].y);
+                    }
+                    __syncwarp();
+                }
+            }
+        }
+        __syncthreads();
+    }
+    // Output: stage [64 rows of X][R CSR rows] so the stores run along n.
+    float* ys = reinterpret_cast<float*>(tsm);
+    constexpr int LDYS = R + 1;
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+        ys[(2 * lane) * LDYS + warp * RPW + r] = acc[r].x;
+        ys[(2 * lane + 1) * LDYS + warp * RPW + r] = acc[r].y;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < kTileMT * R; e += 256) {
+        const int m = e / R, i = e % R;
+        if (m0 + m < M && n0 + i < N) y[static_cast<int64_t>(m0 + m) * ldy + n0 + i] = ys[m * LDYS + i];
     }
     if (bad) report_error(err, kDevBadIndex);
 }
@@ -269,6 +389,44 @@ pfrt_status run_spmm(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, int64_t nnz
     return PFRT_OK;
 }
 
+template <int RPW>
+pfrt_status launch_tiled(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* x, int64_t ldx,
+                         float* y, int64_t ldy, cudaStream_t s) {
+    auto kern = spmm_tiled_kernel<RPW>;
+    PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kTileSmem)));
+    const int64_t mtiles = ceil_div(M, kTileMT);
+    const int64_t units = mtiles * ceil_div(w->N, 8 * RPW);
+    if (units > INT32_MAX) return fail(PFRT_ERR_UNSUPPORTED, "SpMM: too many tiles");
+    kern<<<static_cast<unsigned>(units), 256, kTileSmem, s>>>(
+        static_cast<int>(M), w->N, w->K, w->nchunks, w->cptr, w->cent, x, ldx, y, ldy, mtiles, ctx->d_err);
+    PFRT_CHECK_LAUNCH("spmm_tiled_kernel");
+    return PFRT_OK;
+}
+
+pfrt_status run_spmm_tiled(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* x, int64_t ldx,
+                           float* y, int64_t ldy, cudaStream_t s) {
+    if (M > INT32_MAX - 256) return fail(PFRT_ERR_UNSUPPORTED, "SpMM: M too large");
+    if (!x || !y) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: null pointer");
+    if (ldx < w->K || ldy < w->N) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: row stride too small");
+    if (w->N == 0) return PFRT_OK;
+    // Rows per warp: the largest that still gives every SM two blocks.
+    const int64_t mtiles = ceil_div(M, kTileMT);
+    int rpw = 4;
+    for (int cand : {32, 16, 8}) {
+        if (mtiles * ceil_div(w->N, 8 * cand) >= 2 * ctx->num_sms) {
+            rpw = cand;
+            break;
+        }
+    }
+    switch (rpw) {
+        case 32: return launch_tiled<32>(ctx, w, M, x, ldx, y, ldy, s);
+        case 16: return launch_tiled<16>(ctx, w, M, x, ldx, y, ldy, s);
+        case 8: return launch_tiled<8>(ctx, w, M, x, ldx, y, ldy, s);
+        default: return launch_tiled<4>(ctx, w, M, x, ldx, y, ldy, s);
+    }
+}
+
 }  // namespace
 }  // namespace pfrt
 
@@ -307,6 +465,44 @@ pfrt_status pfrt_csr_create(pfrt_ctx* ctx, int64_t N, int64_t K, int64_t nnz,
         pfrt_csr_destroy(w);
         return cuda_fail(e, "pfrt_csr_create");
     }
+    // Column-blocked copy for the tiled kernel (stable within each row).
+    w->nchunks = static_cast<int>(std::max<int64_t>(1, ceil_div(K, kTileKT)));
+    {
+        const int C = w->nchunks;
+        std::vector<int32_t> cptr(static_cast<size_t>(C) * (N + 1), 0);
+        for (int64_t r = 0; r < N; ++r)
+            for (int32_t j = ip[r]; j < ip[r + 1]; ++j) ++cptr[static_cast<size_t>(ix[j] / kTileKT) * (N + 1) + r + 1];
+        int64_t run = 0;
+        for (int c = 0; c < C; ++c) {
+            int32_t* row = cptr.data() + static_cast<size_t>(c) * (N + 1);
+            row[0] = static_cast<int32_t>(run);
+            for (int64_t r = 0; r < N; ++r) {
+                run += row[r + 1];
+                row[r + 1] = static_cast<int32_t>(run);
+            }
+        }
+        std::vector<int32_t> fill(cptr);
+        std::vector<uint2> cent(static_cast<size_t>(std::max<int64_t>(nnz, 1)));
+        const float* vh = values_host;
+        for (int64_t r = 0; r < N; ++r)
+            for (int32_t j = ip[r]; j < ip[r + 1]; ++j) {
+                const int c = ix[j] / kTileKT;
+                uint32_t bits;
+                std::memcpy(&bits, vh + j, 4);
+                cent[fill[static_cast<size_t>(c) * (N + 1) + r]++] =
+                    make_uint2(static_cast<uint32_t>(ix[j] - c * kTileKT), bits);
+            }
+        e = cudaMalloc(&w->cptr, sizeof(int32_t) * cptr.size());
+        if (e == cudaSuccess) e = cudaMalloc(&w->cent, sizeof(uint2) * cent.size());
+        if (e == cudaSuccess)
+            e = cudaMemcpy(w->cptr, cptr.data(), sizeof(int32_t) * cptr.size(), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(w->cent, cent.data(), sizeof(uint2) * cent.size(), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            pfrt_csr_destroy(w);
+            return cuda_fail(e, "pfrt_csr_create (blocked copy)");
+        }
+    }
     *out = w;
     return PFRT_OK;
 }
@@ -325,6 +521,8 @@ pfrt_status pfrt_csr_destroy(pfrt_csr* w) {
     if (w->indptr) cudaFree(w->indptr);
     if (w->indices) cudaFree(w->indices);
     if (w->values) cudaFree(w->values);
+    if (w->cptr) cudaFree(w->cptr);
+    if (w->cent) cudaFree(w->cent);
     delete w;
     return PFRT_OK;
 }
@@ -343,6 +541,9 @@ pfrt_status pfrt_spmm(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* 
     if (st) return st;
     if (!w) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: null CSR");
     if (w->ctx != ctx) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: CSR belongs to another context");
+    const char* tiled = std::getenv("PFRT_SPMM_TILED");
+    if (M > 8 && tiled && *tiled == '1')
+        return run_spmm_tiled(ctx, w, M, x, ldx, y, ldy, pick_stream(ctx, stream));
     return run_spmm(ctx, M, w->N, w->K, w->nnz, w->indptr, w->indices, w->values, x, ldx, y, ldy,
                     pick_stream(ctx, stream));
 }

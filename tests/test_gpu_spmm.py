@@ -107,3 +107,23 @@ def test_raw_api_bad_index_is_skipped_and_reported(ctx):
     np.testing.assert_array_equal(yy[:, 0], x.cpu().numpy() @ np.array([1, 0, 0, 2], np.float32))
     np.testing.assert_array_equal(yy[:, 1], x.cpu().numpy()[:, 1] * 3.0)
     ctx.check()  # the error was cleared
+
+
+@pytest.mark.parametrize("M", [9, 40, 200])
+def test_raw_api_wide_kernel(ctx, M):
+    """Caller-owned device CSR with M > 8 (the transposed-X wide kernel)."""
+    c = wl.spmm_case(M, 333, 517, sparsity=0.85, seed=70 + M)
+    y = ctx.spmm_csr_raw(M, c.N, c.K, c.values.size, torch.from_numpy(c.indptr).cuda(),
+                         torch.from_numpy(c.indices).cuda(), torch.from_numpy(c.values).cuda(),
+                         torch.from_numpy(c.X).cuda())
+    ctx.check()
+    assert normwise_rel(y.cpu().numpy(), oracle(c)) <= FP32_TOL
+
+
+@pytest.mark.parametrize("M,N,K", [(65, 100, 257), (130, 1000, 700), (64, 8, 4096), (256, 4096, 4096)])
+def test_tiled_kernel(ctx, M, N, K, monkeypatch):
+    """The shared-memory tiled kernel, including its tails: M not a multiple of
+    64, N not a multiple of the rows per block, K not a multiple of 256."""
+    monkeypatch.setenv("PFRT_SPMM_TILED", "1")
+    c = wl.spmm_case(M, N, K, sparsity=0.7 if M < 256 else 0.9, seed=M + N + K)
+    assert normwise_rel(gpu(ctx, c), oracle(c)) <= FP32_TOL
