@@ -350,6 +350,43 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- profiling
+def profile_target(args):
+    """One workload, eager launches, no rotation: the small case an ncu capture
+    of a single kernel wants (a few tens of MB on the device)."""
+    import torch
+
+    import pyflamert_b200 as pf
+    from pyflamert_b200 import workloads as wl
+    global EAGER
+    EAGER = True
+    ctx = pf.Context(0)
+    t = args.profile_target
+    if t in ("qlinear", "qlinear_4096"):
+        m = M if t == "qlinear" else 4096
+        q = wl.qlinear_case(m, N, K, seed=2)
+        w = pf.QWeight(ctx, q.w, q.w_scale)
+        a = torch.from_numpy(q.a).cuda()
+        y = torch.empty((m, N), dtype=torch.int8, device="cuda")
+        fns = [lambda: w(a, q.a_scale, q.a_zp, out="int8", y_scale=q.y_scale, y=y)]
+    elif t in ("spmm_m1", "spmm_cfg3"):
+        c = (wl.spmm_case(1, SPMM_N, SPMM_K, sparsity=SPMM_S, seed=3) if t == "spmm_m1"
+             else wl.spmm_case(256, 4096, 4096, sparsity=0.9, seed=3))
+        w = pf.CSR(ctx, c.N, c.K, c.indptr, c.indices, c.values)
+        x = torch.from_numpy(c.X).cuda()
+        y = torch.empty((c.X.shape[0], c.N), dtype=torch.float32, device="cuda")
+        fns = [lambda: w(x, y=y)]
+    else:
+        g = wl.gemm_case(GEMM_M, GEMM_N, GEMM_K, seed=1)
+        fw = pf.FWeight(ctx, g.B)
+        a, cc = torch.from_numpy(g.A).cuda(), torch.from_numpy(g.C).cuda()
+        y = torch.empty((GEMM_M, GEMM_N), dtype=torch.float32, device="cuda")
+        fns = [lambda: fw(a, cc, y=y)]
+    ms, _, _ = graph_time(fns, args.steps, args.warmup, 1)
+    ctx.check()
+    print(json.dumps({"profile_target": t, "ms_per_step": ms, "note": "eager, not a bench value"}))
+
+
 # --------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -361,9 +398,15 @@ def main():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--eager", action="store_true",
                     help="plain launches without CUDA graph or soak (profiler runs; not a bench value)")
+    ap.add_argument("--profile-target", default=None,
+                    choices=["qlinear", "spmm_m1", "spmm_cfg3", "gemm_cfg1", "qlinear_4096"],
+                    help="run only this workload, eagerly, for a profiler; prints its ms/step")
     args = ap.parse_args()
     global EAGER
     EAGER = args.eager
+    if args.profile_target:
+        profile_target(args)
+        return
     args.warmup = max(3, args.warmup)
 
     if args.impl == "reference":

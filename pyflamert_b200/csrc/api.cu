@@ -92,6 +92,26 @@ pfrt_status make_tmap_2d(CUtensorMap* tm, const void* base, CUtensorMapDataType 
     return PFRT_OK;
 }
 
+pfrt_status make_tmap_2d_plain(CUtensorMap* tm, const void* base, CUtensorMapDataType dt,
+                               int elem_bytes, uint64_t cols, uint64_t rows, uint64_t ld_bytes,
+                               uint32_t box_cols, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn) return fail(PFRT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || ld_bytes % 16 != 0 ||
+        (static_cast<uint64_t>(box_cols) * elem_bytes) % 16 != 0 || box_cols > 256 || box_rows > 256)
+        return fail(PFRT_ERR_INVALID_ARGUMENT, "TMA tensor map: alignment or box size");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld_bytes};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(tm, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(PFRT_ERR_CUDA, "cuTensorMapEncodeTiled failed (code " + std::to_string(r) + ")");
+    return PFRT_OK;
+}
+
 }  // namespace pfrt
 
 using namespace pfrt;

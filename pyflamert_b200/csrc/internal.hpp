@@ -57,4 +57,10 @@ pfrt_status make_tmap_2d(CUtensorMap* tm, const void* base, CUtensorMapDataType 
                          uint64_t cols, uint64_t rows, uint64_t ld_bytes, uint32_t box_cols,
                          uint32_t box_rows);
 
+// 2-D tensor map without swizzle: global [rows, cols] with row stride
+// `ld_bytes`, box [box_rows, box_cols]; box_cols * elem_bytes a multiple of 16.
+pfrt_status make_tmap_2d_plain(CUtensorMap* tm, const void* base, CUtensorMapDataType dt,
+                               int elem_bytes, uint64_t cols, uint64_t rows, uint64_t ld_bytes,
+                               uint32_t box_cols, uint32_t box_rows);
+
 }  // namespace pfrt

@@ -45,6 +45,10 @@ struct pfrt_csr {
     int nchunks = 0;
     int32_t* cptr = nullptr;     // [nchunks][N+1]
     uint2* cent = nullptr;       // [nnz]
+    // Row partition of the streaming kernel for `part_warps` warps.
+    int64_t part_warps = 0;
+    int32_t* part = nullptr;     // [part_warps + 1]
+    std::vector<int32_t> host_indptr;
 };
 
 namespace pfrt {
@@ -60,29 +64,64 @@ __device__ __forceinline__ void row_range(const int32_t* __restrict__ indptr, in
     j1 = j1 < j0 ? j0 : (j1 > nnz ? nnz : j1);
 }
 
-template <int MV>
+// Adds v * X[m, col] for m < M.  X comes from shared memory (xs[col*MV + m],
+// staged once per block) when SMEM, else from global memory through L1.
+template <int MV, bool SMEM>
 __device__ __forceinline__ void skinny_accum(float (&acc)[MV], int M, int32_t col, float v,
                                              const float* __restrict__ x, int64_t ldx, int64_t K,
-                                             bool& bad) {
+                                             const float* xs, bool& bad) {
     if (static_cast<uint32_t>(col) >= static_cast<uint64_t>(K)) {
         bad = true;
         return;
     }
+    if constexpr (SMEM) {
+        if constexpr (MV == 1) {
+            acc[0] = __fmaf_rn(v, xs[col], acc[0]);
+        } else if constexpr (MV == 2) {
+            const float2 xv = reinterpret_cast<const float2*>(xs)[col];
+            acc[0] = __fmaf_rn(v, xv.x, acc[0]);
+            acc[1] = __fmaf_rn(v, xv.y, acc[1]);
+        } else {
 #pragma unroll
-    for (int m = 0; m < MV; ++m)
-        if (m < M) acc[m] = __fmaf_rn(v, __ldg(x + m * ldx + col), acc[m]);
+            for (int q = 0; q < MV; q += 4) {
+                const float4 xv = reinterpret_cast<const float4*>(xs + static_cast<int64_t>(col) * MV)[q / 4];
+                acc[q] = __fmaf_rn(v, xv.x, acc[q]);
+                acc[q + 1] = __fmaf_rn(v, xv.y, acc[q + 1]);
+                acc[q + 2] = __fmaf_rn(v, xv.z, acc[q + 2]);
+                acc[q + 3] = __fmaf_rn(v, xv.w, acc[q + 3]);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int m = 0; m < MV; ++m)
+            if (m < M) acc[m] = __fmaf_rn(v, __ldg(x + m * ldx + col), acc[m]);
+    }
 }
 
 // M <= MV <= 8.  One warp per CSR row; the lanes share the row's nonzeros.
-template <int MV>
-__global__ void __launch_bounds__(kSpmmThreads)
+// With SMEM the block first stages X (all M rows, interleaved as xs[k][m],
+// zero past M) in shared memory, so the per-nonzero gathers of X hit shared
+// memory banks instead of L1 tags; the grid is then persistent (a few blocks
+// per SM) so X is staged only once per block.
+template <int MV, bool SMEM, int THREADS>
+__global__ void __launch_bounds__(THREADS)
     spmm_skinny_kernel(int M, int64_t N, int64_t K, int64_t nnz, const int32_t* __restrict__ indptr,
                        const int32_t* __restrict__ indices, const float* __restrict__ values,
                        const float* __restrict__ x, int64_t ldx, float* __restrict__ y, int64_t ldy,
                        int* err) {
+    extern __shared__ __align__(16) float xs[];
+    if constexpr (SMEM) {
+        const int64_t total = K * MV;
+        for (int64_t i = threadIdx.x; i < total; i += blockDim.x) {
+            const int64_t k = i / MV;
+            const int m = static_cast<int>(i % MV);
+            xs[i] = (m < M) ? __ldg(x + m * ldx + k) : 0.0f;
+        }
+        __syncthreads();
+    }
     const int lane = threadIdx.x & 31;
-    const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * kSpmmThreads + threadIdx.x) >> 5;
-    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kSpmmThreads) >> 5;
+    const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * THREADS + threadIdx.x) >> 5;
+    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * THREADS) >> 5;
     bool bad = false;
     for (int64_t n = warp0; n < N; n += nwarps) {
         int64_t j0, j1;
@@ -93,8 +132,9 @@ __global__ void __launch_bounds__(kSpmmThreads)
         // Head: up to 3 nonzeros until j is a multiple of 4 (16-byte aligned).
         const int64_t ja = min((j0 + 3) & ~int64_t{3}, j1);
         if (j0 + lane < ja)
-            skinny_accum<MV>(acc, M, __ldg(indices + j0 + lane), __ldg(values + j0 + lane), x, ldx, K, bad);
-        // Body: 128-bit loads, 4 nonzeros each, four loads per lane issued
+            skinny_accum<MV, SMEM>(acc, M, __ldg(indices + j0 + lane), __ldg(values + j0 + lane), x, ldx, K,
+                                   xs, bad);
+        // Body: 128-bit loads of 4 nonzeros each, four loads per lane issued
         // back to back before any use, so each lane keeps 8 independent
         // 16-byte loads in flight instead of one dependent load per step.
         const int64_t jb = ja + ((j1 - ja) & ~int64_t{3});
@@ -112,16 +152,17 @@ __global__ void __launch_bounds__(kSpmmThreads)
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 if (j + 128 * u < jb) {
-                    skinny_accum<MV>(acc, M, c4[u].x, v4[u].x, x, ldx, K, bad);
-                    skinny_accum<MV>(acc, M, c4[u].y, v4[u].y, x, ldx, K, bad);
-                    skinny_accum<MV>(acc, M, c4[u].z, v4[u].z, x, ldx, K, bad);
-                    skinny_accum<MV>(acc, M, c4[u].w, v4[u].w, x, ldx, K, bad);
+                    skinny_accum<MV, SMEM>(acc, M, c4[u].x, v4[u].x, x, ldx, K, xs, bad);
+                    skinny_accum<MV, SMEM>(acc, M, c4[u].y, v4[u].y, x, ldx, K, xs, bad);
+                    skinny_accum<MV, SMEM>(acc, M, c4[u].z, v4[u].z, x, ldx, K, xs, bad);
+                    skinny_accum<MV, SMEM>(acc, M, c4[u].w, v4[u].w, x, ldx, K, xs, bad);
                 }
             }
         }
         // Tail: fewer than 4 nonzeros.
         if (jb + lane < j1)
-            skinny_accum<MV>(acc, M, __ldg(indices + jb + lane), __ldg(values + jb + lane), x, ldx, K, bad);
+            skinny_accum<MV, SMEM>(acc, M, __ldg(indices + jb + lane), __ldg(values + jb + lane), x, ldx, K,
+                                   xs, bad);
 #pragma unroll
         for (int m = 0; m < MV; ++m) {
             float v = acc[m];
@@ -136,6 +177,149 @@ __global__ void __launch_bounds__(kSpmmThreads)
                 if (lane == m) v = acc[m];
             y[static_cast<int64_t>(lane) * ldy + n] = v;
         }
+    }
+    if (bad) report_error(err, kDevBadIndex);
+}
+
+// Streaming form of the skinny kernel, for a CSR uploaded with
+// pfrt_csr_create.  Warp w owns the contiguous rows [part[w], part[w+1]),
+// chosen on the host so that every warp gets about the same number of
+// nonzeros; their nonzeros are one contiguous range of the CSR arrays, which
+// the warp streams in 256-entry stages (two 128-bit index loads and two value
+// loads per lane), always loading stage s+1 before it works on stage s.
+// Rows are reduced segment by segment: the part of a row inside a stage is
+// summed over the warp with shuffles and added to the row's running sum, and a
+// row is written when its last stage is done.
+template <int MV, bool SMEM, int THREADS>
+__global__ void __launch_bounds__(THREADS)
+    spmm_stream_kernel(int M, int64_t K, const int32_t* __restrict__ indptr,
+                       const int32_t* __restrict__ indices, const float* __restrict__ values,
+                       const int32_t* __restrict__ part, const float* __restrict__ x, int64_t ldx,
+                       float* __restrict__ y, int64_t ldy, int* err) {
+    extern __shared__ __align__(16) float xs[];
+    if constexpr (SMEM) {
+        const int64_t total = K * MV;
+        for (int64_t i = threadIdx.x; i < total; i += blockDim.x) {
+            const int64_t k = i / MV;
+            const int m = static_cast<int>(i % MV);
+            xs[i] = (m < M) ? __ldg(x + m * ldx + k) : 0.0f;
+        }
+        __syncthreads();
+    }
+    const int lane = threadIdx.x & 31;
+    const int64_t w = (static_cast<int64_t>(blockIdx.x) * THREADS + threadIdx.x) >> 5;
+    const int32_t rb = __ldg(part + w), re = __ldg(part + w + 1);
+    if (rb >= re) return;
+    const int32_t lo = __ldg(indptr + rb), hi = __ldg(indptr + re);
+    bool bad = false;
+    // Row ends of rows base .. base+31, one per lane.
+    int32_t base = rb;
+    int32_t bnd = (base + 1 + lane <= re) ? __ldg(indptr + base + 1 + lane) : hi;
+    int32_t row = rb;
+    int32_t row_start = lo;
+    int32_t row_end = __shfl_sync(0xffffffffu, bnd, 0);
+    float racc[MV];
+#pragma unroll
+    for (int m = 0; m < MV; ++m) racc[m] = 0.0f;
+
+    auto load_stage = [&](int32_t s, int4 (&c)[2], float4 (&v)[2]) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int32_t g = s + 128 * h + 4 * lane;
+            if (g < hi) {
+                c[h] = __ldg(reinterpret_cast<const int4*>(indices + g));
+                v[h] = __ldg(reinterpret_cast<const float4*>(values + g));
+            } else {
+                c[h] = make_int4(0, 0, 0, 0);
+                v[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+    };
+    int32_t s0 = lo & ~3;
+    int4 ci[2];
+    float4 vi[2];
+    load_stage(s0, ci, vi);
+    bool done = false;
+    while (!done) {
+        const int32_t s1 = s0 + 256;
+        int4 cn[2];
+        float4 vn[2];
+        if (s1 < hi) load_stage(s1, cn, vn);
+        // Products of the lane's 8 entries (entry e: j = s0 + 128*(e/4) + 4*lane + e%4).
+        float pv[8][MV];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int h = e >> 2, q = e & 3;
+            const int32_t col = (q == 0) ? ci[h].x : (q == 1) ? ci[h].y : (q == 2) ? ci[h].z : ci[h].w;
+            const float v = (q == 0) ? vi[h].x : (q == 1) ? vi[h].y : (q == 2) ? vi[h].z : vi[h].w;
+            const int32_t j = s0 + 128 * h + 4 * lane + q;
+            const bool live = (j >= lo && j < hi);
+            const bool ok = static_cast<uint32_t>(col) < static_cast<uint64_t>(K);
+            if (live && !ok) bad = true;
+#pragma unroll
+            for (int m = 0; m < MV; ++m) {
+                float xm = 0.0f;
+                if (live && ok) {
+                    if constexpr (SMEM) xm = xs[static_cast<int64_t>(col) * MV + m];
+                    else xm = (m < M) ? __ldg(x + m * ldx + col) : 0.0f;
+                }
+                pv[e][m] = (live && ok) ? __fmul_rn(v, xm) : 0.0f;
+            }
+        }
+        // Segments of this stage: the rows that end in it, then the row that continues.
+        while (true) {
+            const int32_t seg_lo = max(row_start, s0), seg_hi = min(row_end, s1);
+            float sum[MV];
+#pragma unroll
+            for (int m = 0; m < MV; ++m) sum[m] = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int32_t j = s0 + 128 * (e >> 2) + 4 * lane + (e & 3);
+                if (j >= seg_lo && j < seg_hi) {
+#pragma unroll
+                    for (int m = 0; m < MV; ++m) sum[m] = __fadd_rn(sum[m], pv[e][m]);
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < MV; ++m) {
+                float t = sum[m];
+#pragma unroll
+                for (int o = 16; o; o >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
+                racc[m] = __fadd_rn(racc[m], t);
+            }
+            if (row_end > s1) break;  // the row continues in the next stage
+            if (lane < M) {
+                float out = racc[0];
+#pragma unroll
+                for (int m = 1; m < MV; ++m)
+                    if (lane == m) out = racc[m];
+                y[static_cast<int64_t>(lane) * ldy + row] = out;
+            }
+#pragma unroll
+            for (int m = 0; m < MV; ++m) racc[m] = 0.0f;
+            ++row;
+            if (row >= re) {
+                done = true;
+                break;
+            }
+            row_start = row_end;
+            if (row - base >= 32) {
+                base += 32;
+                bnd = (base + 1 + lane <= re) ? __ldg(indptr + base + 1 + lane) : hi;
+            }
+            row_end = __shfl_sync(0xffffffffu, bnd, row - base);
+        }
+        if (done || s1 >= hi) {
+            // Rows left after the last nonzero are empty: write zeros.
+            for (; !done && row < re; ++row)
+                if (lane < M) y[static_cast<int64_t>(lane) * ldy + row] = 0.0f;
+            break;
+        }
+        s0 = s1;
+        ci[0] = cn[0];
+        ci[1] = cn[1];
+        vi[0] = vn[0];
+        vi[1] = vn[1];
     }
     if (bad) report_error(err, kDevBadIndex);
 }
@@ -197,53 +381,59 @@ __global__ void __launch_bounds__(kSpmmThreads)
     if (bad) report_error(err, kDevBadIndex);
 }
 
-constexpr int kTileKT = 256;  // columns of X per staged chunk
+constexpr int kTileKT = 256;  // columns of X (rows of X^T) per staged chunk
 constexpr int kTileMT = 64;   // rows of X per block (2 per lane)
 
-// Dynamic shared memory of spmm_tiled_kernel: the X tile, then one 32-entry
-// nonzero buffer per warp.  The output staging reuses the X tile.
-constexpr size_t kTileSmem = sizeof(float2) * kTileKT * 32 + sizeof(uint2) * 8 * 32;
+// Dynamic shared memory of spmm_tiled_kernel: the X^T tile [256][64] fp32,
+// one 32-entry nonzero buffer per warp, and the tile's mbarrier.  The output
+// staging reuses the first two regions.
+constexpr size_t kTileXsBytes = sizeof(float) * kTileKT * kTileMT;
+constexpr size_t kTileEntBytes = sizeof(uint2) * 8 * 32;
+constexpr size_t kTileSmem = kTileXsBytes + kTileEntBytes + 16;
 
-// Block = (64 rows of X, 8*RPW CSR rows).  For each 256-column chunk the block
-// stages X[m0:m0+64, chunk] transposed into xs[k][pair] (pair p holds rows
-// m0+2p and m0+2p+1, stored at position p ^ (k & 31) so that staging writes
-// spread over the banks and the reads of one k stay a permutation), then
-// each warp walks the chunk's nonzeros of its RPW rows: 32 (index, value)
-// pairs are loaded coalesced into a per-warp buffer and broadcast to all
-// lanes, and lane l accumulates rows m0+2l and m0+2l+1.
+// Block = (64 rows of X, 8*RPW CSR rows).  For each 256-column chunk one TMA
+// load brings X^T[chunk, m0:m0+64] into shared memory (zero-filled past K and
+// past M), then each warp walks the chunk's nonzeros of its RPW rows: 32
+// (index, value) pairs are loaded coalesced into a per-warp buffer and
+// broadcast to all lanes, and lane l accumulates rows m0+2l and m0+2l+1 from
+// xs[k][2l..2l+1] (one conflict-free 256-byte row per nonzero).
 template <int RPW>
 __global__ void __launch_bounds__(256)
-    spmm_tiled_kernel(int M, int64_t N, int64_t K, int nchunks, const int32_t* __restrict__ cptr,
-                      const uint2* __restrict__ cent, const float* __restrict__ x, int64_t ldx,
+    spmm_tiled_kernel(const __grid_constant__ CUtensorMap tmx, int M, int64_t N, int nchunks,
+                      const int32_t* __restrict__ cptr, const uint2* __restrict__ cent,
                       float* __restrict__ y, int64_t ldy, int64_t mtiles, int* err) {
-    extern __shared__ __align__(16) uint8_t tsm[];
-    float2* xs = reinterpret_cast<float2*>(tsm);
-    uint2* ent = reinterpret_cast<uint2*>(tsm + sizeof(float2) * kTileKT * 32);
+    extern __shared__ __align__(128) uint8_t tsm[];
+    float* xs = reinterpret_cast<float*>(tsm);
+    uint2* ent = reinterpret_cast<uint2*>(tsm + kTileXsBytes);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(tsm + kTileXsBytes + kTileEntBytes);
     constexpr int R = 8 * RPW;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t mt = blockIdx.x % mtiles, nt = blockIdx.x / mtiles;
     const int m0 = static_cast<int>(mt) * kTileMT;
     const int64_t n0 = nt * R;
     uint2* wbuf = ent + warp * 32;
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
     float2 acc[RPW];
 #pragma unroll
     for (int r = 0; r < RPW; ++r) acc[r] = make_float2(0.f, 0.f);
     bool bad = false;
+    uint32_t phase = 0;
+    const int zero = 0;
     for (int c = 0; c < nchunks; ++c) {
-        const int64_t k0 = static_cast<int64_t>(c) * kTileKT;
-        const int kt = static_cast<int>((K - k0) < kTileKT ? (K - k0) : kTileKT);
-        // Stage: thread i handles column k = i % 256 of pair p (rows m0+2p, +1).
-        for (int e = threadIdx.x; e < kTileKT * 32; e += 256) {
-            const int k = e % kTileKT, p = e / kTileKT;
-            const int m = m0 + 2 * p;
-            float2 v = make_float2(0.f, 0.f);
-            if (k < kt) {
-                if (m < M) v.x = __ldg(x + static_cast<int64_t>(m) * ldx + k0 + k);
-                if (m + 1 < M) v.y = __ldg(x + static_cast<int64_t>(m + 1) * ldx + k0 + k);
-            }
-            xs[k * 32 + (p ^ (k & 31))] = v;
+        if (threadIdx.x == 0) {
+            mbar_arrive_expect_tx(bar, static_cast<uint32_t>(kTileXsBytes));
+            tma_load_2d(xs, &tmx, bar, m0, c * kTileKT);
         }
-        __syncthreads();
+        const bool got = mbar_wait(bar, phase, &zero);
+        if (!__syncthreads_and(got)) {
+            report_error(err, kDevWaitTimeout);
+            return;
+        }
+        phase ^= 1u;
         const int32_t* cp = cptr + static_cast<int64_t>(c) * (N + 1);
 #pragma unroll
         for (int r = 0; r < RPW; ++r) {
@@ -256,13 +446,12 @@ __global__ void __launch_bounds__(256)
                     const int cnt = static_cast<int>((j1 - jc) < 32 ? (j1 - jc) : 32);
                     for (int t = 0; t < cnt; ++t) {
                         const uint2 en = wbuf[t];
-                        const int k = static_cast<int>(en.x);
-                        if (k >= kt) {  // outside this chunk: skip and record
+                        if (en.x >= static_cast<uint32_t>(kTileKT)) {  // not a column of this chunk
                             bad = true;
                             continue;
                         }
                         const float v = __uint_as_float(en.y);
-                        const float2 xv = xs[k * 32 + (lane ^ (k & 31))];
+                        const float2 xv = reinterpret_cast<const float2*>(xs + en.x * kTileMT)[lane];
                         acc[r].x = __fmaf_rn(v, xv.x, acc[r].x);
                         acc[r].y = __fmaf_rn(v, xv.y, acc[r].y);
                     }
@@ -270,7 +459,7 @@ __global__ void __launch_bounds__(256)
                 }
             }
         }
-        __syncthreads();
+        __syncthreads();  // the tile is no longer read: the next TMA may overwrite it
     }
     // Output: stage [64 rows of X][R CSR rows] so the stores run along n.
     float* ys = reinterpret_cast<float*>(tsm);
@@ -356,15 +545,40 @@ pfrt_status run_spmm(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, int64_t nnz
     if (!aligned) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: indices/values must be 16-byte aligned");
     const int max_blocks = ctx->num_sms * 8;
     if (M <= 8) {
-        const int64_t warps = N;
-        const int blocks = static_cast<int>(std::min<int64_t>(ceil_div(warps, kSpmmThreads / 32), max_blocks));
         const int Mi = static_cast<int>(M);
-#define PFRT_SKINNY(MV)                                                                        \
-    spmm_skinny_kernel<MV><<<blocks, kSpmmThreads, 0, s>>>(Mi, N, K, nnz, indptr, indices, values, \
-                                                           x, ldx, y, ldy, ctx->d_err)
-        if (M == 1) PFRT_SKINNY(1);
-        else if (M == 2) PFRT_SKINNY(2);
-        else if (M <= 4) PFRT_SKINNY(4);
+        const int MV = (M == 1) ? 1 : (M == 2) ? 2 : (M <= 4) ? 4 : 8;
+        const size_t xs_bytes = sizeof(float) * static_cast<size_t>(K) * MV;
+        const char* no_smem = std::getenv("PFRT_SPMM_NO_SMEM");
+        // Staging X costs one copy per block: worth it when the gathers it
+        // replaces (M per nonzero, from separate rows of X when M > 1) cost
+        // more than that copy.
+        const int per_sm = static_cast<int>(std::max<size_t>(1, std::min<size_t>(4, (224 * 1024) / (xs_bytes + 1024))));
+        const int64_t smem_blocks = std::min<int64_t>(ceil_div(N, 16), int64_t{per_sm} * ctx->num_sms);
+        const bool pays = (M >= 2) || (8.0 * nnz >= 3.0 * static_cast<double>(smem_blocks) * xs_bytes);
+        const bool smem = xs_bytes <= 96 * 1024 && K > 0 && pays && !(no_smem && *no_smem == '1');
+        int blocks;
+        if (smem) {
+            blocks = static_cast<int>(smem_blocks);  // persistent, 512 threads: X staged once per block
+        } else {
+            blocks = static_cast<int>(std::min<int64_t>(ceil_div(N, kSpmmThreads / 32), max_blocks));
+        }
+        const size_t shm = smem ? xs_bytes : 0;
+#define PFRT_SKINNY(MVV)                                                                              \
+    do {                                                                                              \
+        if (smem) {                                                                                   \
+            PFRT_CUDA_TRY(cudaFuncSetAttribute(spmm_skinny_kernel<MVV, true, 512>,                    \
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,          \
+                                               static_cast<int>(shm)));                              \
+            spmm_skinny_kernel<MVV, true, 512><<<blocks, 512, shm, s>>>(                              \
+                Mi, N, K, nnz, indptr, indices, values, x, ldx, y, ldy, ctx->d_err);                  \
+        } else {                                                                                      \
+            spmm_skinny_kernel<MVV, false, kSpmmThreads><<<blocks, kSpmmThreads, 0, s>>>(             \
+                Mi, N, K, nnz, indptr, indices, values, x, ldx, y, ldy, ctx->d_err);                  \
+        }                                                                                             \
+    } while (0)
+        if (MV == 1) PFRT_SKINNY(1);
+        else if (MV == 2) PFRT_SKINNY(2);
+        else if (MV == 4) PFRT_SKINNY(4);
         else PFRT_SKINNY(8);
 #undef PFRT_SKINNY
         PFRT_CHECK_LAUNCH("spmm_skinny_kernel");
@@ -389,17 +603,92 @@ pfrt_status run_spmm(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, int64_t nnz
     return PFRT_OK;
 }
 
+// Row partition for `warps` warps with about equal cost per warp, cost of a
+// row = its nonzeros + 16 (per-row overhead).  part[w] is non-decreasing,
+// part[0] = 0, part[warps] = N.
+pfrt_status ensure_partition(pfrt_csr* w, int64_t warps, cudaStream_t s) {
+    if (w->part && w->part_warps == warps) return PFRT_OK;
+    const int64_t N = w->N;
+    std::vector<int32_t> part(static_cast<size_t>(warps + 1));
+    const double total = static_cast<double>(w->nnz) + 16.0 * static_cast<double>(N);
+    int64_t r = 0;
+    for (int64_t k = 0; k <= warps; ++k) {
+        const double target = total * static_cast<double>(k) / static_cast<double>(warps);
+        while (r < N && static_cast<double>(w->host_indptr[r]) + 16.0 * static_cast<double>(r) < target) ++r;
+        part[k] = static_cast<int32_t>(r);
+    }
+    part[warps] = static_cast<int32_t>(N);
+    if (w->part) cudaFree(w->part);
+    w->part = nullptr;
+    w->part_warps = 0;
+    PFRT_CUDA_TRY(cudaMalloc(&w->part, sizeof(int32_t) * part.size()));
+    PFRT_CUDA_TRY(cudaMemcpyAsync(w->part, part.data(), sizeof(int32_t) * part.size(), cudaMemcpyHostToDevice, s));
+    PFRT_CUDA_TRY(cudaStreamSynchronize(s));
+    w->part_warps = warps;
+    return PFRT_OK;
+}
+
+template <int MV, bool SMEM>
+pfrt_status launch_stream(pfrt_ctx* ctx, pfrt_csr* w, int M, const float* x, int64_t ldx, float* y,
+                          int64_t ldy, size_t shm, cudaStream_t s) {
+    constexpr int THREADS = SMEM ? 512 : 256;
+    auto kern = spmm_stream_kernel<MV, SMEM, THREADS>;
+    if (SMEM)
+        PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(shm)));
+    // Exactly the blocks that are resident at once: the partition gives every
+    // warp of this grid its own rows, so no warp waits for a second wave.
+    int occ = 0;
+    PFRT_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, THREADS, shm));
+    occ = std::max(1, std::min(occ, SMEM ? 2 : 8));
+    const int64_t blocks = int64_t{occ} * ctx->num_sms;
+    pfrt_status st = ensure_partition(w, blocks * (THREADS / 32), s);
+    if (st) return st;
+    kern<<<static_cast<unsigned>(blocks), THREADS, shm, s>>>(M, w->K, w->indptr, w->indices, w->values, w->part,
+                                                             x, ldx, y, ldy, ctx->d_err);
+    PFRT_CHECK_LAUNCH("spmm_stream_kernel");
+    return PFRT_OK;
+}
+
+pfrt_status run_spmm_stream(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x, int64_t ldx,
+                            float* y, int64_t ldy, cudaStream_t s) {
+    if (!x || !y) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: null pointer");
+    if (ldx < w->K || ldy < w->N) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: row stride too small");
+    if (w->N == 0 || M == 0) return PFRT_OK;
+    const int Mi = static_cast<int>(M);
+    const int MV = (M == 1) ? 1 : (M == 2) ? 2 : (M <= 4) ? 4 : 8;
+    const size_t xs_bytes = sizeof(float) * static_cast<size_t>(w->K) * MV;
+    const char* no_smem = std::getenv("PFRT_SPMM_NO_SMEM");
+    // Staging X costs one copy per block: worth it when the per-nonzero
+    // gathers it replaces (M of them, from separate rows of X when M > 1)
+    // cost more than that copy.
+    const bool pays = (M >= 2) || (8.0 * w->nnz >= 3.0 * 2.0 * ctx->num_sms * static_cast<double>(xs_bytes));
+    const bool smem = xs_bytes <= 96 * 1024 && w->K > 0 && pays && !(no_smem && *no_smem == '1');
+    const size_t shm = smem ? xs_bytes : 0;
+    switch (MV) {
+        case 1: return smem ? launch_stream<1, true>(ctx, w, Mi, x, ldx, y, ldy, shm, s)
+                            : launch_stream<1, false>(ctx, w, Mi, x, ldx, y, ldy, 0, s);
+        case 2: return smem ? launch_stream<2, true>(ctx, w, Mi, x, ldx, y, ldy, shm, s)
+                            : launch_stream<2, false>(ctx, w, Mi, x, ldx, y, ldy, 0, s);
+        case 4: return smem ? launch_stream<4, true>(ctx, w, Mi, x, ldx, y, ldy, shm, s)
+                            : launch_stream<4, false>(ctx, w, Mi, x, ldx, y, ldy, 0, s);
+        default: return smem ? launch_stream<8, true>(ctx, w, Mi, x, ldx, y, ldy, shm, s)
+                             : launch_stream<8, false>(ctx, w, Mi, x, ldx, y, ldy, 0, s);
+    }
+}
+
 template <int RPW>
-pfrt_status launch_tiled(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* x, int64_t ldx,
+pfrt_status launch_tiled(pfrt_ctx* ctx, const pfrt_csr* w, const CUtensorMap& tmx, int64_t M,
                          float* y, int64_t ldy, cudaStream_t s) {
+    static_assert(sizeof(float) * kTileMT * (8 * RPW + 1) <= kTileXsBytes + kTileEntBytes,
+                  "output staging must fit in the tile buffers");
     auto kern = spmm_tiled_kernel<RPW>;
     PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(kTileSmem)));
     const int64_t mtiles = ceil_div(M, kTileMT);
     const int64_t units = mtiles * ceil_div(w->N, 8 * RPW);
     if (units > INT32_MAX) return fail(PFRT_ERR_UNSUPPORTED, "SpMM: too many tiles");
-    kern<<<static_cast<unsigned>(units), 256, kTileSmem, s>>>(
-        static_cast<int>(M), w->N, w->K, w->nchunks, w->cptr, w->cent, x, ldx, y, ldy, mtiles, ctx->d_err);
+    kern<<<static_cast<unsigned>(units), 256, kTileSmem, s>>>(tmx, static_cast<int>(M), w->N, w->nchunks,
+                                                              w->cptr, w->cent, y, ldy, mtiles, ctx->d_err);
     PFRT_CHECK_LAUNCH("spmm_tiled_kernel");
     return PFRT_OK;
 }
@@ -410,20 +699,35 @@ pfrt_status run_spmm_tiled(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const fl
     if (!x || !y) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: null pointer");
     if (ldx < w->K || ldy < w->N) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: row stride too small");
     if (w->N == 0) return PFRT_OK;
-    // Rows per warp: the largest that still gives every SM two blocks.
+    if (w->K == 0) return run_spmm(ctx, M, w->N, w->K, w->nnz, w->indptr, w->indices, w->values, x, ldx, y, ldy, s);
+    // X^T [K][Mpad], Mpad a multiple of the 64-row tile (zero padded).
+    const int64_t mpad = static_cast<int64_t>(align_up(static_cast<size_t>(M), kTileMT));
+    void* scr = nullptr;
+    pfrt_status st = scratch(ctx, sizeof(float) * mpad * w->K, &scr);
+    if (st) return st;
+    float* xt = static_cast<float*>(scr);
+    dim3 tb(32, 8);
+    dim3 tg(static_cast<unsigned>(ceil_div(w->K, 32)), static_cast<unsigned>(ceil_div(mpad, 32)));
+    transpose_pad_kernel<<<tg, tb, 0, s>>>(x, M, w->K, ldx, xt, mpad);
+    PFRT_CHECK_LAUNCH("transpose_pad_kernel");
+    CUtensorMap tmx;
+    st = make_tmap_2d_plain(&tmx, xt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, static_cast<uint64_t>(mpad),
+                            static_cast<uint64_t>(w->K), static_cast<uint64_t>(mpad) * 4, kTileMT, kTileKT);
+    if (st) return st;
+    // Rows per warp: the largest that still gives every SM a block.
     const int64_t mtiles = ceil_div(M, kTileMT);
     int rpw = 4;
     for (int cand : {32, 16, 8}) {
-        if (mtiles * ceil_div(w->N, 8 * cand) >= 2 * ctx->num_sms) {
+        if (mtiles * ceil_div(w->N, 8 * cand) >= ctx->num_sms) {
             rpw = cand;
             break;
         }
     }
     switch (rpw) {
-        case 32: return launch_tiled<32>(ctx, w, M, x, ldx, y, ldy, s);
-        case 16: return launch_tiled<16>(ctx, w, M, x, ldx, y, ldy, s);
-        case 8: return launch_tiled<8>(ctx, w, M, x, ldx, y, ldy, s);
-        default: return launch_tiled<4>(ctx, w, M, x, ldx, y, ldy, s);
+        case 32: return launch_tiled<32>(ctx, w, tmx, M, y, ldy, s);
+        case 16: return launch_tiled<16>(ctx, w, tmx, M, y, ldy, s);
+        case 8: return launch_tiled<8>(ctx, w, tmx, M, y, ldy, s);
+        default: return launch_tiled<4>(ctx, w, tmx, M, y, ldy, s);
     }
 }
 
@@ -465,6 +769,7 @@ pfrt_status pfrt_csr_create(pfrt_ctx* ctx, int64_t N, int64_t K, int64_t nnz,
         pfrt_csr_destroy(w);
         return cuda_fail(e, "pfrt_csr_create");
     }
+    w->host_indptr = ip;
     // Column-blocked copy for the tiled kernel (stable within each row).
     w->nchunks = static_cast<int>(std::max<int64_t>(1, ceil_div(K, kTileKT)));
     {
@@ -523,6 +828,7 @@ pfrt_status pfrt_csr_destroy(pfrt_csr* w) {
     if (w->values) cudaFree(w->values);
     if (w->cptr) cudaFree(w->cptr);
     if (w->cent) cudaFree(w->cent);
+    if (w->part) cudaFree(w->part);
     delete w;
     return PFRT_OK;
 }
@@ -541,6 +847,14 @@ pfrt_status pfrt_spmm(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* 
     if (st) return st;
     if (!w) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: null CSR");
     if (w->ctx != ctx) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: CSR belongs to another context");
+    // M = 1, 2: one warp per row measured fastest; M = 3..8: the streaming
+    // kernel (its register pipeline pays once each nonzero feeds 4-8 rows).
+    const char* rowwarp = std::getenv("PFRT_SPMM_ROWWARP");
+    const char* stream_env = std::getenv("PFRT_SPMM_STREAM");
+    const bool want_stream = (stream_env && *stream_env == '1') ||
+                             (M >= 3 && M <= 8 && !(rowwarp && *rowwarp == '1'));
+    if (M >= 1 && M <= 8 && want_stream)
+        return run_spmm_stream(ctx, const_cast<pfrt_csr*>(w), M, x, ldx, y, ldy, pick_stream(ctx, stream));
     const char* tiled = std::getenv("PFRT_SPMM_TILED");
     if (M > 8 && tiled && *tiled == '1')
         return run_spmm_tiled(ctx, w, M, x, ldx, y, ldy, pick_stream(ctx, stream));

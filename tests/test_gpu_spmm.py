@@ -127,3 +127,26 @@ def test_tiled_kernel(ctx, M, N, K, monkeypatch):
     monkeypatch.setenv("PFRT_SPMM_TILED", "1")
     c = wl.spmm_case(M, N, K, sparsity=0.7 if M < 256 else 0.9, seed=M + N + K)
     assert normwise_rel(gpu(ctx, c), oracle(c)) <= FP32_TOL
+
+
+@pytest.mark.parametrize("kernel", ["rowwarp", "stream"])
+@pytest.mark.parametrize("M", [1, 2, 4, 8])
+def test_small_batch_kernels(ctx, kernel, M, monkeypatch):
+    """Both small-batch kernels (one warp per row; the nnz-balanced streaming
+    kernel) on rows of uneven length, including empty rows at the ends."""
+    monkeypatch.setenv("PFRT_SPMM_ROWWARP" if kernel == "rowwarp" else "PFRT_SPMM_STREAM", "1")
+    rng = np.random.default_rng(M)
+    N, K = 1500, 900
+    counts = rng.integers(0, 700, N)
+    counts[:3] = 0
+    counts[-5:] = 0
+    counts[100:140] = 0
+    indptr = np.zeros(N + 1, np.int64)
+    indptr[1:] = np.cumsum(counts)
+    indices = np.concatenate([np.sort(rng.choice(K, k, replace=False)) for k in counts]).astype(np.int32)
+    values = rng.standard_normal(indices.size).astype(np.float32)
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    c = wl.CsrCase(N, K, indptr.astype(np.int32), indices, values, X)
+    y = gpu(ctx, c)
+    assert normwise_rel(y, oracle(c)) <= FP32_TOL
+    np.testing.assert_array_equal(y[:, counts == 0], 0.0)
