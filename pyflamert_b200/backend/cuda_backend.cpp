@@ -1,0 +1,599 @@
+// cuda_backend.cpp -- pyflame_rt::Backend over the B200 C ABI (pfrt_cuda.h).
+//
+// execute() follows CPUExecutor::execute (src/backends/cpu/executor.cpp:45-147):
+// validate inputs, walk the graph in topological order, run each node, and
+// return the requested outputs; it differs in keeping every tensor on the
+// device between nodes, preparing initializers once per graph instead of
+// cloning them every run (executor.cpp:71-74), and fusing a QuantizedMatMul ->
+// Add -> Relu -> Quantize chain into one kernel.
+#include "cuda_backend.hpp"
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <numeric>
+#include <sstream>
+#include <unordered_set>
+
+#include "pfrt_cuda.h"
+#include "pyflame_rt/errors.hpp"
+
+namespace pyflame_rt {
+
+namespace {
+
+const std::vector<std::string>& supported_ops() {
+    static const std::vector<std::string> ops = {"Gemm",  "MatMul", "QuantizedMatMul", "SparseMatMul",
+                                                 "Add",   "Relu",   "Quantize"};
+    return ops;
+}
+
+int64_t numel(const std::vector<int64_t>& s) {
+    int64_t n = 1;
+    for (auto d : s) n *= d;
+    return s.empty() ? 0 : n;
+}
+
+std::string shape_str(const std::vector<int64_t>& s) {
+    std::ostringstream o;
+    o << "[";
+    for (size_t i = 0; i < s.size(); ++i) o << (i ? ", " : "") << s[i];
+    o << "]";
+    return o.str();
+}
+
+// A tensor living on the device during one run.
+struct DevTensor {
+    void* ptr = nullptr;
+    std::vector<int64_t> shape;
+    DType dtype = DType::Float32;
+    int64_t numel() const { return pyflame_rt::numel(shape); }
+    size_t bytes() const { return static_cast<size_t>(numel()) * dtype_size(dtype); }
+};
+
+struct DevBuf {
+    void* ptr = nullptr;
+    size_t cap = 0;
+};
+
+}  // namespace
+
+class CudaBackend::Impl {
+public:
+    explicit Impl(int device) : device_(device) {
+        if (pfrt_ctx_create(device, &ctx_) != PFRT_OK)
+            throw BackendError(std::string("cuda backend: ") + pfrt_last_error());
+    }
+
+    ~Impl() {
+        reset_caches();
+        for (auto& [_, b] : act_) pfrt_free(ctx_, b.ptr);
+        pfrt_ctx_destroy(ctx_);
+    }
+
+    std::vector<Tensor> execute(const Graph& graph, const std::unordered_map<std::string, Tensor>& feeds,
+                                const std::vector<std::string>& output_names);
+
+    int device_;
+
+private:
+    // ------------------------------------------------------------- helpers
+    [[noreturn]] void fail_node(const Node& n, const std::string& msg) const { throw BackendError(msg, n.name()); }
+
+    void check(pfrt_status st, const Node* n) const {
+        if (st == PFRT_OK) return;
+        const std::string msg = pfrt_last_error();
+        if (n) throw BackendError(msg, n->name());
+        throw BackendError(msg);
+    }
+
+    void* device_alloc(const std::string& key, size_t bytes) {
+        DevBuf& b = act_[key];
+        if (b.cap < bytes) {
+            if (b.ptr) check(pfrt_free(ctx_, b.ptr), nullptr);
+            b.ptr = nullptr;
+            b.cap = 0;
+            check(pfrt_malloc(ctx_, std::max<size_t>(bytes, 16), &b.ptr), nullptr);
+            b.cap = std::max<size_t>(bytes, 16);
+        }
+        return b.ptr;
+    }
+
+    void reset_caches() {
+        for (auto& [_, w] : fweights_) pfrt_fweight_destroy(w);
+        for (auto& [_, w] : qweights_) pfrt_qweight_destroy(w);
+        for (auto& [_, w] : csrs_) pfrt_csr_destroy(w);
+        for (auto& [_, b] : inits_) pfrt_free(ctx_, b.ptr);
+        fweights_.clear();
+        qweights_.clear();
+        csrs_.clear();
+        inits_.clear();
+    }
+
+    // The graph's initializers are prepared once; a different graph (or one
+    // that changed shape) drops the caches.
+    void bind_graph(const Graph& g) {
+        const size_t sig = g.num_nodes() * 1000003u + g.initializers().size();
+        if (&g == graph_ && sig == graph_sig_) return;
+        reset_caches();
+        graph_ = &g;
+        graph_sig_ = sig;
+    }
+
+    const Tensor* initializer(const Graph& g, const std::string& name) const {
+        auto it = g.initializers().find(name);
+        return it == g.initializers().end() ? nullptr : &it->second;
+    }
+
+    // Device copy of an initializer (uploaded once).
+    DevTensor init_device(const Graph& g, const std::string& name) {
+        const Tensor* t = initializer(g, name);
+        DevTensor d;
+        d.shape = t->shape();
+        d.dtype = t->dtype();
+        auto it = inits_.find(name);
+        if (it == inits_.end()) {
+            DevBuf b;
+            b.cap = std::max<size_t>(t->size_bytes(), 16);
+            check(pfrt_malloc(ctx_, b.cap, &b.ptr), nullptr);
+            check(pfrt_memcpy_h2d(ctx_, b.ptr, t->data(), t->size_bytes(), nullptr), nullptr);
+            it = inits_.emplace(name, b).first;
+        }
+        d.ptr = it->second.ptr;
+        return d;
+    }
+
+    // Tensor `name` on the device: a run value, or an initializer.
+    DevTensor value(const Graph& g, const std::string& name, const Node& n) {
+        auto it = vals_.find(name);
+        if (it != vals_.end()) return it->second;
+        if (initializer(g, name)) return init_device(g, name);
+        fail_node(n, "Input tensor '" + name + "' not found");
+    }
+
+    DevTensor new_value(const std::string& name, std::vector<int64_t> shape, DType dt) {
+        DevTensor d;
+        d.shape = std::move(shape);
+        d.dtype = dt;
+        d.ptr = device_alloc("v:" + name, d.bytes());
+        vals_[name] = d;
+        return d;
+    }
+
+    // ------------------------------------------------------------- ops
+    void run_gemm(const Graph& g, const Node& n);
+    void run_matmul(const Graph& g, const Node& n);
+    void run_qmatmul(const Graph& g, const Node& n, const std::vector<const Node*>& chain);
+    void run_sparse(const Graph& g, const Node& n);
+    void run_add(const Graph& g, const Node& n);
+    void run_relu(const Graph& g, const Node& n);
+    void run_quantize(const Graph& g, const Node& n);
+
+    std::vector<const Node*> fusable_chain(const Graph& g, const Node& q,
+                                           const std::unordered_map<std::string, std::vector<const Node*>>& consumers,
+                                           const std::unordered_set<std::string>& outputs);
+
+    pfrt_ctx* ctx_ = nullptr;
+    std::mutex mu_;
+    const Graph* graph_ = nullptr;
+    size_t graph_sig_ = 0;
+    std::unordered_map<std::string, DevBuf> inits_;
+    std::unordered_map<std::string, pfrt_fweight*> fweights_;
+    std::unordered_map<std::string, pfrt_qweight*> qweights_;
+    std::unordered_map<std::string, pfrt_csr*> csrs_;
+    std::unordered_map<std::string, DevBuf> act_;
+    std::unordered_map<std::string, DevTensor> vals_;
+};
+
+// ----------------------------------------------------------------- Gemm
+void CudaBackend::Impl::run_gemm(const Graph& g, const Node& n) {
+    if (n.inputs().size() < 2) fail_node(n, "Gemm requires at least 2 inputs, got " + std::to_string(n.inputs().size()));
+    const float alpha = n.get_attr<float>("alpha", 1.0f);
+    const float beta = n.get_attr<float>("beta", 1.0f);
+    const int ta = n.get_attr<int64_t>("transA", 0) ? 1 : 0;
+    const int tb = n.get_attr<int64_t>("transB", 0) ? 1 : 0;
+    DevTensor A = value(g, n.inputs()[0], n);
+    const std::string& bname = n.inputs()[1];
+    const Tensor* Binit = initializer(g, bname);
+    std::vector<int64_t> bshape = Binit ? Binit->shape() : value(g, bname, n).shape;
+    if (A.shape.size() < 2) fail_node(n, "Gemm input A requires at least 2 dimensions, got " + std::to_string(A.shape.size()));
+    if (bshape.size() < 2) fail_node(n, "Gemm input B requires at least 2 dimensions, got " + std::to_string(bshape.size()));
+    if (A.dtype != DType::Float32) fail_node(n, "Gemm: the cuda backend computes float32 only");
+    const int64_t M = ta ? A.shape[1] : A.shape[0];
+    const int64_t Ka = ta ? A.shape[0] : A.shape[1];
+    const int64_t Kb = tb ? bshape[1] : bshape[0];
+    const int64_t N = tb ? bshape[0] : bshape[1];
+    if (Ka != Kb)
+        fail_node(n, "Gemm: incompatible dimensions - A has K=" + std::to_string(Ka) + ", B has K=" + std::to_string(Kb));
+    const float* cptr = nullptr;
+    int64_t c_len = 0;
+    if (n.inputs().size() > 2 && !n.inputs()[2].empty()) {
+        DevTensor C = value(g, n.inputs()[2], n);
+        cptr = static_cast<const float*>(C.ptr);
+        c_len = C.numel();
+    }
+    DevTensor Y = new_value(n.outputs()[0], {M, N}, DType::Float32);
+    if (Binit && Ka > 0) {
+        const std::string key = bname + (tb ? "|T" : "|N");
+        auto it = fweights_.find(key);
+        if (it == fweights_.end()) {
+            pfrt_fweight* w = nullptr;
+            check(pfrt_fweight_create(ctx_, Ka, N, tb, Binit->data_ptr<float>(), &w), &n);
+            it = fweights_.emplace(key, w).first;
+        }
+        check(pfrt_gemm_f32(ctx_, M, ta, alpha, static_cast<const float*>(A.ptr), it->second, beta, cptr, c_len,
+                            static_cast<float*>(Y.ptr), nullptr), &n);
+    } else {
+        DevTensor B = value(g, bname, n);
+        check(pfrt_gemm_f32_dense(ctx_, M, N, Ka, ta, tb, alpha, static_cast<const float*>(A.ptr),
+                                  static_cast<const float*>(B.ptr), beta, cptr, c_len, static_cast<float*>(Y.ptr),
+                                  nullptr), &n);
+    }
+}
+
+// ----------------------------------------------------------------- MatMul
+// Batched, broadcasting A[..., M, K] @ B[..., K, N] as cpu_matmul; a 2-D B
+// initializer uses the prepared-weight path with A's batch dims folded into M.
+void CudaBackend::Impl::run_matmul(const Graph& g, const Node& n) {
+    if (n.inputs().size() < 2) fail_node(n, "MatMul requires at least 2 inputs, got " + std::to_string(n.inputs().size()));
+    DevTensor A = value(g, n.inputs()[0], n);
+    const std::string& bname = n.inputs()[1];
+    const Tensor* Binit = initializer(g, bname);
+    DevTensor B = value(g, bname, n);
+    if (A.shape.size() < 2) fail_node(n, "MatMul input A requires at least 2 dimensions, got " + std::to_string(A.shape.size()));
+    if (B.shape.size() < 2) fail_node(n, "MatMul input B requires at least 2 dimensions, got " + std::to_string(B.shape.size()));
+    if (A.dtype != DType::Float32 || B.dtype != DType::Float32) fail_node(n, "MatMul: the cuda backend computes float32 only");
+    const int64_t M = A.shape[A.shape.size() - 2], Ka = A.shape.back();
+    const int64_t Kb = B.shape[B.shape.size() - 2], N = B.shape.back();
+    if (Ka != Kb)
+        fail_node(n, "MatMul: incompatible dimensions - A has inner dim " + std::to_string(Ka) + ", B has inner dim " +
+                         std::to_string(Kb));
+    std::vector<int64_t> ab(A.shape.begin(), A.shape.end() - 2), bb(B.shape.begin(), B.shape.end() - 2);
+    const size_t nd = std::max(ab.size(), bb.size());
+    std::vector<int64_t> batch(nd);
+    for (size_t i = 0; i < nd; ++i) {
+        const int64_t da = i < ab.size() ? ab[ab.size() - 1 - i] : 1;
+        const int64_t db = i < bb.size() ? bb[bb.size() - 1 - i] : 1;
+        if (da != db && da != 1 && db != 1) fail_node(n, "MatMul: batch dimensions are not broadcastable");
+        batch[nd - 1 - i] = std::max(da, db);
+    }
+    std::vector<int64_t> out_shape = batch;
+    out_shape.push_back(M);
+    out_shape.push_back(N);
+    DevTensor Y = new_value(n.outputs()[0], out_shape, DType::Float32);
+    const int64_t total = numel(batch) == 0 && batch.empty() ? 1 : numel(batch);
+    const float* ap = static_cast<const float*>(A.ptr);
+    const float* bp = static_cast<const float*>(B.ptr);
+    float* yp = static_cast<float*>(Y.ptr);
+    if (bb.empty() && Binit && Ka > 0) {
+        // B shared by every batch: one GEMM over (batch * M) rows.
+        auto it = fweights_.find(bname + "|N");
+        if (it == fweights_.end()) {
+            pfrt_fweight* w = nullptr;
+            check(pfrt_fweight_create(ctx_, Ka, N, 0, Binit->data_ptr<float>(), &w), &n);
+            it = fweights_.emplace(bname + "|N", w).first;
+        }
+        check(pfrt_gemm_f32(ctx_, total * M, 0, 1.0f, ap, it->second, 0.0f, nullptr, 0, yp, nullptr), &n);
+        return;
+    }
+    // General case: one GEMM per output batch, with broadcast batch offsets.
+    auto stride_of = [&](const std::vector<int64_t>& dims) {
+        std::vector<int64_t> st(nd, 0);
+        int64_t acc = 1;
+        for (size_t i = 0; i < dims.size(); ++i) {
+            const size_t od = nd - 1 - i, sd = dims.size() - 1 - i;
+            st[od] = dims[sd] == 1 ? 0 : acc;
+            acc *= dims[sd];
+        }
+        return st;
+    };
+    const auto sa = stride_of(ab), sb = stride_of(bb);
+    std::vector<int64_t> idx(nd, 0);
+    for (int64_t b = 0; b < total; ++b) {
+        int64_t rem = b, oa = 0, ob = 0;
+        for (size_t i = nd; i-- > 0;) {
+            idx[i] = rem % batch[i];
+            rem /= batch[i];
+            oa += idx[i] * sa[i];
+            ob += idx[i] * sb[i];
+        }
+        check(pfrt_gemm_f32_dense(ctx_, M, N, Ka, 0, 0, 1.0f, ap + oa * M * Ka, bp + ob * Ka * N, 0.0f, nullptr, 0,
+                                  yp + b * M * N, nullptr), &n);
+    }
+}
+
+// ----------------------------------------------------------------- QuantizedMatMul (+ chain)
+std::vector<const Node*> CudaBackend::Impl::fusable_chain(
+    const Graph& g, const Node& q, const std::unordered_map<std::string, std::vector<const Node*>>& consumers,
+    const std::unordered_set<std::string>& outputs) {
+    std::vector<const Node*> chain;
+    std::string cur = q.outputs()[0];
+    auto sole = [&](const std::string& t) -> const Node* {
+        if (outputs.count(t)) return nullptr;
+        auto it = consumers.find(t);
+        if (it == consumers.end() || it->second.size() != 1) return nullptr;
+        return it->second[0];
+    };
+    const Node* nx = sole(cur);
+    const int64_t N = [&]() -> int64_t {
+        const Tensor* b = initializer(g, q.inputs()[1]);
+        return b ? b->shape().back() : -1;
+    }();
+    if (nx && nx->op_type() == "Add" && nx->inputs().size() == 2) {
+        const std::string& other = nx->inputs()[0] == cur ? nx->inputs()[1] : nx->inputs()[0];
+        const Tensor* bt = initializer(g, other);
+        if (bt && bt->dtype() == DType::Float32 && bt->num_elements() == N && !bt->shape().empty() &&
+            bt->shape().back() == N) {
+            chain.push_back(nx);
+            cur = nx->outputs()[0];
+            nx = sole(cur);
+        }
+    }
+    if (nx && nx->op_type() == "Relu") {
+        chain.push_back(nx);
+        cur = nx->outputs()[0];
+        nx = sole(cur);
+    }
+    if (nx && nx->op_type() == "Quantize") chain.push_back(nx);
+    return chain;
+}
+
+void CudaBackend::Impl::run_qmatmul(const Graph& g, const Node& n, const std::vector<const Node*>& chain) {
+    if (n.inputs().size() < 2)
+        fail_node(n, "QuantizedMatMul requires at least 2 inputs, got " + std::to_string(n.inputs().size()));
+    DevTensor A = value(g, n.inputs()[0], n);
+    const std::string& bname = n.inputs()[1];
+    const Tensor* Binit = initializer(g, bname);
+    DevTensor Bd = value(g, bname, n);
+    if (A.dtype != DType::Int8 && A.dtype != DType::UInt8)
+        fail_node(n, "QuantizedMatMul: input A must be Int8 or UInt8");
+    if (Bd.dtype != DType::Int8) fail_node(n, "QuantizedMatMul: the cuda backend needs Int8 weights (input B)");
+    if (A.shape.size() < 2 || Bd.shape.size() != 2)
+        fail_node(n, "QuantizedMatMul: A needs at least 2 dimensions and B exactly 2 on the cuda backend");
+    const int64_t K = A.shape.back(), Kb = Bd.shape[0], N = Bd.shape[1];
+    if (K != Kb)
+        fail_node(n, "QuantizedMatMul: inner dimensions must match (got " + std::to_string(K) + " and " +
+                         std::to_string(Kb) + ")");
+    const float a_scale = n.get_attr<float>("a_scale", 1.0f);
+    const int32_t a_zp = static_cast<int32_t>(n.get_attr<int64_t>("a_zero_point", 0));
+    const int32_t b_zp = static_cast<int32_t>(n.get_attr<int64_t>("b_zero_point", 0));
+    std::vector<float> b_scales = n.get_attr<std::vector<float>>("b_scales", {});
+    if (b_scales.empty()) b_scales.push_back(n.get_attr<float>("b_scale", 1.0f));
+    if (b_scales.size() != 1 && static_cast<int64_t>(b_scales.size()) != N)
+        fail_node(n, "QuantizedMatMul: b_scales needs 1 or N = " + std::to_string(N) + " values");
+    // Weights: prepared once per (initializer, scales, zero point).
+    std::ostringstream key;
+    key << bname << "|" << b_zp;
+    for (float s : b_scales) key << "," << s;
+    pfrt_qweight* w = nullptr;
+    pfrt_qweight* temp = nullptr;
+    if (Binit) {
+        auto it = qweights_.find(key.str());
+        if (it == qweights_.end()) {
+            check(pfrt_qweight_create(ctx_, K, N, Binit->data_ptr<int8_t>(), b_zp, b_scales.data(),
+                                      static_cast<int64_t>(b_scales.size()), &w), &n);
+            it = qweights_.emplace(key.str(), w).first;
+        }
+        w = it->second;
+    } else {
+        // A runtime weight: prepare it for this run only (from a host copy).
+        std::vector<int8_t> host(static_cast<size_t>(K * N));
+        check(pfrt_memcpy_d2h(ctx_, host.data(), Bd.ptr, host.size(), nullptr), &n);
+        check(pfrt_ctx_check(ctx_, nullptr), &n);
+        check(pfrt_qweight_create(ctx_, K, N, host.data(), b_zp, b_scales.data(), static_cast<int64_t>(b_scales.size()),
+                                  &temp), &n);
+        w = temp;
+    }
+    // Fused tail.
+    const float* bias = nullptr;
+    int relu = 0;
+    int out_mode = PFRT_OUT_F32;
+    float y_scale = 1.0f;
+    int32_t y_zp = 0;
+    const Node* last = &n;
+    for (const Node* c : chain) {
+        if (c->op_type() == "Add") {
+            const std::string& other = c->inputs()[0] == last->outputs()[0] ? c->inputs()[1] : c->inputs()[0];
+            bias = static_cast<const float*>(init_device(g, other).ptr);
+        } else if (c->op_type() == "Relu") {
+            relu = 1;
+        } else if (c->op_type() == "Quantize") {
+            y_scale = c->get_attr<float>("scale", 1.0f);
+            y_zp = static_cast<int32_t>(c->get_attr<int64_t>("zero_point", 0));
+            out_mode = c->get_attr<std::string>("dtype", "int8") == "uint8" ? PFRT_OUT_U8 : PFRT_OUT_S8;
+        }
+        last = c;
+    }
+    const int64_t M = numel(A.shape) / K;
+    std::vector<int64_t> out_shape(A.shape.begin(), A.shape.end() - 1);
+    out_shape.push_back(N);
+    const DType odt = out_mode == PFRT_OUT_F32 ? DType::Float32 : (out_mode == PFRT_OUT_U8 ? DType::UInt8 : DType::Int8);
+    DevTensor Y = new_value(last->outputs()[0], out_shape, odt);
+    const pfrt_status st = pfrt_qlinear(ctx_, w, M, A.ptr, K, A.dtype == DType::UInt8 ? 1 : 0, a_scale, a_zp, bias, relu,
+                                        out_mode, y_scale, y_zp, Y.ptr, N, nullptr, nullptr);
+    if (temp) {
+        pfrt_ctx_check(ctx_, nullptr);
+        pfrt_qweight_destroy(temp);
+    }
+    check(st, last);
+}
+
+// ----------------------------------------------------------------- SparseMatMul
+void CudaBackend::Impl::run_sparse(const Graph& g, const Node& n) {
+    if (n.inputs().size() != 4)
+        fail_node(n, "SparseMatMul requires 4 inputs (X, indptr, indices, values), got " + std::to_string(n.inputs().size()));
+    DevTensor X = value(g, n.inputs()[0], n);
+    const std::vector<int64_t> shape = n.get_attr<std::vector<int64_t>>("shape", {});
+    if (shape.size() != 2) fail_node(n, "SparseMatMul: attribute shape = [N, K] is required");
+    const int64_t N = shape[0], K = shape[1];
+    if (X.dtype != DType::Float32) fail_node(n, "SparseMatMul: X must be float32");
+    if (X.shape.empty() || X.shape.back() != K) fail_node(n, "Dimension mismatch in sparse matmul");
+    auto it = csrs_.find(n.name());
+    if (it == csrs_.end()) {
+        const Tensor* ip = initializer(g, n.inputs()[1]);
+        const Tensor* ix = initializer(g, n.inputs()[2]);
+        const Tensor* v = initializer(g, n.inputs()[3]);
+        if (!ip || !ix || !v) fail_node(n, "SparseMatMul: indptr, indices and values must be initializers");
+        if (ip->dtype() != ix->dtype() || (ip->dtype() != DType::Int32 && ip->dtype() != DType::Int64))
+            fail_node(n, "SparseMatMul: indptr and indices must both be int32 or both int64");
+        if (v->dtype() != DType::Float32) fail_node(n, "SparseMatMul: values must be float32");
+        if (ip->num_elements() != N + 1) fail_node(n, "CSR indptr must have length rows + 1");
+        if (ix->num_elements() != v->num_elements()) fail_node(n, "CSR indices and values must have same length");
+        pfrt_csr* csr = nullptr;
+        check(pfrt_csr_create(ctx_, N, K, v->num_elements(), ip->data(), ix->data(),
+                              ip->dtype() == DType::Int32 ? 32 : 64, v->data_ptr<float>(), &csr), &n);
+        it = csrs_.emplace(n.name(), csr).first;
+    }
+    const int64_t M = numel(X.shape) / std::max<int64_t>(K, 1);
+    std::vector<int64_t> out_shape(X.shape.begin(), X.shape.end() - 1);
+    out_shape.push_back(N);
+    DevTensor Y = new_value(n.outputs()[0], out_shape, DType::Float32);
+    check(pfrt_spmm(ctx_, it->second, M, static_cast<const float*>(X.ptr), K, static_cast<float*>(Y.ptr), N, nullptr),
+          &n);
+}
+
+// ----------------------------------------------------------------- elementwise
+void CudaBackend::Impl::run_add(const Graph& g, const Node& n) {
+    if (n.inputs().size() < 2) fail_node(n, "Add requires at least 2 inputs, got " + std::to_string(n.inputs().size()));
+    DevTensor a = value(g, n.inputs()[0], n);
+    DevTensor b = value(g, n.inputs()[1], n);
+    if (a.dtype != DType::Float32 || b.dtype != DType::Float32) fail_node(n, "Add: the cuda backend computes float32 only");
+    // The larger operand is the matrix, the other must be the same size, a row
+    // vector over its last dimension, or a scalar (addition commutes).
+    if (a.numel() < b.numel()) std::swap(a, b);
+    const int64_t cols = b.numel();
+    const bool ok = cols > 0 && (cols == a.numel() || cols == 1 || (!a.shape.empty() && cols == a.shape.back() &&
+                                                                    (b.shape.size() == 1 || b.shape.back() == cols)));
+    if (!ok) fail_node(n, "Add: the cuda backend broadcasts only a row vector or a scalar (" + shape_str(a.shape) +
+                              " + " + shape_str(b.shape) + ")");
+    DevTensor y = new_value(n.outputs()[0], a.shape, DType::Float32);
+    check(pfrt_add_rowvec_f32(ctx_, a.numel() / cols, cols, static_cast<const float*>(a.ptr),
+                              static_cast<const float*>(b.ptr), static_cast<float*>(y.ptr), nullptr), &n);
+}
+
+void CudaBackend::Impl::run_relu(const Graph& g, const Node& n) {
+    if (n.inputs().empty()) fail_node(n, "Relu requires at least 1 inputs, got 0");
+    DevTensor x = value(g, n.inputs()[0], n);
+    if (x.dtype != DType::Float32) fail_node(n, "Relu: the cuda backend computes float32 only");
+    DevTensor y = new_value(n.outputs()[0], x.shape, DType::Float32);
+    check(pfrt_relu_f32(ctx_, x.numel(), static_cast<const float*>(x.ptr), static_cast<float*>(y.ptr), nullptr), &n);
+}
+
+void CudaBackend::Impl::run_quantize(const Graph& g, const Node& n) {
+    if (n.inputs().empty()) fail_node(n, "Quantize requires at least 1 inputs, got 0");
+    DevTensor x = value(g, n.inputs()[0], n);
+    if (x.dtype != DType::Float32)
+        fail_node(n, "quantize_tensor: input must be Float32, got " + dtype_name(x.dtype));
+    const float scale = n.get_attr<float>("scale", 1.0f);
+    const int32_t zp = static_cast<int32_t>(n.get_attr<int64_t>("zero_point", 0));
+    const bool u8 = n.get_attr<std::string>("dtype", "int8") == "uint8";
+    DevTensor y = new_value(n.outputs()[0], x.shape, u8 ? DType::UInt8 : DType::Int8);
+    check(pfrt_quantize_f32(ctx_, x.numel(), static_cast<const float*>(x.ptr), scale, zp, u8 ? 1 : 0, y.ptr, nullptr),
+          &n);
+}
+
+// ----------------------------------------------------------------- execute
+std::vector<Tensor> CudaBackend::Impl::execute(const Graph& graph, const std::unordered_map<std::string, Tensor>& feeds,
+                                               const std::vector<std::string>& output_names) {
+    std::lock_guard<std::mutex> lock(mu_);
+    bind_graph(graph);
+    vals_.clear();
+    // Inputs to the device.
+    for (const auto& [name, t] : feeds) {
+        DevTensor d;
+        d.shape = t.shape();
+        d.dtype = t.dtype();
+        d.ptr = device_alloc("in:" + name, t.size_bytes());
+        check(pfrt_memcpy_h2d(ctx_, d.ptr, t.data(), t.size_bytes(), nullptr), nullptr);
+        vals_[name] = d;
+    }
+    const auto order = graph.topological_sort();
+    std::unordered_map<std::string, std::vector<const Node*>> consumers;
+    for (const auto& node : order)
+        for (const auto& in : node->inputs()) consumers[in].push_back(node.get());
+    std::unordered_set<std::string> outputs;
+    for (const auto& o : graph.outputs()) outputs.insert(o.name);
+    for (const auto& o : output_names) outputs.insert(o);
+    std::unordered_set<const Node*> fused;
+    for (const auto& node : order) {
+        const Node& n = *node;
+        if (fused.count(&n)) continue;
+        const std::string& op = n.op_type();
+        try {
+            if (op == "Gemm") {
+                run_gemm(graph, n);
+            } else if (op == "MatMul") {
+                run_matmul(graph, n);
+            } else if (op == "QuantizedMatMul") {
+                const auto chain = fusable_chain(graph, n, consumers, outputs);
+                for (const Node* c : chain) fused.insert(c);
+                run_qmatmul(graph, n, chain);
+            } else if (op == "SparseMatMul") {
+                run_sparse(graph, n);
+            } else if (op == "Add") {
+                run_add(graph, n);
+            } else if (op == "Relu") {
+                run_relu(graph, n);
+            } else if (op == "Quantize") {
+                run_quantize(graph, n);
+            } else {
+                throw UnsupportedOperatorError(op, "cuda");
+            }
+        } catch (const PyFlameRTError&) {
+            throw;
+        } catch (const std::exception& e) {
+            throw BackendError(e.what(), n.name());
+        }
+    }
+    // Outputs back to the host.
+    std::vector<std::string> names = output_names;
+    if (names.empty())
+        for (const auto& o : graph.outputs()) names.push_back(o.name);
+    std::vector<Tensor> results;
+    results.reserve(names.size());
+    for (const auto& name : names) {
+        auto it = vals_.find(name);
+        DevTensor d;
+        if (it != vals_.end()) {
+            d = it->second;
+        } else if (initializer(graph, name)) {
+            results.push_back(initializer(graph, name)->clone());
+            continue;
+        } else {
+            throw BackendError("Output tensor '" + name + "' not found");
+        }
+        Tensor out(d.shape, d.dtype);
+        if (d.bytes()) check(pfrt_memcpy_d2h(ctx_, out.data(), d.ptr, d.bytes(), nullptr), nullptr);
+        results.push_back(std::move(out));
+    }
+    check(pfrt_ctx_check(ctx_, nullptr), nullptr);
+    return results;
+}
+
+// ----------------------------------------------------------------- public
+CudaBackend::CudaBackend(int device) : impl_(std::make_unique<Impl>(device)) {}
+CudaBackend::~CudaBackend() = default;
+
+const std::string& CudaBackend::name() const {
+    static const std::string n = "cuda";
+    return n;
+}
+
+bool CudaBackend::supports_op(const std::string& op_type) const {
+    const auto& ops = supported_ops();
+    return std::find(ops.begin(), ops.end(), op_type) != ops.end();
+}
+
+std::vector<std::string> CudaBackend::get_supported_ops() const { return supported_ops(); }
+
+std::vector<Tensor> CudaBackend::execute(const Graph& graph, const std::unordered_map<std::string, Tensor>& input_feed,
+                                         const std::vector<std::string>& output_names) {
+    validate_inputs(graph, input_feed);
+    return impl_->execute(graph, input_feed, output_names);
+}
+
+int CudaBackend::device() const { return impl_->device_; }
+
+std::unique_ptr<Backend> make_cuda_backend(int device) { return std::make_unique<CudaBackend>(device); }
+
+}  // namespace pyflame_rt

@@ -1,0 +1,69 @@
+// cuda_backend.hpp -- PyFlameRT execution backend for B200 (sm_100a).
+//
+// Implements the reference's plugin interface pyflame_rt::Backend
+// (include/pyflame_rt/backend.hpp:14-46) over the C ABI in pfrt_cuda.h, so
+// that InferenceSession can run a graph with device = "cuda" in place of
+// CPUExecutor (src/backends/cpu/executor.cpp:45-147), with no change to the
+// graph, the importers or the session's run().
+//
+// Node types and their reference counterparts:
+//   Gemm             cpu_gemm             (src/backends/cpu/ops/math.cpp:377-438)
+//   MatMul           cpu_matmul           (math.cpp:268-374)
+//   QuantizedMatMul  quantized_matmul     (src/quantization/quant_ops.cpp:387-506);
+//                    per-tensor a_scale/b_scale/a_zero_point/b_zero_point as the
+//                    graph op (quantized_ops.cpp:87-90), or per-output-channel
+//                    b_scales (float vector).  A following Add (initializer
+//                    bias [N]) -> Relu -> Quantize chain is fused into it.
+//   SparseMatMul     sparse_matmul        (src/pruning/sparse_tensor.cpp:473-519):
+//                    inputs X, indptr, indices, values; attr shape = [N, K];
+//                    Y[M,N] = X W^T
+//   Add, Relu        cpu_add, cpu_relu    (math.cpp:222-226, activation.cpp:45-60):
+//                    same shapes, or a row-vector / scalar operand
+//   Quantize         cpu_quantize         (quantized_ops.cpp, quantize_tensor)
+// Any other node type raises UnsupportedOperatorError(op, "cuda"); there is
+// no CPU fallback.  Errors inside a node raise BackendError(message, node name)
+// as CPUExecutor does (executor.cpp:106-110).
+//
+// Initializers (weights, biases, CSR arrays) are uploaded and prepared once
+// per graph and reused across runs; graph inputs are copied to the device and
+// graph outputs back to new host Tensors on every run.  execute() is
+// serialised by a mutex, so a session may call it from several threads.
+#pragma once
+
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "pyflame_rt/backend.hpp"
+
+namespace pyflame_rt {
+
+class CudaBackend : public Backend {
+public:
+    explicit CudaBackend(int device = 0);
+    ~CudaBackend() override;
+
+    CudaBackend(const CudaBackend&) = delete;
+    CudaBackend& operator=(const CudaBackend&) = delete;
+
+    const std::string& name() const override;
+    bool supports_op(const std::string& op_type) const override;
+    std::vector<std::string> get_supported_ops() const override;
+
+    std::vector<Tensor> execute(const Graph& graph,
+                                const std::unordered_map<std::string, Tensor>& input_feed,
+                                const std::vector<std::string>& output_names = {}) override;
+
+    int device() const;
+
+private:
+    class Impl;
+    std::unique_ptr<Impl> impl_;
+};
+
+/// Factory for the session seam (InferenceSession::select_backend): a CudaBackend on
+/// the given device ordinal.
+std::unique_ptr<Backend> make_cuda_backend(int device = 0);
+
+}  // namespace pyflame_rt

@@ -110,10 +110,94 @@ def build_oracle() -> None:
     _run(["make", "-s", "-C", os.path.join(ROOT, "oracle")])
 
 
+def build_native_tests() -> str | None:
+    """tests/native/test_cuda_backend: the Backend plugin against the
+    reference's CPUExecutor (test infrastructure; needs the reference headers
+    and oracle/_ref)."""
+    inc = reference_include()
+    ref_lib = os.path.join(ROOT, "oracle", "_ref", "libpfrt_ref.so")
+    src = os.path.join(ROOT, "tests", "native", "test_cuda_backend.cpp")
+    if inc is None or not os.path.exists(ref_lib) or not os.path.exists(src):
+        return None
+    out_dir = os.path.join(ROOT, "tests", "native", "_build")
+    os.makedirs(out_dir, exist_ok=True)
+    exe = os.path.join(out_dir, "test_cuda_backend")
+    deps = [src, ref_lib, os.path.join(LIB, "libpfrt_cuda_backend.so")]
+    if _stale(exe, deps):
+        cxx = os.environ.get("CXX", "g++")
+        ref_src = os.path.join(os.path.dirname(inc), "src")
+        _run([cxx, "-std=c++17", "-O2", f"-I{inc}", f"-I{ref_src}", f"-I{INCLUDE}",
+              f"-I{os.path.join(PKG, 'backend')}", f"-I{os.path.join(ROOT, 'oracle')}", "-o", exe, src,
+              f"-L{LIB}", "-lpfrt_cuda_backend", "-lpfrt_cuda",
+              f"-L{os.path.dirname(ref_lib)}", "-lpfrt_ref",
+              f"-L{os.path.join(ROOT, 'oracle', '_build')}", "-loracle",
+              "-Wl,-rpath,$ORIGIN/../../../pyflamert_b200/lib:$ORIGIN/../../../oracle/_ref:"
+              "$ORIGIN/../../../oracle/_build",
+              "-lpthread"])
+    return exe
+
+
+# The session seam: the two edits that let SessionOptions.device = "cuda"
+# select the CudaBackend (src/options.cpp:12-17, src/session.cpp:67-95).
+SEAM_EDITS = {
+    "src/options.cpp": [('"cpu", "wse", "wse2", "wse3"', '"cpu", "cuda", "wse", "wse2", "wse3"')],
+    "src/session.cpp": [
+        ('if (options_.device != "cpu") {', 'if (options_.device != "cpu" && options_.device != "cuda") {'),
+        ("    backend_ = std::make_unique<CPUExecutor>(",
+         "    if (options_.device == \"cuda\") { backend_ = ::pyflame_rt::make_cuda_backend(0); return; }\n"
+         "    backend_ = std::make_unique<CPUExecutor>("),
+    ],
+}
+
+SESSION_SRCS = ["src/io/loader.cpp", "src/io/pyflame_format.cpp", "src/quantization/calibrator.cpp",
+                "src/opt/pass_manager.cpp", "src/opt/layout_optimization.cpp"]
+
+
+def build_session_test() -> str | None:
+    """tests/native/test_session_seam: the reference's InferenceSession, with
+    the seam edits applied to copies of its sources, running device="cuda"
+    against device="cpu".  Test infrastructure; needs the reference sources."""
+    inc = reference_include()
+    ref_lib = os.path.join(ROOT, "oracle", "_ref", "libpfrt_ref.so")
+    src = os.path.join(ROOT, "tests", "native", "test_session_seam.cpp")
+    if inc is None or not os.path.exists(ref_lib) or not os.path.exists(src):
+        return None
+    ref = os.path.dirname(inc)
+    out_dir = os.path.join(ROOT, "tests", "native", "_build")
+    os.makedirs(out_dir, exist_ok=True)
+    exe = os.path.join(out_dir, "test_session_seam")
+    stubs = os.path.join(ROOT, "tests", "native", "ref_session_stubs.cpp")
+    deps = [src, stubs, ref_lib, os.path.join(LIB, "libpfrt_cuda_backend.so")]
+    if not _stale(exe, deps):
+        return exe
+    import tempfile
+    srcs = [src, stubs] + [os.path.join(ref, f) for f in SESSION_SRCS]
+    with tempfile.TemporaryDirectory() as tmp:  # patched copies never enter the tree
+        for rel, edits in SEAM_EDITS.items():
+            text = open(os.path.join(ref, rel)).read()
+            for old, new in edits:
+                if old not in text:
+                    raise RuntimeError(f"seam edit does not apply to {rel}: {old!r}")
+                text = text.replace(old, new, 1)
+            patched = os.path.join(tmp, os.path.basename(rel))
+            with open(patched, "w") as f:
+                f.write(text)
+            srcs.append(patched)
+        cxx = os.environ.get("CXX", "g++")
+        _run([cxx, "-std=c++17", "-O2", "-w", f"-I{inc}", f"-I{os.path.join(ref, 'src')}", f"-I{INCLUDE}",
+              f"-I{os.path.join(PKG, 'backend')}", "-include", "pyflame_rt/tensor.hpp", "-include",
+              "cuda_backend.hpp", "-o", exe] + srcs +
+             [f"-L{LIB}", "-lpfrt_cuda_backend", "-lpfrt_cuda", f"-L{os.path.dirname(ref_lib)}", "-lpfrt_ref",
+              "-Wl,-rpath,$ORIGIN/../../../pyflamert_b200/lib:$ORIGIN/../../../oracle/_ref", "-lpthread"])
+    return exe
+
+
 def build_all(verbose: bool = False) -> None:
     build_cuda(verbose=verbose)
     build_backend()
     build_oracle()
+    build_native_tests()
+    build_session_test()
 
 
 if __name__ == "__main__":

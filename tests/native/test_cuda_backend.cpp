@@ -1,0 +1,413 @@
+// test_cuda_backend.cpp -- the PyFlameRT Backend plugin (CudaBackend) against
+// the reference's own CPUExecutor, in the style of the reference's
+// tests/cpp/test_executor.cpp: graphs are built in-process from Graph, Node and
+// Tensor, run on both backends, and compared.
+//
+// Links the reference runtime compiled from its sources (oracle/_ref) and the
+// C restatement (oracle/_build) as checkers, and the product libraries
+// libpfrt_cuda_backend.so / libpfrt_cuda.so.  Needs a B200; run by
+// tests/test_gpu_backend.py.  Prints one "PASS name" or "FAIL name: why" line
+// per test and exits non-zero if any test failed.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <memory>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "backends/cpu/executor.hpp"
+#include "cuda_backend.hpp"
+#include "oracle.h"
+#include "pyflame_rt/errors.hpp"
+#include "pyflame_rt/graph.hpp"
+
+using namespace pyflame_rt;
+
+namespace {
+
+int g_failed = 0;
+
+struct Failure : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+#define EXPECT(cond, msg)                   \
+    do {                                    \
+        if (!(cond)) throw Failure(msg);    \
+    } while (0)
+
+void run_test(const char* name, const std::function<void()>& fn) {
+    try {
+        fn();
+        std::printf("PASS %s\n", name);
+    } catch (const std::exception& e) {
+        std::printf("FAIL %s: %s\n", name, e.what());
+        ++g_failed;
+    }
+    std::fflush(stdout);
+}
+
+Shape sh(std::vector<int64_t> d) {
+    Shape s;
+    for (auto v : d) s.push_back(v);
+    return s;
+}
+
+Tensor randn(std::vector<int64_t> shape, float stddev, uint64_t seed) {
+    Tensor t(shape, DType::Float32);
+    std::mt19937_64 rng(seed);
+    std::normal_distribution<float> nd(0.0f, stddev);
+    float* p = t.data_ptr<float>();
+    for (int64_t i = 0; i < t.num_elements(); ++i) p[i] = nd(rng);
+    return t;
+}
+
+template <class T>
+Tensor randint(std::vector<int64_t> shape, int lo, int hi, DType dt, uint64_t seed) {
+    Tensor t(shape, dt);
+    std::mt19937_64 rng(seed);
+    std::uniform_int_distribution<int> d(lo, hi);
+    T* p = t.data_ptr<T>();
+    for (int64_t i = 0; i < t.num_elements(); ++i) p[i] = static_cast<T>(d(rng));
+    return t;
+}
+
+double normwise(const Tensor& a, const Tensor& b) {
+    const float* x = a.data_ptr<float>();
+    const float* y = b.data_ptr<float>();
+    double num = 0, den = 0;
+    for (int64_t i = 0; i < a.num_elements(); ++i) {
+        num = std::max(num, std::fabs(static_cast<double>(x[i]) - y[i]));
+        den = std::max(den, std::fabs(static_cast<double>(y[i])));
+    }
+    return den > 0 ? num / den : num;
+}
+
+bool same_bytes(const Tensor& a, const Tensor& b) {
+    return a.shape() == b.shape() && a.dtype() == b.dtype() &&
+           std::memcmp(a.data(), b.data(), a.size_bytes()) == 0;
+}
+
+std::shared_ptr<Node> node(const std::string& name, const std::string& op, std::vector<std::string> in,
+                           std::vector<std::string> out) {
+    return std::make_shared<Node>(name, op, std::move(in), std::move(out));
+}
+
+std::vector<Tensor> run(Backend& be, const Graph& g, const std::unordered_map<std::string, Tensor>& feeds) {
+    return be.execute(g, feeds);
+}
+
+}  // namespace
+
+int main() {
+    CudaBackend cuda(0);
+    CPUExecutor cpu(0);
+
+    // ExecutorTest.SupportedOps analogue (tests/cpp/test_executor.cpp:150-158).
+    run_test("SupportedOps", [&] {
+        EXPECT(cuda.name() == "cuda", "name");
+        EXPECT(cuda.supports_op("MatMul") && cuda.supports_op("Gemm") && cuda.supports_op("QuantizedMatMul"),
+               "hot-path ops must be supported");
+        EXPECT(!cuda.supports_op("NonExistentOp"), "unknown op reported as supported");
+    });
+
+    // ExecutorTest.MatMul (tests/cpp/test_executor.cpp:162-208), same graph and values.
+    run_test("MatMulKnownAnswer", [&] {
+        Graph graph("test");
+        graph.add_input(TensorInfo("a", sh({2, 3}), DType::Float32));
+        graph.add_input(TensorInfo("b", sh({3, 2}), DType::Float32));
+        graph.add_output(TensorInfo("c", sh({2, 2}), DType::Float32));
+        graph.add_node(node("matmul_0", "MatMul", {"a", "b"}, {"c"}));
+        Tensor a({2, 3}, DType::Float32), b({3, 2}, DType::Float32);
+        float av[] = {1, 2, 3, 4, 5, 6}, bv[] = {1, 2, 3, 4, 5, 6};
+        std::memcpy(a.data(), av, sizeof(av));
+        std::memcpy(b.data(), bv, sizeof(bv));
+        std::unordered_map<std::string, Tensor> feeds;
+        feeds["a"] = std::move(a);
+        feeds["b"] = std::move(b);
+        auto out = cuda.execute(graph, feeds);
+        EXPECT(out.size() == 1, "one output");
+        const float* o = out[0].data_ptr<float>();
+        EXPECT(o[0] == 22.0f && o[1] == 28.0f && o[2] == 49.0f && o[3] == 64.0f, "[[22,28],[49,64]]");
+    });
+
+    // Config 1: Gemm with initializer B and bias C, alpha = beta = 1.
+    run_test("GemmConfig1", [&] {
+        Graph g("gemm");
+        g.add_input(TensorInfo("A", sh({256, 1024}), DType::Float32));
+        g.add_initializer("B", randn({1024, 1024}, 1.0f / 32.0f, 2));
+        g.add_initializer("C", randn({1024}, 0.1f, 3));
+        auto n = node("gemm_0", "Gemm", {"A", "B", "C"}, {"Y"});
+        n->set_attr("alpha", 1.0f);
+        n->set_attr("beta", 1.0f);
+        g.add_node(n);
+        g.add_output(TensorInfo("Y", sh({256, 1024}), DType::Float32));
+        std::unordered_map<std::string, Tensor> feeds;
+        feeds["A"] = randn({256, 1024}, 1.0f, 1);
+        auto y = run(cuda, g, feeds);
+        auto r = run(cpu, g, feeds);
+        const double e = normwise(y[0], r[0]);
+        EXPECT(e <= 1e-5, "normwise error " + std::to_string(e));
+        auto y2 = run(cuda, g, feeds);  // second run reuses the prepared weight
+        EXPECT(same_bytes(y[0], y2[0]), "second run differs");
+    });
+
+    run_test("GemmTransposedRuntimeB", [&] {
+        Graph g("gemm_t");
+        g.add_input(TensorInfo("A", sh({70, 33}), DType::Float32));
+        g.add_input(TensorInfo("B", sh({45, 70}), DType::Float32));
+        auto n = node("gemm_t", "Gemm", {"A", "B"}, {"Y"});
+        n->set_attr("alpha", 0.5f);
+        n->set_attr("transA", int64_t{1});
+        n->set_attr("transB", int64_t{1});
+        g.add_node(n);
+        g.add_output(TensorInfo("Y", sh({33, 45}), DType::Float32));
+        std::unordered_map<std::string, Tensor> feeds;
+        feeds["A"] = randn({70, 33}, 1.0f, 4);
+        feeds["B"] = randn({45, 70}, 1.0f, 5);
+        const double e = normwise(run(cuda, g, feeds)[0], run(cpu, g, feeds)[0]);
+        EXPECT(e <= 1e-5, "normwise error " + std::to_string(e));
+    });
+
+    run_test("MatMulBatchedBroadcast", [&] {
+        Graph g("bmm");
+        g.add_input(TensorInfo("A", sh({2, 3, 5, 7}), DType::Float32));
+        g.add_initializer("W", randn({7, 4}, 1.0f, 6));
+        g.add_input(TensorInfo("B", sh({3, 7, 4}), DType::Float32));
+        g.add_node(node("mm_w", "MatMul", {"A", "W"}, {"Y1"}));
+        g.add_node(node("mm_b", "MatMul", {"A", "B"}, {"Y2"}));
+        g.add_output(TensorInfo("Y1", sh({2, 3, 5, 4}), DType::Float32));
+        g.add_output(TensorInfo("Y2", sh({2, 3, 5, 4}), DType::Float32));
+        std::unordered_map<std::string, Tensor> feeds;
+        feeds["A"] = randn({2, 3, 5, 7}, 1.0f, 7);
+        feeds["B"] = randn({3, 7, 4}, 1.0f, 8);
+        auto y = run(cuda, g, feeds);
+        auto r = run(cpu, g, feeds);
+        EXPECT(normwise(y[0], r[0]) <= 1e-5 && normwise(y[1], r[1]) <= 1e-5, "batched MatMul differs");
+    });
+
+    // QuantizedMatMul -> Add -> Relu -> Quantize on int8 x int8, where the
+    // reference graph op (quantized_ops.cpp:77-167) is exact: fused kernel vs
+    // the reference's four CPU ops, bit for bit.
+    auto quant_chain = [&](bool expose_intermediate) {
+        const int64_t M = 96, K = 256, N = 160;
+        Graph g("qchain");
+        g.add_input(TensorInfo("X", sh({M, K}), DType::Int8));
+        g.add_initializer("W", randint<int8_t>({K, N}, -127, 127, DType::Int8, 9));
+        g.add_initializer("bias", randn({N}, 10.0f, 10));
+        auto q = node("qmm", "QuantizedMatMul", {"X", "W"}, {"t0"});
+        q->set_attr("a_scale", 0.02f);
+        q->set_attr("b_scale", 0.0125f);
+        q->set_attr("a_zero_point", int64_t{3});
+        q->set_attr("b_zero_point", int64_t{0});
+        g.add_node(q);
+        g.add_node(node("add", "Add", {"t0", "bias"}, {"t1"}));
+        g.add_node(node("relu", "Relu", {"t1"}, {"t2"}));
+        auto qz = node("quant", "Quantize", {"t2"}, {"Y"});
+        qz->set_attr("scale", 0.7f);
+        qz->set_attr("zero_point", int64_t{4});
+        qz->set_attr("dtype", std::string("uint8"));
+        g.add_node(qz);
+        g.add_output(TensorInfo("Y", sh({M, N}), DType::UInt8));
+        if (expose_intermediate) g.add_output(TensorInfo("t1", sh({M, N}), DType::Float32));
+        std::unordered_map<std::string, Tensor> feeds;
+        feeds["X"] = randint<int8_t>({M, K}, -128, 127, DType::Int8, 11);
+        auto y = run(cuda, g, feeds);
+        auto r = run(cpu, g, feeds);
+        EXPECT(y.size() == r.size(), "output count");
+        for (size_t i = 0; i < y.size(); ++i) EXPECT(same_bytes(y[i], r[i]), "output " + std::to_string(i) + " differs");
+    };
+    run_test("QuantizedChainFused", [&] { quant_chain(false); });
+    run_test("QuantizedChainUnfused", [&] { quant_chain(true); });
+
+    // uint8 activations with per-output-channel scales (b_scales): checked
+    // against the C restatement of quant_ops.cpp (the reference graph op
+    // reads uint8 as int8, quantized_ops.cpp:143).
+    run_test("QuantizedPerChannelUint8", [&] {
+        const int64_t M = 64, K = 512, N = 200;
+        Graph g("qpc");
+        g.add_input(TensorInfo("X", sh({M, K}), DType::UInt8));
+        Tensor w = randint<int8_t>({K, N}, -127, 127, DType::Int8, 12);
+        g.add_initializer("W", w);
+        Tensor bias = randn({N}, 10.0f, 13);
+        g.add_initializer("bias", bias);
+        std::vector<float> scales(N);
+        std::mt19937_64 rng(14);
+        std::uniform_real_distribution<float> ud(0.005f, 0.02f);
+        for (auto& s : scales) s = ud(rng);
+        auto q = node("qmm", "QuantizedMatMul", {"X", "W"}, {"t0"});
+        q->set_attr("a_scale", 0.02f);
+        q->set_attr("a_zero_point", int64_t{128});
+        q->set_attr("b_scales", scales);
+        g.add_node(q);
+        g.add_node(node("add", "Add", {"t0", "bias"}, {"t1"}));
+        g.add_node(node("relu", "Relu", {"t1"}, {"t2"}));
+        auto qz = node("quant", "Quantize", {"t2"}, {"Y"});
+        qz->set_attr("scale", 2.0f);
+        qz->set_attr("dtype", std::string("uint8"));
+        g.add_node(qz);
+        g.add_output(TensorInfo("Y", sh({M, N}), DType::UInt8));
+        Tensor x = randint<uint8_t>({M, K}, 0, 255, DType::UInt8, 15);
+        std::unordered_map<std::string, Tensor> feeds;
+        feeds["X"] = x;
+        auto y = run(cuda, g, feeds);
+        Tensor ref({M, N}, DType::UInt8);
+        oracle_qlinear(M, N, K, x.data(), 1, 0.02f, 128, w.data_ptr<int8_t>(), 0, scales.data(),
+                       bias.data_ptr<float>(), 1, 2, 2.0f, 0, nullptr, ref.data(), nullptr);
+        EXPECT(same_bytes(y[0], ref), "per-channel uint8 chain differs from the reference arithmetic");
+    });
+
+    // The config-4 network at a small batch: 4 x (QuantizedMatMul -> Add -> Relu -> Quantize).
+    run_test("Int8MlpFourLayers", [&] {
+        const int64_t M = 32, H = 512;
+        Graph g("mlp");
+        g.add_input(TensorInfo("X", sh({M, H}), DType::UInt8));
+        std::string cur = "X";
+        float a_scale = 0.02f;
+        int64_t a_zp = 128;
+        const float y_scales[4] = {2.86f, 103.25f, 3800.03f, 189326.23f};
+        std::vector<Tensor> ws, bs;
+        std::vector<std::vector<float>> scs;
+        Tensor x = randint<uint8_t>({M, H}, 0, 255, DType::UInt8, 16);
+        for (int l = 0; l < 4; ++l) {
+            const std::string s = std::to_string(l);
+            ws.push_back(randint<int8_t>({H, H}, -127, 127, DType::Int8, 20 + l));
+            bs.push_back(randn({H}, 10.0f, 30 + l));
+            std::vector<float> sc(H);
+            std::mt19937_64 rng(40 + l);
+            std::uniform_real_distribution<float> ud(0.005f, 0.02f);
+            for (auto& v : sc) v = ud(rng);
+            scs.push_back(sc);
+            g.add_initializer("W" + s, ws.back());
+            g.add_initializer("b" + s, bs.back());
+            auto q = node("qmm" + s, "QuantizedMatMul", {cur, "W" + s}, {"q" + s});
+            q->set_attr("a_scale", a_scale);
+            q->set_attr("a_zero_point", a_zp);
+            q->set_attr("b_scales", sc);
+            g.add_node(q);
+            g.add_node(node("add" + s, "Add", {"q" + s, "b" + s}, {"a" + s}));
+            g.add_node(node("relu" + s, "Relu", {"a" + s}, {"r" + s}));
+            auto qz = node("quant" + s, "Quantize", {"r" + s}, {"h" + s});
+            qz->set_attr("scale", y_scales[l]);
+            qz->set_attr("dtype", std::string("uint8"));
+            g.add_node(qz);
+            cur = "h" + s;
+            a_scale = y_scales[l];
+            a_zp = 0;
+        }
+        g.add_output(TensorInfo(cur, sh({M, H}), DType::UInt8));
+        std::unordered_map<std::string, Tensor> feeds;
+        feeds["X"] = x;
+        auto y = run(cuda, g, feeds);
+        Tensor h = x;
+        float as = 0.02f;
+        int32_t az = 128;
+        for (int l = 0; l < 4; ++l) {
+            Tensor nh({M, H}, DType::UInt8);
+            oracle_qlinear(M, H, H, h.data(), 1, as, az, ws[l].data_ptr<int8_t>(), 0, scs[l].data(),
+                           bs[l].data_ptr<float>(), 1, 2, y_scales[l], 0, nullptr, nh.data(), nullptr);
+            h = nh;
+            as = y_scales[l];
+            az = 0;
+        }
+        EXPECT(same_bytes(y[0], h), "4-layer MLP output differs from the reference arithmetic");
+    });
+
+    // SparseMatMul (pruned Linear): Y = X W^T, W [N,K] CSR int64.
+    run_test("SparseMatMul", [&] {
+        const int64_t M = 9, N = 300, K = 700;
+        std::mt19937_64 rng(17);
+        std::bernoulli_distribution keep(0.1);
+        std::normal_distribution<float> nd(0.0f, 0.02f);
+        std::vector<int64_t> ip(1, 0), ix;
+        std::vector<float> vv;
+        for (int64_t r = 0; r < N; ++r) {
+            for (int64_t c = 0; c < K; ++c)
+                if (keep(rng)) {
+                    ix.push_back(c);
+                    vv.push_back(nd(rng));
+                }
+            ip.push_back(static_cast<int64_t>(ix.size()));
+        }
+        Graph g("spmm");
+        g.add_input(TensorInfo("X", sh({M, K}), DType::Float32));
+        Tensor tip({N + 1}, DType::Int64), tix({static_cast<int64_t>(ix.size())}, DType::Int64),
+            tv({static_cast<int64_t>(vv.size())}, DType::Float32);
+        std::memcpy(tip.data(), ip.data(), 8 * ip.size());
+        std::memcpy(tix.data(), ix.data(), 8 * ix.size());
+        std::memcpy(tv.data(), vv.data(), 4 * vv.size());
+        g.add_initializer("indptr", tip);
+        g.add_initializer("indices", tix);
+        g.add_initializer("values", tv);
+        auto n = node("spmm", "SparseMatMul", {"X", "indptr", "indices", "values"}, {"Y"});
+        n->set_attr("shape", std::vector<int64_t>{N, K});
+        g.add_node(n);
+        g.add_output(TensorInfo("Y", sh({M, N}), DType::Float32));
+        Tensor x = randn({M, K}, 1.0f, 18);
+        std::unordered_map<std::string, Tensor> feeds;
+        feeds["X"] = x;
+        auto y = run(cuda, g, feeds);
+        std::vector<int32_t> ip32(ip.begin(), ip.end()), ix32(ix.begin(), ix.end());
+        Tensor ref({M, N}, DType::Float32);
+        oracle_spmm_linear(M, N, K, ip32.data(), ix32.data(), vv.data(), x.data_ptr<float>(), ref.data_ptr<float>());
+        const double e = normwise(y[0], ref);
+        EXPECT(e <= 1e-5, "normwise error " + std::to_string(e));
+    });
+
+    // Error behaviour mirrors CPUExecutor (executor.cpp:80-110, 150-212).
+    run_test("UnsupportedOperator", [&] {
+        Graph g("bad");
+        g.add_input(TensorInfo("x", sh({2, 2}), DType::Float32));
+        g.add_node(node("sm", "Softmax", {"x"}, {"y"}));
+        g.add_output(TensorInfo("y", sh({2, 2}), DType::Float32));
+        std::unordered_map<std::string, Tensor> feeds;
+        feeds["x"] = randn({2, 2}, 1.0f, 19);
+        bool thrown = false;
+        try {
+            cuda.execute(g, feeds);
+        } catch (const UnsupportedOperatorError& e) {
+            thrown = std::string(e.what()).find("'cuda'") != std::string::npos;
+        }
+        EXPECT(thrown, "UnsupportedOperatorError naming the cuda backend expected");
+    });
+
+    run_test("MissingInput", [&] {
+        Graph g("missing");
+        g.add_input(TensorInfo("a", sh({2, 3}), DType::Float32));
+        g.add_input(TensorInfo("b", sh({3, 2}), DType::Float32));
+        g.add_node(node("mm", "MatMul", {"a", "b"}, {"c"}));
+        g.add_output(TensorInfo("c", sh({2, 2}), DType::Float32));
+        std::unordered_map<std::string, Tensor> feeds;
+        feeds["a"] = randn({2, 3}, 1.0f, 20);
+        bool thrown = false;
+        try {
+            cuda.execute(g, feeds);
+        } catch (const InputError&) {
+            thrown = true;
+        }
+        EXPECT(thrown, "InputError expected for a missing input");
+    });
+
+    run_test("ShapeErrorNamesNode", [&] {
+        Graph g("k");
+        g.add_input(TensorInfo("A", sh({4, 5}), DType::Float32));
+        g.add_initializer("B", randn({6, 3}, 1.0f, 21));
+        g.add_node(node("gemm_bad", "Gemm", {"A", "B"}, {"Y"}));
+        g.add_output(TensorInfo("Y", sh({4, 3}), DType::Float32));
+        std::unordered_map<std::string, Tensor> feeds;
+        feeds["A"] = randn({4, 5}, 1.0f, 22);
+        bool ok = false;
+        try {
+            cuda.execute(g, feeds);
+        } catch (const BackendError& e) {
+            ok = e.node_name().has_value() && *e.node_name() == "gemm_bad" &&
+                 std::string(e.what()).find("incompatible dimensions") != std::string::npos;
+        }
+        EXPECT(ok, "BackendError naming the node expected");
+    });
+
+    std::printf("%s: %d failed\n", g_failed ? "FAILED" : "OK", g_failed);
+    return g_failed ? 1 : 0;
+}
