@@ -267,6 +267,55 @@ def spmm_setup(ctx, n_copies):
     return c, copies, fns, alg_bytes
 
 
+def spmm_nshard(ctx, args, world, rank, peaks, peak_src):
+    """Config 5's M=1 point with W's output channels sharded over the ranks and
+    one NCCL all-gather of the output per step (strong scaling: the problem
+    is fixed, each rank holds 1/world of W)."""
+    import torch
+
+    from pyflamert_b200 import sharding
+    from pyflamert_b200 import workloads as wl
+    c = wl.spmm_case(1, SPMM_N, SPMM_K, sparsity=SPMM_S, seed=3)
+    nnz = c.values.size
+    alg_bytes = 8 * nnz + 4 * (c.N + 1) + 4 * c.K + 4 * c.N
+    per_rank = 8 * nnz / world
+    n_copies = max(2, math.ceil(2 * L2_BYTES / per_rank))
+    x = torch.from_numpy(c.X).cuda()
+    objs, fns = [], []
+    for i in range(n_copies):
+        sh = sharding.NShardSpMM(ctx, c.N, c.K, c.indptr, c.indices, c.values, rank, world)
+        lb = torch.empty((1, sh.ns), dtype=torch.float32, device="cuda")
+        gb = torch.empty((world * sh.ns,), dtype=torch.float32, device="cuda")
+        objs.append((sh, lb, gb))
+        # M = 1: the gathered buffer already is Y (rank-major column blocks).
+        fns.append(lambda sh=sh, lb=lb, gb=gb: sh(x, gather_buf=gb, local_buf=lb))
+    try:
+        ms, _, _ = graph_time(fns, args.steps, args.warmup, world)
+        how = "K steps (SpMM + all-gather) in one CUDA graph"
+    except Exception as e:  # capture of the collective unavailable: plain launches
+        global EAGER
+        old, EAGER = EAGER, True
+        ms, _, _ = graph_time(fns, args.steps, args.warmup, world)
+        EAGER = old
+        how = f"eager launches (graph capture failed: {type(e).__name__})"
+    ctx.check()
+    y = objs[0][0](x)
+    ok = bool(torch.isfinite(y).all().item())
+    gbs = alg_bytes / (ms * 1e-3) / 1e9
+    for o in objs:
+        o[0].local.close()
+    return {
+        "metric": "CSR SpMM HBM GB/s (config 5: M=1, W 8192x8192 90% sparse), W sharded by output channel",
+        "value": gbs, "unit": "GB/s", "ms_per_step": ms, "scaling": "strong",
+        "parallelism": f"W rows split {world} ways, NCCL all_gather_into_tensor of Y per step",
+        "timing": how, "finite": ok,
+        "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / world / peaks["hbm_gbs"], "per": "GPU (whole-job bytes / world / time)",
+                     "algorithmic_bytes": alg_bytes, "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)"},
+        "gpu_launches": args.steps,
+    }
+
+
 def gemm_setup(ctx, n_copies):
     import torch
 
@@ -465,21 +514,24 @@ def main():
         for obj in copies:
             obj[0].close()
         del copies, fns
-        c, sc, sfns, alg_bytes = spmm_setup(ctx, max(2, math.ceil(2 * L2_BYTES / (8 * 6.7e6))))
-        sms, _, _ = graph_time(sfns, args.steps, args.warmup, world)
-        ctx.check()
-        gbs = alg_bytes / (sms * 1e-3) / 1e9
-        line["spmm"] = {
-            "metric": "CSR SpMM HBM GB/s (config 5: M=1, W 8192x8192 90% sparse)",
-            "value": world * gbs, "unit": "GB/s", "ms_per_step": sms,
-            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": gbs / peaks["hbm_gbs"], "traffic": profile_traffic("spmm_config5_m1"),
-                         "algorithmic_bytes": alg_bytes,
-                         "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)"},
-            "gpu_launches": args.steps,
-        }
-        for obj in sc:
-            obj[0].close()
+        if world == 1:
+            c, sc, sfns, alg_bytes = spmm_setup(ctx, max(2, math.ceil(2 * L2_BYTES / (8 * 6.7e6))))
+            sms, _, _ = graph_time(sfns, args.steps, args.warmup, world)
+            ctx.check()
+            gbs = alg_bytes / (sms * 1e-3) / 1e9
+            line["spmm"] = {
+                "metric": "CSR SpMM HBM GB/s (config 5: M=1, W 8192x8192 90% sparse)",
+                "value": gbs, "unit": "GB/s", "ms_per_step": sms, "scaling": "single GPU",
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                             "frac": gbs / peaks["hbm_gbs"], "traffic": profile_traffic("spmm_config5_m1"),
+                             "algorithmic_bytes": alg_bytes,
+                             "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)"},
+                "gpu_launches": args.steps,
+            }
+            for obj in sc:
+                obj[0].close()
+        else:
+            line["spmm"] = spmm_nshard(ctx, args, world, rank, peaks, peak_src)
         g, gc, gfns = gemm_setup(ctx, 2)
         gms, _, _ = graph_time(gfns, args.steps, args.warmup, world)
         ctx.check()
