@@ -125,7 +125,7 @@ def dist_init(n_gpus):
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         import datetime
         dist.init_process_group("nccl", rank=rank, world_size=world,
-                                timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+                                timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
     elif n_gpus > 1:
         raise SystemExit("--gpus N > 1 must be launched with torch.distributed.run (one process per GPU)")
     return world, rank, local
@@ -179,11 +179,17 @@ def graph_time(step_fns, K, W, world, sampler=None):
             for i in range(K):
                 step_fns[i % n]()
     torch.cuda.synchronize()
-    # soak: replay until ~1 s has passed so the clock samples see the load
+    # Soak for ~1 s so the clock samples see the load.  The number of replays
+    # is agreed over the ranks first: a graph may hold collectives, and every
+    # rank must issue the same collectives in the same order.
     t_soak = time.time()
-    while time.time() - t_soak < 1.0:
+    g.replay()
+    torch.cuda.synchronize()
+    one = max(time.time() - t_soak, 1e-4)
+    n_soak = int(max_over_ranks(float(max(1, min(10000, int(1.0 / one)))), world))
+    for _ in range(n_soak):
         g.replay()
-        torch.cuda.synchronize()
+    torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
