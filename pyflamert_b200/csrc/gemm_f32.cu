@@ -113,6 +113,11 @@ int env_int(const char* name, int dflt) {
     return (v && *v) ? std::atoi(v) : dflt;
 }
 
+int default_splits(const pfrt_ctx* ctx, int64_t tiles, int kb_total) {
+    if (tiles * 2 > ctx->num_sms || kb_total < 16) return 1;
+    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({8, ctx->num_sms / tiles, kb_total / 4})));
+}
+
 pfrt_status launch_split(const float* src, int64_t rows, int64_t K, int64_t ld, int trans,
                          float* hi, float* lo, int64_t Kpad, cudaStream_t s) {
     dim3 tb(32, 8);
@@ -126,16 +131,16 @@ pfrt_status launch_split(const float* src, int64_t rows, int64_t K, int64_t ld, 
 pfrt_status run_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad, const CUtensorMap& tmAh,
                     const CUtensorMap& tmAl, const CUtensorMap& tmBh, const CUtensorMap& tmBl,
                     float alpha, float beta, const float* c, int64_t c_len, float* y,
-                    void* scratch_tail, size_t tail_bytes, cudaStream_t s) {
+                    void* scratch_tail, size_t tail_bytes, cudaStream_t s, int max_splits = 1 << 20) {
     using Cfg = GemmCfg<KIND_TF32X3, kF32BN, kF32Stages>;
     const int64_t mblk = ceil_div(M, 128), nblk = ceil_div(N, kF32BN);
     const int64_t tiles = mblk * nblk;
     const int kb_total = static_cast<int>(ceil_div(Kpad, Cfg::BK));
-    (void)tiles;
-    // Split-K is opt-in (PFRT_GEMM_SPLITS): one pass measured faster at the
-    // benchmark shapes.
-    int splits = env_int("PFRT_GEMM_SPLITS", 1);
-    splits = std::max(1, std::min(splits, kb_total));
+    // Split K when the tiles alone would leave most SMs idle (config 1: 16
+    // tiles on 148 SMs ran in 28 us unsplit, 14.7 us with 8 splits).
+    int splits = default_splits(ctx, tiles, kb_total);
+    splits = env_int("PFRT_GEMM_SPLITS", splits);
+    splits = std::max(1, std::min({splits, kb_total, max_splits}));
     const int kb_per = static_cast<int>(ceil_div(kb_total, splits));
     splits = static_cast<int>(ceil_div(kb_total, kb_per));
     if (splits > 1 && sizeof(float) * splits * M * N > tail_bytes)
@@ -182,9 +187,9 @@ pfrt_status run_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad, const CUt
 
 size_t splitk_bytes(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad) {
     // Upper bound of the split-K partial buffer run_f32 may ask for.
-    (void)ctx;
     const int64_t kb_total = ceil_div(Kpad, 32);
-    int64_t splits = std::max<int64_t>(1, env_int("PFRT_GEMM_SPLITS", 1));
+    const int64_t tiles = ceil_div(M, 128) * ceil_div(N, kF32BN);
+    int64_t splits = std::max<int64_t>(1, env_int("PFRT_GEMM_SPLITS", default_splits(ctx, tiles, static_cast<int>(kb_total))));
     splits = std::min<int64_t>(splits, kb_total);
     return splits > 1 ? align_up(sizeof(float) * splits * M * N, 256) : 0;
 }
@@ -253,6 +258,29 @@ pfrt_status noalloc_scratch(int device, void** out) {
 }
 
 }  // namespace
+
+pfrt_status fweight_from_device_split(pfrt_ctx* ctx, int64_t N, int64_t K, float* hi, float* lo,
+                                      pfrt_fweight** out) {
+    auto* w = new pfrt_fweight();
+    w->ctx = ctx;
+    w->K = K;
+    w->N = N;
+    w->Kpad = static_cast<int64_t>(align_up(K, 32));
+    w->hi = hi;
+    w->lo = lo;
+    pfrt_status st = make_tmap_2d(&w->tm_hi, w->hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, w->Kpad, N,
+                                  w->Kpad * 4, 32, kF32BN);
+    if (st == PFRT_OK)
+        st = make_tmap_2d(&w->tm_lo, w->lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, w->Kpad, N,
+                          w->Kpad * 4, 32, kF32BN);
+    if (st != PFRT_OK) {
+        pfrt_fweight_destroy(w);
+        return st;
+    }
+    *out = w;
+    return PFRT_OK;
+}
+
 }  // namespace pfrt
 
 using namespace pfrt;
@@ -421,7 +449,7 @@ pfrt_status pfrt_gemm_f32_noalloc(pfrt_ctx* ctx, int64_t M, int trans_a, float a
         st = make_tmap_2d(&tal, alo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, b->Kpad, M, b->Kpad * 4, 32, 128);
     if (st) return st;
     return run_f32(ctx, M, N, b->Kpad, tah, tal, b->tm_hi, b->tm_lo, alpha, beta, c, c_len, y,
-                   nullptr, 0, s);
+                   nullptr, 0, s, /*max_splits=*/1);
 }
 
 }  // extern "C"

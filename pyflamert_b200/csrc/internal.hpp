@@ -63,4 +63,10 @@ pfrt_status make_tmap_2d_plain(CUtensorMap* tm, const void* base, CUtensorMapDat
                                int elem_bytes, uint64_t cols, uint64_t rows, uint64_t ld_bytes,
                                uint32_t box_cols, uint32_t box_rows);
 
+// Wraps device buffers hi/lo [N][Kpad] (K-major, tf32 split, zero padded,
+// Kpad = K rounded up to 32) as a prepared fp32 weight.  The weight takes
+// ownership of both buffers.
+pfrt_status fweight_from_device_split(pfrt_ctx* ctx, int64_t N, int64_t K, float* hi, float* lo,
+                                      pfrt_fweight** out);
+
 }  // namespace pfrt

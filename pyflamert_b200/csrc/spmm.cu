@@ -45,6 +45,8 @@ struct pfrt_csr {
     int nchunks = 0;
     int32_t* cptr = nullptr;     // [nchunks][N+1]
     uint2* cent = nullptr;       // [nnz]
+    // Dense tf32-split copy of W for large batches (built on first use).
+    pfrt_fweight* dense = nullptr;
     // Row partition of the streaming kernel for `part_warps` warps.
     int64_t part_warps = 0;
     int32_t* part = nullptr;     // [part_warps + 1]
@@ -477,6 +479,24 @@ __global__ void __launch_bounds__(256)
     if (bad) report_error(err, kDevBadIndex);
 }
 
+// Dense tf32 split of a CSR matrix: hi[n][k] = tf32(v), lo[n][k] = v - hi
+// for every stored (n, k, v); the buffers are zero beforehand.  Warp per row.
+__global__ void csr_scatter_split_kernel(int64_t N, int64_t Kpad, const int32_t* __restrict__ indptr,
+                                         const int32_t* __restrict__ indices, const float* __restrict__ values,
+                                         float* __restrict__ hi, float* __restrict__ lo) {
+    const int64_t n = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (n >= N) return;
+    for (int32_t j = indptr[n] + lane; j < indptr[n + 1]; j += 32) {
+        const float v = values[j];
+        uint32_t h;
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
+        const int64_t at = n * Kpad + indices[j];
+        hi[at] = __uint_as_float(h);
+        lo[at] = __fsub_rn(v, __uint_as_float(h));
+    }
+}
+
 // xt[k, m] = x[m, k] for m < M, 0 for M <= m < ldxt.  32x32 tiles.
 __global__ void transpose_pad_kernel(const float* __restrict__ x, int64_t M, int64_t K, int64_t ldx,
                                      float* __restrict__ xt, int64_t ldxt) {
@@ -556,13 +576,29 @@ pfrt_status run_spmm(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, int64_t nnz
         const int64_t smem_blocks = std::min<int64_t>(ceil_div(N, 16), int64_t{per_sm} * ctx->num_sms);
         const bool pays = (M >= 2) || (8.0 * nnz >= 3.0 * static_cast<double>(smem_blocks) * xs_bytes);
         const bool smem = xs_bytes <= 96 * 1024 && K > 0 && pays && !(no_smem && *no_smem == '1');
-        int blocks;
-        if (smem) {
-            blocks = static_cast<int>(smem_blocks);  // persistent, 512 threads: X staged once per block
-        } else {
-            blocks = static_cast<int>(std::min<int64_t>(ceil_div(N, kSpmmThreads / 32), max_blocks));
-        }
         const size_t shm = smem ? xs_bytes : 0;
+        // One persistent wave: exactly the blocks that are resident at once.
+        int occ = 1;
+        {
+            cudaError_t oe;
+            switch (MV) {
+                case 1: oe = smem ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, spmm_skinny_kernel<1, true, 512>, 512, shm)
+                                  : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, spmm_skinny_kernel<1, false, kSpmmThreads>, kSpmmThreads, 0); break;
+                case 2: oe = smem ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, spmm_skinny_kernel<2, true, 512>, 512, shm)
+                                  : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, spmm_skinny_kernel<2, false, kSpmmThreads>, kSpmmThreads, 0); break;
+                case 4: oe = smem ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, spmm_skinny_kernel<4, true, 512>, 512, shm)
+                                  : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, spmm_skinny_kernel<4, false, kSpmmThreads>, kSpmmThreads, 0); break;
+                default: oe = smem ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, spmm_skinny_kernel<8, true, 512>, 512, shm)
+                                   : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, spmm_skinny_kernel<8, false, kSpmmThreads>, kSpmmThreads, 0); break;
+            }
+            if (oe != cudaSuccess) return cuda_fail(oe, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+            occ = std::max(1, occ);
+        }
+        const int tpb = smem ? 512 : kSpmmThreads;
+        const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(N, tpb / 32),
+                                                                                   int64_t{occ} * ctx->num_sms)));
+        (void)smem_blocks;
+        (void)max_blocks;
 #define PFRT_SKINNY(MVV)                                                                              \
     do {                                                                                              \
         if (smem) {                                                                                   \
@@ -626,6 +662,33 @@ pfrt_status ensure_partition(pfrt_csr* w, int64_t warps, cudaStream_t s) {
     PFRT_CUDA_TRY(cudaStreamSynchronize(s));
     w->part_warps = warps;
     return PFRT_OK;
+}
+
+// Dense copy of W for the tensor-core path, built once on the device.
+pfrt_status ensure_dense(pfrt_ctx* ctx, pfrt_csr* w, cudaStream_t s) {
+    if (w->dense) return PFRT_OK;
+    const int64_t kpad = static_cast<int64_t>(align_up(static_cast<size_t>(w->K), 32));
+    const size_t bytes = sizeof(float) * static_cast<size_t>(w->N) * kpad;
+    float *hi = nullptr, *lo = nullptr;
+    cudaError_t e = cudaMalloc(&hi, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&lo, bytes);
+    if (e == cudaSuccess) e = cudaMemsetAsync(hi, 0, bytes, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(lo, 0, bytes, s);
+    if (e != cudaSuccess) {
+        if (hi) cudaFree(hi);
+        if (lo) cudaFree(lo);
+        return cuda_fail(e, "SpMM dense copy");
+    }
+    csr_scatter_split_kernel<<<static_cast<unsigned>(ceil_div(w->N * 32, 256)), 256, 0, s>>>(
+        w->N, kpad, w->indptr, w->indices, w->values, hi, lo);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        cudaFree(hi);
+        cudaFree(lo);
+        return cuda_fail(e, "csr_scatter_split_kernel");
+    }
+    return fweight_from_device_split(ctx, w->N, w->K, hi, lo, &w->dense);
 }
 
 template <int MV, bool SMEM>
@@ -829,6 +892,7 @@ pfrt_status pfrt_csr_destroy(pfrt_csr* w) {
     if (w->cptr) cudaFree(w->cptr);
     if (w->cent) cudaFree(w->cent);
     if (w->part) cudaFree(w->part);
+    if (w->dense) pfrt_fweight_destroy(w->dense);
     delete w;
     return PFRT_OK;
 }
@@ -858,6 +922,23 @@ pfrt_status pfrt_spmm(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* 
     const char* tiled = std::getenv("PFRT_SPMM_TILED");
     if (M > 8 && tiled && *tiled == '1')
         return run_spmm_tiled(ctx, w, M, x, ldx, y, ldy, pick_stream(ctx, stream));
+    // Large batches: the product is compute-bound, and the CSR kernels reach
+    // ~5 TFLOP/s while the 3xTF32 tensor-core GEMM reaches ~200 TFLOP/s on the
+    // same product with W stored dense, so above ~2.5% density (and M >= 32)
+    // Y = X W^T runs as a GEMM on a dense copy of W made once (the copy,
+    // 8 bytes per element of W, is capped at 8 GiB).
+    const char* dense_env = std::getenv("PFRT_SPMM_DENSE");
+    const double dense_bytes = 8.0 * static_cast<double>(w->N) * static_cast<double>(align_up(w->K, 32));
+    const bool dense_auto = M >= 32 && 40.0 * static_cast<double>(w->nnz) > static_cast<double>(w->N) * w->K &&
+                            dense_bytes <= 8.0 * (1ull << 30);
+    const bool use_dense = dense_env && *dense_env ? (*dense_env == '1') : dense_auto;
+    if (M > 8 && use_dense && w->N > 0 && w->K > 0 && ldx == w->K && ldy == w->N) {
+        pfrt_csr* wm = const_cast<pfrt_csr*>(w);
+        cudaStream_t s = pick_stream(ctx, stream);
+        st = ensure_dense(ctx, wm, s);
+        if (st) return st;
+        return pfrt_gemm_f32(ctx, M, 0, 1.0f, x, wm->dense, 0.0f, nullptr, 0, y, s);
+    }
     return run_spmm(ctx, M, w->N, w->K, w->nnz, w->indptr, w->indices, w->values, x, ldx, y, ldy,
                     pick_stream(ctx, stream));
 }

@@ -150,3 +150,41 @@ def test_small_batch_kernels(ctx, kernel, M, monkeypatch):
     y = gpu(ctx, c)
     assert normwise_rel(y, oracle(c)) <= FP32_TOL
     np.testing.assert_array_equal(y[:, counts == 0], 0.0)
+
+
+@pytest.mark.parametrize("dense", ["0", "1"])
+@pytest.mark.parametrize("M,N,K,sparsity", [(32, 300, 700, 0.9), (130, 1000, 333, 0.5),
+                                            (512, 4096, 4096, 0.9), (1024, 2048, 8192, 0.97)])
+def test_large_batch_dense_and_csr_paths(ctx, dense, M, N, K, sparsity, monkeypatch):
+    """Large batches take the tensor-core GEMM on a dense copy of W above ~2.5%
+    density; both that path and the CSR wide kernel, forced in turn, match the
+    oracle, with tails in M, N and K."""
+    monkeypatch.setenv("PFRT_SPMM_DENSE", dense)
+    c = wl.spmm_case(M, N, K, sparsity=sparsity, seed=M + N + K)
+    y = gpu(ctx, c)
+    ref = oracle(c)
+    assert normwise_rel(y, ref) <= FP32_TOL
+    f64 = po.spmm_linear_f64(c.indptr, c.indices, c.values, c.X, c.N)
+    assert normwise_rel(y, f64) <= 2 * normwise_rel(ref, f64) + 1e-6
+
+
+def test_dense_path_reuses_copy_and_keeps_empty_rows_zero(ctx, monkeypatch):
+    """The dense copy is built once per CSR and reused; rows of W with no
+    nonzeros still give exact zeros."""
+    monkeypatch.setenv("PFRT_SPMM_DENSE", "1")
+    rng = np.random.default_rng(9)
+    N, K, M = 257, 129, 96
+    counts = rng.integers(0, 60, N)
+    counts[::5] = 0
+    indptr = np.zeros(N + 1, np.int64)
+    indptr[1:] = np.cumsum(counts)
+    indices = np.concatenate([np.sort(rng.choice(K, k, replace=False)) for k in counts]).astype(np.int32)
+    values = rng.standard_normal(indices.size).astype(np.float32)
+    w = pf.CSR(ctx, N, K, indptr.astype(np.int32), indices, values)
+    for seed in (1, 2):
+        X = np.random.default_rng(seed).standard_normal((M, K)).astype(np.float32)
+        y = w(torch.from_numpy(X).cuda()).cpu().numpy()
+        ctx.check()
+        c = wl.CsrCase(N, K, indptr.astype(np.int32), indices, values, X)
+        assert normwise_rel(y, oracle(c)) <= FP32_TOL
+        np.testing.assert_array_equal(y[:, counts == 0], 0.0)
