@@ -18,9 +18,10 @@ its operands from HBM.  `e2e` is the same metric through the public API
 with host buffers: pinned-host -> device copy of the activations, the layer,
 device -> pinned-host copy of the output, every step.
 
-The secondary objects report the CSR SpMM (config 5, M=1, 90% sparse,
-8192 x 8192: the HBM-bound point) and the fp32 Gemm (config 1) measured the
-same way.  `--impl reference` times the reference's own CPU implementation
+The secondary objects report, measured the same way: the CSR SpMM (config 5,
+M=1, 90% sparse, 8192 x 8192: the HBM-bound point), the 4096^3 int8 GEMM (the
+tensor-peak target), the 4-layer int8 MLP of config 4 (batch 8192 split over
+the ranks) and the fp32 Gemm (config 1).  `--impl reference` times the reference's own CPU implementation
 (its sources compiled into oracle/_ref) on the host cores instead.
 """
 from __future__ import annotations
@@ -43,6 +44,7 @@ L2_BYTES = 126 * 1024 * 1024
 M, N, K = 512, 4096, 4096                         # config 2
 SPMM_N, SPMM_K, SPMM_S = 8192, 8192, 0.90         # config 5 HBM-bound point (M = 1)
 GEMM_M, GEMM_N, GEMM_K = 256, 1024, 1024          # config 1
+MLP_BATCH, MLP_HIDDEN, MLP_LAYERS = 8192, 4096, 4  # config 4
 
 
 def measured_peaks():
@@ -339,6 +341,56 @@ def gemm_setup(ctx, n_copies):
     return g, copies, fns
 
 
+def cube_setup(ctx, n_copies, D=4096):
+    """The 4096^3 int8 GEMM of the tensor-peak target (config 2's layer at
+    M = 4096), int8 out, rotating over copies larger than L2 together."""
+    import torch
+
+    import pyflamert_b200 as pf
+    from pyflamert_b200 import workloads as wl
+    q = wl.qlinear_case(D, D, D, seed=12)
+    copies = []
+    for i in range(n_copies):
+        w = pf.QWeight(ctx, q.w, q.w_scale)
+        a = torch.from_numpy(q.a).cuda()
+        y = torch.empty((D, D), dtype=torch.int8, device="cuda")
+        copies.append((w, a, y))
+    fns = [(lambda w=w, a=a, y=y: w(a, q.a_scale, q.a_zp, out="int8", y_scale=q.y_scale, y=y))
+           for (w, a, y) in copies]
+    return copies, fns, 2.0 * D * D * D
+
+
+def mlp_setup(ctx, world, rank, n_weight_sets=2):
+    """Config 4: MatMul -> Add bias -> Relu -> requantize to uint8, x4 layers,
+    hidden 4096, batch 8192 split over the ranks (strong scaling).  Each layer
+    is one pfrt_qlinear launch with bias, ReLU and the uint8 requantization in
+    its epilogue; layer l+1 reads layer l's uint8 output.  Steps alternate over
+    `n_weight_sets` copies of the four weights (128 MiB of weights, plus
+    160 MiB of activations per step: more than L2)."""
+    import numpy as np
+    import torch
+
+    import pyflamert_b200 as pf
+    from pyflamert_b200 import sharding
+    from pyflamert_b200 import workloads as wl
+    x, layers = wl.mlp_case(MLP_BATCH, MLP_HIDDEN, MLP_LAYERS)
+    m0, m1 = sharding.batch_slice(MLP_BATCH, rank, world)
+    rows = m1 - m0
+    sets = []
+    for _ in range(n_weight_sets):
+        sets.append([(pf.QWeight(ctx, L.w, L.w_scale), torch.from_numpy(L.bias).cuda()) for L in layers])
+    acts = [torch.from_numpy(np.ascontiguousarray(x[m0:m1])).cuda()] + \
+        [torch.empty((rows, MLP_HIDDEN), dtype=torch.uint8, device="cuda") for _ in layers]
+
+    def step(ws):
+        for l, (L, (w, b)) in enumerate(zip(layers, ws)):
+            w(acts[l], L.a_scale, L.a_zp, bias=b, relu=True, out="uint8", y_scale=L.y_scale, y=acts[l + 1])
+
+    fns = [(lambda ws=ws: step(ws)) for ws in sets]
+    ops_rank = 2.0 * rows * MLP_HIDDEN * MLP_HIDDEN * MLP_LAYERS
+    return sets, acts, fns, ops_rank, (m0, m1)
+
+
 # --------------------------------------------------------------------------- CPU reference
 def cpu_reference_rate(budget_s=12.0, threads=None):
     """The reference's own quantized_matmul + quantize_tensor (compiled from its
@@ -538,6 +590,39 @@ def main():
                 obj[0].close()
         else:
             line["spmm"] = spmm_nshard(ctx, args, world, rank, peaks, peak_src)
+        # the 4096^3 int8 GEMM (the tensor-peak target)
+        cc, cfns, cops = cube_setup(ctx, max(2, math.ceil(2 * L2_BYTES / (3 * 4096 * 4096))))
+        cms, _, _ = graph_time(cfns, args.steps, args.warmup, world)
+        ctx.check()
+        ca = cops / (cms * 1e-3) / 1e12
+        line["int8_4096"] = {
+            "metric": "int8 GEMM TOPS (u8[4096,4096] x s8[4096,4096] -> s8, per-channel)",
+            "value": world * ca, "unit": "TFLOP/s", "ms_per_step": cms, "scaling": "weak",
+            "roofline": {"bound": "tensor", "achieved": ca, "peak": int8_peak, "unit": "TFLOP/s",
+                         "frac": ca / int8_peak, "traffic": profile_traffic("qlinear_4096"),
+                         "peak_source": "int8 dense = 2 x bf16_tflops (measured)"},
+            "gpu_launches": args.steps,
+        }
+        for obj in cc:
+            obj[0].close()
+        del cc, cfns
+        # config 4: the 4-layer int8 MLP, batch 8192 split over the ranks
+        ms4, acts4, mfns, mops = mlp_setup(ctx, world, rank)[:4]
+        mms, _, _ = graph_time(mfns, args.steps, args.warmup, world)
+        ctx.check()
+        line["mlp_config4"] = {
+            "metric": "int8 MLP TOPS (config 4: 4 x [MatMul -> Add -> Relu -> uint8], hidden 4096, batch 8192)",
+            "value": world * mops / (mms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": mms,
+            "scaling": "strong", "parallelism": f"batch 8192 split {world} ways, no collective",
+            "roofline": {"bound": "tensor", "achieved": mops / (mms * 1e-3) / 1e12, "peak": int8_peak,
+                         "unit": "TFLOP/s", "frac": mops / (mms * 1e-3) / 1e12 / int8_peak,
+                         "per": "GPU", "peak_source": "int8 dense = 2 x bf16_tflops (measured)"},
+            "gpu_launches": MLP_LAYERS * args.steps,
+        }
+        for ws in ms4:
+            for w, _ in ws:
+                w.close()
+        del ms4, acts4, mfns
         g, gc, gfns = gemm_setup(ctx, 2)
         gms, _, _ = graph_time(gfns, args.steps, args.warmup, world)
         ctx.check()

@@ -82,6 +82,32 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     return false;
 }
 
+// ------------------------------------------------------------- cp.async, ld
+// 16-byte asynchronous global -> shared copy (both addresses 16-byte aligned).
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// 16-byte read-only global loads, written so that a batch of them is issued
+// back to back before the first use.
+__device__ __forceinline__ int4 ldg_nc_v4s32(const int32_t* p) {
+    int4 r;
+    asm volatile("ld.global.nc.v4.s32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+__device__ __forceinline__ float4 ldg_nc_v4f32(const float* p) {
+    float4 r;
+    asm volatile("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "l"(p));
+    return r;
+}
+
 // ----------------------------------------------------------------------- TMA
 // 2-D tiled load of one box into shared memory, completing on `bar` with the
 // box's byte count.  No cluster multicast: every CTA loads its own tiles.

@@ -183,6 +183,118 @@ __global__ void __launch_bounds__(THREADS)
     if (bad) report_error(err, kDevBadIndex);
 }
 
+// M = 1.  One warp per CSR row on a persistent grid, X staged once per block
+// in shared memory (cp.async when X is 16-byte aligned and K % 4 == 0).  Lane
+// l takes the entries ja + 128 (R i + u) + 4 l .. + 3 (u < R) of the row's
+// 16-byte-aligned body [ja, jb) as R 128-bit index loads and R value loads
+// issued together, so a row of up to 128 R + 6 nonzeros costs one round trip;
+// the head [j0, ja) and tail [jb, j1) are single loads.  The latency chain of
+// a warp is cut in two places: the first row's loads go out before the block
+// waits for X, and each row's indptr pair and first round of the NEXT row are
+// loaded before the current row's warp reduction.  CHECK: the CSR is not
+// known to be valid (caller-owned arrays), so every index is range-checked
+// and indptr clamped.
+template <int R, int THREADS, bool CHECK>
+__global__ void __launch_bounds__(THREADS)
+    spmm_row1_kernel(int64_t N, int64_t K, int64_t nnz, const int32_t* __restrict__ indptr,
+                     const int32_t* __restrict__ indices, const float* __restrict__ values,
+                     const float* __restrict__ x, int vec_x, float* __restrict__ y, int* err) {
+    extern __shared__ __align__(16) float xs[];
+    const int lane = threadIdx.x & 31;
+    const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * THREADS + threadIdx.x) >> 5;
+    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * THREADS) >> 5;
+    if (vec_x) {
+        for (int64_t i = threadIdx.x; i < K / 4; i += THREADS) cp_async_16(xs + 4 * i, x + 4 * i);
+        cp_async_commit();
+    }
+    auto bounds = [&](int64_t r, int32_t& a, int32_t& b) {
+        if constexpr (CHECK) {
+            int64_t j0, j1;
+            row_range(indptr, r, nnz, j0, j1);
+            a = static_cast<int32_t>(j0);
+            b = static_cast<int32_t>(j1);
+        } else {
+            a = __ldg(indptr + r);
+            b = __ldg(indptr + r + 1);
+        }
+    };
+    // One round: R 16-byte loads of indices and of values from j (a multiple
+    // of 4, j < jb); loads past jb repeat j's and are masked at use.
+    int4 c4[R];
+    float4 v4[R];
+    auto load_round = [&](int32_t j, int32_t jb) {
+#pragma unroll
+        for (int u = 0; u < R; ++u) {
+            const int32_t jj = (j + 128 * u < jb) ? j + 128 * u : j;
+            c4[u] = ldg_nc_v4s32(indices + jj);
+            v4[u] = ldg_nc_v4f32(values + jj);
+        }
+    };
+    int64_t n = warp0;
+    int32_t j0 = 0, j1 = 0;
+    if (n < N) bounds(n, j0, j1);
+    int32_t ja = min((j0 + 3) & ~3, j1);
+    int32_t jb = ja + ((j1 - ja) & ~3);
+    if (ja + 4 * lane < jb) load_round(ja + 4 * lane, jb);
+    if (vec_x) {
+        cp_async_wait_all();
+    } else {
+        for (int64_t i = threadIdx.x; i < K; i += THREADS) xs[i] = __ldg(x + i);
+    }
+    __syncthreads();
+    bool bad = false;
+    auto gx = [&](int32_t c) -> float {
+        if constexpr (CHECK) {
+            if (static_cast<uint32_t>(c) >= static_cast<uint64_t>(K)) {
+                bad = true;
+                return 0.0f;
+            }
+        }
+        return xs[c];
+    };
+    for (; n < N; n += nwarps) {
+        const int64_t nn = n + nwarps;
+        int32_t k0 = 0, k1 = 0;
+        if (nn < N) bounds(nn, k0, k1);
+        float hv = 0.0f, tv = 0.0f;
+        int32_t hc = 0, tc = 0;
+        if (j0 + lane < ja) {
+            hc = __ldg(indices + j0 + lane);
+            hv = __ldg(values + j0 + lane);
+        }
+        if (jb + lane < j1) {
+            tc = __ldg(indices + jb + lane);
+            tv = __ldg(values + jb + lane);
+        }
+        float acc = 0.0f;
+        for (int32_t j = ja + 4 * lane; j < jb;) {
+#pragma unroll
+            for (int u = 0; u < R; ++u) {
+                if (j + 128 * u < jb) {
+                    acc = __fmaf_rn(v4[u].x, gx(c4[u].x), acc);
+                    acc = __fmaf_rn(v4[u].y, gx(c4[u].y), acc);
+                    acc = __fmaf_rn(v4[u].z, gx(c4[u].z), acc);
+                    acc = __fmaf_rn(v4[u].w, gx(c4[u].w), acc);
+                }
+            }
+            j += 128 * R;
+            if (j < jb) load_round(j, jb);
+        }
+        if (j0 + lane < ja) acc = __fmaf_rn(hv, gx(hc), acc);
+        if (jb + lane < j1) acc = __fmaf_rn(tv, gx(tc), acc);
+        // the next row's first round goes out before this row's reduction
+        j0 = k0;
+        j1 = k1;
+        ja = min((j0 + 3) & ~3, j1);
+        jb = ja + ((j1 - ja) & ~3);
+        if (nn < N && ja + 4 * lane < jb) load_round(ja + 4 * lane, jb);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+        if (lane == 0) y[n] = acc;
+    }
+    if (bad) report_error(err, kDevBadIndex);
+}
+
 // Streaming form of the skinny kernel, for a CSR uploaded with
 // pfrt_csr_create.  Warp w owns the contiguous rows [part[w], part[w+1]),
 // chosen on the host so that every warp gets about the same number of
@@ -516,6 +628,47 @@ __global__ void transpose_pad_kernel(const float* __restrict__ x, int64_t M, int
 
 namespace {
 
+// Device order of the nonzeros inside each row.  The row kernel gives lane l
+// the entries ja + 128 t + 4 l + q (q = 0..3) of a row's 16-byte-aligned body
+// [ja, jb), ja = j0 rounded up to a multiple of 4, and one shared-memory
+// gather of X covers the 32 entries with the same (t, q): a "group".  Entries
+// whose columns share a bank (col mod 32) in one group serialise that gather.
+// The body's entries are therefore dealt out in bank order over the groups,
+// one slot of every group before the next slot of any, so the entries of one
+// bank fall into different groups while there are groups left.  The set of
+// (column, value) pairs of every row is unchanged; only the order in which
+// the kernels sum them differs.
+void bank_order_rows(const std::vector<int32_t>& ip, std::vector<int32_t>& ix, std::vector<float>& v) {
+    const int64_t N = static_cast<int64_t>(ip.size()) - 1;
+    std::vector<int32_t> slot, order, tmp_i;
+    std::vector<float> tmp_v;
+    for (int64_t n = 0; n < N; ++n) {
+        const int32_t j0 = ip[n], j1 = ip[n + 1];
+        const int32_t ja = std::min((j0 + 3) & ~3, j1);
+        const int32_t jb = ja + ((j1 - ja) & ~3);
+        const int32_t L = jb - ja;
+        if (L <= 4) continue;
+        const int32_t groups = 4 * ((L + 127) / 128);
+        slot.clear();
+        for (int32_t l = 0; l < 32; ++l)
+            for (int32_t g = 0; g < groups; ++g) {
+                const int32_t p = 128 * (g / 4) + 4 * l + (g % 4);
+                if (p < L) slot.push_back(p);
+            }
+        int32_t cnt[33] = {0};
+        for (int32_t k = 0; k < L; ++k) ++cnt[(ix[ja + k] & 31) + 1];
+        for (int b = 0; b < 32; ++b) cnt[b + 1] += cnt[b];
+        order.assign(static_cast<size_t>(L), 0);
+        for (int32_t k = 0; k < L; ++k) order[cnt[ix[ja + k] & 31]++] = k;
+        tmp_i.assign(ix.begin() + ja, ix.begin() + jb);
+        tmp_v.assign(v.begin() + ja, v.begin() + jb);
+        for (int32_t k = 0; k < L; ++k) {
+            ix[ja + slot[k]] = tmp_i[order[k]];
+            v[ja + slot[k]] = tmp_v[order[k]];
+        }
+    }
+}
+
 pfrt_status validate_host_csr(int64_t N, int64_t K, int64_t nnz, const void* indptr,
                               const void* indices, int bits, std::vector<int32_t>& ip32,
                               std::vector<int32_t>& ix32) {
@@ -554,7 +707,8 @@ pfrt_status validate_host_csr(int64_t N, int64_t K, int64_t nnz, const void* ind
 
 pfrt_status run_spmm(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, int64_t nnz,
                      const int32_t* indptr, const int32_t* indices, const float* values,
-                     const float* x, int64_t ldx, float* y, int64_t ldy, cudaStream_t s) {
+                     const float* x, int64_t ldx, float* y, int64_t ldy, cudaStream_t s,
+                     bool validated = false) {
     if (M < 0 || N < 0 || K < 0) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: negative size");
     if (M == 0 || N == 0) return PFRT_OK;
     if (M > INT32_MAX - 256) return fail(PFRT_ERR_UNSUPPORTED, "SpMM: M too large");
@@ -593,6 +747,33 @@ pfrt_status run_spmm(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, int64_t nnz
             }
             if (oe != cudaSuccess) return cuda_fail(oe, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
             occ = std::max(1, occ);
+        }
+        // M = 1 with X in shared memory: the row kernel (batched loads, next
+        // row prefetched).  Its 32-bit entry arithmetic needs nnz well inside
+        // int32.
+        const char* row1_env = std::getenv("PFRT_SPMM_ROW1");
+        if (MV == 1 && smem && nnz <= INT32_MAX - 4096 && !(row1_env && *row1_env == '0')) {
+            const int vec_x = ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (K & 3) == 0) ? 1 : 0;
+            int occ1 = 1;
+            cudaError_t oe = validated
+                ? cudaFuncSetAttribute(spmm_row1_kernel<4, 512, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(shm))
+                : cudaFuncSetAttribute(spmm_row1_kernel<4, 512, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(shm));
+            if (oe == cudaSuccess)
+                oe = validated ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, spmm_row1_kernel<4, 512, false>, 512, shm)
+                               : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, spmm_row1_kernel<4, 512, true>, 512, shm);
+            if (oe != cudaSuccess) return cuda_fail(oe, "spmm_row1_kernel occupancy");
+            const int b1 = static_cast<int>(std::max<int64_t>(
+                1, std::min<int64_t>(ceil_div(N, 16), int64_t{std::max(1, occ1)} * ctx->num_sms)));
+            if (validated)
+                spmm_row1_kernel<4, 512, false><<<b1, 512, shm, s>>>(N, K, nnz, indptr, indices, values, x, vec_x,
+                                                                     y, ctx->d_err);
+            else
+                spmm_row1_kernel<4, 512, true><<<b1, 512, shm, s>>>(N, K, nnz, indptr, indices, values, x, vec_x,
+                                                                    y, ctx->d_err);
+            PFRT_CHECK_LAUNCH("spmm_row1_kernel");
+            return PFRT_OK;
         }
         const int tpb = smem ? 512 : kSpmmThreads;
         const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(N, tpb / 32),
@@ -824,10 +1005,23 @@ pfrt_status pfrt_csr_create(pfrt_ctx* ctx, int64_t N, int64_t K, int64_t nnz,
     if (e == cudaSuccess) e = cudaMalloc(&w->indices, sizeof(int32_t) * cap);
     if (e == cudaSuccess) e = cudaMalloc(&w->values, sizeof(float) * cap);
     if (e == cudaSuccess) e = cudaMemcpy(w->indptr, ip.data(), sizeof(int32_t) * (N + 1), cudaMemcpyHostToDevice);
+    // Device copy in bank order (bank_order_rows); PFRT_CSR_BANK_ORDER=0
+    // keeps the caller's order.
+    std::vector<int32_t> ix_dev;
+    std::vector<float> v_dev;
+    const char* bank_env = std::getenv("PFRT_CSR_BANK_ORDER");
+    const bool bank_order = nnz > 0 && !(bank_env && *bank_env == '0');
+    if (bank_order) {
+        ix_dev = ix;
+        v_dev.assign(values_host, values_host + nnz);
+        bank_order_rows(ip, ix_dev, v_dev);
+    }
     if (e == cudaSuccess && nnz > 0)
-        e = cudaMemcpy(w->indices, ix.data(), sizeof(int32_t) * nnz, cudaMemcpyHostToDevice);
+        e = cudaMemcpy(w->indices, bank_order ? ix_dev.data() : ix.data(), sizeof(int32_t) * nnz,
+                       cudaMemcpyHostToDevice);
     if (e == cudaSuccess && nnz > 0)
-        e = cudaMemcpy(w->values, values_host, sizeof(float) * nnz, cudaMemcpyHostToDevice);
+        e = cudaMemcpy(w->values, bank_order ? v_dev.data() : values_host, sizeof(float) * nnz,
+                       cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         pfrt_csr_destroy(w);
         return cuda_fail(e, "pfrt_csr_create");
@@ -940,7 +1134,7 @@ pfrt_status pfrt_spmm(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* 
         return pfrt_gemm_f32(ctx, M, 0, 1.0f, x, wm->dense, 0.0f, nullptr, 0, y, s);
     }
     return run_spmm(ctx, M, w->N, w->K, w->nnz, w->indptr, w->indices, w->values, x, ldx, y, ldy,
-                    pick_stream(ctx, stream));
+                    pick_stream(ctx, stream), /*validated=*/true);
 }
 
 pfrt_status pfrt_spmm_csr_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, int64_t nnz,

@@ -188,3 +188,82 @@ def test_dense_path_reuses_copy_and_keeps_empty_rows_zero(ctx, monkeypatch):
         c = wl.CsrCase(N, K, indptr.astype(np.int32), indices, values, X)
         assert normwise_rel(y, oracle(c)) <= FP32_TOL
         np.testing.assert_array_equal(y[:, counts == 0], 0.0)
+
+
+def _ragged_csr(rng, N, K, max_row, zero_every=7):
+    counts = rng.integers(0, max_row, N)
+    counts[::zero_every] = 0
+    counts[1::11] = rng.integers(1, 4, counts[1::11].size)   # rows shorter than one 16-byte group
+    counts[-3:] = 0
+    indptr = np.zeros(N + 1, np.int64)
+    indptr[1:] = np.cumsum(counts)
+    indices = np.concatenate([np.sort(rng.choice(K, k, replace=False)) for k in counts]).astype(np.int32)
+    values = rng.standard_normal(indices.size).astype(np.float32)
+    return counts, indptr.astype(np.int32), indices, values
+
+
+@pytest.mark.parametrize("K,x_offset", [(1001, 0), (1024, 1), (1024, 0)])
+@pytest.mark.parametrize("bank_order", ["1", "0"])
+def test_single_row_batch_kernel(ctx, K, x_offset, bank_order, monkeypatch):
+    """M = 1 (the row kernel with X in shared memory): rows from empty to
+    several load rounds long, X staged by 16-byte async copies (K % 4 == 0,
+    X aligned) or element by element (odd K, or X at a 4-byte offset), and
+    the CSR uploaded in bank order or in the caller's order."""
+    monkeypatch.setenv("PFRT_CSR_BANK_ORDER", bank_order)
+    rng = np.random.default_rng(K + x_offset)
+    N = 2000
+    counts, indptr, indices, values = _ragged_csr(rng, N, K, 1000)
+    X = rng.standard_normal((1, K)).astype(np.float32)
+    buf = torch.zeros(K + 4, dtype=torch.float32, device="cuda")
+    buf[x_offset:x_offset + K] = torch.from_numpy(X[0]).cuda()
+    x = buf[x_offset:x_offset + K].reshape(1, K)
+    w = pf.CSR(ctx, N, K, indptr, indices, values)
+    y = w(x).cpu().numpy()
+    ctx.check()
+    c = wl.CsrCase(N, K, indptr, indices, values, X)
+    assert normwise_rel(y, oracle(c)) <= FP32_TOL
+    np.testing.assert_array_equal(y[:, counts == 0], 0.0)
+
+
+def test_bank_order_keeps_rows(ctx, monkeypatch):
+    """Bank order only reorders entries inside rows: with every value a power
+    of two and X integer-valued, each row sum is exact in any order, so the
+    two uploads agree bit for bit (and with the oracle)."""
+    rng = np.random.default_rng(3)
+    N, K = 1500, 4096
+    counts, indptr, indices, _ = _ragged_csr(rng, N, K, 900)
+    values = (2.0 ** rng.integers(-4, 4, indices.size)).astype(np.float32)
+    X = rng.integers(-8, 9, (1, K)).astype(np.float32)
+    ys = []
+    for flag in ("1", "0"):
+        monkeypatch.setenv("PFRT_CSR_BANK_ORDER", flag)
+        w = pf.CSR(ctx, N, K, indptr, indices, values)
+        ys.append(w(torch.from_numpy(X).cuda()).cpu().numpy())
+        ctx.check()
+    np.testing.assert_array_equal(ys[0], ys[1])
+    np.testing.assert_array_equal(ys[0], oracle(wl.CsrCase(N, K, indptr, indices, values, X)))
+
+
+def test_raw_api_single_row_batch_bad_index(ctx):
+    """Caller-owned CSR at M = 1 large enough for the shared-memory row
+    kernel: an index >= K is skipped and reported, the other rows are exact
+    against the oracle."""
+    rng = np.random.default_rng(21)
+    N, K = 3000, 512
+    counts, indptr, indices, values = _ragged_csr(rng, N, K, 200)
+    bad_row = int(np.argmax(counts))
+    indices = indices.copy()
+    indices[indptr[bad_row]] = K + 5
+    X = rng.standard_normal((1, K)).astype(np.float32)
+    y = ctx.spmm_csr_raw(1, N, K, indices.size, torch.from_numpy(indptr).cuda(), torch.from_numpy(indices).cuda(),
+                         torch.from_numpy(values).cuda(), torch.from_numpy(X).cuda())
+    with pytest.raises(pf.PfrtError) as ei:
+        ctx.check()
+    assert ei.value.status == 2
+    keep = np.ones(indices.size, bool)
+    keep[indptr[bad_row]] = False
+    rows = np.repeat(np.arange(N), counts)
+    W = np.zeros((N, K), np.float64)
+    np.add.at(W, (rows[keep], indices[keep]), values[keep].astype(np.float64))
+    ref = (X.astype(np.float64) @ W.T)
+    assert np.abs(y.cpu().numpy() - ref).max() <= 1e-5 * np.abs(ref).max()
