@@ -207,6 +207,25 @@ def graph_time(step_fns, K, W, world, sampler=None):
     return max_over_ranks(ms, world), t_soak, t1
 
 
+def tensor_roofline(achieved, clocks, peaks, peak_src, traffic):
+    """int8 tensor roofline of a line.  The denominator follows the clocks
+    sampled over that line's soak and timed replay: the burst bf16 figure when
+    the SM clock held its maximum, the sustained (power-capped) one when
+    sw_power_cap was active or the clock sat below 95 % of its maximum.  Both
+    fractions are given.  int8 dense = 2 x bf16 dense (a multiply-add counts
+    as 2 ops)."""
+    burst = 2.0 * peaks["bf16_tflops"]
+    sustained = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    mhz, mx = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
+    capped = "sw_power_cap" in clocks.get("reasons", []) or bool(mhz and mx and mhz < 0.95 * mx)
+    peak = sustained if capped else burst
+    return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "frac_of_burst": achieved / burst, "traffic": traffic,
+            "peak_source": (f"int8 dense = 2 x {'bf16_tflops_sustained' if capped else 'bf16_tflops'} "
+                            f"({peak_src} MEASURED_PEAKS.json); "
+                            + ("power-capped clocks in this line's samples" if capped else "clocks at maximum"))}
+
+
 # --------------------------------------------------------------------------- workloads
 def qlinear_setup(ctx, n_copies):
     import numpy as np
@@ -275,10 +294,14 @@ def spmm_setup(ctx, n_copies):
     return c, copies, fns, alg_bytes
 
 
-def spmm_nshard(ctx, args, world, rank, peaks, peak_src):
-    """Config 5's M=1 point with W's output channels sharded over the ranks and
-    one NCCL all-gather of the output per step (strong scaling: the problem
-    is fixed, each rank holds 1/world of W)."""
+def spmm_nshard(ctx, args, world, rank, peaks, peak_src):  # noqa: C901
+    """Config 5's M=1 point with W's output channels sharded over the ranks
+    (strong scaling: the problem is fixed, each rank holds 1/world of W).
+    The product path is the fused kernel (pfrt_spmm_allgather): each rank's
+    SpMM stores its rows of Y straight into every rank's output over NVLink.
+    The same step with NCCL's all_gather_into_tensor after a plain SpMM is
+    timed beside it as the library baseline."""
+    import numpy as np
     import torch
 
     from pyflamert_b200 import sharding
@@ -289,34 +312,45 @@ def spmm_nshard(ctx, args, world, rank, peaks, peak_src):
     per_rank = 8 * nnz / world
     n_copies = max(2, math.ceil(2 * L2_BYTES / per_rank))
     x = torch.from_numpy(c.X).cuda()
+    fused = [sharding.FusedNShardSpMM(ctx, c.N, c.K, c.indptr, c.indices, c.values, rank, world)
+             for _ in range(n_copies)]
+    ms, t0_, t1_ = graph_time([(lambda f=f: f(x)) for f in fused], args.steps, args.warmup, world)
+    ctx.check()
+    y_fused = fused[0](x).cpu().numpy()
+    ctx.check()
+    for f in fused:
+        f.close()
+    # NCCL baseline
     objs, fns = [], []
     for i in range(n_copies):
         sh = sharding.NShardSpMM(ctx, c.N, c.K, c.indptr, c.indices, c.values, rank, world)
         lb = torch.empty((1, sh.ns), dtype=torch.float32, device="cuda")
         gb = torch.empty((world * sh.ns,), dtype=torch.float32, device="cuda")
         objs.append((sh, lb, gb))
-        # M = 1: the gathered buffer already is Y (rank-major column blocks).
         fns.append(lambda sh=sh, lb=lb, gb=gb: sh(x, gather_buf=gb, local_buf=lb))
     try:
-        ms, _, _ = graph_time(fns, args.steps, args.warmup, world)
-        how = "K steps (SpMM + all-gather) in one CUDA graph"
+        ms_nccl, _, _ = graph_time(fns, args.steps, args.warmup, world)
     except Exception as e:  # capture of the collective unavailable: plain launches
         global EAGER
         old, EAGER = EAGER, True
-        ms, _, _ = graph_time(fns, args.steps, args.warmup, world)
+        ms_nccl, _, _ = graph_time(fns, args.steps, args.warmup, world)
         EAGER = old
-        how = f"eager launches (graph capture failed: {type(e).__name__})"
     ctx.check()
-    y = objs[0][0](x)
-    ok = bool(torch.isfinite(y).all().item())
-    gbs = alg_bytes / (ms * 1e-3) / 1e9
+    # the fused path's gathered Y equals the NCCL path's (same per-rank kernel
+    # and summation order, so bit for bit)
+    y_nccl = objs[0][0](x).cpu().numpy()
+    same = bool(np.array_equal(y_fused, y_nccl))
     for o in objs:
         o[0].local.close()
+    gbs = alg_bytes / (ms * 1e-3) / 1e9
     return {
         "metric": "CSR SpMM HBM GB/s (config 5: M=1, W 8192x8192 90% sparse), W sharded by output channel",
         "value": gbs, "unit": "GB/s", "ms_per_step": ms, "scaling": "strong",
-        "parallelism": f"W rows split {world} ways, NCCL all_gather_into_tensor of Y per step",
-        "timing": how, "finite": ok,
+        "parallelism": f"W rows split {world} ways; the all-gather of Y fused into the SpMM kernel "
+                       "(NVLink stores to every rank's output)",
+        "timing": "K steps in one CUDA graph", "equals_nccl_path": same,
+        "nccl_baseline": {"path": "pfrt_spmm + NCCL all_gather_into_tensor per step",
+                          "value": alg_bytes / (ms_nccl * 1e-3) / 1e9, "ms_per_step": ms_nccl},
         "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": gbs / world / peaks["hbm_gbs"], "per": "GPU (whole-job bytes / world / time)",
                      "algorithmic_bytes": alg_bytes, "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)"},
@@ -574,9 +608,10 @@ def main():
         del copies, fns
         if world == 1:
             c, sc, sfns, alg_bytes = spmm_setup(ctx, max(2, math.ceil(2 * L2_BYTES / (8 * 6.7e6))))
-            sms, _, _ = graph_time(sfns, args.steps, args.warmup, world)
+            sms, s0_, s1_ = graph_time(sfns, args.steps, args.warmup, world)
             ctx.check()
             gbs = alg_bytes / (sms * 1e-3) / 1e9
+            sclk = sampler.summary(s0_, s1_)
             line["spmm"] = {
                 "metric": "CSR SpMM HBM GB/s (config 5: M=1, W 8192x8192 90% sparse)",
                 "value": gbs, "unit": "GB/s", "ms_per_step": sms, "scaling": "single GPU",
@@ -584,6 +619,7 @@ def main():
                              "frac": gbs / peaks["hbm_gbs"], "traffic": profile_traffic("spmm_config5_m1"),
                              "algorithmic_bytes": alg_bytes,
                              "peak_source": f"hbm_gbs ({peak_src} MEASURED_PEAKS.json)"},
+                "clocks": sclk,
                 "gpu_launches": args.steps,
             }
             for obj in sc:
@@ -592,15 +628,15 @@ def main():
             line["spmm"] = spmm_nshard(ctx, args, world, rank, peaks, peak_src)
         # the 4096^3 int8 GEMM (the tensor-peak target)
         cc, cfns, cops = cube_setup(ctx, max(2, math.ceil(2 * L2_BYTES / (3 * 4096 * 4096))))
-        cms, _, _ = graph_time(cfns, args.steps, args.warmup, world)
+        cms, c0, c1 = graph_time(cfns, args.steps, args.warmup, world)
         ctx.check()
         ca = cops / (cms * 1e-3) / 1e12
+        cclk = sampler.summary(c0, c1)
         line["int8_4096"] = {
             "metric": "int8 GEMM TOPS (u8[4096,4096] x s8[4096,4096] -> s8, per-channel)",
             "value": world * ca, "unit": "TFLOP/s", "ms_per_step": cms, "scaling": "weak",
-            "roofline": {"bound": "tensor", "achieved": ca, "peak": int8_peak, "unit": "TFLOP/s",
-                         "frac": ca / int8_peak, "traffic": profile_traffic("qlinear_4096"),
-                         "peak_source": "int8 dense = 2 x bf16_tflops (measured)"},
+            "roofline": tensor_roofline(ca, cclk, peaks, peak_src, profile_traffic("qlinear_4096")),
+            "clocks": cclk,
             "gpu_launches": args.steps,
         }
         for obj in cc:
@@ -608,15 +644,18 @@ def main():
         del cc, cfns
         # config 4: the 4-layer int8 MLP, batch 8192 split over the ranks
         ms4, acts4, mfns, mops = mlp_setup(ctx, world, rank)[:4]
-        mms, _, _ = graph_time(mfns, args.steps, args.warmup, world)
+        mms, m0_, m1_ = graph_time(mfns, args.steps, args.warmup, world)
         ctx.check()
+        mclk = sampler.summary(m0_, m1_)
+        ma = mops / (mms * 1e-3) / 1e12
+        mroof = tensor_roofline(ma, mclk, peaks, peak_src, None)
+        mroof["per"] = "GPU"
         line["mlp_config4"] = {
             "metric": "int8 MLP TOPS (config 4: 4 x [MatMul -> Add -> Relu -> uint8], hidden 4096, batch 8192)",
-            "value": world * mops / (mms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": mms,
+            "value": world * ma, "unit": "TFLOP/s", "ms_per_step": mms,
             "scaling": "strong", "parallelism": f"batch 8192 split {world} ways, no collective",
-            "roofline": {"bound": "tensor", "achieved": mops / (mms * 1e-3) / 1e12, "peak": int8_peak,
-                         "unit": "TFLOP/s", "frac": mops / (mms * 1e-3) / 1e12 / int8_peak,
-                         "per": "GPU", "peak_source": "int8 dense = 2 x bf16_tflops (measured)"},
+            "roofline": mroof,
+            "clocks": mclk,
             "gpu_launches": MLP_LAYERS * args.steps,
         }
         for ws in ms4:

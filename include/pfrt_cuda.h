@@ -189,6 +189,54 @@ PFRT_API pfrt_status pfrt_spmm_csr_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int6
                               const float* values, const float* x, int64_t ldx, float* y,
                               int64_t ldy, pfrt_stream stream);
 
+/* ------------------------------------------------------------ peer memory
+ * No counterpart in the reference: it has no communication backend (its
+ * partitioner, src/partition/graph_partitioner.cpp:111-200, only plans
+ * CommOps).  These entry points let the ranks of one node (one process per
+ * GPU) map each other's device buffers over NVLink.
+ *
+ * pfrt_ipc_get_handle: a process-shareable handle (64 opaque bytes) of a
+ * buffer from pfrt_malloc; pfrt_ipc_open maps a handle made by another
+ * process into this context; pfrt_ipc_close unmaps it. */
+typedef struct pfrt_ipc_handle {
+    unsigned char bytes[64];
+} pfrt_ipc_handle;
+PFRT_API pfrt_status pfrt_ipc_get_handle(pfrt_ctx* ctx, const void* dev_ptr, pfrt_ipc_handle* out);
+PFRT_API pfrt_status pfrt_ipc_open(pfrt_ctx* ctx, const pfrt_ipc_handle* handle, void** dev_ptr);
+PFRT_API pfrt_status pfrt_ipc_close(pfrt_ctx* ctx, void* dev_ptr);
+
+/* Output-channel-sharded SpMM fused with the all-gather of its output
+ * (M = 1).  Rank r holds rows [r*ns, r*ns + ns) of W as its CSR w_shard
+ * (ns = w_shard's N) and the whole X; the kernel writes every output value
+ * y[n] straight into every rank's gathered output, at y[p][r*ns + n], with
+ * stores over NVLink, so the all-gather overlaps the SpMM row by row.
+ * Ordering, per call e (counted on the device, so the call can sit in a CUDA
+ * graph): a rank writes into rank p's output only after p has entered call e
+ * (p's earlier work on its stream, including readers of its output, is
+ * done), and the call ends only after every rank has finished its stores, so
+ * y[rank] holds all world*ns values when the call completes on the stream.
+ * Every rank must make the same sequence of calls.
+ *
+ *   y[p]     rank p's output [world*ns] floats, mapped into this process
+ *            (pfrt_ipc_open; y[rank] is this rank's own buffer);
+ *   flags[p] rank p's flag array [2*world] uint32, mapped the same way;
+ *            zeroed once before the first call;
+ *   state    this rank's private [4] uint32, zeroed once.
+ *
+ * Waits on other ranks give up after about 2 s: the call then reports
+ * PFRT_ERR_DEVICE_TIMEOUT through pfrt_ctx_check and the peer set must be made
+ * anew (its flags are out of step).  M != 1: PFRT_ERR_UNSUPPORTED. */
+#define PFRT_MAX_PEERS 8
+typedef struct pfrt_peer_set {
+    int32_t rank;
+    int32_t world;
+    float* y[PFRT_MAX_PEERS];
+    uint32_t* flags[PFRT_MAX_PEERS];
+    uint32_t* state;
+} pfrt_peer_set;
+PFRT_API pfrt_status pfrt_spmm_allgather(pfrt_ctx* ctx, const pfrt_csr* w_shard, int64_t M, const float* x,
+                                         int64_t ldx, const pfrt_peer_set* peers, pfrt_stream stream);
+
 /* ------------------------------------------------------------ elementwise
  * Standalone forms of the ops the backend normally fuses into epilogues:
  * quantize_tensor per-tensor (quant_ops.cpp:33-55), bias Add broadcast over

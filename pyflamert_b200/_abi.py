@@ -15,6 +15,21 @@ STATUS_NAMES = {
 
 _P, _I64, _I32, _F32, _INT, _SZ = C.c_void_p, C.c_int64, C.c_int32, C.c_float, C.c_int, C.c_size_t
 
+PFRT_MAX_PEERS = 8
+
+
+class IpcHandle(C.Structure):
+    """pfrt_ipc_handle: 64 opaque bytes."""
+    _fields_ = [("bytes", C.c_ubyte * 64)]
+
+
+class PeerSet(C.Structure):
+    """pfrt_peer_set (include/pfrt_cuda.h)."""
+    _fields_ = [("rank", C.c_int32), ("world", C.c_int32),
+                ("y", C.c_void_p * PFRT_MAX_PEERS), ("flags", C.c_void_p * PFRT_MAX_PEERS),
+                ("state", C.c_void_p)]
+
+
 # name -> argument types; every function returns pfrt_status (int) unless listed in _RESTYPE.
 PROTOTYPES = {
     "pfrt_version": [],
@@ -47,6 +62,10 @@ PROTOTYPES = {
     "pfrt_csr_info": [_P, _P, _P, _P],
     "pfrt_spmm": [_P, _P, _I64, _P, _I64, _P, _I64, _P],
     "pfrt_spmm_csr_f32": [_P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P, _I64, _P],
+    "pfrt_ipc_get_handle": [_P, _P, _P],
+    "pfrt_ipc_open": [_P, _P, _P],
+    "pfrt_ipc_close": [_P, _P],
+    "pfrt_spmm_allgather": [_P, _P, _I64, _P, _I64, _P, _P],
     "pfrt_quantize_f32": [_P, _I64, _P, _F32, _I32, _INT, _P, _P],
     "pfrt_add_rowvec_f32": [_P, _I64, _I64, _P, _P, _P, _P],
     "pfrt_relu_f32": [_P, _I64, _P, _P, _P],

@@ -209,6 +209,36 @@ pfrt_status pfrt_ctx_check(pfrt_ctx* ctx, pfrt_stream stream) {
     return fail(PFRT_ERR_CUDA, "device error code " + std::to_string(h));
 }
 
+pfrt_status pfrt_ipc_get_handle(pfrt_ctx* ctx, const void* dev_ptr, pfrt_ipc_handle* out) {
+    pfrt_status st = enter(ctx);
+    if (st) return st;
+    if (!dev_ptr || !out) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_ipc_get_handle: null argument");
+    static_assert(sizeof(cudaIpcMemHandle_t) <= sizeof(pfrt_ipc_handle), "IPC handle size");
+    cudaIpcMemHandle_t h;
+    PFRT_CUDA_TRY(cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr)));
+    std::memset(out, 0, sizeof(*out));
+    std::memcpy(out->bytes, &h, sizeof(h));
+    return PFRT_OK;
+}
+
+pfrt_status pfrt_ipc_open(pfrt_ctx* ctx, const pfrt_ipc_handle* handle, void** dev_ptr) {
+    pfrt_status st = enter(ctx);
+    if (st) return st;
+    if (!handle || !dev_ptr) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_ipc_open: null argument");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle->bytes, sizeof(h));
+    PFRT_CUDA_TRY(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return PFRT_OK;
+}
+
+pfrt_status pfrt_ipc_close(pfrt_ctx* ctx, void* dev_ptr) {
+    pfrt_status st = enter(ctx);
+    if (st) return st;
+    if (!dev_ptr) return PFRT_OK;
+    PFRT_CUDA_TRY(cudaIpcCloseMemHandle(dev_ptr));
+    return PFRT_OK;
+}
+
 pfrt_status pfrt_malloc(pfrt_ctx* ctx, size_t bytes, void** dptr) {
     pfrt_status st = enter(ctx);
     if (st) return st;

@@ -108,6 +108,47 @@ __device__ __forceinline__ float4 ldg_nc_v4f32(const float* p) {
     return r;
 }
 
+// ------------------------------------------------- system-scope flags
+// Release/acquire accesses of 32-bit flags that other GPUs write or read over
+// NVLink (peer mappings), and a bounded wait on them.
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Waits until flags[i] has reached e (modulo 2^32) for every i < n.  Gives
+// up after kWaitLimitNs, or as soon as *abort is non-zero; returns false then.
+__device__ __forceinline__ bool wait_flags_reached(const uint32_t* flags, int n, uint32_t e,
+                                                   const uint32_t* abort) {
+    const uint64_t t0 = global_timer_ns();
+    for (int i = 0; i < n; ++i) {
+        uint32_t it = 0;
+        while (static_cast<int32_t>(ld_acquire_sys(flags + i) - e) < 0) {
+            if ((++it & 63u) == 0) {
+                if (ld_relaxed_gpu(abort) != 0) return false;
+                if (global_timer_ns() - t0 > kWaitLimitNs || it > kWaitLimitIters) return false;
+            }
+            __nanosleep(32);
+        }
+    }
+    return true;
+}
+
 // ----------------------------------------------------------------------- TMA
 // 2-D tiled load of one box into shared memory, completing on `bar` with the
 // box's byte count.  No cluster multicast: every CTA loads its own tiles.

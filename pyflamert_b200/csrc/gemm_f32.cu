@@ -170,6 +170,7 @@ pfrt_status run_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad, const CUt
     sched.kb_total = kb_total;
     sched.kb_per_split = kb_per;
     sched.num_units = static_cast<int>(mblk * nblk * splits);
+    sched.wide_units = sched.num_units;  // no narrow tail on the fp32 path
 
     auto kern = umma_gemm_kernel<KIND_TF32X3, kF32BN, kF32Stages, FEpi>;
     PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,

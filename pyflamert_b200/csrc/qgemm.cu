@@ -126,15 +126,18 @@ int env_int(const char* name, int dflt) {
     return (v && *v) ? std::atoi(v) : dflt;
 }
 
+// tmB: B with a BN-row box; tmBn: B with a BN/2-row box, for the half-width
+// units of a narrow tail (passed in the kernel's second-part B slot, which
+// the int8 kernel does not otherwise use).
 template <int BN, int STAGES>
-pfrt_status launch_q(pfrt_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB,
+pfrt_status launch_q(pfrt_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmBn,
                      const GemmSched& s, const QEpi& e, cudaStream_t st) {
     using Cfg = GemmCfg<KIND_I8, BN, STAGES>;
     auto kern = umma_gemm_kernel<KIND_I8, BN, STAGES, QEpi>;
     PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        Cfg::SMEM_BYTES));
     const int grid = std::min(s.num_units, ctx->num_sms);
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(tmA, tmB, tmA, tmB, s, e, ctx->d_err);
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(tmA, tmB, tmA, tmBn, s, e, ctx->d_err);
     PFRT_CHECK_LAUNCH("umma_gemm_kernel<i8>");
     return PFRT_OK;
 }
@@ -254,7 +257,17 @@ pfrt_status pfrt_qlinear(pfrt_ctx* ctx, const pfrt_qweight* w, int64_t M, const 
     // Tile shape and split-K.
     const int64_t mblk = ceil_div(M, 128);
     const int64_t t256 = mblk * ceil_div(N, 256), t128 = mblk * ceil_div(N, 128);
-    int bn = (t256 >= ctx->num_sms) ? 256 : 128;
+    // Tile width from the waves each choice takes on the persistent grid,
+    // in units of one 128x256 tile's time; a 128x128 tile costs ~0.7 of that
+    // (measured on B200: per MAC it moves more bytes from L2).  With 256-wide
+    // tiles, a last wave that fills at most half the SMs runs as 128-wide
+    // halves (the narrow tail of umma_gemm_kernel).
+    const int64_t G = ctx->num_sms;
+    const int64_t wfull = t256 / G, rem = t256 % G;
+    const bool tail_narrow = rem > 0 && 2 * rem <= G;
+    const double cost256 = static_cast<double>(wfull) + (rem == 0 ? 0.0 : (tail_narrow ? 0.7 : 1.0));
+    const double cost128 = 0.7 * static_cast<double>(ceil_div(t128, G));
+    int bn = (cost256 < cost128) ? 256 : 128;
     bn = env_int("PFRT_QGEMM_BN", bn);
     if (bn != 128 && bn != 256) bn = 128;
     const int64_t tiles = (bn == 256) ? t256 : t128;
@@ -335,6 +348,11 @@ pfrt_status pfrt_qlinear(pfrt_ctx* ctx, const pfrt_qweight* w, int64_t M, const 
     sched.kb_total = kb_total;
     sched.kb_per_split = kb_per;
     sched.num_units = sched.num_m_blk * sched.num_n_blk * splits;
+    sched.wide_units = sched.num_units;
+    if (bn == 256 && splits == 1 && tail_narrow && env_int("PFRT_QGEMM_NARROW", 1) != 0) {
+        sched.wide_units = static_cast<int>(wfull * G);
+        sched.num_units = sched.wide_units + static_cast<int>(2 * rem);
+    }
 
     QEpi eg = e;
     if (splits > 1) {
@@ -343,8 +361,8 @@ pfrt_status pfrt_qlinear(pfrt_ctx* ctx, const pfrt_qweight* w, int64_t M, const 
         eg.acc_out = nullptr;
         e.partial = eg.partial;
     }
-    st = (bn == 256) ? launch_q<256, 4>(ctx, tmA, w->tm_b256, sched, eg, s)
-                     : launch_q<128, 6>(ctx, tmA, w->tm_b128, sched, eg, s);
+    st = (bn == 256) ? launch_q<256, 4>(ctx, tmA, w->tm_b256, w->tm_b128, sched, eg, s)
+                     : launch_q<128, 6>(ctx, tmA, w->tm_b128, w->tm_b128, sched, eg, s);
     if (st) return st;
     if (splits > 1) {
         const int64_t threads = M * ceil_div(N, 4);

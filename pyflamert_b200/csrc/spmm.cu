@@ -194,15 +194,51 @@ __global__ void __launch_bounds__(THREADS)
 // loaded before the current row's warp reduction.  CHECK: the CSR is not
 // known to be valid (caller-owned arrays), so every index is range-checked
 // and indptr clamped.
-template <int R, int THREADS, bool CHECK>
+//
+// PEER: the output-channel-sharded form fused with the all-gather of Y
+// (pfrt_spmm_allgather).  Row n's value goes to y_p[col0 + n] of every rank
+// p, by stores over NVLink.  Call e (state[1] + 1, counted on the device and
+// read once per block):
+//   - block 0 announces "entered e" in every rank's flags[0][rank] (a relaxed
+//     store: everything that preceded this kernel on the stream is complete);
+//   - before its first store to other ranks, a warp waits until every rank
+//     has entered e, i.e. finished the work that preceded call e on its stream;
+//   - each block, when its rows are done, fences at GPU scope and counts
+//     itself in state[0]; the last one fences at system scope (cumulative over
+//     the other blocks' stores, which it has synchronised with through the
+//     counter), announces "finished e" in every rank's flags[1][rank], waits
+//     until every rank has finished e, and advances state[1].
+// Waits are bounded; one that gives up sets state[3] (the others then stop
+// waiting) and reports kDevWaitTimeout.
+struct PeerArgs {
+    int rank;
+    int world;
+    int64_t col0;
+    float* y[PFRT_MAX_PEERS];
+    uint32_t* flags[PFRT_MAX_PEERS];
+    uint32_t* state;
+};
+
+template <int R, int THREADS, bool CHECK, bool PEER = false>
 __global__ void __launch_bounds__(THREADS)
     spmm_row1_kernel(int64_t N, int64_t K, int64_t nnz, const int32_t* __restrict__ indptr,
                      const int32_t* __restrict__ indices, const float* __restrict__ values,
-                     const float* __restrict__ x, int vec_x, float* __restrict__ y, int* err) {
+                     const float* __restrict__ x, int vec_x, float* __restrict__ y, int* err,
+                     const PeerArgs pa = PeerArgs{}) {
     extern __shared__ __align__(16) float xs[];
     const int lane = threadIdx.x & 31;
     const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * THREADS + threadIdx.x) >> 5;
     const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * THREADS) >> 5;
+    uint32_t epoch = 0;
+    bool entered = false;  // lane 0: every rank has entered this call
+    __shared__ uint32_t s_epoch;
+    if constexpr (PEER) {
+        if (threadIdx.x == 0) {
+            s_epoch = ld_relaxed_gpu(pa.state + 1) + 1u;
+            if (blockIdx.x == 0)
+                for (int p = 0; p < pa.world; ++p) st_relaxed_sys(pa.flags[p] + pa.rank, s_epoch);
+        }
+    }
     if (vec_x) {
         for (int64_t i = threadIdx.x; i < K / 4; i += THREADS) cp_async_16(xs + 4 * i, x + 4 * i);
         cp_async_commit();
@@ -242,6 +278,7 @@ __global__ void __launch_bounds__(THREADS)
         for (int64_t i = threadIdx.x; i < K; i += THREADS) xs[i] = __ldg(x + i);
     }
     __syncthreads();
+    if constexpr (PEER) epoch = s_epoch;
     bool bad = false;
     auto gx = [&](int32_t c) -> float {
         if constexpr (CHECK) {
@@ -290,9 +327,41 @@ __global__ void __launch_bounds__(THREADS)
         if (nn < N && ja + 4 * lane < jb) load_round(ja + 4 * lane, jb);
 #pragma unroll
         for (int o = 16; o; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
-        if (lane == 0) y[n] = acc;
+        if (lane == 0) {
+            if constexpr (PEER) {
+                if (!entered) {
+                    entered = wait_flags_reached(pa.flags[pa.rank], pa.world, epoch, pa.state + 3);
+                    if (!entered) {
+                        atomicExch(pa.state + 3, 1u);
+                        report_error(err, kDevWaitTimeout);
+                    }
+                }
+                if (entered)
+                    for (int p = 0; p < pa.world; ++p) pa.y[p][pa.col0 + n] = acc;
+            } else {
+                y[n] = acc;
+            }
+        }
     }
     if (bad) report_error(err, kDevBadIndex);
+    if constexpr (PEER) {
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            const uint32_t done = atomicAdd(pa.state, 1u);
+            if (done == gridDim.x - 1) {
+                // last block of this call: every block's stores are issued and fenced
+                pa.state[0] = 0u;
+                __threadfence_system();
+                for (int p = 0; p < pa.world; ++p) st_release_sys(pa.flags[p] + pa.world + pa.rank, epoch);
+                if (!wait_flags_reached(pa.flags[pa.rank] + pa.world, pa.world, epoch, pa.state + 3)) {
+                    atomicExch(pa.state + 3, 1u);
+                    report_error(err, kDevWaitTimeout);
+                }
+                st_release_gpu(pa.state + 1, epoch);
+            }
+        }
+    }
 }
 
 // Streaming form of the skinny kernel, for a CSR uploaded with
@@ -1135,6 +1204,46 @@ pfrt_status pfrt_spmm(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* 
     }
     return run_spmm(ctx, M, w->N, w->K, w->nnz, w->indptr, w->indices, w->values, x, ldx, y, ldy,
                     pick_stream(ctx, stream), /*validated=*/true);
+}
+
+pfrt_status pfrt_spmm_allgather(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* x, int64_t ldx,
+                                const pfrt_peer_set* peers, pfrt_stream stream) {
+    pfrt_status st = enter(ctx);
+    if (st) return st;
+    if (!w || !x || !peers) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: null argument");
+    if (w->ctx != ctx) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: CSR belongs to another context");
+    if (M != 1) return fail(PFRT_ERR_UNSUPPORTED, "pfrt_spmm_allgather: only M = 1 is fused");
+    if (ldx < w->K) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: row stride too small");
+    const int world = peers->world, rank = peers->rank;
+    if (world < 1 || world > PFRT_MAX_PEERS || rank < 0 || rank >= world || !peers->state)
+        return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: bad rank/world or null state");
+    for (int p = 0; p < world; ++p)
+        if (!peers->y[p] || !peers->flags[p])
+            return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: null peer buffer");
+    const size_t shm = sizeof(float) * static_cast<size_t>(std::max<int64_t>(w->K, 1));
+    if (shm > 96 * 1024 || w->nnz > INT32_MAX - 4096)
+        return fail(PFRT_ERR_UNSUPPORTED, "pfrt_spmm_allgather: K or nnz too large for the fused kernel");
+    PeerArgs pa{};
+    pa.rank = rank;
+    pa.world = world;
+    pa.col0 = static_cast<int64_t>(rank) * w->N;
+    for (int p = 0; p < world; ++p) {
+        pa.y[p] = peers->y[p];
+        pa.flags[p] = peers->flags[p];
+    }
+    pa.state = peers->state;
+    cudaStream_t s = pick_stream(ctx, stream);
+    auto kern = spmm_row1_kernel<4, 512, false, true>;
+    PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(shm)));
+    int occ = 1;
+    PFRT_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 512, shm));
+    const int blocks = static_cast<int>(
+        std::max<int64_t>(1, std::min<int64_t>(ceil_div(w->N, 16), int64_t{std::max(1, occ)} * ctx->num_sms)));
+    const int vec_x = ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (w->K & 3) == 0) ? 1 : 0;
+    kern<<<blocks, 512, shm, s>>>(w->N, w->K, w->nnz, w->indptr, w->indices, w->values, x, vec_x, nullptr,
+                                   ctx->d_err, pa);
+    PFRT_CHECK_LAUNCH("spmm_row1_kernel<peer>");
+    return PFRT_OK;
 }
 
 pfrt_status pfrt_spmm_csr_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, int64_t nnz,

@@ -26,7 +26,11 @@
 //
 // Work unit = (m block, n block, k split).  With k_splits > 1 the epilogue
 // writes raw partial accumulators and a separate reduction applies the final
-// epilogue.  No cluster launch and no TMA multicast: each CTA loads its own
+// epilogue.  Narrow tail (KIND_I8, one split): when the tiles do not fill
+// the last wave of the persistent grid, the units past `wide_units` are
+// half-width tiles (BN/2 columns, one MMA of N = BN/2 per K step) so the
+// last wave's work is spread over twice as many CTAs; their B tiles come
+// through tmB1, a tensor map of B with a BN/2-row box.  No cluster launch and no TMA multicast: each CTA loads its own
 // tiles, so the same binary is safe in multi-GPU jobs.
 #pragma once
 
@@ -43,7 +47,9 @@ struct GemmSched {
     int splits;        // k splits per (m,n) tile
     int kb_total;      // number of BK blocks covering K
     int kb_per_split;  // BK blocks per split (the last split may have fewer)
-    int num_units;     // num_m_blk * num_n_blk * splits
+    int num_units;     // wide_units + 2 * (tiles past wide_units) with a narrow tail, else
+                       // num_m_blk * num_n_blk * splits
+    int wide_units;    // units [0, wide_units) are full-width tiles; the rest are half tiles
 };
 
 template <int KIND, int BN, int STAGES>
@@ -83,6 +89,25 @@ __device__ __forceinline__ void decode_unit(const GemmSched& s, int unit, int& m
     const int t = unit / s.splits;
     mb = t % s.num_m_blk;
     nb = t / s.num_m_blk;
+}
+
+// Unit -> (m block, first column n0, width, k split).  Full-width units cover
+// columns [nb*BN, nb*BN + BN); the half tiles of the narrow tail (one split)
+// cover [nb*BN + h*BN/2, +BN/2) for h = 0, 1.
+template <int BN>
+__device__ __forceinline__ void decode_unit_w(const GemmSched& s, int unit, int& mb, int& n0, int& width,
+                                              int& ks) {
+    int nb;
+    if (unit < s.wide_units) {
+        decode_unit(s, unit, mb, nb, ks);
+        n0 = nb * BN;
+        width = BN;
+    } else {
+        const int v = unit - s.wide_units;
+        decode_unit(s, s.wide_units + (v >> 1), mb, nb, ks);
+        n0 = nb * BN + (v & 1) * (BN / 2);
+        width = BN / 2;
+    }
 }
 
 // Epi must provide:
@@ -172,8 +197,8 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
             uint32_t last_par[STAGES];    // parity of the last load issued per stage
             bool ok = true;
             for (int unit = blockIdx.x; ok && unit < sched.num_units; unit += gridDim.x) {
-                int mb, nb, ks;
-                decode_unit(sched, unit, mb, nb, ks);
+                int mb, n0, width, ks;
+                decode_unit_w<BN>(sched, unit, mb, n0, width, ks);
                 const int kb0 = ks * sched.kb_per_split;
                 const int kb1 = min(kb0 + sched.kb_per_split, sched.kb_total);
                 for (int kb = kb0; kb < kb1; ++kb) {
@@ -181,15 +206,20 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
                     uint8_t* st = tiles + stage * Cfg::STAGE_BYTES;
                     const int kx = kb * Cfg::BK;
-                    tma_load_2d(st, &tmA0, &full[stage], kx, mb * BM);
-                    tma_load_2d(st + Cfg::NPARTS * Cfg::A_TILE, &tmB0, &full[stage], kx, nb * BN);
                     if constexpr (Cfg::NPARTS == 2) {
+                        mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+                        tma_load_2d(st, &tmA0, &full[stage], kx, mb * BM);
+                        tma_load_2d(st + 2 * Cfg::A_TILE, &tmB0, &full[stage], kx, n0);
                         tma_load_2d(st + Cfg::A_TILE, &tmA1, &full[stage], kx, mb * BM);
-                        tma_load_2d(st + 2 * Cfg::A_TILE + Cfg::B_TILE, &tmB1, &full[stage], kx,
-                                    nb * BN);
+                        tma_load_2d(st + 2 * Cfg::A_TILE + Cfg::B_TILE, &tmB1, &full[stage], kx, n0);
+                    } else {
+                        const bool narrow = width != BN;
+                        mbar_arrive_expect_tx(&full[stage], narrow ? Cfg::A_TILE + Cfg::B_TILE / 2
+                                                                   : Cfg::STAGE_BYTES);
+                        tma_load_2d(st, &tmA0, &full[stage], kx, mb * BM);
+                        tma_load_2d(st + Cfg::A_TILE, narrow ? &tmB1 : &tmB0, &full[stage], kx, n0);
                     }
                     issued |= 1u << stage;
                     last_par[stage] = phase;
@@ -210,16 +240,19 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            uint32_t idesc;
-            if constexpr (KIND == KIND_I8) idesc = epi.idesc;
-            else idesc = idesc_make(1, 2, 2, BM, BN);
+            uint32_t idesc_w;
+            if constexpr (KIND == KIND_I8) idesc_w = epi.idesc;
+            else idesc_w = idesc_make(1, 2, 2, BM, BN);
+            // Same descriptor with N = BN/2 (bits 17..22 hold N >> 3).
+            const uint32_t idesc_n = (idesc_w & ~(0x3Fu << 17)) | (static_cast<uint32_t>((BN / 2) >> 3) << 17);
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
             int t = 0;  // accumulation chunks issued so far (selects the TMEM slot)
             for (int unit = blockIdx.x; ok && unit < sched.num_units; unit += gridDim.x) {
-                int mb, nb, ks;
-                decode_unit(sched, unit, mb, nb, ks);
+                int mb, n0, width, ks;
+                decode_unit_w<BN>(sched, unit, mb, n0, width, ks);
+                const uint32_t idesc = (width == BN) ? idesc_w : idesc_n;
                 const int kb0 = ks * sched.kb_per_split;
                 const int kb1 = min(kb0 + sched.kb_per_split, sched.kb_total);
                 for (int kc = kb0; ok && kc < kb1; kc += Cfg::CHUNK_KB, ++t) {
@@ -287,8 +320,8 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
         constexpr int CHUNKS = BN / 32 / 2;        // 32-column chunks per warp
         int t = 0;                                 // accumulation chunks consumed so far
         for (int unit = blockIdx.x; unit < sched.num_units; unit += gridDim.x) {
-            int mb, nb, ks;
-            decode_unit(sched, unit, mb, nb, ks);
+            int mb, n0, width, ks;
+            decode_unit_w<BN>(sched, unit, mb, n0, width, ks);
             const int kb0 = ks * sched.kb_per_split;
             const int kb1 = min(kb0 + sched.kb_per_split, sched.kb_total);
             const int row = mb * BM + q * 32 + lane;
@@ -329,7 +362,7 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
                 }
                 // The barrier of the last chunk also ensures the previous tile's
                 // parameters are no longer being read.
-                epi.prepare(params, nb * BN, BN, etid, Cfg::EPI_THREADS);
+                epi.prepare(params, n0, BN, etid, Cfg::EPI_THREADS);
                 epi_barrier(Cfg::EPI_THREADS);
 #pragma unroll
                 for (int c = 0; c < CHUNKS; ++c) {
@@ -337,7 +370,7 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
 #pragma unroll
                     for (int j = 0; j < 32; ++j) bits[j] = __float_as_uint(racc[c][j]);
                     const int cl = (half * CHUNKS + c) * 32;
-                    epi.store(params, BN, row, nb * BN + cl, cl, ks, bits);
+                    epi.store(params, BN, row, n0 + cl, cl, ks, bits);
                 }
                 epi_barrier(Cfg::EPI_THREADS);  // parameters stay valid until every warp stored
             } else {
@@ -353,15 +386,16 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
                     break;
                 }
                 tc_fence_after();
-                epi.prepare(params, nb * BN, BN, etid, Cfg::EPI_THREADS);
+                epi.prepare(params, n0, width, etid, Cfg::EPI_THREADS);
                 epi_barrier(Cfg::EPI_THREADS);
                 const uint32_t taddr = tmem_base + static_cast<uint32_t>(slot * BN) + lane_off;
+                const int wchunks = width / 64;  // 32-column chunks per warp half
 #pragma unroll 1
-                for (int c = half * CHUNKS; c < (half + 1) * CHUNKS; ++c) {
+                for (int c = half * wchunks; c < (half + 1) * wchunks; ++c) {
                     uint32_t acc[32];
                     tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), acc);
                     tmem_ld_wait();
-                    epi.store(params, BN, row, nb * BN + c * 32, c * 32, ks, acc);
+                    epi.store(params, width, row, n0 + c * 32, c * 32, ks, acc);
                 }
                 tc_fence_before();
                 mbar_arrive(&tempty[slot]);

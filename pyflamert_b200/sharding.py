@@ -80,3 +80,104 @@ class NShardSpMM:
             out.copy_(y)
             return out
         return y.contiguous()
+
+
+class _DeviceArray:
+    """A device buffer from pfrt_malloc, exposed to torch without a copy."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3, "strides": None}
+
+
+class FusedNShardSpMM:
+    """Output-channel-sharded SpMM with the all-gather fused into the kernel
+    (pfrt_spmm_allgather, M = 1): every rank's kernel stores its rows of Y
+    straight into every rank's output over NVLink.  The output, the flags and
+    the state live in library-allocated device memory; the ranks exchange
+    CUDA IPC handles of the first two once, through the default process group
+    (any backend: only host objects travel).  All ranks must construct the
+    object together and then make the same calls."""
+
+    def __init__(self, ctx, N: int, K: int, indptr, indices, values, rank: int, world: int):
+        import ctypes as C
+
+        import torch.distributed as dist
+
+        from . import CSR, _abi, lib
+        if world > _abi.PFRT_MAX_PEERS:
+            raise ValueError(f"at most {_abi.PFRT_MAX_PEERS} ranks")
+        self.ctx, self.N, self.K, self.rank, self.world = ctx, int(N), int(K), rank, world
+        self.ns = -(-self.N // world)
+        n0, nreal, ip, ix, v = csr_row_shard(indptr, indices, values, rank, world)
+        self.local = CSR(ctx, self.ns, self.K, ip, ix, v)
+        L = lib()
+        self._own = []
+        ptrs = {}
+        for name, nbytes in (("y", 4 * world * self.ns), ("flags", 4 * 2 * world), ("state", 16)):
+            p = C.c_void_p()
+            _abi.check(L.pfrt_malloc(ctx.handle, nbytes, C.byref(p)), "pfrt_malloc")
+            self._own.append(p.value)
+            _abi.check(L.pfrt_memset(ctx.handle, p, 0, nbytes, None), "pfrt_memset")
+            ptrs[name] = p.value
+        _abi.check(L.pfrt_ctx_check(ctx.handle, None), "pfrt_ctx_check")  # zeroed before anyone sees them
+        mine = []
+        for name in ("y", "flags"):
+            h = _abi.IpcHandle()
+            _abi.check(L.pfrt_ipc_get_handle(ctx.handle, C.c_void_p(ptrs[name]), C.byref(h)), "pfrt_ipc_get_handle")
+            mine.append(bytes(h.bytes))
+        allh = [None] * world
+        if world > 1:
+            dist.all_gather_object(allh, mine)
+        else:
+            allh = [mine]
+        self._opened = []
+        ps = _abi.PeerSet()
+        ps.rank, ps.world = rank, world
+        for p in range(world):
+            if p == rank:
+                ps.y[p], ps.flags[p] = ptrs["y"], ptrs["flags"]
+                continue
+            got = []
+            for hb in allh[p]:
+                h = _abi.IpcHandle()
+                C.memmove(h.bytes, hb, 64)
+                d = C.c_void_p()
+                _abi.check(L.pfrt_ipc_open(ctx.handle, C.byref(h), C.byref(d)), "pfrt_ipc_open")
+                self._opened.append(d.value)
+                got.append(d.value)
+            ps.y[p], ps.flags[p] = got
+        ps.state = ptrs["state"]
+        self.peers = ps
+        self._y_ptr = ptrs["y"]
+        if world > 1:
+            dist.barrier()  # every rank has mapped every other rank's buffers
+
+    def output(self):
+        """This rank's gathered output Y [1, N] (a view of the library buffer)."""
+        import torch
+        y = torch.as_tensor(_DeviceArray(self._y_ptr, (1, self.world * self.ns), "<f4"), device="cuda")
+        return y[:, : self.N]
+
+    def __call__(self, x, stream=None):
+        import ctypes as C
+
+        from . import _abi, _dptr, _stream, lib
+        if x.shape[0] != 1 or x.shape[1] != self.K:
+            raise ValueError("FusedNShardSpMM: X must be [1, K]")
+        _abi.check(lib().pfrt_spmm_allgather(self.ctx.handle, self.local._h, 1, _dptr(x), x.shape[1],
+                                             C.byref(self.peers), _stream(stream)), "pfrt_spmm_allgather")
+        return self.output()
+
+    def close(self):
+        import ctypes as C
+
+        from . import lib
+        L = lib()
+        for d in self._opened:
+            L.pfrt_ipc_close(self.ctx.handle, C.c_void_p(d))
+        self._opened = []
+        for d in self._own:
+            L.pfrt_free(self.ctx.handle, C.c_void_p(d))
+        self._own = []
+        self.local.close()

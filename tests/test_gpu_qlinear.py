@@ -154,3 +154,24 @@ def test_invalid_arguments(ctx):
     a = torch.zeros((2, 16), dtype=torch.uint8, device="cuda")
     with pytest.raises(pf.PfrtError, match="invalid scale"):
         w(a, 0.02, 128, out="int8", y_scale=0.0)
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(1100, 4100, 1000, None), (512, 4096, 1024, "256"), (2048, 600, 777, "256"),
+                                      (4096, 4096, 512, None)])
+def test_narrow_tail_units(ctx, M, N, K, bn, monkeypatch):
+    """Shapes whose 128x256 tiles leave the last wave at most half full run
+    that wave as 128x128 half tiles.  Outputs and accumulators are bit-exact,
+    with the tail half tiles past N (N = 4100: a half tile of 4 columns and
+    one of none), and equal to the run without the narrow tail."""
+    if bn:
+        monkeypatch.setenv("PFRT_QGEMM_BN", bn)
+    q = wl.qlinear_case(M, N, K, seed=M + N + K, bias=True, relu=True, out="int8", y_scale=4.0)
+    y, acc = run(ctx, q)
+    ex = exact_acc(q.a, q.a_zp, q.w)
+    np.testing.assert_array_equal(acc.astype(np.int64), ex)
+    np.testing.assert_array_equal(y, po.qepilogue(ex, q.a_scale, q.w_scale, q.bias, True, "int8", 4.0, 0))
+    np.testing.assert_array_equal(y[:3], oracle(q, rows=3))
+    monkeypatch.setenv("PFRT_QGEMM_NARROW", "0")
+    y0, acc0 = run(ctx, q)
+    np.testing.assert_array_equal(y0, y)
+    np.testing.assert_array_equal(acc0, acc)
