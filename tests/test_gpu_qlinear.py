@@ -163,6 +163,7 @@ def test_narrow_tail_units(ctx, M, N, K, bn, monkeypatch):
     that wave as 128x128 half tiles.  Outputs and accumulators are bit-exact,
     with the tail half tiles past N (N = 4100: a half tile of 4 columns and
     one of none), and equal to the run without the narrow tail."""
+    monkeypatch.setenv("PFRT_QGEMM_PAIR", "0")  # the one-CTA kernel is the one with the narrow tail
     if bn:
         monkeypatch.setenv("PFRT_QGEMM_BN", bn)
     q = wl.qlinear_case(M, N, K, seed=M + N + K, bias=True, relu=True, out="int8", y_scale=4.0)
@@ -175,3 +176,18 @@ def test_narrow_tail_units(ctx, M, N, K, bn, monkeypatch):
     y0, acc0 = run(ctx, q)
     np.testing.assert_array_equal(y0, y)
     np.testing.assert_array_equal(acc0, acc)
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(512, 4096, 4096, "128"), (1024, 4096, 1024, "256"), (300, 1000, 777, "128"),
+                                      (1, 384, 96, "128"), (700, 520, 4096, "256"), (4096, 4096, 4096, "256")])
+def test_pair_kernel(ctx, M, N, K, bn, monkeypatch):
+    """The CTA-pair kernel (tcgen05 cta_group::2, 256-row tiles split over two
+    SMs, B halves in each SM): outputs and accumulators bit-exact, with M, N
+    and K tails (M = 1 leaves the second CTA's rows all past M)."""
+    monkeypatch.setenv("PFRT_QGEMM_PAIR", "1")
+    monkeypatch.setenv("PFRT_QGEMM_BN", bn)
+    q = wl.qlinear_case(M, N, K, seed=M + 3 * N + K, bias=True, relu=True, out="int8", y_scale=8.0)
+    y, acc = run(ctx, q)
+    ex = exact_acc(q.a, q.a_zp, q.w)
+    np.testing.assert_array_equal(acc.astype(np.int64), ex)
+    np.testing.assert_array_equal(y, po.qepilogue(ex, q.a_scale, q.w_scale, q.bias, True, "int8", 8.0, 0))
