@@ -151,7 +151,7 @@ __device__ __forceinline__ bool wait_flags_reached(const uint32_t* flags, int n,
 
 // ----------------------------------------------------------------------- TMA
 // 2-D tiled load of one box into shared memory, completing on `bar` with the
-// box's byte count.  No cluster multicast: every CTA loads its own tiles.
+// box's byte count.  Every CTA loads its own tiles.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* tm,
                                             uint64_t* bar, int32_t c_inner, int32_t c_outer) {
     asm volatile(

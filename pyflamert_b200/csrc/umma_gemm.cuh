@@ -30,7 +30,7 @@
 // the last wave of the persistent grid, the units past `wide_units` are
 // half-width tiles (BN/2 columns, one MMA of N = BN/2 per K step) so the
 // last wave's work is spread over twice as many CTAs; their B tiles come
-// through tmB1, a tensor map of B with a BN/2-row box.  No cluster launch and no TMA multicast: each CTA loads its own
+// through tmB1, a tensor map of B with a BN/2-row box.  No cluster launch: each CTA loads its own
 // tiles, so the same binary is safe in multi-GPU jobs.
 #pragma once
 

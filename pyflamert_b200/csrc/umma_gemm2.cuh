@@ -16,12 +16,13 @@
 //   warp 0      TMA producer of this CTA's A and B halves.  The copies use
 //               the .cta_group::2 form and complete on the LEADER's full
 //               barrier, which the leader's producer armed with both CTAs'
-//               bytes.  No multicast: each CTA loads its own halves.
+//               bytes.  Each CTA loads only its own halves.
 //   warp 1      leader: MMA issuer; both CTAs: the TMEM allocation, made
 //               jointly with cta_group::2.
 //   warps 2..9  epilogue of this CTA's 128 rows (TMEM -> registers -> Epi).
-// Hand-offs: the leader's MMA commit multicasts to the empty[stage] and
-// tfull[slot] barriers of both CTAs; every epilogue warp of both CTAs arrives
+// Hand-offs: the leader's MMA commits arrive on the empty[stage] and
+// tfull[slot] barriers of both CTAs (one commit per CTA, addressed through
+// the cluster window); every epilogue warp of both CTAs arrives
 // on the leader's tempty[slot] (16 arrivals free a TMEM slot).
 // Every mbarrier wait is bounded; a stop is propagated to the peer's abort
 // word.  Both CTAs always reach the closing cluster barrier.
@@ -91,18 +92,20 @@ __device__ __forceinline__ void umma_i8_pair(uint32_t d_tmem, uint64_t adesc, ui
 }
 
 // Arrives once on the barrier at this shared-memory offset in both CTAs of
-// the pair when the MMAs issued so far have completed.
+// the pair when the MMAs issued so far have completed: one commit to each
+// CTA's barrier, addressed in the cluster's shared window.
 __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
-    const uint16_t mask = 0x3;
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-            smem_u32(bar)),
-        "h"(mask)
-        : "memory");
+    const uint32_t own = smem_u32(bar);
+#pragma unroll
+    for (uint32_t r = 0; r < 2; ++r) {
+        const uint32_t a = mapa_shared(own, r);
+        asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(a)
+                     : "memory");
+    }
 }
 
 // 2-D tiled load into this CTA's shared memory, completing on the barrier at
-// cluster address `bar_cluster` (the leader's).  No multicast.
+// cluster address `bar_cluster` (the leader's).
 __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* tm, uint32_t bar_cluster,
                                                  int32_t c_inner, int32_t c_outer) {
     asm volatile(
