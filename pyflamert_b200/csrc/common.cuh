@@ -82,6 +82,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     return false;
 }
 
+// ------------------------------------------------ programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start before
+// the previous kernel on its stream has finished.  pdl_wait() blocks until
+// that kernel has completed and its memory is visible; it must precede every
+// read of data the previous kernel may write and every write the previous
+// kernel may read.  pdl_launch_dependents() lets the next such kernel start.
+// Both are no-ops for kernels launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------------- cp.async, ld
 // 16-byte asynchronous global -> shared copy (both addresses 16-byte aligned).
 __device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gmem_src) {

@@ -176,8 +176,15 @@ pfrt_status run_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad, const CUt
     PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        Cfg::SMEM_BYTES));
     const int grid = std::min(sched.num_units, ctx->num_sms);
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(tmAh, tmBh, tmAl, tmBl, sched, eg, ctx->d_err);
-    PFRT_CHECK_LAUNCH("umma_gemm_kernel<tf32x3>");
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(Cfg::THREADS);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = s;
+    cfg.numAttrs = pdl_attr(attr);
+    cfg.attrs = attr;
+    PFRT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tmAh, tmBh, tmAl, tmBl, sched, eg, ctx->d_err));
     if (splits > 1) {
         const int64_t threads = M * ceil_div(N, 4);
         f_splitk_reduce_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, s>>>(e, splits);

@@ -2,6 +2,7 @@
 // the context object, error reporting, scratch memory and TMA descriptors.
 #pragma once
 
+#include <cstdlib>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -68,5 +69,20 @@ pfrt_status make_tmap_2d_plain(CUtensorMap* tm, const void* base, CUtensorMapDat
 // ownership of both buffers.
 pfrt_status fweight_from_device_split(pfrt_ctx* ctx, int64_t N, int64_t K, float* hi, float* lo,
                                       pfrt_fweight** out);
+
+// Fills `a` with the programmatic-stream-serialization launch attribute
+// (the kernel may start while the previous kernel on the stream finishes;
+// it calls pdl_wait before touching that kernel's data) and returns 1, or
+// returns 0 when PFRT_PDL=0.
+inline int pdl_attr(cudaLaunchAttribute* a) {
+    static const bool on = [] {
+        const char* v = std::getenv("PFRT_PDL");
+        return !(v && *v == '0');
+    }();
+    if (!on) return 0;
+    a->id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    a->val.programmaticStreamSerializationAllowed = 1;
+    return 1;
+}
 
 }  // namespace pfrt

@@ -139,8 +139,15 @@ pfrt_status launch_q(pfrt_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& t
     PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        Cfg::SMEM_BYTES));
     const int grid = std::min(s.num_units, ctx->num_sms);
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(tmA, tmB, tmA, tmBn, s, e, ctx->d_err);
-    PFRT_CHECK_LAUNCH("umma_gemm_kernel<i8>");
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(Cfg::THREADS);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = st;
+    cfg.numAttrs = pdl_attr(attr);
+    cfg.attrs = attr;
+    PFRT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmA, tmBn, s, e, ctx->d_err));
     return PFRT_OK;
 }
 
@@ -153,7 +160,7 @@ pfrt_status launch_q2(pfrt_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& 
     auto kern = umma_gemm2_kernel<BN, STAGES, QEpi>;
     PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
     cudaLaunchConfig_t cfg{};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
@@ -169,6 +176,7 @@ pfrt_status launch_q2(pfrt_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& 
     if (clusters < 1) return fail(PFRT_ERR_UNSUPPORTED, "int8 GEMM: no CTA pair fits on this device");
     const int pairs = std::min(s.num_units, clusters);
     cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+    cfg.numAttrs = 1 + pdl_attr(attr + 1);
     PFRT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tmA, tmBh, s, e, ctx->d_err));
     return PFRT_OK;
 }

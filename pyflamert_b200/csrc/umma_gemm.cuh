@@ -182,6 +182,9 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Every CTA is resident (persistent grid), so the next kernel may launch
+    // now; its CTAs wait in pdl_wait until this grid completes.
+    if (threadIdx.x == 0) pdl_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -196,6 +199,7 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
             uint32_t issued = 0;          // stages with a load issued
             uint32_t last_par[STAGES];    // parity of the last load issued per stage
             bool ok = true;
+            pdl_wait();  // A (and B, C) may come from the previous kernel
             for (int unit = blockIdx.x; ok && unit < sched.num_units; unit += gridDim.x) {
                 int mb, n0, width, ks;
                 decode_unit_w<BN>(sched, unit, mb, n0, width, ks);
@@ -316,6 +320,7 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
     } else {
         const int q = warp & 3;                    // TMEM lane quarter this warp may access
         const int etid = threadIdx.x - 64;         // 0 .. EPI_THREADS-1
+        pdl_wait();  // bias/rowsum/C reads and the output writes follow the previous kernel
         const int half = (warp - 2) >> 2;          // which half of the tile's columns
         constexpr int CHUNKS = BN / 32 / 2;        // 32-column chunks per warp
         int t = 0;                                 // accumulation chunks consumed so far

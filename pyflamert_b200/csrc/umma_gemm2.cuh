@@ -186,6 +186,7 @@ __global__ void __launch_bounds__(64 + 32 * Gemm2Cfg<BN, STAGES>::EPI_WARPS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    if (threadIdx.x == 0) pdl_launch_dependents();
     auto stop = [&]() {
         *abort_flag = 1;
         st_cluster_u32(peer_abort, 1u);
@@ -196,6 +197,7 @@ __global__ void __launch_bounds__(64 + 32 * Gemm2Cfg<BN, STAGES>::EPI_WARPS, 1)
         if (lane == 0) {
             tma_prefetch_desc(&tmA);
             tma_prefetch_desc(&tmB);
+            pdl_wait();
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
@@ -271,6 +273,7 @@ __global__ void __launch_bounds__(64 + 32 * Gemm2Cfg<BN, STAGES>::EPI_WARPS, 1)
         const int etid = threadIdx.x - 64;
         const int half = (warp - 2) >> 2;
         constexpr int CHUNKS = BN / 32 / 2;
+        pdl_wait();
         const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0u);
         const uint32_t tempty_leader1 = mapa_shared(smem_u32(&tempty[1]), 0u);
         int t = 0;
