@@ -43,8 +43,12 @@ struct pfrt_csr {
     // c (columns [c*KT, (c+1)*KT)) of every row, chunk-major, as packed
     // (local column, value bits) pairs, with row pointers cptr[c][N+1].
     int nchunks = 0;
-    int32_t* cptr = nullptr;     // [nchunks][N+1]
-    uint2* cent = nullptr;       // [nnz]
+    int32_t* cptr = nullptr;     // [nchunks][N+1] (+4 entries of slack for 16-byte bulk copies)
+    uint2* cent = nullptr;       // [nnz] (+2 entries of slack)
+    std::vector<int32_t> host_cptr;
+    // Row groups of the mid-batch kernel (spmm_xtile_kernel), built on first use.
+    int32_t* xt_part = nullptr;  // [xt_groups + 1]
+    int64_t xt_groups = 0;
     // Dense tf32-split copy of W for large batches (built on first use).
     pfrt_fweight* dense = nullptr;
     // Row partition of the streaming kernel for `part_warps` warps.
@@ -564,98 +568,194 @@ __global__ void __launch_bounds__(kSpmmThreads)
     if (bad) report_error(err, kDevBadIndex);
 }
 
-constexpr int kTileKT = 256;  // columns of X (rows of X^T) per staged chunk
-constexpr int kTileMT = 64;   // rows of X per block (2 per lane)
+// Mid-batch kernel (M > 8): one block per row group, over the column-blocked
+// copy of the CSR.  The groups are contiguous row ranges chosen on the host
+// (about equal nonzeros; at most kXtRows rows and kXtEntMax nonzeros of any
+// one column chunk), so the nonzeros of a group in chunk c are one
+// contiguous range of `cent`, and its row pointers one range of cptr[c].
+// Per chunk, a producer warp brings into a two-stage shared-memory ring:
+//   - the tile X^T[c*KT .. +KT][m0 .. m0+MT] by TMA,
+//   - the group's entries (local column, value) by a 1-D bulk copy,
+//   - the group's row pointers by a 1-D bulk copy,
+// all completing on the stage's mbarrier.  The compute warps then work from
+// shared memory only: warp w owns rows w, w + kXtWarps, ... of the group;
+// lane l owns MV consecutive rows of X (columns of Y), so each nonzero is one
+// broadcast read of its (column, value) and one MV-wide read of X^T[k].
+// Outputs are staged through shared memory and stored along n.
+constexpr int kTileKT = 256;    // columns of X (rows of X^T) per chunk, = the column-blocked copy's block
+constexpr int kXtWarps = 16;    // compute warps per block
+constexpr int kXtRowsPerWarp = 8;
+constexpr int kXtRows = kXtWarps * kXtRowsPerWarp;
+constexpr int kXtEntMax = 4096; // nonzeros of one group in one chunk
+constexpr int kXtOffMax = kXtRows + 8;
 
-// Dynamic shared memory of spmm_tiled_kernel: the X^T tile [256][64] fp32,
-// one 32-entry nonzero buffer per warp, and the tile's mbarrier.  The output
-// staging reuses the first two regions.
-constexpr size_t kTileXsBytes = sizeof(float) * kTileKT * kTileMT;
-constexpr size_t kTileEntBytes = sizeof(uint2) * 8 * 32;
-constexpr size_t kTileSmem = kTileXsBytes + kTileEntBytes + 16;
+template <int MV>
+struct XtCfg {
+    static constexpr int MT = 32 * MV;
+    static constexpr int XS_BYTES = 4 * MT * kTileKT;
+    static constexpr int ENT_BYTES = 8 * (kXtEntMax + 2);
+    static constexpr int OFF_BYTES = 4 * kXtOffMax;
+    static constexpr int STAGE_BYTES = (XS_BYTES + ENT_BYTES + OFF_BYTES + 1023) / 1024 * 1024;
+    static constexpr int SMEM = 2 * STAGE_BYTES + 128 + 1024;
+    static_assert(4 * MT * (kXtRows + 1) <= STAGE_BYTES, "output staging fits in a stage");
+    static_assert(OFF_BYTES % 16 == 0 && ENT_BYTES % 16 == 0 && XS_BYTES % 1024 == 0, "alignment");
+};
 
-// Block = (64 rows of X, 8*RPW CSR rows).  For each 256-column chunk one TMA
-// load brings X^T[chunk, m0:m0+64] into shared memory (zero-filled past K and
-// past M), then each warp walks the chunk's nonzeros of its RPW rows: 32
-// (index, value) pairs are loaded coalesced into a per-warp buffer and
-// broadcast to all lanes, and lane l accumulates rows m0+2l and m0+2l+1 from
-// xs[k][2l..2l+1] (one conflict-free 256-byte row per nonzero).
-template <int RPW>
-__global__ void __launch_bounds__(256)
-    spmm_tiled_kernel(const __grid_constant__ CUtensorMap tmx, int M, int64_t N, int nchunks,
-                      const int32_t* __restrict__ cptr, const uint2* __restrict__ cent,
-                      float* __restrict__ y, int64_t ldy, int64_t mtiles, int* err) {
-    extern __shared__ __align__(128) uint8_t tsm[];
-    float* xs = reinterpret_cast<float*>(tsm);
-    uint2* ent = reinterpret_cast<uint2*>(tsm + kTileXsBytes);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(tsm + kTileXsBytes + kTileEntBytes);
-    constexpr int R = 8 * RPW;
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+template <int MV>
+__global__ void __launch_bounds__((kXtWarps + 1) * 32, 1)
+    spmm_xtile_kernel(const __grid_constant__ CUtensorMap tmx, int M, int mtiles, int64_t N, int nchunks,
+                      const int32_t* __restrict__ gpart, const int32_t* __restrict__ cptr,
+                      const uint2* __restrict__ cent, float* __restrict__ y, int64_t ldy, int* err) {
+    using Cfg = XtCfg<MV>;
+    constexpr int MT = Cfg::MT;
+    extern __shared__ uint8_t xsm_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(xsm_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + 2 * Cfg::STAGE_BYTES);
+    uint64_t* empty = full + 2;
+    int32_t* meta = reinterpret_cast<int32_t*>(empty + 2);  // [2][2]: first entry, first row pointer
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 4);
+
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t mt = blockIdx.x % mtiles, nt = blockIdx.x / mtiles;
-    const int m0 = static_cast<int>(mt) * kTileMT;
-    const int64_t n0 = nt * R;
-    uint2* wbuf = ent + warp * 32;
+    const int mt = static_cast<int>(blockIdx.x % mtiles);
+    const int64_t g = blockIdx.x / mtiles;
+    const int m0 = mt * MT;
+    const int32_t r0 = __ldg(gpart + g), r1 = __ldg(gpart + g + 1);
+    const int nr = r1 - r0;
     if (threadIdx.x == 0) {
-        mbar_init(bar, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kXtWarps);
+        }
+        *abort_flag = 0;
         fence_mbar_init();
     }
     __syncthreads();
-    float2 acc[RPW];
+
+    float acc[kXtRowsPerWarp][MV];
 #pragma unroll
-    for (int r = 0; r < RPW; ++r) acc[r] = make_float2(0.f, 0.f);
+    for (int i = 0; i < kXtRowsPerWarp; ++i)
+#pragma unroll
+        for (int v = 0; v < MV; ++v) acc[i][v] = 0.0f;
     bool bad = false;
-    uint32_t phase = 0;
-    const int zero = 0;
-    for (int c = 0; c < nchunks; ++c) {
-        if (threadIdx.x == 0) {
-            mbar_arrive_expect_tx(bar, static_cast<uint32_t>(kTileXsBytes));
-            tma_load_2d(xs, &tmx, bar, m0, c * kTileKT);
+
+    if (warp == kXtWarps) {
+        if (lane == 0) {
+            tma_prefetch_desc(&tmx);
+            bool ok = true;
+            int issued = 0;
+            for (int c = 0; c < nchunks; ++c) {
+                const int st = c & 1;
+                const uint32_t ph = static_cast<uint32_t>(c >> 1) & 1u;
+                if (!mbar_wait(&empty[st], ph ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                const int32_t* cp = cptr + static_cast<int64_t>(c) * (N + 1);
+                const int32_t e0 = __ldg(cp + r0), e1 = __ldg(cp + r1);
+                const int32_t elo = e0 & ~1, ehi = (e1 + 1) & ~1;
+                const int64_t olo = (static_cast<int64_t>(c) * (N + 1) + r0) & ~int64_t{3};
+                const int64_t ohi = (static_cast<int64_t>(c) * (N + 1) + r1 + 1 + 3) & ~int64_t{3};
+                uint8_t* sb = base + st * Cfg::STAGE_BYTES;
+                meta[2 * st] = elo;
+                meta[2 * st + 1] = static_cast<int32_t>(olo - static_cast<int64_t>(c) * (N + 1));
+                const uint32_t ebytes = 8u * static_cast<uint32_t>(ehi - elo);
+                const uint32_t obytes = 4u * static_cast<uint32_t>(ohi - olo);
+                mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(Cfg::XS_BYTES) + ebytes + obytes);
+                tma_load_2d(sb, &tmx, &full[st], m0, c * kTileKT);
+                if (ebytes) bulk_g2s(sb + Cfg::XS_BYTES, cent + elo, ebytes, &full[st]);
+                bulk_g2s(sb + Cfg::XS_BYTES + Cfg::ENT_BYTES, cptr + olo, obytes, &full[st]);
+                ++issued;
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                report_error(err, kDevWaitTimeout);
+            }
+            // Everything issued has been consumed by the compute warps, or,
+            // after an abort, is waited for here before the block may exit.
+            const int zero = 0;
+            for (int c = (issued > 2 ? issued - 2 : 0); c < issued && !ok; ++c)
+                mbar_wait(&full[c & 1], static_cast<uint32_t>(c >> 1) & 1u, &zero);
         }
-        const bool got = mbar_wait(bar, phase, &zero);
-        if (!__syncthreads_and(got)) {
-            report_error(err, kDevWaitTimeout);
-            return;
-        }
-        phase ^= 1u;
-        const int32_t* cp = cptr + static_cast<int64_t>(c) * (N + 1);
+    } else {
+        for (int c = 0; c < nchunks; ++c) {
+            const int st = c & 1;
+            const uint32_t ph = static_cast<uint32_t>(c >> 1) & 1u;
+            if (!mbar_wait(&full[st], ph, abort_flag)) {
+                if (lane == 0) {
+                    *abort_flag = 1;
+                    report_error(err, kDevWaitTimeout);
+                }
+                break;
+            }
+            const uint8_t* sb = base + st * Cfg::STAGE_BYTES;
+            const float* xs = reinterpret_cast<const float*>(sb);
+            const uint2* ents = reinterpret_cast<const uint2*>(sb + Cfg::XS_BYTES);
+            const int32_t* offs = reinterpret_cast<const int32_t*>(sb + Cfg::XS_BYTES + Cfg::ENT_BYTES);
+            const int32_t elo = meta[2 * st], olo = meta[2 * st + 1];
 #pragma unroll
-        for (int r = 0; r < RPW; ++r) {
-            const int64_t n = n0 + warp * RPW + r;
-            if (n < N) {
-                const int64_t j0 = __ldg(cp + n), j1 = __ldg(cp + n + 1);
-                for (int64_t jc = j0; jc < j1; jc += 32) {
-                    if (jc + lane < j1) wbuf[lane] = __ldg(cent + jc + lane);
-                    __syncwarp();
-                    const int cnt = static_cast<int>((j1 - jc) < 32 ? (j1 - jc) : 32);
-                    for (int t = 0; t < cnt; ++t) {
-                        const uint2 en = wbuf[t];
-                        if (en.x >= static_cast<uint32_t>(kTileKT)) {  // not a column of this chunk
-                            bad = true;
-                            continue;
+            for (int i = 0; i < kXtRowsPerWarp; ++i) {
+                const int rl = warp + i * kXtWarps;
+                if (rl < nr) {
+                    const int32_t e0 = offs[r0 + rl - olo] - elo, e1 = offs[r0 + rl + 1 - olo] - elo;
+                    int32_t e = e0;
+                    for (; e + 3 < e1; e += 4) {
+                        uint2 en[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) en[u] = ents[e + u];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const uint32_t k = en[u].x < static_cast<uint32_t>(kTileKT) ? en[u].x : 0u;
+                            bad |= en[u].x >= static_cast<uint32_t>(kTileKT);
+                            const float v = en[u].x < static_cast<uint32_t>(kTileKT) ? __uint_as_float(en[u].y) : 0.0f;
+                            if constexpr (MV == 2) {
+                                const float2 xv = reinterpret_cast<const float2*>(xs + k * MT)[lane];
+                                acc[i][0] = __fmaf_rn(v, xv.x, acc[i][0]);
+                                acc[i][1] = __fmaf_rn(v, xv.y, acc[i][1]);
+                            } else {
+                                acc[i][0] = __fmaf_rn(v, xs[k * MT + lane], acc[i][0]);
+                            }
                         }
-                        const float v = __uint_as_float(en.y);
-                        const float2 xv = reinterpret_cast<const float2*>(xs + en.x * kTileMT)[lane];
-                        acc[r].x = __fmaf_rn(v, xv.x, acc[r].x);
-                        acc[r].y = __fmaf_rn(v, xv.y, acc[r].y);
                     }
-                    __syncwarp();
+                    for (; e < e1; ++e) {
+                        const uint2 en = ents[e];
+                        const uint32_t k = en.x < static_cast<uint32_t>(kTileKT) ? en.x : 0u;
+                        bad |= en.x >= static_cast<uint32_t>(kTileKT);
+                        const float v = en.x < static_cast<uint32_t>(kTileKT) ? __uint_as_float(en.y) : 0.0f;
+#pragma unroll
+                        for (int q = 0; q < MV; ++q) acc[i][q] = __fmaf_rn(v, xs[k * MT + lane * MV + q], acc[i][q]);
+                    }
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
         }
-        __syncthreads();  // the tile is no longer read: the next TMA may overwrite it
-    }
-    // Output: stage [64 rows of X][R CSR rows] so the stores run along n.
-    float* ys = reinterpret_cast<float*>(tsm);
-    constexpr int LDYS = R + 1;
-#pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-        ys[(2 * lane) * LDYS + warp * RPW + r] = acc[r].x;
-        ys[(2 * lane + 1) * LDYS + warp * RPW + r] = acc[r].y;
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < kTileMT * R; e += 256) {
-        const int m = e / R, i = e % R;
-        if (m0 + m < M && n0 + i < N) y[static_cast<int64_t>(m0 + m) * ldy + n0 + i] = ys[m * LDYS + i];
+    // Output: stage [MT rows of X][nr CSR rows] in stage 0, then store along n.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    float* ys = reinterpret_cast<float*>(base);
+    const int ld = nr + 1;
+    if (warp < kXtWarps) {
+#pragma unroll
+        for (int i = 0; i < kXtRowsPerWarp; ++i) {
+            const int rl = warp + i * kXtWarps;
+            if (rl < nr)
+#pragma unroll
+                for (int q = 0; q < MV; ++q) ys[(lane * MV + q) * ld + rl] = acc[i][q];
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < MT * nr; e += blockDim.x) {
+        const int m = e / nr, i = e % nr;
+        if (m0 + m < M && !*abort_flag) y[static_cast<int64_t>(m0 + m) * ldy + r0 + i] = ys[m * ld + i];
     }
     if (bad) report_error(err, kDevBadIndex);
 }
@@ -989,34 +1089,94 @@ pfrt_status run_spmm_stream(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* 
     }
 }
 
-template <int RPW>
-pfrt_status launch_tiled(pfrt_ctx* ctx, const pfrt_csr* w, const CUtensorMap& tmx, int64_t M,
-                         float* y, int64_t ldy, cudaStream_t s) {
-    static_assert(sizeof(float) * kTileMT * (8 * RPW + 1) <= kTileXsBytes + kTileEntBytes,
-                  "output staging must fit in the tile buffers");
-    auto kern = spmm_tiled_kernel<RPW>;
-    PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(kTileSmem)));
-    const int64_t mtiles = ceil_div(M, kTileMT);
-    const int64_t units = mtiles * ceil_div(w->N, 8 * RPW);
-    if (units > INT32_MAX) return fail(PFRT_ERR_UNSUPPORTED, "SpMM: too many tiles");
-    kern<<<static_cast<unsigned>(units), 256, kTileSmem, s>>>(tmx, static_cast<int>(M), w->N, w->nchunks,
-                                                              w->cptr, w->cent, y, ldy, mtiles, ctx->d_err);
-    PFRT_CHECK_LAUNCH("spmm_tiled_kernel");
+// Row groups of spmm_xtile_kernel: contiguous rows, closed when adding the
+// next row would exceed kXtRows rows, kXtEntMax nonzeros in some column chunk,
+// or the per-group share of nonzeros (total / min_groups, so that there are
+// at least about min_groups groups to fill the SMs).  A single row with more
+// than kXtEntMax nonzeros in one chunk cannot be placed (returns false).
+bool ensure_xt_groups(pfrt_csr* w, int64_t min_groups, cudaStream_t s, pfrt_status* st_out) {
+    *st_out = PFRT_OK;
+    if (w->xt_part) return true;
+    const int64_t N = w->N;
+    const int C = w->nchunks;
+    // Aim a little under min_groups so that rounding does not spill one group
+    // into a second wave.
+    const double target = std::max(1.0, 1.04 * static_cast<double>(w->nnz) /
+                                             static_cast<double>(std::max<int64_t>(1, min_groups)));
+    std::vector<int32_t> part{0};
+    std::vector<int32_t> cnt(static_cast<size_t>(C), 0);
+    int64_t rows = 0, nz = 0;
+    for (int64_t r = 0; r < N; ++r) {
+        int64_t rnz = w->host_indptr[r + 1] - w->host_indptr[r];
+        bool fits = rows < kXtRows && (rows == 0 || static_cast<double>(nz + rnz) <= target);
+        for (int c = 0; c < C && fits; ++c) {
+            const int32_t* cp = w->host_cptr.data() + static_cast<size_t>(c) * (N + 1);
+            fits = cnt[c] + (cp[r + 1] - cp[r]) <= kXtEntMax;
+        }
+        if (!fits) {
+            part.push_back(static_cast<int32_t>(r));
+            std::fill(cnt.begin(), cnt.end(), 0);
+            rows = 0;
+            nz = 0;
+        }
+        for (int c = 0; c < C; ++c) {
+            const int32_t* cp = w->host_cptr.data() + static_cast<size_t>(c) * (N + 1);
+            cnt[c] += cp[r + 1] - cp[r];
+            if (cnt[c] > kXtEntMax) return false;
+        }
+        ++rows;
+        nz += rnz;
+    }
+    part.push_back(static_cast<int32_t>(N));
+    cudaError_t e = cudaMalloc(&w->xt_part, sizeof(int32_t) * part.size());
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(w->xt_part, part.data(), sizeof(int32_t) * part.size(), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        if (w->xt_part) cudaFree(w->xt_part);
+        w->xt_part = nullptr;
+        *st_out = cuda_fail(e, "SpMM row groups");
+        return false;
+    }
+    w->xt_groups = static_cast<int64_t>(part.size()) - 1;
+    return true;
+}
+
+template <int MV>
+pfrt_status launch_xtile(pfrt_ctx* ctx, const pfrt_csr* w, const CUtensorMap& tmx, int64_t M, float* y,
+                         int64_t ldy, cudaStream_t s) {
+    using Cfg = XtCfg<MV>;
+    auto kern = spmm_xtile_kernel<MV>;
+    PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    const int64_t mtiles = ceil_div(M, Cfg::MT);
+    const int64_t blocks = mtiles * w->xt_groups;
+    if (blocks > INT32_MAX) return fail(PFRT_ERR_UNSUPPORTED, "SpMM: too many tiles");
+    kern<<<static_cast<unsigned>(blocks), (kXtWarps + 1) * 32, Cfg::SMEM, s>>>(
+        tmx, static_cast<int>(M), static_cast<int>(mtiles), w->N, w->nchunks, w->xt_part, w->cptr, w->cent, y, ldy,
+        ctx->d_err);
+    PFRT_CHECK_LAUNCH("spmm_xtile_kernel");
     return PFRT_OK;
 }
 
-pfrt_status run_spmm_tiled(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* x, int64_t ldx,
-                           float* y, int64_t ldy, cudaStream_t s) {
+// M > 8 on an uploaded CSR through spmm_xtile_kernel.  Returns
+// PFRT_ERR_UNSUPPORTED (nothing launched) when some row has more than
+// kXtEntMax nonzeros in one 256-column chunk.
+pfrt_status run_spmm_xtile(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x, int64_t ldx, float* y,
+                           int64_t ldy, cudaStream_t s) {
     if (M > INT32_MAX - 256) return fail(PFRT_ERR_UNSUPPORTED, "SpMM: M too large");
     if (!x || !y) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: null pointer");
     if (ldx < w->K || ldy < w->N) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: row stride too small");
-    if (w->N == 0) return PFRT_OK;
+    if (w->N == 0 || M == 0) return PFRT_OK;
     if (w->K == 0) return run_spmm(ctx, M, w->N, w->K, w->nnz, w->indptr, w->indices, w->values, x, ldx, y, ldy, s);
-    // X^T [K][Mpad], Mpad a multiple of the 64-row tile (zero padded).
-    const int64_t mpad = static_cast<int64_t>(align_up(static_cast<size_t>(M), kTileMT));
+    pfrt_status st;
+    if (!ensure_xt_groups(w, ctx->num_sms, s, &st))
+        return st ? st : fail(PFRT_ERR_UNSUPPORTED, "SpMM: a row is too dense for the tiled kernel");
+    const int mv = (M <= 32) ? 1 : 2;
+    const int64_t mt = 32 * mv;
+    // X^T [K][Mpad], Mpad a multiple of the tile height (zero padded).
+    const int64_t mpad = static_cast<int64_t>(align_up(static_cast<size_t>(M), static_cast<size_t>(mt)));
     void* scr = nullptr;
-    pfrt_status st = scratch(ctx, sizeof(float) * mpad * w->K, &scr);
+    st = scratch(ctx, sizeof(float) * mpad * w->K, &scr);
     if (st) return st;
     float* xt = static_cast<float*>(scr);
     dim3 tb(32, 8);
@@ -1025,23 +1185,10 @@ pfrt_status run_spmm_tiled(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const fl
     PFRT_CHECK_LAUNCH("transpose_pad_kernel");
     CUtensorMap tmx;
     st = make_tmap_2d_plain(&tmx, xt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, static_cast<uint64_t>(mpad),
-                            static_cast<uint64_t>(w->K), static_cast<uint64_t>(mpad) * 4, kTileMT, kTileKT);
+                            static_cast<uint64_t>(w->K), static_cast<uint64_t>(mpad) * 4, static_cast<uint32_t>(mt),
+                            kTileKT);
     if (st) return st;
-    // Rows per warp: the largest that still gives every SM a block.
-    const int64_t mtiles = ceil_div(M, kTileMT);
-    int rpw = 4;
-    for (int cand : {32, 16, 8}) {
-        if (mtiles * ceil_div(w->N, 8 * cand) >= ctx->num_sms) {
-            rpw = cand;
-            break;
-        }
-    }
-    switch (rpw) {
-        case 32: return launch_tiled<32>(ctx, w, tmx, M, y, ldy, s);
-        case 16: return launch_tiled<16>(ctx, w, tmx, M, y, ldy, s);
-        case 8: return launch_tiled<8>(ctx, w, tmx, M, y, ldy, s);
-        default: return launch_tiled<4>(ctx, w, tmx, M, y, ldy, s);
-    }
+    return mv == 1 ? launch_xtile<1>(ctx, w, tmx, M, y, ldy, s) : launch_xtile<2>(ctx, w, tmx, M, y, ldy, s);
 }
 
 }  // namespace
@@ -1123,12 +1270,15 @@ pfrt_status pfrt_csr_create(pfrt_ctx* ctx, int64_t N, int64_t K, int64_t nnz,
                 cent[fill[static_cast<size_t>(c) * (N + 1) + r]++] =
                     make_uint2(static_cast<uint32_t>(ix[j] - c * kTileKT), bits);
             }
-        e = cudaMalloc(&w->cptr, sizeof(int32_t) * cptr.size());
-        if (e == cudaSuccess) e = cudaMalloc(&w->cent, sizeof(uint2) * cent.size());
+        e = cudaMalloc(&w->cptr, sizeof(int32_t) * (cptr.size() + 4));
+        if (e == cudaSuccess) e = cudaMalloc(&w->cent, sizeof(uint2) * (cent.size() + 2));
+        if (e == cudaSuccess) e = cudaMemset(w->cptr, 0, sizeof(int32_t) * (cptr.size() + 4));
+        if (e == cudaSuccess) e = cudaMemset(w->cent, 0, sizeof(uint2) * (cent.size() + 2));
         if (e == cudaSuccess)
             e = cudaMemcpy(w->cptr, cptr.data(), sizeof(int32_t) * cptr.size(), cudaMemcpyHostToDevice);
         if (e == cudaSuccess)
             e = cudaMemcpy(w->cent, cent.data(), sizeof(uint2) * cent.size(), cudaMemcpyHostToDevice);
+        w->host_cptr = std::move(cptr);
         if (e != cudaSuccess) {
             pfrt_csr_destroy(w);
             return cuda_fail(e, "pfrt_csr_create (blocked copy)");
@@ -1154,6 +1304,7 @@ pfrt_status pfrt_csr_destroy(pfrt_csr* w) {
     if (w->values) cudaFree(w->values);
     if (w->cptr) cudaFree(w->cptr);
     if (w->cent) cudaFree(w->cent);
+    if (w->xt_part) cudaFree(w->xt_part);
     if (w->part) cudaFree(w->part);
     if (w->dense) pfrt_fweight_destroy(w->dense);
     delete w;
@@ -1182,25 +1333,44 @@ pfrt_status pfrt_spmm(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* 
                              (M >= 3 && M <= 8 && !(rowwarp && *rowwarp == '1'));
     if (M >= 1 && M <= 8 && want_stream)
         return run_spmm_stream(ctx, const_cast<pfrt_csr*>(w), M, x, ldx, y, ldy, pick_stream(ctx, stream));
-    const char* tiled = std::getenv("PFRT_SPMM_TILED");
-    if (M > 8 && tiled && *tiled == '1')
-        return run_spmm_tiled(ctx, w, M, x, ldx, y, ldy, pick_stream(ctx, stream));
-    // Large batches: the product is compute-bound, and the CSR kernels reach
-    // ~5 TFLOP/s while the 3xTF32 tensor-core GEMM reaches ~200 TFLOP/s on the
-    // same product with W stored dense, so above ~2.5% density (and M >= 32)
-    // Y = X W^T runs as a GEMM on a dense copy of W made once (the copy,
-    // 8 bytes per element of W, is capped at 8 GiB).
+    if (M <= 8)
+        return run_spmm(ctx, M, w->N, w->K, w->nnz, w->indptr, w->indices, w->values, x, ldx, y, ldy,
+                        pick_stream(ctx, stream), /*validated=*/true);
+    // M > 8: the tiled CSR kernel (spmm_xtile_kernel) or a 3xTF32 tensor-core
+    // GEMM on a dense copy of W made once (8 bytes per element of W, capped
+    // at 8 GiB), whichever the cost model below expects to be faster.  Both
+    // estimates are fits to B200 measurements (8192^2 and 4096^2 at 50-99 %
+    // sparsity, M = 16..256): the tiled kernel costs ~0.9 us per 256-column
+    // chunk (the load pipeline) plus ~20 ps per nonzero and 32*MV-row tile of
+    // X (it is bound by the instructions per nonzero, not by memory); the GEMM
+    // the larger of reading the dense copy at ~5.5 TB/s and its tensor work.
+    // The dense copy wins down to ~5 % density; the tiled kernel serves
+    // sparser weights and strided X or Y.
+    // PFRT_SPMM_TILED / PFRT_SPMM_DENSE = 0|1 override the choice.
+    cudaStream_t s = pick_stream(ctx, stream);
+    pfrt_csr* wm = const_cast<pfrt_csr*>(w);
+    const char* tiled_env = std::getenv("PFRT_SPMM_TILED");
     const char* dense_env = std::getenv("PFRT_SPMM_DENSE");
-    const double dense_bytes = 8.0 * static_cast<double>(w->N) * static_cast<double>(align_up(w->K, 32));
-    const bool dense_auto = M >= 32 && 40.0 * static_cast<double>(w->nnz) > static_cast<double>(w->N) * w->K &&
-                            dense_bytes <= 8.0 * (1ull << 30);
-    const bool use_dense = dense_env && *dense_env ? (*dense_env == '1') : dense_auto;
-    if (M > 8 && use_dense && w->N > 0 && w->K > 0 && ldx == w->K && ldy == w->N) {
-        pfrt_csr* wm = const_cast<pfrt_csr*>(w);
-        cudaStream_t s = pick_stream(ctx, stream);
+    const double Nd = static_cast<double>(w->N), Kd = static_cast<double>(w->K), Md = static_cast<double>(M);
+    const double dense_bytes = 8.0 * Nd * static_cast<double>(align_up(w->K, 32));
+    const bool packed = ldx == w->K && ldy == w->N && w->N > 0 && w->K > 0;
+    const bool dense_ok = packed && dense_bytes <= 8.0 * (1ull << 30);
+    const double mv = (M <= 32) ? 1.0 : 2.0;
+    const double mtiles = std::ceil(Md / (32.0 * mv));
+    const double t_tiled = 0.9e-6 * static_cast<double>(w->nchunks) +
+                           static_cast<double>(w->nnz) * mtiles * 20.0e-12 * (148.0 / static_cast<double>(ctx->num_sms));
+    const double t_dense = std::max((dense_bytes + 8.0 * Md * Kd) / 5.5e12, 6.0 * Md * Nd * Kd / 6.0e14);
+    bool use_dense = dense_ok && t_dense < t_tiled;
+    if (dense_env && *dense_env) use_dense = dense_ok && *dense_env == '1';
+    if (tiled_env && *tiled_env) use_dense = use_dense && *tiled_env == '0';
+    if (use_dense) {
         st = ensure_dense(ctx, wm, s);
         if (st) return st;
         return pfrt_gemm_f32(ctx, M, 0, 1.0f, x, wm->dense, 0.0f, nullptr, 0, y, s);
+    }
+    if (!(tiled_env && *tiled_env == '0')) {
+        st = run_spmm_xtile(ctx, wm, M, x, ldx, y, ldy, s);
+        if (st != PFRT_ERR_UNSUPPORTED) return st;  // else a row too dense for the tile: the wide kernel
     }
     return run_spmm(ctx, M, w->N, w->K, w->nnz, w->indptr, w->indices, w->values, x, ldx, y, ldy,
                     pick_stream(ctx, stream), /*validated=*/true);
