@@ -189,6 +189,24 @@ PFRT_API pfrt_status pfrt_spmm_csr_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int6
                               const float* values, const float* x, int64_t ldx, float* y,
                               int64_t ldy, pfrt_stream stream);
 
+/* Magnitude pruning of a dense fp32 weight straight into a CSR weight (the
+ * "pruning -> CSR" step that feeds SparseMatMul).  Reproduces
+ * pruning::MagnitudePruning::compute_mask (src/pruning/magnitude_pruning.cpp:
+ * 22-102) followed by pruning::to_sparse of W * mask with threshold 0
+ * (src/pruning/sparse_tensor.cpp:560-587): the threshold is the
+ * floor(n*sparsity)-th smallest |w|, weights above it are kept, ties at it
+ * are kept in index order while more than (size_t)((float)n * sparsity)
+ * weights would be pruned, and the CSR holds the kept nonzeros row by row.
+ * w_dev: device W [N, K] (one CSR row per row of W).  The threshold search,
+ * the tie ranking and the compaction run on the GPU; the CSR is then prepared
+ * as by pfrt_csr_create.  mask_dev (optional, device [N*K] floats) receives
+ * compute_mask's 0/1 mask.  NaN weights: PFRT_ERR_INVALID_ARGUMENT (the
+ * reference's sort is undefined for them); N*K = 0 with 0 < sparsity < 1:
+ * PFRT_ERR_INVALID_ARGUMENT "Cannot prune empty weight tensor", as the
+ * reference throws. */
+PFRT_API pfrt_status pfrt_csr_from_magnitude_pruning(pfrt_ctx* ctx, int64_t N, int64_t K, const float* w_dev,
+                                                     float sparsity, float* mask_dev, pfrt_csr** out);
+
 /* ------------------------------------------------------------ peer memory
  * No counterpart in the reference: it has no communication backend (its
  * partitioner, src/partition/graph_partitioner.cpp:111-200, only plans

@@ -211,3 +211,60 @@ void oracle_gemm_f64(int64_t M, int64_t N, int64_t K, int trans_a, int trans_b,
     if (C && c_len > 0)
         for (int64_t i = 0; i < M * N; ++i) Y[i] += beta * (double)C[i % c_len];
 }
+
+/* ---------------------------------------------------------------- pruning */
+static int cmp_float(const void* a, const void* b) {
+    const float x = *(const float*)a, y = *(const float*)b;
+    return (x > y) - (x < y);
+}
+
+int oracle_magnitude_mask(int64_t n, const float* w, float sparsity, float* mask) {
+    if (sparsity <= 0.0f) { /* magnitude_pruning.cpp:33-39 */
+        for (int64_t i = 0; i < n; ++i) mask[i] = 1.0f;
+        return 0;
+    }
+    if (sparsity >= 1.0f) { /* :41-47 */
+        for (int64_t i = 0; i < n; ++i) mask[i] = 0.0f;
+        return 0;
+    }
+    if (n == 0) return -1; /* :54-56 */
+    float* scores = (float*)malloc(sizeof(float) * (size_t)n);
+    for (int64_t i = 0; i < n; ++i) scores[i] = fabsf(w[i]);
+    qsort(scores, (size_t)n, sizeof(float), cmp_float); /* :66 */
+    size_t idx = (size_t)floor((double)n * (double)sparsity); /* :70-73, double */
+    if (idx > (size_t)n - 1) idx = (size_t)n - 1;
+    const float thr = scores[idx];
+    free(scores);
+    for (int64_t i = 0; i < n; ++i) mask[i] = (fabsf(w[i]) > thr) ? 1.0f : 0.0f; /* :79-81 */
+    /* :84: size_t * float is evaluated in float */
+    const size_t target = (size_t)((float)n * sparsity);
+    size_t zeros = 0;
+    for (int64_t i = 0; i < n; ++i) zeros += (mask[i] == 0.0f);
+    if (zeros > target) { /* :91-98: restore ties in index order */
+        size_t restore = zeros - target;
+        for (int64_t i = 0; i < n && restore > 0; ++i) {
+            if (mask[i] == 0.0f && fabsf(w[i]) == thr) {
+                mask[i] = 1.0f;
+                --restore;
+            }
+        }
+    }
+    return 0;
+}
+
+void oracle_masked_csr(int64_t rows, int64_t cols, const float* w, const float* mask, int32_t* indptr,
+                       int32_t* indices, float* values) {
+    int64_t nz = 0;
+    indptr[0] = 0;
+    for (int64_t r = 0; r < rows; ++r) {
+        for (int64_t c = 0; c < cols; ++c) {
+            const float d = w[r * cols + c] * mask[r * cols + c];
+            if (fabsf(d) > 0.0f) {
+                indices[nz] = (int32_t)c;
+                values[nz] = d;
+                ++nz;
+            }
+        }
+        indptr[r + 1] = (int32_t)nz;
+    }
+}

@@ -96,6 +96,24 @@ void oracle_gemm_f64(int64_t M, int64_t N, int64_t K, int trans_a, int trans_b,
                      double alpha, double beta, const float* A, const float* B,
                      const float* C, int64_t c_len, double* Y);
 
+/* pruning::MagnitudePruning::compute_mask (src/pruning/magnitude_pruning.cpp:
+ * 22-102) on n weights: mask[i] = 1 keeps w[i], 0 prunes it.
+ *   sparsity <= 0: keep all; sparsity >= 1: prune all;
+ *   threshold = the floor(n*sparsity)-th smallest |w| (0-based, capped at
+ *   n-1), keep |w| > threshold; if more than (size_t)((float)n * sparsity)
+ *   weights are pruned, keep again the first entries (in index order) with
+ *   |w| == threshold until that count is reached.
+ * Returns -1 for n == 0 with 0 < sparsity < 1 (the reference throws), else 0.
+ * Weights must not be NaN (the reference's sort is then undefined). */
+int oracle_magnitude_mask(int64_t n, const float* w, float sparsity, float* mask);
+
+/* pruning::to_sparse(D, threshold, CSR) (src/pruning/sparse_tensor.cpp:
+ * 560-587) on D = W * mask (elementwise, fp32), threshold 0: row r keeps the
+ * columns with |D[r][c]| > 0, in column order.  indptr [rows+1]; indices and
+ * values must hold the number of nonzeros (at most rows*cols). */
+void oracle_masked_csr(int64_t rows, int64_t cols, const float* w, const float* mask, int32_t* indptr,
+                       int32_t* indices, float* values);
+
 #ifdef __cplusplus
 }
 #endif

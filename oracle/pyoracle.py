@@ -50,6 +50,8 @@ def lib():
         L.oracle_spmm_linear.argtypes = [_i64, _i64, _i64, _p, _p, _p, _p, _p]
         L.oracle_spmm_linear_f64.argtypes = [_i64, _i64, _i64, _p, _p, _p, _p, _p]
         L.oracle_gemm_f64.argtypes = [_i64, _i64, _i64, _int, _int, _f64, _f64, _p, _p, _p, _i64, _p]
+        L.oracle_magnitude_mask.argtypes = [_i64, _p, _f32, _p]
+        L.oracle_masked_csr.argtypes = [_i64, _i64, _p, _p, _p, _p, _p]
         _lib = L
     return _lib
 
@@ -74,6 +76,8 @@ def ref():
         L.pfref_quantized_matmul_op.argtypes = [_i64, _i64, _i64, _p, _int, _f32, _i32, _p, _f32, _i32, _p]
         L.pfref_quantize.argtypes = [_i64, _p, _f32, _i32, _int, _p]
         L.pfref_sparse_matmul.argtypes = [_i64, _i64, _i64, _p, _p, _p, _i64, _p, _p, _int]
+        L.pfref_magnitude_mask.argtypes = [_i64, _i64, _p, _f32, _p]
+        L.pfref_to_sparse_csr.argtypes = [_i64, _i64, _p, _f32, _i64, _p, _p, _p, _p]
         _ref = L
     return _ref
 
@@ -276,3 +280,46 @@ def ref_sparse_matmul(indptr, indices, values, B, nthreads=1):
     _check_ref(ref().pfref_sparse_matmul(R, B.shape[0], B.shape[1], _ptr(ip), _ptr(ix), _ptr(v),
                                          v.size, _ptr(B), _ptr(out), nthreads))
     return out
+
+
+def magnitude_mask(w, sparsity):
+    """Restated MagnitudePruning::compute_mask on W (any shape): 0/1 float mask."""
+    w = _c(w, np.float32)
+    mask = np.empty(w.shape, np.float32)
+    rc = lib().oracle_magnitude_mask(w.size, _ptr(w), float(sparsity), _ptr(mask))
+    if rc != 0:
+        raise RuntimeError("Cannot prune empty weight tensor")
+    return mask
+
+
+def masked_csr(w, mask):
+    """to_sparse(W * mask, 0, CSR) of W [rows, cols]: (indptr, indices, values) int32/int32/fp32."""
+    w, mask = _c(w, np.float32), _c(mask, np.float32)
+    rows, cols = w.shape
+    nnz_max = int(np.count_nonzero(mask))
+    ip = np.empty(rows + 1, np.int32)
+    ix = np.empty(max(nnz_max, 1), np.int32)
+    v = np.empty(max(nnz_max, 1), np.float32)
+    lib().oracle_masked_csr(rows, cols, _ptr(w), _ptr(mask), _ptr(ip), _ptr(ix), _ptr(v))
+    return ip, ix[: ip[-1]], v[: ip[-1]]
+
+
+def ref_magnitude_mask(w, sparsity):
+    w = _c(w, np.float32)
+    rows, cols = (w.shape if w.ndim == 2 else (1, w.size))
+    mask = np.empty(w.shape, np.float32)
+    _check_ref(ref().pfref_magnitude_mask(rows, cols, _ptr(w), float(sparsity), _ptr(mask)))
+    return mask
+
+
+def ref_to_sparse_csr(d, threshold=0.0):
+    d = _c(d, np.float32)
+    rows, cols = d.shape
+    cap = int(np.count_nonzero(np.abs(d) > threshold))
+    ip = np.empty(rows + 1, np.int64)
+    ix = np.empty(max(cap, 1), np.int64)
+    v = np.empty(max(cap, 1), np.float32)
+    nnz = np.zeros(1, np.int64)
+    _check_ref(ref().pfref_to_sparse_csr(rows, cols, _ptr(d), float(threshold), cap, _ptr(ip), _ptr(ix), _ptr(v),
+                                         _ptr(nnz)))
+    return ip, ix[: nnz[0]], v[: nnz[0]]

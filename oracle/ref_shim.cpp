@@ -8,6 +8,7 @@
 //
 // Every function returns 0 on success and -1 on a C++ exception, whose
 // message is available from pfref_last_error().
+#include "pyflame_rt/pruning/pruning.hpp"
 #include "pyflame_rt/graph.hpp"
 #include "pyflame_rt/node.hpp"
 #include "pyflame_rt/tensor.hpp"
@@ -290,6 +291,34 @@ int pfref_sparse_matmul(int64_t R, int64_t Kw, int64_t C, const int64_t* indptr,
             std::memcpy(out + r0 * C, r.data(), sizeof(float) * (r1 - r0) * C);
         });
         (void)nnz;
+    });
+}
+
+// pruning::MagnitudePruning::compute_mask (src/pruning/magnitude_pruning.cpp:
+// 22-102) on W [rows, cols]: mask_out [rows*cols] of 0/1 floats.
+int pfref_magnitude_mask(int64_t rows, int64_t cols, const float* w, float sparsity, float* mask_out) {
+    return guarded([&] {
+        pruning::MagnitudePruning mp;
+        auto m = mp.compute_mask("w", view(w, {rows, cols}, DType::Float32), sparsity);
+        std::memcpy(mask_out, m.mask.data(), sizeof(float) * rows * cols);
+    });
+}
+
+// pruning::to_sparse(dense, threshold, CSR) (src/pruning/sparse_tensor.cpp:
+// 560-587) on D [rows, cols]; writes indptr [rows+1], and indices/values up
+// to `cap` entries, and *nnz_out.
+int pfref_to_sparse_csr(int64_t rows, int64_t cols, const float* d, float threshold, int64_t cap,
+                        int64_t* indptr, int64_t* indices, float* values, int64_t* nnz_out) {
+    return guarded([&] {
+        auto sp = pruning::to_sparse(view(d, {rows, cols}, DType::Float32), threshold, pruning::SparseFormat::CSR);
+        const auto& ip = sp.indptr();
+        const auto& ix = sp.indices();
+        const float* v = sp.values().data();
+        *nnz_out = static_cast<int64_t>(ix.size());
+        std::copy(ip.begin(), ip.end(), indptr);
+        const int64_t n = std::min<int64_t>(cap, static_cast<int64_t>(ix.size()));
+        std::copy(ix.begin(), ix.begin() + n, indices);
+        std::copy(v, v + n, values);
     });
 }
 

@@ -236,6 +236,23 @@ class CSR:
                                      ix.ctypes.data_as(C.c_void_p), 32 if ip.dtype == np.int32 else 64,
                                      v.ctypes.data_as(C.c_void_p), C.byref(self._h)), "pfrt_csr_create")
 
+    @classmethod
+    def from_magnitude_pruning(cls, ctx: Context, w, sparsity: float, mask=None):
+        """Magnitude-prune the device weight W [N, K] (a CUDA fp32 tensor) to
+        `sparsity` as MagnitudePruning::compute_mask does and keep the result
+        as a CSR weight (pfrt_csr_from_magnitude_pruning).  `mask` (optional,
+        a CUDA fp32 tensor of W's size) receives the 0/1 mask."""
+        N, K = int(w.shape[0]), int(w.shape[1])
+        self = cls.__new__(cls)
+        self.ctx, self.N, self.K = ctx, N, K
+        self._h = C.c_void_p()
+        _check(lib().pfrt_csr_from_magnitude_pruning(ctx.handle, N, K, _dptr(w), float(sparsity), _dptr(mask),
+                                                     C.byref(self._h)), "pfrt_csr_from_magnitude_pruning")
+        nnz = C.c_int64()
+        _check(lib().pfrt_csr_info(self._h, None, None, C.byref(nnz)), "pfrt_csr_info")
+        self.nnz = int(nnz.value)
+        return self
+
     def __call__(self, x, y=None, stream=None):
         import torch
         M = x.shape[0]

@@ -22,6 +22,7 @@
 #include "oracle.h"
 #include "pyflame_rt/errors.hpp"
 #include "pyflame_rt/graph.hpp"
+#include "sparsify.hpp"
 
 using namespace pyflame_rt;
 
@@ -354,6 +355,99 @@ int main() {
         oracle_spmm_linear(M, N, K, ip32.data(), ix32.data(), vv.data(), x.data_ptr<float>(), ref.data_ptr<float>());
         const double e = normwise(y[0], ref);
         EXPECT(e <= 1e-5, "normwise error " + std::to_string(e));
+    });
+
+    // The pruning -> CSR graph pass: compute_mask's criterion (checked against
+    // the oracle's restatement, itself pinned to the reference), MatMul and
+    // Gemm (transB, bias) rewritten to SparseMatMul, and the rewritten graph
+    // on the GPU against CPUExecutor on the original graph with pruned weights.
+    run_test("MagnitudeMaskCriterion", [&] {
+        for (int kind = 0; kind < 3; ++kind) {
+            const int64_t n = 97 * 131;
+            Tensor w = kind == 0 ? randn({n}, 1.0f, 40) : randint<float>({n}, -3, 3, DType::Float32, 41);
+            if (kind == 2) std::fill(w.data_ptr<float>(), w.data_ptr<float>() + n / 2, 0.0f);
+            for (float s : {-0.1f, 0.0f, 0.3f, 0.9f, 0.95f, 0.999f, 1.0f}) {
+                auto m = cuda::magnitude_mask(w.data_ptr<float>(), n, s);
+                std::vector<float> ref(static_cast<size_t>(n));
+                EXPECT(oracle_magnitude_mask(n, w.data_ptr<float>(), s, ref.data()) == 0, "oracle");
+                EXPECT(std::memcmp(m.data(), ref.data(), 4 * n) == 0,
+                       "mask differs (kind " + std::to_string(kind) + ", s " + std::to_string(s) + ")");
+            }
+        }
+    });
+
+    run_test("SparsifyPrunedMatMulAndGemm", [&] {
+        const int64_t M = 64, K = 1024, N = 768;
+        Graph g("prunable");
+        g.add_input(TensorInfo("X", sh({M, K}), DType::Float32));
+        g.add_initializer("B1", randn({K, N}, 0.05f, 50));   // MatMul weight [K, N]
+        g.add_initializer("B2", randn({N, K}, 0.05f, 51));   // Gemm weight, transB = 1
+        g.add_initializer("C2", randn({N}, 0.1f, 52));
+        g.add_node(node("mm", "MatMul", {"X", "B1"}, {"Y1"}));
+        auto gm = node("gemm", "Gemm", {"X", "B2", "C2"}, {"Y2"});
+        gm->set_attr("transB", static_cast<int64_t>(1));
+        gm->set_attr("alpha", 1.0f);
+        gm->set_attr("beta", 1.0f);
+        g.add_node(gm);
+        g.add_output(TensorInfo("Y1", sh({M, N}), DType::Float32));
+        g.add_output(TensorInfo("Y2", sh({M, N}), DType::Float32));
+        cuda::SparsifyOptions opt;
+        opt.prune_sparsity = 0.9f;
+        cuda::SparsifyReport rep;
+        Graph sg = cuda::sparsify_matmuls(g, opt, &rep);
+        EXPECT(rep.rewritten == 2, "two nodes rewritten, got " + std::to_string(rep.rewritten));
+        EXPECT(!sg.has_initializer("B1") && !sg.has_initializer("B2") && sg.has_initializer("C2"),
+               "dense weights dropped, bias kept");
+        // The CSR of the MatMul weight equals to_sparse((B1 * mask)^T) with the oracle's mask.
+        const Tensor& B1 = g.get_initializer("B1")->get();
+        std::vector<float> m1(static_cast<size_t>(K * N));
+        oracle_magnitude_mask(K * N, B1.data_ptr<float>(), 0.9f, m1.data());
+        std::vector<int32_t> ip(1, 0), ix;
+        std::vector<float> vv;
+        for (int64_t n = 0; n < N; ++n) {
+            for (int64_t k = 0; k < K; ++k) {
+                const float d = B1.data_ptr<float>()[k * N + n] * m1[k * N + n];
+                if (std::fabs(d) > 0.0f) {
+                    ix.push_back(static_cast<int32_t>(k));
+                    vv.push_back(d);
+                }
+            }
+            ip.push_back(static_cast<int32_t>(ix.size()));
+        }
+        const Tensor& sip = sg.get_initializer("mm_csr_indptr")->get();
+        const Tensor& six = sg.get_initializer("mm_csr_indices")->get();
+        const Tensor& sv = sg.get_initializer("mm_csr_values")->get();
+        EXPECT(sip.num_elements() == N + 1 && six.num_elements() == static_cast<int64_t>(ix.size()), "CSR sizes");
+        EXPECT(std::memcmp(sip.data(), ip.data(), 4 * ip.size()) == 0 &&
+                   std::memcmp(six.data(), ix.data(), 4 * ix.size()) == 0 &&
+                   std::memcmp(sv.data(), vv.data(), 4 * vv.size()) == 0,
+               "CSR of the pruned MatMul weight differs from to_sparse(W * mask)");
+        // GPU on the rewritten graph vs CPUExecutor on the original graph with masked weights.
+        Graph pg("pruned");
+        pg.add_input(TensorInfo("X", sh({M, K}), DType::Float32));
+        Tensor pb1({K, N}, DType::Float32), pb2({N, K}, DType::Float32);
+        const Tensor& B2 = g.get_initializer("B2")->get();
+        std::vector<float> m2(static_cast<size_t>(K * N));
+        oracle_magnitude_mask(K * N, B2.data_ptr<float>(), 0.9f, m2.data());
+        for (int64_t i = 0; i < K * N; ++i) {
+            pb1.data_ptr<float>()[i] = B1.data_ptr<float>()[i] * m1[i];
+            pb2.data_ptr<float>()[i] = B2.data_ptr<float>()[i] * m2[i];
+        }
+        pg.add_initializer("B1", pb1);
+        pg.add_initializer("B2", pb2);
+        pg.add_initializer("C2", g.get_initializer("C2")->get());
+        pg.add_node(node("mm", "MatMul", {"X", "B1"}, {"Y1"}));
+        pg.add_node(gm);
+        pg.add_output(TensorInfo("Y1", sh({M, N}), DType::Float32));
+        pg.add_output(TensorInfo("Y2", sh({M, N}), DType::Float32));
+        std::unordered_map<std::string, Tensor> feeds;
+        feeds["X"] = randn({M, K}, 1.0f, 53);
+        auto y = run(cuda, sg, feeds);
+        auto r = run(cpu, pg, feeds);
+        for (int i = 0; i < 2; ++i) {
+            const double e = normwise(y[i], r[i]);
+            EXPECT(e <= 1e-5, "output " + std::to_string(i) + " normwise error " + std::to_string(e));
+        }
     });
 
     // Error behaviour mirrors CPUExecutor (executor.cpp:80-110, 150-212).

@@ -139,3 +139,37 @@ def test_qmm_accumulators_exact_vs_float64_matmul():
     acc = po.qmm_acc(q.a, q.w, q.a_zp)
     ref = (q.a.astype(np.float64) - q.a_zp) @ q.w.astype(np.float64)
     np.testing.assert_array_equal(acc, ref.astype(np.int64))
+
+
+@pytest.mark.skipif(not po.ref_available(), reason="compiled reference not built")
+@pytest.mark.parametrize("kind", ["normal", "ties", "zeros", "equal"])
+@pytest.mark.parametrize("sparsity", [-0.1, 0.0, 0.3, 0.5, 0.9, 0.95, 0.999, 1.0])
+def test_magnitude_mask_matches_reference(kind, sparsity):
+    """The restated MagnitudePruning::compute_mask (threshold by sorted
+    magnitude, ties restored in index order) and to_sparse(W*mask) equal the
+    reference's own, compiled from src/pruning/{magnitude_pruning,sparse_tensor}.cpp."""
+    rng = np.random.default_rng(abs(hash((kind, sparsity))) % 2**32)
+    shape = (97, 131)
+    if kind == "normal":
+        w = rng.standard_normal(shape).astype(np.float32)
+    elif kind == "ties":
+        w = (rng.integers(-3, 4, shape) / 4).astype(np.float32)
+    elif kind == "zeros":
+        w = np.where(rng.random(shape) < 0.5, 0.0, rng.standard_normal(shape)).astype(np.float32)
+    else:
+        w = np.full(shape, -0.5, np.float32)
+    m = po.magnitude_mask(w, sparsity)
+    np.testing.assert_array_equal(m, po.ref_magnitude_mask(w, sparsity))
+    ip, ix, v = po.masked_csr(w, m)
+    rip, rix, rv = po.ref_to_sparse_csr(w * m)
+    np.testing.assert_array_equal(ip, rip)
+    np.testing.assert_array_equal(ix, rix)
+    np.testing.assert_array_equal(v, rv)
+
+
+@pytest.mark.skipif(not po.ref_available(), reason="compiled reference not built")
+def test_magnitude_mask_empty_weight_raises():
+    with pytest.raises(RuntimeError, match="empty"):
+        po.magnitude_mask(np.zeros((0, 4), np.float32), 0.5)
+    with pytest.raises(RuntimeError, match="empty"):
+        po.ref_magnitude_mask(np.zeros((1, 0), np.float32), 0.5)
