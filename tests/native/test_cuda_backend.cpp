@@ -8,6 +8,7 @@
 // libpfrt_cuda_backend.so / libpfrt_cuda.so.  Needs a B200; run by
 // tests/test_gpu_backend.py.  Prints one "PASS name" or "FAIL name: why" line
 // per test and exits non-zero if any test failed.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -23,6 +24,9 @@
 #include "pyflame_rt/errors.hpp"
 #include "pyflame_rt/graph.hpp"
 #include "sparsify.hpp"
+#include "quantize_pass.hpp"
+#include "pyflame_rt/quantization/quant_ops.hpp"
+#include "pyflame_rt/quantization/quant_params.hpp"
 
 using namespace pyflame_rt;
 
@@ -448,6 +452,61 @@ int main() {
             const double e = normwise(y[i], r[i]);
             EXPECT(e <= 1e-5, "output " + std::to_string(i) + " normwise error " + std::to_string(e));
         }
+    });
+
+    // Quantizer output -> per-channel QuantizedMatMul: the weight scales and
+    // int8 weight equal the reference's compute_dynamic_params_per_channel +
+    // quantize_tensor, the activation parameters its compute_from_minmax, and
+    // the rewritten graph on the GPU is bit-exact to the int8 oracle.
+    run_test("QuantizePassPerChannel", [&] {
+        namespace q = quantization;
+        const int64_t M = 96, K = 512, N = 384;
+        Graph g("fp32_layer");
+        g.add_input(TensorInfo("X", sh({M, K}), DType::Float32));
+        g.add_initializer("W", randn({K, N}, 0.05f, 60));
+        g.add_initializer("bias", randn({N}, 0.1f, 61));
+        g.add_node(node("mm", "MatMul", {"X", "W"}, {"t"}));
+        g.add_node(node("add", "Add", {"t", "bias"}, {"u"}));
+        g.add_node(node("relu", "Relu", {"u"}, {"Y"}));
+        g.add_output(TensorInfo("Y", sh({M, N}), DType::Float32));
+        Tensor x = randn({M, K}, 1.0f, 62);
+        const float* xp = x.data_ptr<float>();
+        const float xmin = *std::min_element(xp, xp + M * K), xmax = *std::max_element(xp, xp + M * K);
+        cuda::QuantizePassOptions opt;
+        opt.act_ranges["X"] = {xmin, xmax};
+        cuda::QuantizePassReport rep;
+        Graph qg = cuda::quantize_matmuls_per_channel(g, opt, &rep);
+        EXPECT(rep.rewritten == 1, "one MatMul rewritten");
+        const Node* qm = qg.get_node("mm");
+        EXPECT(qm && qm->op_type() == "QuantizedMatMul", "mm is a QuantizedMatMul");
+        // reference parameters
+        const Tensor& W = g.get_initializer("W")->get();
+        auto wp = q::compute_dynamic_params_per_channel(W, 1, DType::Int8, true);
+        Tensor wq = q::quantize_tensor(W, wp);  // per-channel over axis 1
+        const auto scales = qm->get_attr<std::vector<float>>("b_scales", {});
+        EXPECT(scales.size() == static_cast<size_t>(N) &&
+                   std::memcmp(scales.data(), wp.scales.data(), 4 * N) == 0,
+               "b_scales differ from compute_dynamic_params_per_channel");
+        const Tensor& Wq = qg.get_initializer("W_q8")->get();
+        EXPECT(same_bytes(Wq, wq), "int8 weight differs from quantize_tensor");
+        auto ap = q::QuantParams::compute_from_minmax(xmin, xmax, DType::UInt8, false);
+        EXPECT(qm->get_attr<float>("a_scale", 0.0f) == ap.scales[0] &&
+                   qm->get_attr<int64_t>("a_zero_point", -1) == ap.zero_points[0],
+               "activation parameters differ from compute_from_minmax");
+        // GPU run vs the oracle on the reference-quantized activations
+        std::unordered_map<std::string, Tensor> feeds;
+        feeds["X"] = x;
+        auto y = run(cuda, qg, feeds);
+        Tensor xq = q::quantize_tensor(x, ap);
+        std::vector<float> ref(static_cast<size_t>(M * N));
+        oracle_qlinear(M, N, K, xq.data(), 1, ap.scales[0], ap.zero_points[0], Wq.data_ptr<int8_t>(), 0,
+                       scales.data(), g.get_initializer("bias")->get().data_ptr<float>(), 1, 0, 1.0f, 0,
+                       ref.data(), nullptr, nullptr);
+        EXPECT(std::memcmp(y[0].data(), ref.data(), 4 * M * N) == 0, "quantized layer not bit-exact to the oracle");
+        // and close to the fp32 layer it replaces
+        auto f = run(cpu, g, feeds);
+        const double e = normwise(y[0], f[0]);
+        EXPECT(e < 0.02, "int8 layer far from fp32: normwise " + std::to_string(e));
     });
 
     // Error behaviour mirrors CPUExecutor (executor.cpp:80-110, 150-212).
