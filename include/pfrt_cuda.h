@@ -225,31 +225,31 @@ PFRT_API pfrt_status pfrt_ipc_close(pfrt_ctx* ctx, void* dev_ptr);
 
 /* Output-channel-sharded SpMM fused with the all-gather of its output
  * (M = 1).  Rank r holds rows [r*ns, r*ns + ns) of W as its CSR w_shard
- * (ns = w_shard's N) and the whole X; the kernel writes every output value
- * y[n] straight into every rank's gathered output, at y[p][r*ns + n], with
- * stores over NVLink, so the all-gather overlaps the SpMM row by row.
- * Ordering, per call e (counted on the device, so the call can sit in a CUDA
- * graph): a rank writes into rank p's output only after p has entered call e
- * (p's earlier work on its stream, including readers of its output, is
- * done), and the call ends only after every rank has finished its stores, so
- * y[rank] holds all world*ns values when the call completes on the stream.
- * Every rank must make the same sequence of calls.
+ * (ns = w_shard's N) and the whole X.  The kernel sends every output value
+ * straight to every other rank as it is computed, together with the call's
+ * number in one 8-byte store over NVLink (no fences), and each rank's blocks
+ * unpack the values that arrive into its own gathered output y [world*ns]
+ * floats.  The call ends when y is complete.  The call number lives on the
+ * device (the call can sit in a CUDA graph) and the receive buffers are used
+ * by its parity, so a rank can run at most one call ahead of another without
+ * overwriting values not yet read.  Every rank must make the same sequence
+ * of calls.
  *
- *   y[p]     rank p's output [world*ns] floats, mapped into this process
- *            (pfrt_ipc_open; y[rank] is this rank's own buffer);
- *   flags[p] rank p's flag array [2*world] uint32, mapped the same way;
- *            zeroed once before the first call;
+ *   y        this rank's gathered output [world*ns] floats (device);
+ *   recv[p]  rank p's receive buffer [2][world*ns] uint64, mapped into this
+ *            process (pfrt_ipc_open; recv[rank] is this rank's own); zeroed
+ *            once before the first call;
  *   state    this rank's private [4] uint32, zeroed once.
  *
  * Waits on other ranks give up after about 2 s: the call then reports
  * PFRT_ERR_DEVICE_TIMEOUT through pfrt_ctx_check and the peer set must be made
- * anew (its flags are out of step).  M != 1: PFRT_ERR_UNSUPPORTED. */
+ * anew (its buffers are out of step).  M != 1: PFRT_ERR_UNSUPPORTED. */
 #define PFRT_MAX_PEERS 8
 typedef struct pfrt_peer_set {
     int32_t rank;
     int32_t world;
-    float* y[PFRT_MAX_PEERS];
-    uint32_t* flags[PFRT_MAX_PEERS];
+    float* y;
+    uint64_t* recv[PFRT_MAX_PEERS];
     uint32_t* state;
 } pfrt_peer_set;
 PFRT_API pfrt_status pfrt_spmm_allgather(pfrt_ctx* ctx, const pfrt_csr* w_shard, int64_t M, const float* x,

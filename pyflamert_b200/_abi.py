@@ -25,9 +25,8 @@ class IpcHandle(C.Structure):
 
 class PeerSet(C.Structure):
     """pfrt_peer_set (include/pfrt_cuda.h)."""
-    _fields_ = [("rank", C.c_int32), ("world", C.c_int32),
-                ("y", C.c_void_p * PFRT_MAX_PEERS), ("flags", C.c_void_p * PFRT_MAX_PEERS),
-                ("state", C.c_void_p)]
+    _fields_ = [("rank", C.c_int32), ("world", C.c_int32), ("y", C.c_void_p),
+                ("recv", C.c_void_p * PFRT_MAX_PEERS), ("state", C.c_void_p)]
 
 
 # name -> argument types; every function returns pfrt_status (int) unless listed in _RESTYPE.

@@ -143,22 +143,33 @@ __device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
     return v;
 }
 
-// Waits until flags[i] has reached e (modulo 2^32) for every i < n.  Gives
-// up after kWaitLimitNs, or as soon as *abort is non-zero; returns false then.
+// Waits until flags[i] has reached e (modulo 2^32) for every i < n (n <= 8).
+// Each poll reads all n flags with relaxed system-scope loads, issued
+// together; once all have reached e, one acquire fence at system scope orders
+// the caller's later accesses after the writers' releases.  Gives up after
+// kWaitLimitNs, or as soon as *abort is non-zero; returns false then.
 __device__ __forceinline__ bool wait_flags_reached(const uint32_t* flags, int n, uint32_t e,
                                                    const uint32_t* abort) {
     const uint64_t t0 = global_timer_ns();
-    for (int i = 0; i < n; ++i) {
-        uint32_t it = 0;
-        while (static_cast<int32_t>(ld_acquire_sys(flags + i) - e) < 0) {
-            if ((++it & 63u) == 0) {
-                if (ld_relaxed_gpu(abort) != 0) return false;
-                if (global_timer_ns() - t0 > kWaitLimitNs || it > kWaitLimitIters) return false;
-            }
-            __nanosleep(32);
+    for (uint32_t it = 0;; ++it) {
+        uint32_t v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (i < n) asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v[i]) : "l"(flags + i) : "memory");
+        bool all = true;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (i < n) all &= static_cast<int32_t>(v[i] - e) >= 0;
+        if (all) {
+            asm volatile("fence.acq_rel.sys;" ::: "memory");
+            return true;
         }
+        if ((it & 63u) == 63u) {
+            if (ld_relaxed_gpu(abort) != 0) return false;
+            if (global_timer_ns() - t0 > kWaitLimitNs || it > kWaitLimitIters) return false;
+        }
+        __nanosleep(20);
     }
-    return true;
 }
 
 // ----------------------------------------------------------------------- TMA

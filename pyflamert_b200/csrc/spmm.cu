@@ -200,26 +200,26 @@ __global__ void __launch_bounds__(THREADS)
 // and indptr clamped.
 //
 // PEER: the output-channel-sharded form fused with the all-gather of Y
-// (pfrt_spmm_allgather).  Row n's value goes to y_p[col0 + n] of every rank
-// p, by stores over NVLink.  Call e (state[1] + 1, counted on the device and
-// read once per block):
-//   - block 0 announces "entered e" in every rank's flags[0][rank] (a relaxed
-//     store: everything that preceded this kernel on the stream is complete);
-//   - before its first store to other ranks, a warp waits until every rank
-//     has entered e, i.e. finished the work that preceded call e on its stream;
-//   - each block, when its rows are done, fences at GPU scope and counts
-//     itself in state[0]; the last one fences at system scope (cumulative over
-//     the other blocks' stores, which it has synchronised with through the
-//     counter), announces "finished e" in every rank's flags[1][rank], waits
-//     until every rank has finished e, and advances state[1].
-// Waits are bounded; one that gives up sets state[3] (the others then stop
-// waiting) and reports kDevWaitTimeout.
+// (pfrt_spmm_allgather).  Rank r computes rows [col0, col0 + N) of the
+// gathered output y.  Each value is written to y locally and sent to every
+// other rank p in one 8-byte relaxed store of (call number << 32 | value
+// bits) into recv_p[parity][col0 + n]: the value and its "ready" mark arrive
+// together, so no fence or flag is needed (the low-latency protocol NCCL
+// uses for small messages).  After its own rows, each block takes a share of
+// the values this rank receives, waits for each to carry the current call
+// number and unpacks it into y.  The call number e = state[1] + 1 is read
+// once per block; the last block to finish (state[0] counts blocks)
+// advances state[1].  recv is used by the parity of e: a rank that has
+// finished call e has received everyone's values of e, so nobody can be more
+// than one call ahead of a reader, and call e+1 writes the other half.
+// A wait that runs out (2 s) sets state[3], so the others stop waiting, and
+// reports kDevWaitTimeout.
 struct PeerArgs {
     int rank;
     int world;
     int64_t col0;
-    float* y[PFRT_MAX_PEERS];
-    uint32_t* flags[PFRT_MAX_PEERS];
+    float* y;
+    uint64_t* recv[PFRT_MAX_PEERS];
     uint32_t* state;
 };
 
@@ -234,14 +234,9 @@ __global__ void __launch_bounds__(THREADS)
     const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * THREADS + threadIdx.x) >> 5;
     const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * THREADS) >> 5;
     uint32_t epoch = 0;
-    bool entered = false;  // lane 0: every rank has entered this call
     __shared__ uint32_t s_epoch;
     if constexpr (PEER) {
-        if (threadIdx.x == 0) {
-            s_epoch = ld_relaxed_gpu(pa.state + 1) + 1u;
-            if (blockIdx.x == 0)
-                for (int p = 0; p < pa.world; ++p) st_relaxed_sys(pa.flags[p] + pa.rank, s_epoch);
-        }
+        if (threadIdx.x == 0) s_epoch = ld_relaxed_gpu(pa.state + 1) + 1u;
     }
     if (vec_x) {
         for (int64_t i = threadIdx.x; i < K / 4; i += THREADS) cp_async_16(xs + 4 * i, x + 4 * i);
@@ -333,15 +328,13 @@ __global__ void __launch_bounds__(THREADS)
         for (int o = 16; o; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
         if (lane == 0) {
             if constexpr (PEER) {
-                if (!entered) {
-                    entered = wait_flags_reached(pa.flags[pa.rank], pa.world, epoch, pa.state + 3);
-                    if (!entered) {
-                        atomicExch(pa.state + 3, 1u);
-                        report_error(err, kDevWaitTimeout);
-                    }
-                }
-                if (entered)
-                    for (int p = 0; p < pa.world; ++p) pa.y[p][pa.col0 + n] = acc;
+                pa.y[pa.col0 + n] = acc;
+                const uint64_t msg = (static_cast<uint64_t>(epoch) << 32) | __float_as_uint(acc);
+                const int64_t at = static_cast<int64_t>(epoch & 1u) * pa.world * N + pa.col0 + n;
+                for (int p = 0; p < pa.world; ++p)
+                    if (p != pa.rank)
+                        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(pa.recv[p] + at), "l"(msg)
+                                     : "memory");
             } else {
                 y[n] = acc;
             }
@@ -349,19 +342,41 @@ __global__ void __launch_bounds__(THREADS)
     }
     if (bad) report_error(err, kDevBadIndex);
     if constexpr (PEER) {
+        // Unpack this block's share of the values the other ranks send.
+        const int64_t incoming = static_cast<int64_t>(pa.world - 1) * N;
+        const int64_t share = (incoming + gridDim.x - 1) / gridDim.x;
+        const int64_t q0 = static_cast<int64_t>(blockIdx.x) * share;
+        const int64_t q1 = q0 + share < incoming ? q0 + share : incoming;
+        const uint64_t* box = pa.recv[pa.rank] + static_cast<int64_t>(epoch & 1u) * pa.world * N;
+        const uint64_t t0 = global_timer_ns();
+        bool ok = true;
+        for (int64_t q = q0 + threadIdx.x; q < q1 && ok; q += THREADS) {
+            const int64_t p = q / N, i = q - p * N;
+            const int64_t src = p < pa.rank ? p : p + 1;  // skip this rank's own slot
+            const int64_t at = src * N + i;
+            for (uint32_t it = 0;; ++it) {
+                uint64_t m;
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(m) : "l"(box + at) : "memory");
+                if (static_cast<uint32_t>(m >> 32) == epoch) {
+                    pa.y[at] = __uint_as_float(static_cast<uint32_t>(m));
+                    break;
+                }
+                if ((it & 255u) == 255u &&
+                    (ld_relaxed_gpu(pa.state + 3) != 0 || global_timer_ns() - t0 > kWaitLimitNs)) {
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        if (!ok) {
+            atomicExch(pa.state + 3, 1u);
+            report_error(err, kDevWaitTimeout);
+        }
         __syncthreads();
         if (threadIdx.x == 0) {
             __threadfence();
-            const uint32_t done = atomicAdd(pa.state, 1u);
-            if (done == gridDim.x - 1) {
-                // last block of this call: every block's stores are issued and fenced
+            if (atomicAdd(pa.state, 1u) == gridDim.x - 1) {
                 pa.state[0] = 0u;
-                __threadfence_system();
-                for (int p = 0; p < pa.world; ++p) st_release_sys(pa.flags[p] + pa.world + pa.rank, epoch);
-                if (!wait_flags_reached(pa.flags[pa.rank] + pa.world, pa.world, epoch, pa.state + 3)) {
-                    atomicExch(pa.state + 3, 1u);
-                    report_error(err, kDevWaitTimeout);
-                }
                 st_release_gpu(pa.state + 1, epoch);
             }
         }
@@ -1387,9 +1402,9 @@ pfrt_status pfrt_spmm_allgather(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, con
     const int world = peers->world, rank = peers->rank;
     if (world < 1 || world > PFRT_MAX_PEERS || rank < 0 || rank >= world || !peers->state)
         return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: bad rank/world or null state");
+    if (!peers->y) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: null output");
     for (int p = 0; p < world; ++p)
-        if (!peers->y[p] || !peers->flags[p])
-            return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: null peer buffer");
+        if (!peers->recv[p]) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: null receive buffer");
     const size_t shm = sizeof(float) * static_cast<size_t>(std::max<int64_t>(w->K, 1));
     if (shm > 96 * 1024 || w->nnz > INT32_MAX - 4096)
         return fail(PFRT_ERR_UNSUPPORTED, "pfrt_spmm_allgather: K or nnz too large for the fused kernel");
@@ -1397,10 +1412,8 @@ pfrt_status pfrt_spmm_allgather(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, con
     pa.rank = rank;
     pa.world = world;
     pa.col0 = static_cast<int64_t>(rank) * w->N;
-    for (int p = 0; p < world; ++p) {
-        pa.y[p] = peers->y[p];
-        pa.flags[p] = peers->flags[p];
-    }
+    pa.y = peers->y;
+    for (int p = 0; p < world; ++p) pa.recv[p] = peers->recv[p];
     pa.state = peers->state;
     cudaStream_t s = pick_stream(ctx, stream);
     auto kern = spmm_row1_kernel<4, 512, false, true>;

@@ -92,12 +92,13 @@ class _DeviceArray:
 
 class FusedNShardSpMM:
     """Output-channel-sharded SpMM with the all-gather fused into the kernel
-    (pfrt_spmm_allgather, M = 1): every rank's kernel stores its rows of Y
-    straight into every rank's output over NVLink.  The output, the flags and
-    the state live in library-allocated device memory; the ranks exchange
-    CUDA IPC handles of the first two once, through the default process group
-    (any backend: only host objects travel).  All ranks must construct the
-    object together and then make the same calls."""
+    (pfrt_spmm_allgather, M = 1): each rank's kernel sends every value of its
+    rows of Y to every other rank as it computes it, and unpacks the values it
+    receives into its own gathered output.  The output, the receive buffer and
+    the state live in library-allocated device memory; the ranks exchange CUDA
+    IPC handles of their receive buffers once, through the default process
+    group (any backend: only host objects travel).  All ranks must construct
+    the object together and then make the same calls."""
 
     def __init__(self, ctx, N: int, K: int, indptr, indices, values, rank: int, world: int):
         import ctypes as C
@@ -114,18 +115,16 @@ class FusedNShardSpMM:
         L = lib()
         self._own = []
         ptrs = {}
-        for name, nbytes in (("y", 4 * world * self.ns), ("flags", 4 * 2 * world), ("state", 16)):
+        for name, nbytes in (("y", 4 * world * self.ns), ("recv", 8 * 2 * world * self.ns), ("state", 16)):
             p = C.c_void_p()
             _abi.check(L.pfrt_malloc(ctx.handle, nbytes, C.byref(p)), "pfrt_malloc")
             self._own.append(p.value)
             _abi.check(L.pfrt_memset(ctx.handle, p, 0, nbytes, None), "pfrt_memset")
             ptrs[name] = p.value
         _abi.check(L.pfrt_ctx_check(ctx.handle, None), "pfrt_ctx_check")  # zeroed before anyone sees them
-        mine = []
-        for name in ("y", "flags"):
-            h = _abi.IpcHandle()
-            _abi.check(L.pfrt_ipc_get_handle(ctx.handle, C.c_void_p(ptrs[name]), C.byref(h)), "pfrt_ipc_get_handle")
-            mine.append(bytes(h.bytes))
+        h = _abi.IpcHandle()
+        _abi.check(L.pfrt_ipc_get_handle(ctx.handle, C.c_void_p(ptrs["recv"]), C.byref(h)), "pfrt_ipc_get_handle")
+        mine = bytes(h.bytes)
         allh = [None] * world
         if world > 1:
             dist.all_gather_object(allh, mine)
@@ -134,24 +133,22 @@ class FusedNShardSpMM:
         self._opened = []
         ps = _abi.PeerSet()
         ps.rank, ps.world = rank, world
+        ps.y = ptrs["y"]
         for p in range(world):
             if p == rank:
-                ps.y[p], ps.flags[p] = ptrs["y"], ptrs["flags"]
+                ps.recv[p] = ptrs["recv"]
                 continue
-            got = []
-            for hb in allh[p]:
-                h = _abi.IpcHandle()
-                C.memmove(h.bytes, hb, 64)
-                d = C.c_void_p()
-                _abi.check(L.pfrt_ipc_open(ctx.handle, C.byref(h), C.byref(d)), "pfrt_ipc_open")
-                self._opened.append(d.value)
-                got.append(d.value)
-            ps.y[p], ps.flags[p] = got
+            hp = _abi.IpcHandle()
+            C.memmove(hp.bytes, allh[p], 64)
+            d = C.c_void_p()
+            _abi.check(L.pfrt_ipc_open(ctx.handle, C.byref(hp), C.byref(d)), "pfrt_ipc_open")
+            self._opened.append(d.value)
+            ps.recv[p] = d.value
         ps.state = ptrs["state"]
         self.peers = ps
         self._y_ptr = ptrs["y"]
         if world > 1:
-            dist.barrier()  # every rank has mapped every other rank's buffers
+            dist.barrier()  # every rank has mapped every other rank's receive buffer
 
     def output(self):
         """This rank's gathered output Y [1, N] (a view of the library buffer)."""

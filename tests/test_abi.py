@@ -88,11 +88,11 @@ def test_struct_layouts_match_header(tmp_path):
     src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "pfrt_cuda.h"\n'
                    'int main(void){printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(pfrt_peer_set),'
                    ' offsetof(pfrt_peer_set, world), offsetof(pfrt_peer_set, y),'
-                   ' offsetof(pfrt_peer_set, flags), offsetof(pfrt_peer_set, state),'
+                   ' offsetof(pfrt_peer_set, recv), offsetof(pfrt_peer_set, state),'
                    ' sizeof(pfrt_ipc_handle)); return 0;}\n')
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-std=c99", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
     got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
     P = _abi.PeerSet
-    assert got == [C.sizeof(P), P.world.offset, P.y.offset, P.flags.offset, P.state.offset,
+    assert got == [C.sizeof(P), P.world.offset, P.y.offset, P.recv.offset, P.state.offset,
                    C.sizeof(_abi.IpcHandle)]

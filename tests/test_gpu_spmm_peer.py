@@ -1,11 +1,12 @@
 """The output-channel-sharded SpMM fused with its all-gather
-(pfrt_spmm_allgather): every rank's kernel stores its rows of Y straight into
-every rank's output over NVLink, with device-side entry/finish flags.  The
+(pfrt_spmm_allgather): every rank's kernel sends each value of its rows of Y
+to every other rank over NVLink, marked with the call's number, and unpacks
+the values it receives into its own gathered output.  The
 gathered Y must match pruning::sparse_matmul (src/pruning/sparse_tensor.cpp:
 473-519) on the whole W, normwise <= 1e-5, on every rank, call after call
 (the call counter lives on the device) and inside CUDA graph replays.
 
-World 1 runs on one GPU (the rank's own buffers and flags only); world 2
+World 1 runs on one GPU (the rank's own buffers only); world 2
 needs two GPUs and is skipped with fewer."""
 import os
 import socket
