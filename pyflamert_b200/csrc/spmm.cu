@@ -238,9 +238,13 @@ __global__ void __launch_bounds__(THREADS)
     if constexpr (PEER) {
         if (threadIdx.x == 0) s_epoch = ld_relaxed_gpu(pa.state + 1) + 1u;
     }
-    if (vec_x) {
-        for (int64_t i = threadIdx.x; i < K / 4; i += THREADS) cp_async_16(xs + 4 * i, x + 4 * i);
-        cp_async_commit();
+    // Programmatic dependent launch (non-PEER): the CSR of an uploaded weight
+    // is immutable, so the first row's index and value loads go out before
+    // this grid waits for the previous kernel; X and y follow the wait.  A
+    // caller-owned CSR (CHECK) may come from the previous kernel: wait first.
+    if constexpr (!PEER) {
+        if (threadIdx.x == 0) pdl_launch_dependents();
+        if constexpr (CHECK) pdl_wait();
     }
     auto bounds = [&](int64_t r, int32_t& a, int32_t& b) {
         if constexpr (CHECK) {
@@ -271,7 +275,10 @@ __global__ void __launch_bounds__(THREADS)
     int32_t ja = min((j0 + 3) & ~3, j1);
     int32_t jb = ja + ((j1 - ja) & ~3);
     if (ja + 4 * lane < jb) load_round(ja + 4 * lane, jb);
+    if constexpr (!PEER && !CHECK) pdl_wait();
     if (vec_x) {
+        for (int64_t i = threadIdx.x; i < K / 4; i += THREADS) cp_async_16(xs + 4 * i, x + 4 * i);
+        cp_async_commit();
         cp_async_wait_all();
     } else {
         for (int64_t i = threadIdx.x; i < K; i += THREADS) xs[i] = __ldg(x + i);
@@ -907,12 +914,13 @@ pfrt_status run_spmm(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, int64_t nnz
         const int MV = (M == 1) ? 1 : (M == 2) ? 2 : (M <= 4) ? 4 : 8;
         const size_t xs_bytes = sizeof(float) * static_cast<size_t>(K) * MV;
         const char* no_smem = std::getenv("PFRT_SPMM_NO_SMEM");
-        // Staging X costs one copy per block: worth it when the gathers it
-        // replaces (M per nonzero, from separate rows of X when M > 1) cost
-        // more than that copy.
+        // Staging X costs one coalesced copy per block out of L2: worth it
+        // when the gathers it replaces cost more.  Each gathered X element
+        // moves a 32-byte L2 sector (M of them per nonzero, from separate
+        // rows of X when M > 1).
         const int per_sm = static_cast<int>(std::max<size_t>(1, std::min<size_t>(4, (224 * 1024) / (xs_bytes + 1024))));
         const int64_t smem_blocks = std::min<int64_t>(ceil_div(N, 16), int64_t{per_sm} * ctx->num_sms);
-        const bool pays = (M >= 2) || (8.0 * nnz >= 3.0 * static_cast<double>(smem_blocks) * xs_bytes);
+        const bool pays = (M >= 2) || (32.0 * nnz >= static_cast<double>(smem_blocks) * xs_bytes);
         const bool smem = xs_bytes <= 96 * 1024 && K > 0 && pays && !(no_smem && *no_smem == '1');
         const size_t shm = smem ? xs_bytes : 0;
         // One persistent wave: exactly the blocks that are resident at once.
@@ -950,13 +958,21 @@ pfrt_status run_spmm(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, int64_t nnz
             if (oe != cudaSuccess) return cuda_fail(oe, "spmm_row1_kernel occupancy");
             const int b1 = static_cast<int>(std::max<int64_t>(
                 1, std::min<int64_t>(ceil_div(N, 16), int64_t{std::max(1, occ1)} * ctx->num_sms)));
+            cudaLaunchConfig_t lc{};
+            cudaLaunchAttribute la[1];
+            lc.gridDim = dim3(static_cast<unsigned>(b1));
+            lc.blockDim = dim3(512);
+            lc.dynamicSmemBytes = shm;
+            lc.stream = s;
+            lc.numAttrs = pdl_attr(la);
+            lc.attrs = la;
+            const PeerArgs none{};
             if (validated)
-                spmm_row1_kernel<4, 512, false><<<b1, 512, shm, s>>>(N, K, nnz, indptr, indices, values, x, vec_x,
-                                                                     y, ctx->d_err);
+                PFRT_CUDA_TRY(cudaLaunchKernelEx(&lc, spmm_row1_kernel<4, 512, false>, N, K, nnz, indptr, indices,
+                                                 values, x, vec_x, y, ctx->d_err, none));
             else
-                spmm_row1_kernel<4, 512, true><<<b1, 512, shm, s>>>(N, K, nnz, indptr, indices, values, x, vec_x,
-                                                                    y, ctx->d_err);
-            PFRT_CHECK_LAUNCH("spmm_row1_kernel");
+                PFRT_CUDA_TRY(cudaLaunchKernelEx(&lc, spmm_row1_kernel<4, 512, true>, N, K, nnz, indptr, indices,
+                                                 values, x, vec_x, y, ctx->d_err, none));
             return PFRT_OK;
         }
         const int tpb = smem ? 512 : kSpmmThreads;
