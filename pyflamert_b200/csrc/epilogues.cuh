@@ -34,12 +34,32 @@ __device__ __forceinline__ int32_t f2i_like_x86(float r) {
     return (r >= -2147483648.0f && r < 2147483648.0f) ? static_cast<int32_t>(r) : INT32_MIN;
 }
 
+// (int32)std::round(t) as the reference's x86-64 build computes it, in three
+// instructions.  std::round rounds half away from zero; for every float t,
+// round(t) == trunc(t + copysign(p, t)) with p = 0.49999997f, the largest
+// float below 1/2, when the addition rounds to nearest (p instead of 1/2 keeps
+// t = 0.49999997 from rounding up, and the sum's own rounding carries exact
+// halves away from zero).  The truncating conversion saturates: below -2^31
+// it already gives INT32_MIN as cvttss2si does, and the `s < 2^31` test
+// sends +2^31 and above, and NaN, to INT32_MIN.  Checked against
+// f2i_like_x86(roundf(t)) for all 2^32 bit patterns of t.
+__device__ __forceinline__ int32_t round_to_i32_like_x86(float t) {
+    const float p = __int_as_float(0x3EFFFFFF | (__float_as_int(t) & static_cast<int>(0x80000000u)));
+    const float s = __fadd_rn(t, p);
+    return (s < 2147483648.0f) ? __float2int_rz(s) : INT32_MIN;
+}
+
 // quant_ops.cpp:44-46: clamp((int32)std::round(y * inv_scale) + zp, qmin, qmax),
 // with the int32 addition wrapping as it does on the reference's target.
 __device__ __forceinline__ int32_t requant_rn(float y, float inv_scale, int32_t zp, bool u8) {
-    const int32_t r = f2i_like_x86(roundf(__fmul_rn(y, inv_scale)));
+    const int32_t r = round_to_i32_like_x86(__fmul_rn(y, inv_scale));
     const int32_t q = static_cast<int32_t>(static_cast<uint32_t>(r) + static_cast<uint32_t>(zp));
     return u8 ? min(max(q, 0), 255) : min(max(q, -128), 127);
+}
+
+// Low bytes of four values packed little-endian into one word.
+__device__ __forceinline__ uint32_t pack_bytes4(int32_t a, int32_t b, int32_t c, int32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
 struct QEpi {
@@ -110,15 +130,11 @@ struct QEpi {
             uint8_t* d = static_cast<uint8_t*>(out) + static_cast<int64_t>(row) * ldo + col0;
             uint32_t packed[W / 4];
 #pragma unroll
-            for (int w = 0; w < W / 4; ++w) {
-                uint32_t v = 0;
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const uint32_t q = static_cast<uint32_t>(requant_rn(y[4 * w + b], inv_y_scale, y_zp, u8)) & 0xFFu;
-                    v |= q << (8 * b);
-                }
-                packed[w] = v;
-            }
+            for (int w = 0; w < W / 4; ++w)
+                packed[w] = pack_bytes4(requant_rn(y[4 * w], inv_y_scale, y_zp, u8),
+                                        requant_rn(y[4 * w + 1], inv_y_scale, y_zp, u8),
+                                        requant_rn(y[4 * w + 2], inv_y_scale, y_zp, u8),
+                                        requant_rn(y[4 * w + 3], inv_y_scale, y_zp, u8));
             if constexpr (W == 32) {
                 if (full && vec_ok) {
                     *reinterpret_cast<uint4*>(d) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
@@ -162,6 +178,51 @@ struct QEpi {
         }
     }
 
+    // The requantized int8/uint8 tile row (no accumulator copy, int32-exact
+    // zero-point correction): the common case, specialised on the fused
+    // bias, ReLU and output type so each output costs ~15 instructions.
+    template <bool HB, bool RL, bool U8>
+    __device__ __forceinline__ void store_q8(const uint8_t* p, int bn, int row, int col0, int cl, int32_t rterm,
+                                             const uint32_t (&acc)[32]) const {
+        const int4* zc4 = reinterpret_cast<const int4*>(p) + cl / 4;
+        const float4* os4 = reinterpret_cast<const float4*>(p + 4 * bn) + cl / 4;
+        const float4* b4 = reinterpret_cast<const float4*>(p + 8 * bn) + cl / 4;
+        uint32_t packed[8];
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+            const int4 z = zc4[v];
+            const float4 o = os4[v];
+            const int zz[4] = {z.x, z.y, z.z, z.w};
+            const float oo[4] = {o.x, o.y, o.z, o.w};
+            float bb[4] = {0.f, 0.f, 0.f, 0.f};
+            if constexpr (HB) {
+                const float4 b = b4[v];
+                bb[0] = b.x; bb[1] = b.y; bb[2] = b.z; bb[3] = b.w;
+            }
+            int32_t q[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int32_t a = static_cast<int32_t>(acc[4 * v + u]) - zz[u] - rterm;
+                float t = __fmul_rn(__int2float_rn(a), oo[u]);
+                if constexpr (HB) t = __fadd_rn(t, bb[u]);
+                // max(0, t) as activation.cpp:56 computes it, up to the sign of
+                // a zero result, which the integer conversion below discards.
+                if constexpr (RL) t = fmaxf(t, 0.0f);
+                q[u] = requant_rn(t, inv_y_scale, y_zp, U8);
+            }
+            packed[v] = pack_bytes4(q[0], q[1], q[2], q[3]);
+        }
+        uint8_t* d = static_cast<uint8_t*>(out) + static_cast<int64_t>(row) * ldo + col0;
+        if (col0 + 32 <= N && vec_ok) {
+            *reinterpret_cast<uint4*>(d) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            *reinterpret_cast<uint4*>(d + 16) = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (col0 + j < N) d[j] = static_cast<uint8_t>((packed[j >> 2] >> (8 * (j & 3))) & 0xFFu);
+        }
+    }
+
     __device__ __forceinline__ void store(const uint8_t* p, int bn, int row, int col0, int cl, int ks,
                                           const uint32_t (&acc)[32]) const {
         if (row >= M) return;
@@ -172,6 +233,22 @@ struct QEpi {
         int32_t at[32];
         float y[32];
         const int32_t rs = (w_zp != 0) ? rowsum[row] : 0;
+        if (fast32 && out_mode != kOutF32 && acc_out == nullptr) {
+            const int32_t rterm = (w_zp != 0) ? w_zp * rs - K * a_zp * w_zp : 0;
+            const bool u8 = (out_mode == kOutU8);
+            if (bias != nullptr) {
+                if (relu) u8 ? store_q8<true, true, true>(p, bn, row, col0, cl, rterm, acc)
+                             : store_q8<true, true, false>(p, bn, row, col0, cl, rterm, acc);
+                else u8 ? store_q8<true, false, true>(p, bn, row, col0, cl, rterm, acc)
+                        : store_q8<true, false, false>(p, bn, row, col0, cl, rterm, acc);
+            } else {
+                if (relu) u8 ? store_q8<false, true, true>(p, bn, row, col0, cl, rterm, acc)
+                             : store_q8<false, true, false>(p, bn, row, col0, cl, rterm, acc);
+                else u8 ? store_q8<false, false, true>(p, bn, row, col0, cl, rterm, acc)
+                        : store_q8<false, false, false>(p, bn, row, col0, cl, rterm, acc);
+            }
+            return;
+        }
         if (fast32) {
             // Exact in int32: the host checked that no intermediate can overflow.
             const int32_t rterm = (w_zp != 0) ? w_zp * rs - K * a_zp * w_zp : 0;

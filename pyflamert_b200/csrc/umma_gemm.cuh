@@ -67,9 +67,6 @@ struct GemmCfg {
     static constexpr int BAR_BYTES = 256;
     static constexpr int EPI_WARPS = 8;
     static constexpr int EPI_THREADS = 32 * EPI_WARPS;
-    static constexpr int PARAM_BYTES = 16 * BN;  // up to 4 words of per-column parameters
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + PARAM_BYTES + 1024;
-    static constexpr int THREADS = 64 + EPI_THREADS;
     // fp32 (3xTF32) accumulation: the tensor core's fp32 accumulator is not
     // an IEEE round-to-nearest sum, and its error grows with the number of
     // K steps it adds up.  So the MMAs accumulate PROMOTE_KB k-blocks
@@ -77,6 +74,13 @@ struct GemmCfg {
     // such partial into fp32 registers with IEEE adds.  int8 accumulation is
     // exact, so one TMEM accumulation covers the whole K range.
     static constexpr bool PROMOTE = (KIND == KIND_TF32X3);
+    // Per-column parameters: up to 4 words per column, one buffer per tile
+    // in flight.  With one accumulation per tile, two buffers let the
+    // epilogue stage the next tile's parameters while that tile's MMAs run.
+    static constexpr int PARAM_BUF = 16 * BN;
+    static constexpr int PARAM_BYTES = PROMOTE ? PARAM_BUF : 2 * PARAM_BUF;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + PARAM_BYTES + 1024;
+    static constexpr int THREADS = 64 + EPI_THREADS;
     static constexpr int PROMOTE_KB = 4;
     static constexpr int CHUNK_KB = PROMOTE ? PROMOTE_KB : (1 << 30);
     static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns must be a power of two");
@@ -113,7 +117,8 @@ __device__ __forceinline__ void decode_unit_w(const GemmSched& s, int unit, int&
 // Epi must provide:
 //   __device__ void prepare(uint8_t* params, int n0, int bn, int tid, int nthreads) const;
 //       stage the per-column parameters of columns [n0, n0 + bn) (called by
-//       all epilogue threads before a tile's stores; params holds 16*bn bytes)
+//       all epilogue threads, ahead of the tile's accumulator wait where the
+//       kernel double-buffers them; params holds 16*bn bytes)
 //   __device__ void store(const uint8_t* params, int bn, int row, int col0, int c_local,
 //                         int ks, const uint32_t (&acc)[32]) const;
 //       row is the global row of this thread; col0 (= n0 + c_local) the first
@@ -324,6 +329,15 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
         const int half = (warp - 2) >> 2;          // which half of the tile's columns
         constexpr int CHUNKS = BN / 32 / 2;        // 32-column chunks per warp
         int t = 0;                                 // accumulation chunks consumed so far
+        if constexpr (!Cfg::PROMOTE) {
+            // The first tile's parameters, staged while its MMAs run (the
+            // accumulator wait's barrier publishes them).
+            if (static_cast<int>(blockIdx.x) < sched.num_units) {
+                int mb, n0, width, ks;
+                decode_unit_w<BN>(sched, blockIdx.x, mb, n0, width, ks);
+                epi.prepare(params, n0, width, etid, Cfg::EPI_THREADS);
+            }
+        }
         for (int unit = blockIdx.x; unit < sched.num_units; unit += gridDim.x) {
             int mb, n0, width, ks;
             decode_unit_w<BN>(sched, unit, mb, n0, width, ks);
@@ -381,18 +395,19 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
             } else {
                 const int slot = t & 1;
                 const uint32_t ap = static_cast<uint32_t>(t >> 1) & 1u;
+                const uint8_t* pcur = params + slot * Cfg::PARAM_BUF;  // staged before the wait
                 ++t;
                 const bool got = mbar_wait(&tfull[slot], ap, abort_flag);
-                // Uniform stop decision across the epilogue warps; this barrier also
-                // ensures the previous tile's parameters are no longer being read.
+                // Uniform stop decision across the epilogue warps.  The barrier
+                // also publishes this tile's staged parameters, and every warp
+                // passing it has finished the previous tile, whose parameter
+                // buffer is restaged below.
                 if (epi_barrier_or(!got || *abort_flag != 0, Cfg::EPI_THREADS)) {
                     *abort_flag = 1;
                     report_error(err, kDevWaitTimeout);
                     break;
                 }
                 tc_fence_after();
-                epi.prepare(params, n0, width, etid, Cfg::EPI_THREADS);
-                epi_barrier(Cfg::EPI_THREADS);
                 const uint32_t taddr = tmem_base + static_cast<uint32_t>(slot * BN) + lane_off;
                 const int wchunks = width / 64;  // 32-column chunks per warp half
 #pragma unroll 1
@@ -400,10 +415,16 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
                     uint32_t acc[32];
                     tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), acc);
                     tmem_ld_wait();
-                    epi.store(params, width, row, n0 + c * 32, c * 32, ks, acc);
+                    epi.store(pcur, width, row, n0 + c * 32, c * 32, ks, acc);
                 }
                 tc_fence_before();
                 mbar_arrive(&tempty[slot]);
+                const int next = unit + static_cast<int>(gridDim.x);
+                if (next < sched.num_units) {
+                    int mb2, n2, width2, ks2;
+                    decode_unit_w<BN>(sched, next, mb2, n2, width2, ks2);
+                    epi.prepare(params + (t & 1) * Cfg::PARAM_BUF, n2, width2, etid, Cfg::EPI_THREADS);
+                }
             }
         }
     }

@@ -129,7 +129,8 @@ struct Gemm2Cfg {
     static constexpr int BAR_BYTES = 256;
     static constexpr int EPI_WARPS = 8;
     static constexpr int EPI_THREADS = 32 * EPI_WARPS;
-    static constexpr int PARAM_BYTES = 16 * BN;
+    static constexpr int PARAM_BUF = 16 * BN;  // per-column parameters of one tile
+    static constexpr int PARAM_BYTES = 2 * PARAM_BUF;  // the tile in the epilogue and the next
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + PARAM_BYTES + 1024;
     static constexpr int THREADS = 64 + EPI_THREADS;
     static_assert(BN == 128 || BN == 256, "pair tile width");
@@ -277,19 +278,26 @@ __global__ void __launch_bounds__(64 + 32 * Gemm2Cfg<BN, STAGES>::EPI_WARPS, 1)
         const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0u);
         const uint32_t tempty_leader1 = mapa_shared(smem_u32(&tempty[1]), 0u);
         int t = 0;
+        if (pair < sched.num_units) {
+            // The first tile's parameters, staged while its MMAs run.
+            int mb, nb, ks;
+            decode_unit(sched, pair, mb, nb, ks);
+            epi.prepare(params, nb * BN, BN, etid, Cfg::EPI_THREADS);
+        }
         for (int unit = pair; unit < sched.num_units; unit += npairs, ++t) {
             int mb, nb, ks;
             decode_unit(sched, unit, mb, nb, ks);
             const int slot = t & 1;
+            const uint8_t* pcur = params + slot * Cfg::PARAM_BUF;
             const uint32_t ap = static_cast<uint32_t>(t >> 1) & 1u;
             const bool got = mbar_wait(&tfull[slot], ap, abort_flag);
+            // Also publishes this tile's staged parameters; every warp passing
+            // it has finished the previous tile, whose buffer is restaged below.
             if (epi_barrier_or(!got || *abort_flag != 0, Cfg::EPI_THREADS)) {
                 if (etid == 0) stop();
                 break;
             }
             tc_fence_after();
-            epi.prepare(params, nb * BN, BN, etid, Cfg::EPI_THREADS);
-            epi_barrier(Cfg::EPI_THREADS);
             const int row = mb * 2 * BM + static_cast<int>(rank) * BM + q * 32 + lane;
             const uint32_t taddr =
                 tmem_base + static_cast<uint32_t>(slot * BN) + (static_cast<uint32_t>(q * 32) << 16);
@@ -298,11 +306,16 @@ __global__ void __launch_bounds__(64 + 32 * Gemm2Cfg<BN, STAGES>::EPI_WARPS, 1)
                 uint32_t acc[32];
                 tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), acc);
                 tmem_ld_wait();
-                epi.store(params, BN, row, nb * BN + c * 32, c * 32, 0, acc);
+                epi.store(pcur, BN, row, nb * BN + c * 32, c * 32, 0, acc);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(slot ? tempty_leader1 : tempty_leader0);
+            if (unit + npairs < sched.num_units) {
+                int mb2, nb2, ks2;
+                decode_unit(sched, unit + npairs, mb2, nb2, ks2);
+                epi.prepare(params + (slot ^ 1) * Cfg::PARAM_BUF, nb2 * BN, BN, etid, Cfg::EPI_THREADS);
+            }
         }
     }
 
