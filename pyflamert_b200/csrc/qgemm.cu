@@ -19,6 +19,7 @@
 #include "internal.hpp"
 #include "umma_gemm.cuh"
 #include "umma_gemm2.cuh"
+#include "umma_gemm_sk.cuh"
 
 struct pfrt_qweight {
     pfrt_ctx* ctx = nullptr;
@@ -181,6 +182,30 @@ pfrt_status launch_q2(pfrt_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& 
     return PFRT_OK;
 }
 
+// The split-K cluster kernel (umma_gemm_sk.cuh): one 128 x BN tile per
+// cluster of two CTAs, each taking half of K.
+template <int BN, int STAGES>
+pfrt_status launch_qsk2(pfrt_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmSched& s,
+                        const QEpi& e, uint4* xchg, cudaStream_t st) {
+    using Cfg = GemmSkCfg<BN, STAGES>;
+    auto kern = umma_gemm_sk2_kernel<BN, STAGES, QEpi>;
+    PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * s.num_units));
+    cfg.blockDim = dim3(Cfg::THREADS);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1 + pdl_attr(attr + 1);
+    PFRT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tmA, tmB, s, e, xchg, ctx->d_err));
+    return PFRT_OK;
+}
+
 }  // namespace
 }  // namespace pfrt
 
@@ -322,9 +347,24 @@ pfrt_status pfrt_qlinear(pfrt_ctx* ctx, const pfrt_qweight* w, int64_t M, const 
     const int kb_per = static_cast<int>(ceil_div(kb_total, splits));
     splits = static_cast<int>(ceil_div(kb_total, kb_per));
     const size_t part_bytes = (splits > 1) ? align_up(sizeof(int32_t) * splits * M * N, 256) : 0;
+    // K split over CTA pairs (umma_gemm_sk.cuh): 128 x 256 tiles, one per
+    // cluster of two CTAs, where those clusters fit on the GPU at once.  It
+    // pulls a quarter fewer bytes through L2 per SM than 128 x 128 tiles but
+    // pays ~2 us more per call for the exchange of partial sums, so it is
+    // chosen from 28 k-blocks (K >= 3457) on (measured on B200 at M = 512,
+    // N = 4096: 4.7 % faster at K = 4096, 2 % slower at K = 3072, 24 % faster
+    // at K = 16384).  PFRT_QGEMM_SK2 = 0|1 overrides.
+    const int64_t tiles256 = mblk * ceil_div(N, 256);
+    const bool sk2_fits = splits == 1 && kb_total >= 2 && 2 * tiles256 <= G;
+    const int sk2_env = env_int("PFRT_QGEMM_SK2", -1);
+    // An explicit tile width or pair choice (PFRT_QGEMM_BN / _PAIR) selects
+    // those kernels instead.
+    const bool forced = env_int("PFRT_QGEMM_BN", 0) != 0 || env_int("PFRT_QGEMM_PAIR", -1) >= 0;
+    const bool use_sk2 = sk2_fits && (sk2_env >= 0 ? sk2_env != 0 : (kb_total >= 28 && !forced));
+    const size_t xchg_bytes = use_sk2 ? align_up(gemm_sk_xchg_bytes<256>(tiles256), 256) : 0;
 
     void* scr = nullptr;
-    st = scratch(ctx, pad_bytes + rs_bytes + part_bytes, &scr);
+    st = scratch(ctx, pad_bytes + rs_bytes + part_bytes + xchg_bytes, &scr);
     if (st) return st;
     uint8_t* base = static_cast<uint8_t*>(scr);
     const uint8_t* a_use = static_cast<const uint8_t*>(a);
@@ -402,6 +442,20 @@ pfrt_status pfrt_qlinear(pfrt_ctx* ctx, const pfrt_qweight* w, int64_t M, const 
         eg.partial = reinterpret_cast<int32_t*>(base + pad_bytes + rs_bytes);
         eg.acc_out = nullptr;
         e.partial = eg.partial;
+    }
+    if (use_sk2) {
+        GemmSched ks2 = sched;
+        ks2.num_n_blk = static_cast<int>(ceil_div(N, 256));
+        ks2.num_units = static_cast<int>(tiles256);
+        ks2.wide_units = ks2.num_units;
+        ks2.kb_per_split = kb_total;
+        QEpi ek = eg;
+        ek.idesc = idesc_make(2, a_is_u8 ? 0u : 1u, 1u, 128, 256);
+        st = launch_qsk2<256, 4>(ctx, tmA, w->tm_b256, ks2, ek,
+                                 reinterpret_cast<uint4*>(base + pad_bytes + rs_bytes + part_bytes), s);
+        if (st) return st;
+        PFRT_CHECK_LAUNCH("umma_gemm_sk2_kernel<i8>");
+        return PFRT_OK;
     }
     // CTA pairs (256-row tiles over two SMs) where the tile width is 256:
     // measured 5-7 % faster than one CTA per tile at M = 1024..8192, N = K =

@@ -191,3 +191,41 @@ def test_pair_kernel(ctx, M, N, K, bn, monkeypatch):
     ex = exact_acc(q.a, q.a_zp, q.w)
     np.testing.assert_array_equal(acc.astype(np.int64), ex)
     np.testing.assert_array_equal(y, po.qepilogue(ex, q.a_scale, q.w_scale, q.bias, True, "int8", 8.0, 0))
+
+
+@pytest.mark.parametrize("M,N,K,out,relu,bias,y_zp", [
+    (512, 4096, 4096, "int8", False, False, 0),     # config 2
+    (512, 4096, 4096, "int8", True, True, 0),
+    (100, 300, 256, "uint8", True, True, 3),         # two k-blocks, N and M tails
+    (129, 520, 384, "f32", False, True, 0),          # odd k-block count: halves of 2 and 1
+    (7, 256, 4000, "int8", True, False, -4),         # K tail inside the last k-block
+    (256, 1000, 777, "uint8", False, False, 0),
+])
+def test_split_k_cluster_kernel(ctx, M, N, K, out, relu, bias, y_zp, monkeypatch):
+    """K split over a cluster of two CTAs (umma_gemm_sk.cuh): each CTA
+    accumulates half of the k-blocks of a 128 x 256 tile and the partials meet
+    through distributed shared memory.  Outputs and accumulators bit-exact and
+    equal to the one-CTA kernel's."""
+    monkeypatch.setenv("PFRT_QGEMM_SK2", "1")
+    q = wl.qlinear_case(M, N, K, seed=M + 5 * N + K, bias=bias, relu=relu, out=out, y_scale=6.0, y_zp=y_zp)
+    y, acc = run(ctx, q)
+    ex = exact_acc(q.a, q.a_zp, q.w)
+    np.testing.assert_array_equal(acc.astype(np.int64), ex)
+    np.testing.assert_array_equal(bits(y), bits(po.qepilogue(ex, q.a_scale, q.w_scale, q.bias, relu, out, 6.0,
+                                                             y_zp)))
+    np.testing.assert_array_equal(bits(y[:2]), bits(oracle(q, rows=2)))
+    y1, _ = run(ctx, q, want_acc=False)  # the int8 fast epilogue (no accumulator copy)
+    np.testing.assert_array_equal(bits(y1), bits(y))
+    monkeypatch.setenv("PFRT_QGEMM_SK2", "0")
+    y0, acc0 = run(ctx, q)
+    np.testing.assert_array_equal(bits(y0), bits(y))
+    np.testing.assert_array_equal(acc0, acc)
+
+
+def test_split_k_cluster_weight_zero_point(ctx, monkeypatch):
+    monkeypatch.setenv("PFRT_QGEMM_SK2", "1")
+    q = wl.qlinear_case(150, 512, 640, seed=21, a_signed=True, w_zp=-3, out="int8", y_scale=2.0, y_zp=-5)
+    q.a_zp = 7
+    y, acc = run(ctx, q)
+    np.testing.assert_array_equal(y, oracle(q))
+    np.testing.assert_array_equal(acc.astype(np.int64), exact_acc(q.a, q.a_zp, q.w, q.w_zp))
