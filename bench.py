@@ -593,7 +593,8 @@ def main():
                      "frac": achieved / int8_peak, "traffic": profile_traffic("qlinear_config2"),
                      "peak_source": f"int8 dense = 2 x bf16_tflops ({peak_src} MEASURED_PEAKS.json); "
                                     f"counts a multiply-add as 2 ops",
-                     "kernel": "umma_gemm_kernel<i8> (1 launch per step)"},
+                     "kernel": "umma_gemm_sk2_kernel<i8, 256> (1 launch per step: 64 clusters of two CTAs, "
+                               "K split between them)"},
         "e2e": {"value": world * ops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_ms, "path": "pinned host -> device, pfrt_qlinear, device -> pinned host"},
