@@ -9,8 +9,11 @@
 #include "cuda_backend.hpp"
 
 #include <algorithm>
+#include <chrono>
+#include <condition_variable>
 #include <cstring>
 #include <mutex>
+#include <thread>
 #include <numeric>
 #include <sstream>
 #include <unordered_set>
@@ -23,8 +26,8 @@ namespace pyflame_rt {
 namespace {
 
 const std::vector<std::string>& supported_ops() {
-    static const std::vector<std::string> ops = {"Gemm",  "MatMul", "QuantizedMatMul", "SparseMatMul",
-                                                 "Add",   "Relu",   "Quantize"};
+    static const std::vector<std::string> ops = {"Gemm", "MatMul", "QuantizedMatMul", "SparseMatMul",
+                                                 "Add",  "Relu",   "FusedAddRelu",    "Quantize"};
     return ops;
 }
 
@@ -73,6 +76,7 @@ public:
 
     std::vector<Tensor> execute(const Graph& graph, const std::unordered_map<std::string, Tensor>& feeds,
                                 const std::vector<std::string>& output_names);
+    CudaBackend::PrepareStats prepare(const Graph& graph);
 
     int device_;
 
@@ -160,6 +164,16 @@ private:
         return d;
     }
 
+    // ------------------------------------------------------------- prepared weights
+    // Each creates (once) and returns the device form of a node's weight; the
+    // ops and prepare() share them.
+    pfrt_fweight* ensure_fweight(const Graph& g, const Node& n, const std::string& bname, int tb);
+    pfrt_qweight* ensure_qweight(const Graph& g, const Node& n, int64_t K, int64_t N, bool& temporary);
+    pfrt_csr* ensure_csr(const Graph& g, const Node& n, int64_t N, int64_t K);
+    // The initializers a node's preparation reads (prepare() stages them).
+    std::vector<std::string> prepared_inputs(const Graph& g, const Node& n) const;
+    void prepare_node(const Graph& g, const Node& n);
+
     // ------------------------------------------------------------- ops
     void run_gemm(const Graph& g, const Node& n);
     void run_matmul(const Graph& g, const Node& n);
@@ -167,6 +181,7 @@ private:
     void run_sparse(const Graph& g, const Node& n);
     void run_add(const Graph& g, const Node& n);
     void run_relu(const Graph& g, const Node& n);
+    void run_fused_add_relu(const Graph& g, const Node& n);
     void run_quantize(const Graph& g, const Node& n);
 
     std::vector<const Node*> fusable_chain(const Graph& g, const Node& q,
@@ -184,6 +199,72 @@ private:
     std::unordered_map<std::string, DevBuf> act_;
     std::unordered_map<std::string, DevTensor> vals_;
 };
+
+// ----------------------------------------------------------------- prepared weights
+pfrt_fweight* CudaBackend::Impl::ensure_fweight(const Graph& g, const Node& n, const std::string& bname, int tb) {
+    const std::string key = bname + (tb ? "|T" : "|N");
+    auto it = fweights_.find(key);
+    if (it != fweights_.end()) return it->second;
+    const Tensor* B = initializer(g, bname);
+    const int64_t K = tb ? B->shape()[1] : B->shape()[0];
+    const int64_t N = tb ? B->shape()[0] : B->shape()[1];
+    pfrt_fweight* w = nullptr;
+    check(pfrt_fweight_create(ctx_, K, N, tb, B->data_ptr<float>(), &w), &n);
+    return fweights_.emplace(key, w).first->second;
+}
+
+pfrt_qweight* CudaBackend::Impl::ensure_qweight(const Graph& g, const Node& n, int64_t K, int64_t N, bool& temporary) {
+    const std::string& bname = n.inputs()[1];
+    const Tensor* Binit = initializer(g, bname);
+    const int32_t b_zp = static_cast<int32_t>(n.get_attr<int64_t>("b_zero_point", 0));
+    std::vector<float> b_scales = n.get_attr<std::vector<float>>("b_scales", {});
+    if (b_scales.empty()) b_scales.push_back(n.get_attr<float>("b_scale", 1.0f));
+    if (b_scales.size() != 1 && static_cast<int64_t>(b_scales.size()) != N)
+        fail_node(n, "QuantizedMatMul: b_scales needs 1 or N = " + std::to_string(N) + " values");
+    temporary = false;
+    pfrt_qweight* w = nullptr;
+    if (Binit) {
+        // Prepared once per (initializer, scales, zero point).
+        std::ostringstream key;
+        key << bname << "|" << b_zp;
+        for (float s : b_scales) key << "," << s;
+        auto it = qweights_.find(key.str());
+        if (it == qweights_.end()) {
+            check(pfrt_qweight_create(ctx_, K, N, Binit->data_ptr<int8_t>(), b_zp,
+                                      b_scales.data(), static_cast<int64_t>(b_scales.size()), &w), &n);
+            it = qweights_.emplace(key.str(), w).first;
+        }
+        return it->second;
+    }
+    // A runtime weight: prepared for this run only (from a host copy).
+    DevTensor Bd = value(g, bname, n);
+    std::vector<int8_t> host(static_cast<size_t>(K * N));
+    check(pfrt_memcpy_d2h(ctx_, host.data(), Bd.ptr, host.size(), nullptr), &n);
+    check(pfrt_ctx_check(ctx_, nullptr), &n);
+    check(pfrt_qweight_create(ctx_, K, N, host.data(), b_zp, b_scales.data(), static_cast<int64_t>(b_scales.size()),
+                              &w), &n);
+    temporary = true;
+    return w;
+}
+
+pfrt_csr* CudaBackend::Impl::ensure_csr(const Graph& g, const Node& n, int64_t N, int64_t K) {
+    auto it = csrs_.find(n.name());
+    if (it != csrs_.end()) return it->second;
+    const Tensor* ip = initializer(g, n.inputs()[1]);
+    const Tensor* ix = initializer(g, n.inputs()[2]);
+    const Tensor* v = initializer(g, n.inputs()[3]);
+    if (!ip || !ix || !v) fail_node(n, "SparseMatMul: indptr, indices and values must be initializers");
+    if (ip->dtype() != ix->dtype() || (ip->dtype() != DType::Int32 && ip->dtype() != DType::Int64))
+        fail_node(n, "SparseMatMul: indptr and indices must both be int32 or both int64");
+    if (v->dtype() != DType::Float32) fail_node(n, "SparseMatMul: values must be float32");
+    if (ip->num_elements() != N + 1) fail_node(n, "CSR indptr must have length rows + 1");
+    if (ix->num_elements() != v->num_elements()) fail_node(n, "CSR indices and values must have same length");
+    pfrt_csr* csr = nullptr;
+    check(pfrt_csr_create(ctx_, N, K, v->num_elements(), ip->data(), ix->data(),
+                          ip->dtype() == DType::Int32 ? 32 : 64,
+                          v->data_ptr<float>(), &csr), &n);
+    return csrs_.emplace(n.name(), csr).first->second;
+}
 
 // ----------------------------------------------------------------- Gemm
 void CudaBackend::Impl::run_gemm(const Graph& g, const Node& n) {
@@ -213,15 +294,9 @@ void CudaBackend::Impl::run_gemm(const Graph& g, const Node& n) {
         c_len = C.numel();
     }
     DevTensor Y = new_value(n.outputs()[0], {M, N}, DType::Float32);
-    if (Binit && Ka > 0) {
-        const std::string key = bname + (tb ? "|T" : "|N");
-        auto it = fweights_.find(key);
-        if (it == fweights_.end()) {
-            pfrt_fweight* w = nullptr;
-            check(pfrt_fweight_create(ctx_, Ka, N, tb, Binit->data_ptr<float>(), &w), &n);
-            it = fweights_.emplace(key, w).first;
-        }
-        check(pfrt_gemm_f32(ctx_, M, ta, alpha, static_cast<const float*>(A.ptr), it->second, beta, cptr, c_len,
+    if (Binit && Ka > 0 && bshape.size() == 2) {
+        pfrt_fweight* w = ensure_fweight(g, n, bname, tb);
+        check(pfrt_gemm_f32(ctx_, M, ta, alpha, static_cast<const float*>(A.ptr), w, beta, cptr, c_len,
                             static_cast<float*>(Y.ptr), nullptr), &n);
     } else {
         DevTensor B = value(g, bname, n);
@@ -239,7 +314,14 @@ void CudaBackend::Impl::run_matmul(const Graph& g, const Node& n) {
     DevTensor A = value(g, n.inputs()[0], n);
     const std::string& bname = n.inputs()[1];
     const Tensor* Binit = initializer(g, bname);
-    DevTensor B = value(g, bname, n);
+    // A 2-D initializer B is used in its prepared form only (no raw copy).
+    DevTensor B;
+    if (Binit && Binit->ndim() == 2) {
+        B.shape = Binit->shape();
+        B.dtype = Binit->dtype();
+    } else {
+        B = value(g, bname, n);
+    }
     if (A.shape.size() < 2) fail_node(n, "MatMul input A requires at least 2 dimensions, got " + std::to_string(A.shape.size()));
     if (B.shape.size() < 2) fail_node(n, "MatMul input B requires at least 2 dimensions, got " + std::to_string(B.shape.size()));
     if (A.dtype != DType::Float32 || B.dtype != DType::Float32) fail_node(n, "MatMul: the cuda backend computes float32 only");
@@ -263,19 +345,15 @@ void CudaBackend::Impl::run_matmul(const Graph& g, const Node& n) {
     DevTensor Y = new_value(n.outputs()[0], out_shape, DType::Float32);
     const int64_t total = numel(batch) == 0 && batch.empty() ? 1 : numel(batch);
     const float* ap = static_cast<const float*>(A.ptr);
-    const float* bp = static_cast<const float*>(B.ptr);
     float* yp = static_cast<float*>(Y.ptr);
     if (bb.empty() && Binit && Ka > 0) {
         // B shared by every batch: one GEMM over (batch * M) rows.
-        auto it = fweights_.find(bname + "|N");
-        if (it == fweights_.end()) {
-            pfrt_fweight* w = nullptr;
-            check(pfrt_fweight_create(ctx_, Ka, N, 0, Binit->data_ptr<float>(), &w), &n);
-            it = fweights_.emplace(bname + "|N", w).first;
-        }
-        check(pfrt_gemm_f32(ctx_, total * M, 0, 1.0f, ap, it->second, 0.0f, nullptr, 0, yp, nullptr), &n);
+        pfrt_fweight* w = ensure_fweight(g, n, bname, 0);
+        check(pfrt_gemm_f32(ctx_, total * M, 0, 1.0f, ap, w, 0.0f, nullptr, 0, yp, nullptr), &n);
         return;
     }
+    if (!B.ptr) B = value(g, bname, n);  // a 2-D initializer with an empty K
+    const float* bp = static_cast<const float*>(B.ptr);
     // General case: one GEMM per output batch, with broadcast batch offsets.
     auto stride_of = [&](const std::vector<int64_t>& dims) {
         std::vector<int64_t> st(nd, 0);
@@ -319,7 +397,8 @@ std::vector<const Node*> CudaBackend::Impl::fusable_chain(
         const Tensor* b = initializer(g, q.inputs()[1]);
         return b ? b->shape().back() : -1;
     }();
-    if (nx && nx->op_type() == "Add" && nx->inputs().size() == 2) {
+    const bool fused_add_relu = nx && nx->op_type() == "FusedAddRelu";
+    if (nx && (nx->op_type() == "Add" || fused_add_relu) && nx->inputs().size() == 2) {
         const std::string& other = nx->inputs()[0] == cur ? nx->inputs()[1] : nx->inputs()[0];
         const Tensor* bt = initializer(g, other);
         if (bt && bt->dtype() == DType::Float32 && bt->num_elements() == N && !bt->shape().empty() &&
@@ -327,9 +406,11 @@ std::vector<const Node*> CudaBackend::Impl::fusable_chain(
             chain.push_back(nx);
             cur = nx->outputs()[0];
             nx = sole(cur);
+        } else if (fused_add_relu) {
+            return chain;  // not a per-column bias: FusedAddRelu runs on its own
         }
     }
-    if (nx && nx->op_type() == "Relu") {
+    if (nx && nx->op_type() == "Relu" && !(chain.size() == 1 && chain[0]->op_type() == "FusedAddRelu")) {
         chain.push_back(nx);
         cur = nx->outputs()[0];
         nx = sole(cur);
@@ -344,7 +425,14 @@ void CudaBackend::Impl::run_qmatmul(const Graph& g, const Node& n, const std::ve
     DevTensor A = value(g, n.inputs()[0], n);
     const std::string& bname = n.inputs()[1];
     const Tensor* Binit = initializer(g, bname);
-    DevTensor Bd = value(g, bname, n);
+    // An initializer B is used in its prepared form only (no raw copy).
+    DevTensor Bd;
+    if (Binit) {
+        Bd.shape = Binit->shape();
+        Bd.dtype = Binit->dtype();
+    } else {
+        Bd = value(g, bname, n);
+    }
     if (A.dtype != DType::Int8 && A.dtype != DType::UInt8)
         fail_node(n, "QuantizedMatMul: input A must be Int8 or UInt8");
     if (Bd.dtype != DType::Int8) fail_node(n, "QuantizedMatMul: the cuda backend needs Int8 weights (input B)");
@@ -356,34 +444,9 @@ void CudaBackend::Impl::run_qmatmul(const Graph& g, const Node& n, const std::ve
                          std::to_string(Kb) + ")");
     const float a_scale = n.get_attr<float>("a_scale", 1.0f);
     const int32_t a_zp = static_cast<int32_t>(n.get_attr<int64_t>("a_zero_point", 0));
-    const int32_t b_zp = static_cast<int32_t>(n.get_attr<int64_t>("b_zero_point", 0));
-    std::vector<float> b_scales = n.get_attr<std::vector<float>>("b_scales", {});
-    if (b_scales.empty()) b_scales.push_back(n.get_attr<float>("b_scale", 1.0f));
-    if (b_scales.size() != 1 && static_cast<int64_t>(b_scales.size()) != N)
-        fail_node(n, "QuantizedMatMul: b_scales needs 1 or N = " + std::to_string(N) + " values");
-    // Weights: prepared once per (initializer, scales, zero point).
-    std::ostringstream key;
-    key << bname << "|" << b_zp;
-    for (float s : b_scales) key << "," << s;
-    pfrt_qweight* w = nullptr;
-    pfrt_qweight* temp = nullptr;
-    if (Binit) {
-        auto it = qweights_.find(key.str());
-        if (it == qweights_.end()) {
-            check(pfrt_qweight_create(ctx_, K, N, Binit->data_ptr<int8_t>(), b_zp, b_scales.data(),
-                                      static_cast<int64_t>(b_scales.size()), &w), &n);
-            it = qweights_.emplace(key.str(), w).first;
-        }
-        w = it->second;
-    } else {
-        // A runtime weight: prepare it for this run only (from a host copy).
-        std::vector<int8_t> host(static_cast<size_t>(K * N));
-        check(pfrt_memcpy_d2h(ctx_, host.data(), Bd.ptr, host.size(), nullptr), &n);
-        check(pfrt_ctx_check(ctx_, nullptr), &n);
-        check(pfrt_qweight_create(ctx_, K, N, host.data(), b_zp, b_scales.data(), static_cast<int64_t>(b_scales.size()),
-                                  &temp), &n);
-        w = temp;
-    }
+    bool temporary = false;
+    pfrt_qweight* w = ensure_qweight(g, n, K, N, temporary);
+    pfrt_qweight* temp = temporary ? w : nullptr;
     // Fused tail.
     const float* bias = nullptr;
     int relu = 0;
@@ -392,9 +455,10 @@ void CudaBackend::Impl::run_qmatmul(const Graph& g, const Node& n, const std::ve
     int32_t y_zp = 0;
     const Node* last = &n;
     for (const Node* c : chain) {
-        if (c->op_type() == "Add") {
+        if (c->op_type() == "Add" || c->op_type() == "FusedAddRelu") {
             const std::string& other = c->inputs()[0] == last->outputs()[0] ? c->inputs()[1] : c->inputs()[0];
             bias = static_cast<const float*>(init_device(g, other).ptr);
+            if (c->op_type() == "FusedAddRelu") relu = 1;
         } else if (c->op_type() == "Relu") {
             relu = 1;
         } else if (c->op_type() == "Quantize") {
@@ -428,28 +492,12 @@ void CudaBackend::Impl::run_sparse(const Graph& g, const Node& n) {
     const int64_t N = shape[0], K = shape[1];
     if (X.dtype != DType::Float32) fail_node(n, "SparseMatMul: X must be float32");
     if (X.shape.empty() || X.shape.back() != K) fail_node(n, "Dimension mismatch in sparse matmul");
-    auto it = csrs_.find(n.name());
-    if (it == csrs_.end()) {
-        const Tensor* ip = initializer(g, n.inputs()[1]);
-        const Tensor* ix = initializer(g, n.inputs()[2]);
-        const Tensor* v = initializer(g, n.inputs()[3]);
-        if (!ip || !ix || !v) fail_node(n, "SparseMatMul: indptr, indices and values must be initializers");
-        if (ip->dtype() != ix->dtype() || (ip->dtype() != DType::Int32 && ip->dtype() != DType::Int64))
-            fail_node(n, "SparseMatMul: indptr and indices must both be int32 or both int64");
-        if (v->dtype() != DType::Float32) fail_node(n, "SparseMatMul: values must be float32");
-        if (ip->num_elements() != N + 1) fail_node(n, "CSR indptr must have length rows + 1");
-        if (ix->num_elements() != v->num_elements()) fail_node(n, "CSR indices and values must have same length");
-        pfrt_csr* csr = nullptr;
-        check(pfrt_csr_create(ctx_, N, K, v->num_elements(), ip->data(), ix->data(),
-                              ip->dtype() == DType::Int32 ? 32 : 64, v->data_ptr<float>(), &csr), &n);
-        it = csrs_.emplace(n.name(), csr).first;
-    }
+    pfrt_csr* csr = ensure_csr(g, n, N, K);
     const int64_t M = numel(X.shape) / std::max<int64_t>(K, 1);
     std::vector<int64_t> out_shape(X.shape.begin(), X.shape.end() - 1);
     out_shape.push_back(N);
     DevTensor Y = new_value(n.outputs()[0], out_shape, DType::Float32);
-    check(pfrt_spmm(ctx_, it->second, M, static_cast<const float*>(X.ptr), K, static_cast<float*>(Y.ptr), N, nullptr),
-          &n);
+    check(pfrt_spmm(ctx_, csr, M, static_cast<const float*>(X.ptr), K, static_cast<float*>(Y.ptr), N, nullptr), &n);
 }
 
 // ----------------------------------------------------------------- elementwise
@@ -477,6 +525,15 @@ void CudaBackend::Impl::run_relu(const Graph& g, const Node& n) {
     if (x.dtype != DType::Float32) fail_node(n, "Relu: the cuda backend computes float32 only");
     DevTensor y = new_value(n.outputs()[0], x.shape, DType::Float32);
     check(pfrt_relu_f32(ctx_, x.numel(), static_cast<const float*>(x.ptr), static_cast<float*>(y.ptr), nullptr), &n);
+}
+
+// FusedAddRelu (the reference's fusion pass output, fusion_patterns.cpp:40-70):
+// max(0, a + b) with Add's broadcasting.  After a QuantizedMatMul with an
+// initializer bias it is fused into that kernel's epilogue instead.
+void CudaBackend::Impl::run_fused_add_relu(const Graph& g, const Node& n) {
+    run_add(g, n);
+    DevTensor y = vals_.at(n.outputs()[0]);
+    check(pfrt_relu_f32(ctx_, y.numel(), static_cast<const float*>(y.ptr), static_cast<float*>(y.ptr), nullptr), &n);
 }
 
 void CudaBackend::Impl::run_quantize(const Graph& g, const Node& n) {
@@ -534,6 +591,8 @@ std::vector<Tensor> CudaBackend::Impl::execute(const Graph& graph, const std::un
                 run_add(graph, n);
             } else if (op == "Relu") {
                 run_relu(graph, n);
+            } else if (op == "FusedAddRelu") {
+                run_fused_add_relu(graph, n);
             } else if (op == "Quantize") {
                 run_quantize(graph, n);
             } else {
@@ -570,6 +629,176 @@ std::vector<Tensor> CudaBackend::Impl::execute(const Graph& graph, const std::un
     return results;
 }
 
+// ----------------------------------------------------------------- prepare
+std::vector<std::string> CudaBackend::Impl::prepared_inputs(const Graph& g, const Node& n) const {
+    std::vector<std::string> in;
+    auto add = [&](const std::string& name) {
+        const Tensor* t = initializer(g, name);
+        if (t && t->size_bytes() > 0 && std::find(in.begin(), in.end(), name) == in.end()) in.push_back(name);
+    };
+    const std::string& op = n.op_type();
+    if (op == "Gemm" || op == "MatMul" || op == "QuantizedMatMul") {
+        if (n.inputs().size() >= 2) add(n.inputs()[1]);
+        if (op == "Gemm" && n.inputs().size() > 2 && !n.inputs()[2].empty()) add(n.inputs()[2]);
+    } else if (op == "SparseMatMul") {
+        for (size_t i = 1; i < n.inputs().size(); ++i) add(n.inputs()[i]);
+    } else {
+        for (const auto& name : n.inputs()) add(name);
+    }
+    return in;
+}
+
+// The device-side state execute() would create for node n on its first run.
+void CudaBackend::Impl::prepare_node(const Graph& g, const Node& n) {
+    const std::string& op = n.op_type();
+    if (op == "Gemm" || op == "MatMul") {
+        if (n.inputs().size() < 2) return;
+        const Tensor* B = initializer(g, n.inputs()[1]);
+        const int tb = (op == "Gemm" && n.get_attr<int64_t>("transB", 0)) ? 1 : 0;
+        if (B && B->ndim() == 2 && B->dtype() == DType::Float32 && B->shape()[tb ? 1 : 0] > 0)
+            ensure_fweight(g, n, n.inputs()[1], tb);
+        else if (B && op == "MatMul")
+            init_device(g, n.inputs()[1]);
+        if (op == "Gemm" && n.inputs().size() > 2 && !n.inputs()[2].empty() && initializer(g, n.inputs()[2]))
+            init_device(g, n.inputs()[2]);
+    } else if (op == "QuantizedMatMul") {
+        if (n.inputs().size() < 2) return;
+        const Tensor* B = initializer(g, n.inputs()[1]);
+        if (B && B->ndim() == 2 && B->dtype() == DType::Int8) {
+            bool temporary = false;
+            ensure_qweight(g, n, B->shape()[0], B->shape()[1], temporary);
+        }
+    } else if (op == "SparseMatMul") {
+        const std::vector<int64_t> shape = n.get_attr<std::vector<int64_t>>("shape", {});
+        if (n.inputs().size() == 4 && shape.size() == 2) ensure_csr(g, n, shape[0], shape[1]);
+    } else {
+        for (const auto& name : prepared_inputs(g, n)) init_device(g, name);
+    }
+}
+
+namespace {
+
+// Reads one byte per page of [p, p + bytes) over several threads, so that the
+// page faults of a file mapping are taken in parallel ahead of the copy that
+// needs the pages.  Returns a value derived from the bytes read (so the reads
+// are kept).
+unsigned touch_pages(const void* p, size_t bytes) {
+    constexpr size_t kPage = 4096, kChunk = 4u << 20;
+    const uint8_t* b = static_cast<const uint8_t*>(p);
+    auto run = [b](size_t lo, size_t hi) {
+        unsigned acc = 0;
+        for (size_t i = lo; i < hi; i += kPage) acc += b[i];
+        return acc;
+    };
+    const size_t hw = std::max(1u, std::thread::hardware_concurrency());
+    const size_t nt = std::min<size_t>(std::min<size_t>(hw, 16), (bytes + kChunk - 1) / kChunk);
+    if (nt <= 1) return run(0, bytes);
+    const size_t per = ((bytes / nt) + kPage - 1) / kPage * kPage;
+    std::vector<unsigned> part(nt, 0);
+    std::vector<std::thread> ts;
+    for (size_t i = 1; i < nt; ++i)
+        ts.emplace_back([&, i] { part[i] = run(std::min(bytes, i * per), std::min(bytes, (i + 1) * per)); });
+    part[0] = run(0, std::min(bytes, per));
+    unsigned acc = 0;
+    for (size_t i = 0; i < nt; ++i) {
+        if (i) ts[i - 1].join();
+        acc += part[i];
+    }
+    return acc;
+}
+
+}  // namespace
+
+// Builds the device forms node by node, in graph order, straight from the
+// initializers' host memory (for a PfmImage graph, the file mapping), while a
+// second thread faults in the pages of the next node's initializers over
+// several threads: the copies then run at the driver's copy rate instead of
+// stalling on one page fault at a time.  (Staging through pinned buffers was
+// measured slower: pinning the buffers cost more than the copies it sped up.)
+CudaBackend::PrepareStats CudaBackend::Impl::prepare(const Graph& g) {
+    std::lock_guard<std::mutex> lock(mu_);
+    const auto t0 = std::chrono::steady_clock::now();
+    bind_graph(g);
+    std::vector<std::pair<const Node*, std::vector<std::string>>> jobs;
+    const auto& ops = supported_ops();
+    size_t total = 0;
+    for (const auto& node : g.topological_sort()) {
+        if (std::find(ops.begin(), ops.end(), node->op_type()) == ops.end()) continue;
+        jobs.emplace_back(node.get(), prepared_inputs(g, *node));
+        for (const auto& name : jobs.back().second) total += initializer(g, name)->size_bytes();
+    }
+    struct Toucher {
+        std::thread t;
+        std::mutex m;
+        std::condition_variable cv;
+        int touched = -1;   // last job whose pages are in
+        int consumed = -1;  // last job built
+        bool stop = false;
+        double busy = 0.0;
+        ~Toucher() {
+            {
+                std::lock_guard<std::mutex> l(m);
+                stop = true;
+            }
+            cv.notify_all();
+            if (t.joinable()) t.join();
+        }
+    } tc;
+    volatile unsigned sink = 0;
+    tc.t = std::thread([&] {
+        for (int j = 0; j < static_cast<int>(jobs.size()); ++j) {
+            {
+                std::unique_lock<std::mutex> l(tc.m);
+                tc.cv.wait(l, [&] { return tc.stop || tc.consumed >= j - 2; });  // at most one job ahead
+                if (tc.stop) return;
+            }
+            const auto a = std::chrono::steady_clock::now();
+            for (const auto& name : jobs[j].second) {
+                const Tensor* t = initializer(g, name);
+                sink = sink + touch_pages(t->data(), t->size_bytes());
+            }
+            {
+                std::lock_guard<std::mutex> l(tc.m);
+                tc.busy += std::chrono::duration<double>(std::chrono::steady_clock::now() - a).count();
+                tc.touched = j;
+            }
+            tc.cv.notify_all();
+        }
+    });
+    double build = 0.0;
+    for (int j = 0; j < static_cast<int>(jobs.size()); ++j) {
+        {
+            std::unique_lock<std::mutex> l(tc.m);
+            tc.cv.wait(l, [&] { return tc.touched >= j; });
+        }
+        const Node& n = *jobs[j].first;
+        const auto a = std::chrono::steady_clock::now();
+        try {
+            prepare_node(g, n);
+        } catch (const PyFlameRTError&) {
+            throw;
+        } catch (const std::exception& e) {
+            throw BackendError(e.what(), n.name());
+        }
+        check(pfrt_ctx_check(ctx_, nullptr), &n);
+        build += std::chrono::duration<double>(std::chrono::steady_clock::now() - a).count();
+        {
+            std::lock_guard<std::mutex> l(tc.m);
+            tc.consumed = j;
+        }
+        tc.cv.notify_all();
+    }
+    PrepareStats out;
+    out.bytes = total;
+    out.seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    out.build_seconds = build;
+    {
+        std::lock_guard<std::mutex> l(tc.m);
+        out.fault_seconds = tc.busy;
+    }
+    return out;
+}
+
 // ----------------------------------------------------------------- public
 CudaBackend::CudaBackend(int device) : impl_(std::make_unique<Impl>(device)) {}
 CudaBackend::~CudaBackend() = default;
@@ -593,6 +822,8 @@ std::vector<Tensor> CudaBackend::execute(const Graph& graph, const std::unordere
 }
 
 int CudaBackend::device() const { return impl_->device_; }
+
+CudaBackend::PrepareStats CudaBackend::prepare(const Graph& graph) { return impl_->prepare(graph); }
 
 std::unique_ptr<Backend> make_cuda_backend(int device) { return std::make_unique<CudaBackend>(device); }
 

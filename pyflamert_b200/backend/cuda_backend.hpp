@@ -19,6 +19,9 @@
 //                    Y[M,N] = X W^T
 //   Add, Relu        cpu_add, cpu_relu    (math.cpp:222-226, activation.cpp:45-60):
 //                    same shapes, or a row-vector / scalar operand
+//   FusedAddRelu     the fusion pass's Add -> Relu (src/opt/fusion_patterns.cpp:40-70),
+//                    max(0, a + b); fused into a preceding QuantizedMatMul as
+//                    its bias + ReLU
 //   Quantize         cpu_quantize         (quantized_ops.cpp, quantize_tensor)
 // Any other node type raises UnsupportedOperatorError(op, "cuda"); there is
 // no CPU fallback.  Errors inside a node raise BackendError(message, node name)
@@ -56,6 +59,23 @@ public:
                                 const std::vector<std::string>& output_names = {}) override;
 
     int device() const;
+
+    /// Uploads and prepares every initializer the graph's nodes consume (the
+    /// device forms of Gemm/MatMul/QuantizedMatMul weights, CSR arrays,
+    /// biases), as the first execute() would, and keeps them for later runs.
+    /// A second thread faults in the next node's initializer pages (several
+    /// threads per tensor) while the current node's device forms are built,
+    /// so a PfmImage graph, whose initializers view the mapped file, is read
+    /// once, in parallel, with no host copy of a weight.  Raises what
+    /// execute() would for a bad weight.  Not needed for correctness:
+    /// execute() prepares lazily.
+    struct PrepareStats {
+        size_t bytes = 0;            // initializer bytes prepared
+        double seconds = 0.0;        // wall time of the call
+        double build_seconds = 0.0;  // building device forms (copies, kernels)
+        double fault_seconds = 0.0;  // the page-in thread's busy time (overlapped)
+    };
+    PrepareStats prepare(const Graph& graph);
 
 private:
     class Impl;
