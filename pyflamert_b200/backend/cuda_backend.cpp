@@ -110,6 +110,7 @@ private:
         for (auto& [_, b] : inits_) pfrt_free(ctx_, b.ptr);
         fweights_.clear();
         qweights_.clear();
+        qnode_.clear();
         csrs_.clear();
         inits_.clear();
     }
@@ -195,6 +196,7 @@ private:
     std::unordered_map<std::string, DevBuf> inits_;
     std::unordered_map<std::string, pfrt_fweight*> fweights_;
     std::unordered_map<std::string, pfrt_qweight*> qweights_;
+    std::unordered_map<const Node*, pfrt_qweight*> qnode_;  // the entry of qweights_ each node uses
     std::unordered_map<std::string, pfrt_csr*> csrs_;
     std::unordered_map<std::string, DevBuf> act_;
     std::unordered_map<std::string, DevTensor> vals_;
@@ -216,12 +218,18 @@ pfrt_fweight* CudaBackend::Impl::ensure_fweight(const Graph& g, const Node& n, c
 pfrt_qweight* CudaBackend::Impl::ensure_qweight(const Graph& g, const Node& n, int64_t K, int64_t N, bool& temporary) {
     const std::string& bname = n.inputs()[1];
     const Tensor* Binit = initializer(g, bname);
+    temporary = false;
+    if (Binit) {
+        // This node's weight, once found (the lookup below copies the
+        // per-channel scales and formats each into a key: more than a launch).
+        auto hit = qnode_.find(&n);
+        if (hit != qnode_.end()) return hit->second;
+    }
     const int32_t b_zp = static_cast<int32_t>(n.get_attr<int64_t>("b_zero_point", 0));
     std::vector<float> b_scales = n.get_attr<std::vector<float>>("b_scales", {});
     if (b_scales.empty()) b_scales.push_back(n.get_attr<float>("b_scale", 1.0f));
     if (b_scales.size() != 1 && static_cast<int64_t>(b_scales.size()) != N)
         fail_node(n, "QuantizedMatMul: b_scales needs 1 or N = " + std::to_string(N) + " values");
-    temporary = false;
     pfrt_qweight* w = nullptr;
     if (Binit) {
         // Prepared once per (initializer, scales, zero point).
@@ -234,6 +242,7 @@ pfrt_qweight* CudaBackend::Impl::ensure_qweight(const Graph& g, const Node& n, i
                                       b_scales.data(), static_cast<int64_t>(b_scales.size()), &w), &n);
             it = qweights_.emplace(key.str(), w).first;
         }
+        qnode_[&n] = it->second;
         return it->second;
     }
     // A runtime weight: prepared for this run only (from a host copy).

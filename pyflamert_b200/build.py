@@ -215,6 +215,28 @@ def build_pfm_test() -> str | None:
     return exe
 
 
+def build_batcher_test() -> str | None:
+    """tests/native/test_batcher: cuda::DynamicBatcher against each request run
+    alone, on the reference's CPUExecutor (CPU) and on CudaBackend (GPU).
+    Test infrastructure."""
+    inc = reference_include()
+    ref_lib = os.path.join(ROOT, "oracle", "_ref", "libpfrt_ref.so")
+    src = os.path.join(ROOT, "tests", "native", "test_batcher.cpp")
+    if inc is None or not os.path.exists(ref_lib) or not os.path.exists(src):
+        return None
+    out_dir = os.path.join(ROOT, "tests", "native", "_build")
+    os.makedirs(out_dir, exist_ok=True)
+    exe = os.path.join(out_dir, "test_batcher")
+    deps = [src, ref_lib, os.path.join(LIB, "libpfrt_cuda_backend.so")]
+    if _stale(exe, deps):
+        cxx = os.environ.get("CXX", "g++")
+        _run([cxx, "-std=c++17", "-O2", "-w", f"-I{inc}", f"-I{os.path.join(os.path.dirname(inc), 'src')}",
+              f"-I{INCLUDE}", f"-I{os.path.join(PKG, 'backend')}", "-o", exe, src,
+              f"-L{LIB}", "-lpfrt_cuda_backend", "-lpfrt_cuda", f"-L{os.path.dirname(ref_lib)}", "-lpfrt_ref",
+              "-Wl,-rpath,$ORIGIN/../../../pyflamert_b200/lib:$ORIGIN/../../../oracle/_ref", "-lpthread"])
+    return exe
+
+
 def build_all(verbose: bool = False) -> None:
     build_cuda(verbose=verbose)
     build_backend()
@@ -222,6 +244,7 @@ def build_all(verbose: bool = False) -> None:
     build_native_tests()
     build_session_test()
     build_pfm_test()
+    build_batcher_test()
 
 
 if __name__ == "__main__":
