@@ -207,6 +207,18 @@ PFRT_API pfrt_status pfrt_spmm_csr_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int6
 PFRT_API pfrt_status pfrt_csr_from_magnitude_pruning(pfrt_ctx* ctx, int64_t N, int64_t K, const float* w_dev,
                                                      float sparsity, float* mask_dev, pfrt_csr** out);
 
+/* Replaces pruning::NMSparsityPruning(n, m).compute_mask (src/pruning/
+ * nm_sparsity.cpp:45-126) followed by to_sparse(W * mask) (sparse_tensor.cpp:
+ * 560-587) for a device weight W [N, K]: in every m consecutive weights of W
+ * in row-major order (a group may span rows; the last may be shorter) the n
+ * largest |w| are kept, equal ones chosen as the reference's
+ * std::partial_sort (libstdc++) chooses them.  mask_dev (nullable, N*K
+ * floats) receives the 0/1 mask.  Errors as the reference's constructor:
+ * n > m "N must be <= M in N:M sparsity", n or m 0 "N and M must be > 0";
+ * m above 32 is PFRT_ERR_UNSUPPORTED. */
+PFRT_API pfrt_status pfrt_csr_from_nm_pruning(pfrt_ctx* ctx, int64_t N, int64_t K, const float* w_dev, int32_t n,
+                                              int32_t m, float* mask_dev, pfrt_csr** out);
+
 /* ------------------------------------------------------------ peer memory
  * No counterpart in the reference: it has no communication backend (its
  * partitioner, src/partition/graph_partitioner.cpp:111-200, only plans

@@ -268,3 +268,71 @@ void oracle_masked_csr(int64_t rows, int64_t cols, const float* w, const float* 
         indptr[r + 1] = (int32_t)nz;
     }
 }
+
+
+/* ------------------------------------------------------------ N:M pruning
+ * std::partial_sort(first, middle, last, comp) of libstdc++ (GCC 13) keeps in
+ * [first, middle) the set its heap selection leaves there: a binary heap over
+ * [first, middle) whose top is the element no other precedes under comp,
+ * built bottom-up; then each later element that precedes the top under comp
+ * replaces it (pop into the hole at the top).  Each sift moves the hole from
+ * the given position to a leaf along the preferred child (the right child
+ * unless it precedes the left one under comp), then sifts the new value up
+ * from that leaf.  The order of these moves decides which of equal elements
+ * stay, so it is restated exactly.  comp(a, b) = |w[a]| > |w[b]| (float
+ * compare: any NaN compares false). */
+static int nm_gt(const float* w, int a, int b) { return fabsf(w[a]) > fabsf(w[b]); }
+
+static void nm_sift(const float* w, int* h, int hole, int len, int v) {
+    const int top = hole;
+    int child = hole;
+    while (child < (len - 1) / 2) {
+        child = 2 * (child + 1);
+        if (nm_gt(w, h[child], h[child - 1])) child--;
+        h[hole] = h[child];
+        hole = child;
+    }
+    if ((len & 1) == 0 && child == (len - 2) / 2) {
+        child = 2 * (child + 1);
+        h[hole] = h[child - 1];
+        hole = child - 1;
+    }
+    int parent = (hole - 1) / 2;
+    while (hole > top && nm_gt(w, h[parent], v)) {
+        h[hole] = h[parent];
+        hole = parent;
+        parent = (hole - 1) / 2;
+    }
+    h[hole] = v;
+}
+
+/* Marks in keep[0..g) the k elements of w[0..g) that partial_sort leaves in
+ * its first k positions. */
+static void nm_select(const float* w, int g, int k, float* keep) {
+    int h[64];
+    for (int j = 0; j < k; ++j) h[j] = j;
+    if (k >= 2)
+        for (int parent = (k - 2) / 2;; --parent) {
+            nm_sift(w, h, parent, k, h[parent]);
+            if (parent == 0) break;
+        }
+    for (int j = k; j < g; ++j)
+        if (nm_gt(w, j, h[0])) nm_sift(w, h, 0, k, j);
+    for (int j = 0; j < g; ++j) keep[j] = 0.0f;
+    for (int j = 0; j < k; ++j) keep[h[j]] = 1.0f;
+}
+
+int oracle_nm_mask(int64_t total, const float* w, int n, int m, float* mask) {
+    if (n <= 0 || m <= 0 || n > m || m > 64) return -1;
+    for (int64_t i = 0; i < total; i += m) {
+        const int g = (int)((total - i) < m ? (total - i) : m);
+        int k = n;
+        if (g < m) {
+            /* nm_sparsity.cpp:88-90: ceil of a float quotient, capped at g */
+            k = (int)ceilf((float)((size_t)g * (size_t)n) / (float)m);
+            if (k > g) k = g;
+        }
+        nm_select(w + i, g, k, mask + i);
+    }
+    return 0;
+}

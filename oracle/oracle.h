@@ -107,6 +107,15 @@ void oracle_gemm_f64(int64_t M, int64_t N, int64_t K, int trans_a, int trans_b,
  * Weights must not be NaN (the reference's sort is then undefined). */
 int oracle_magnitude_mask(int64_t n, const float* w, float sparsity, float* mask);
 
+/* pruning::NMSparsityPruning(n, m).compute_mask (src/pruning/nm_sparsity.cpp:
+ * 45-126) on `total` weights in flat order: every m consecutive weights keep
+ * the n with the largest |w|; a last group of g < m weights keeps
+ * min(ceil((float)(g*n) / m), g).  Which of equal |w| are kept follows the
+ * reference's std::partial_sort as libstdc++ (GCC 13) implements it: a heap
+ * selection keyed by |w[a]| > |w[b]| (oracle.c restates it step for step).
+ * Returns 0, or -1 for n == 0, m == 0 or n > m (the constructor's errors). */
+int oracle_nm_mask(int64_t total, const float* w, int n, int m, float* mask);
+
 /* pruning::to_sparse(D, threshold, CSR) (src/pruning/sparse_tensor.cpp:
  * 560-587) on D = W * mask (elementwise, fp32), threshold 0: row r keeps the
  * columns with |D[r][c]| > 0, in column order.  indptr [rows+1]; indices and

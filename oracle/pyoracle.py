@@ -51,6 +51,7 @@ def lib():
         L.oracle_spmm_linear_f64.argtypes = [_i64, _i64, _i64, _p, _p, _p, _p, _p]
         L.oracle_gemm_f64.argtypes = [_i64, _i64, _i64, _int, _int, _f64, _f64, _p, _p, _p, _i64, _p]
         L.oracle_magnitude_mask.argtypes = [_i64, _p, _f32, _p]
+        L.oracle_nm_mask.argtypes = [_i64, _p, _int, _int, _p]
         L.oracle_masked_csr.argtypes = [_i64, _i64, _p, _p, _p, _p, _p]
         _lib = L
     return _lib
@@ -77,6 +78,7 @@ def ref():
         L.pfref_quantize.argtypes = [_i64, _p, _f32, _i32, _int, _p]
         L.pfref_sparse_matmul.argtypes = [_i64, _i64, _i64, _p, _p, _p, _i64, _p, _p, _int]
         L.pfref_magnitude_mask.argtypes = [_i64, _i64, _p, _f32, _p]
+        L.pfref_nm_mask.argtypes = [_i64, _p, _i64, _i64, _p]
         L.pfref_to_sparse_csr.argtypes = [_i64, _i64, _p, _f32, _i64, _p, _p, _p, _p]
         _ref = L
     return _ref
@@ -309,6 +311,22 @@ def ref_magnitude_mask(w, sparsity):
     rows, cols = (w.shape if w.ndim == 2 else (1, w.size))
     mask = np.empty(w.shape, np.float32)
     _check_ref(ref().pfref_magnitude_mask(rows, cols, _ptr(w), float(sparsity), _ptr(mask)))
+    return mask
+
+
+def nm_mask(w, n, m):
+    """Restated NMSparsityPruning(n, m).compute_mask on W (flat order): 0/1 float mask."""
+    w = _c(w, np.float32)
+    mask = np.empty(w.shape, np.float32)
+    if lib().oracle_nm_mask(w.size, _ptr(w), int(n), int(m), _ptr(mask)) != 0:
+        raise ValueError("N:M pruning needs 0 < n <= m <= 64")
+    return mask
+
+
+def ref_nm_mask(w, n, m):
+    w = _c(w, np.float32)
+    mask = np.empty(w.shape, np.float32)
+    _check_ref(ref().pfref_nm_mask(w.size, _ptr(w), int(n), int(m), _ptr(mask)))
     return mask
 
 

@@ -304,6 +304,16 @@ int pfref_magnitude_mask(int64_t rows, int64_t cols, const float* w, float spars
     });
 }
 
+// pruning::NMSparsityPruning(n, m).compute_mask (src/pruning/nm_sparsity.cpp:
+// 45-126) on `total` weights taken in flat order: mask_out [total] of 0/1.
+int pfref_nm_mask(int64_t total, const float* w, int64_t n, int64_t m, float* mask_out) {
+    return guarded([&] {
+        pruning::NMSparsityPruning nm(static_cast<size_t>(n), static_cast<size_t>(m));
+        auto mk = nm.compute_mask("w", view(w, {total}, DType::Float32), 0.0f);
+        if (total > 0) std::memcpy(mask_out, mk.mask.data(), sizeof(float) * total);
+    });
+}
+
 // pruning::to_sparse(dense, threshold, CSR) (src/pruning/sparse_tensor.cpp:
 // 560-587) on D [rows, cols]; writes indptr [rows+1], and indices/values up
 // to `cap` entries, and *nnz_out.

@@ -253,6 +253,24 @@ class CSR:
         self.nnz = int(nnz.value)
         return self
 
+    @classmethod
+    def from_nm_pruning(cls, ctx: Context, w, n: int = 2, m: int = 4, mask=None):
+        """N:M-prune the device weight W [N, K] (a CUDA fp32 tensor) as
+        NMSparsityPruning(n, m).compute_mask does (groups of m consecutive
+        weights in row-major order keep their n largest |w|) and keep the
+        result as a CSR weight (pfrt_csr_from_nm_pruning).  `mask` (optional,
+        a CUDA fp32 tensor of W's size) receives the 0/1 mask."""
+        N, K = int(w.shape[0]), int(w.shape[1])
+        self = cls.__new__(cls)
+        self.ctx, self.N, self.K = ctx, N, K
+        self._h = C.c_void_p()
+        _check(lib().pfrt_csr_from_nm_pruning(ctx.handle, N, K, _dptr(w), int(n), int(m), _dptr(mask),
+                                              C.byref(self._h)), "pfrt_csr_from_nm_pruning")
+        nnz = C.c_int64()
+        _check(lib().pfrt_csr_info(self._h, None, None, C.byref(nnz)), "pfrt_csr_info")
+        self.nnz = int(nnz.value)
+        return self
+
     def __call__(self, x, y=None, stream=None):
         import torch
         M = x.shape[0]

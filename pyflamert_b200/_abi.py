@@ -62,6 +62,7 @@ PROTOTYPES = {
     "pfrt_spmm": [_P, _P, _I64, _P, _I64, _P, _I64, _P],
     "pfrt_spmm_csr_f32": [_P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P, _I64, _P],
     "pfrt_csr_from_magnitude_pruning": [_P, _I64, _I64, _P, _F32, _P, _P],
+    "pfrt_csr_from_nm_pruning": [_P, _I64, _I64, _P, _I32, _I32, _P, _P],
     "pfrt_ipc_get_handle": [_P, _P, _P],
     "pfrt_ipc_open": [_P, _P, _P],
     "pfrt_ipc_close": [_P, _P],

@@ -96,6 +96,64 @@ Tensor to_tensor_f32(const std::vector<float>& v) {
 
 }  // namespace
 
+// The heap selection of libstdc++'s std::partial_sort over one group: a
+// binary heap over the first k slots, top = the element no other precedes
+// under |w[a]| > |w[b]|, built bottom-up; each later element that precedes the
+// top replaces it.  A sift moves the hole to a leaf along the preferred child
+// (the right one unless it precedes the left), then sifts the value up.  The
+// order of these moves decides which of equal |w| stay.
+namespace {
+void nm_sift(const float* a, int* h, int hole, int len, int v) {
+    const int top = hole;
+    int child = hole;
+    while (child < (len - 1) / 2) {
+        child = 2 * (child + 1);
+        if (a[h[child]] > a[h[child - 1]]) child--;
+        h[hole] = h[child];
+        hole = child;
+    }
+    if ((len & 1) == 0 && child == (len - 2) / 2) {
+        child = 2 * (child + 1);
+        h[hole] = h[child - 1];
+        hole = child - 1;
+    }
+    int parent = (hole - 1) / 2;
+    while (hole > top && a[h[parent]] > a[v]) {
+        h[hole] = h[parent];
+        hole = parent;
+        parent = (hole - 1) / 2;
+    }
+    h[hole] = v;
+}
+}  // namespace
+
+std::vector<float> nm_mask(const float* w, int64_t total, int n, int m) {
+    if (n > m) throw std::invalid_argument("N must be <= M in N:M sparsity");
+    if (n <= 0 || m <= 0) throw std::invalid_argument("N and M must be > 0");
+    if (m > 64) throw std::invalid_argument("N:M pruning: M above 64");
+    std::vector<float> mask(static_cast<size_t>(total), 0.0f);
+    float a[64];
+    int h[64];
+    for (int64_t i = 0; i < total; i += m) {
+        const int g = static_cast<int>(std::min<int64_t>(m, total - i));
+        int k = n;
+        if (g < m)
+            k = std::min(g, static_cast<int>(std::ceil(static_cast<float>(static_cast<size_t>(g) * n) /
+                                                       static_cast<float>(m))));
+        for (int j = 0; j < g; ++j) a[j] = std::fabs(w[i + j]);
+        for (int j = 0; j < k; ++j) h[j] = j;
+        if (k >= 2)
+            for (int parent = (k - 2) / 2;; --parent) {
+                nm_sift(a, h, parent, k, h[parent]);
+                if (parent == 0) break;
+            }
+        for (int j = k; j < g; ++j)
+            if (a[j] > a[h[0]]) nm_sift(a, h, 0, k, j);
+        for (int j = 0; j < k; ++j) mask[static_cast<size_t>(i + h[j])] = 1.0f;
+    }
+    return mask;
+}
+
 Graph sparsify_matmuls(const Graph& g, const SparsifyOptions& opt, SparsifyReport* report) {
     SparsifyReport rep;
     Graph out(g.name());
@@ -129,7 +187,8 @@ Graph sparsify_matmuls(const Graph& g, const SparsifyOptions& opt, SparsifyRepor
         const int64_t N = trans ? B->shape()[0] : B->shape()[1];
         const int64_t total = K * N;
         std::vector<float> mask;
-        if (opt.prune_sparsity > 0.0f) mask = magnitude_mask(B->data_ptr<float>(), total, opt.prune_sparsity);
+        if (opt.nm_n > 0) mask = nm_mask(B->data_ptr<float>(), total, opt.nm_n, opt.nm_m);
+        else if (opt.prune_sparsity > 0.0f) mask = magnitude_mask(B->data_ptr<float>(), total, opt.prune_sparsity);
         Csr csr = build_csr(B->data_ptr<float>(), mask.empty() ? nullptr : mask.data(), N, K, trans);
         const double zero_frac = total > 0 ? 1.0 - static_cast<double>(csr.values.size()) / static_cast<double>(total) : 0.0;
         if (zero_frac < opt.min_zero_fraction) {

@@ -16,7 +16,9 @@
 //                              with C an [N] initializer (kept as an Add)
 // and at least min_zero_fraction of the (pruned) weight is zero.  With
 // prune_sparsity > 0 each such weight is first masked by compute_mask's
-// criterion over its own element order.  The graph is returned as a new
+// criterion over its own element order; with nm_n > 0 instead, by
+// NMSparsityPruning(nm_n, nm_m)'s (src/pruning/nm_sparsity.cpp:45-126), also
+// over the weight's storage order.  The graph is returned as a new
 // Graph; initializers no longer used by any node are dropped.
 #pragma once
 
@@ -31,6 +33,8 @@ namespace cuda {
 struct SparsifyOptions {
     float prune_sparsity = 0.0f;
     float min_zero_fraction = 0.5f;
+    int nm_n = 0;  // > 0: N:M pruning (keep nm_n of every nm_m) instead of magnitude
+    int nm_m = 4;
 };
 
 struct SparsifyReport {
@@ -48,6 +52,14 @@ Graph sparsify_matmuls(const Graph& graph, const SparsifyOptions& options = {}, 
 // prunes all; n == 0 with 0 < s < 1 throws std::runtime_error, as the
 // reference does.
 std::vector<float> magnitude_mask(const float* w, int64_t n, float sparsity);
+
+// NMSparsityPruning(n, m)::compute_mask on `total` weights in storage order
+// (1 keeps): every m consecutive weights keep the n largest |w|; a last group
+// of g < m keeps min(ceil((float)(g*n) / m), g).  Equal |w| are chosen as the
+// reference's std::partial_sort (libstdc++, a heap selection) chooses them.
+// Throws std::invalid_argument for n > m or n, m == 0, as the reference's
+// constructor; m above 64 is rejected too.
+std::vector<float> nm_mask(const float* w, int64_t total, int n, int m);
 
 }  // namespace cuda
 }  // namespace pyflame_rt

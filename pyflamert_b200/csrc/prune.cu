@@ -115,6 +115,102 @@ __global__ void prune_compact_kernel(const float* __restrict__ w, int64_t N, int
     }
 }
 
+// ------------------------------------------------------------ N:M pruning
+// pruning::NMSparsityPruning::compute_mask (src/pruning/nm_sparsity.cpp:45-126):
+// each group of m consecutive weights in flat order keeps its n largest |w|
+// (a last group of g < m keeps min(ceil((float)(g*n) / m), g)).  Which of
+// equal |w| stay is decided by the reference's std::partial_sort; libstdc++
+// (GCC 13) implements it as a heap selection, restated here move for move:
+// a binary heap over the first k slots, top = the element no other precedes
+// under gt(a, b) = |w[a]| > |w[b]|, built bottom-up; each later element that
+// precedes the top replaces it.  A sift moves the hole to a leaf along the
+// preferred child (the right one unless it precedes the left), then sifts the
+// value up from there.
+constexpr int kNmMax = 32;
+
+__device__ __forceinline__ void nm_sift(const float* a, int* h, int hole, int len, int v) {
+    const int top = hole;
+    int child = hole;
+    while (child < (len - 1) / 2) {
+        child = 2 * (child + 1);
+        if (a[h[child]] > a[h[child - 1]]) child--;
+        h[hole] = h[child];
+        hole = child;
+    }
+    if ((len & 1) == 0 && child == (len - 2) / 2) {
+        child = 2 * (child + 1);
+        h[hole] = h[child - 1];
+        hole = child - 1;
+    }
+    int parent = (hole - 1) / 2;
+    while (hole > top && a[h[parent]] > a[v]) {
+        h[hole] = h[parent];
+        hole = parent;
+        parent = (hole - 1) / 2;
+    }
+    h[hole] = v;
+}
+
+// One thread per group: mask[i] = 1 for the kept weights of the group, else 0.
+__global__ void nm_mask_kernel(const float* __restrict__ w, int64_t total, int n, int m, float* __restrict__ mask) {
+    const int64_t grp = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t i0 = grp * m;
+    if (i0 >= total) return;
+    const int g = static_cast<int>(min(static_cast<int64_t>(m), total - i0));
+    int k = n;
+    if (g < m) k = min(g, static_cast<int>(ceilf(__fdiv_rn(static_cast<float>(static_cast<uint64_t>(g) * n),
+                                                        static_cast<float>(m)))));
+    float a[kNmMax];
+    int h[kNmMax];
+    for (int j = 0; j < g; ++j) a[j] = fabsf(w[i0 + j]);
+    for (int j = 0; j < k; ++j) h[j] = j;
+    if (k >= 2)
+        for (int parent = (k - 2) / 2;; --parent) {
+            nm_sift(a, h, parent, k, h[parent]);
+            if (parent == 0) break;
+        }
+    for (int j = k; j < g; ++j)
+        if (a[j] > a[h[0]]) nm_sift(a, h, 0, k, j);
+    uint32_t kept = 0;
+    for (int j = 0; j < k; ++j) kept |= 1u << h[j];
+    for (int j = 0; j < g; ++j) mask[i0 + j] = ((kept >> j) & 1u) ? 1.0f : 0.0f;
+}
+
+// Per row: the entries to_sparse keeps of W * mask (|w| > 0 where kept).  Warp per row.
+__global__ void masked_rowcount_kernel(const float* __restrict__ w, const float* __restrict__ mask, int64_t N,
+                                       int64_t K, int32_t* __restrict__ cnt) {
+    const int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= N) return;
+    int c = 0;
+    for (int64_t j = lane; j < K; j += 32) c += (mask[r * K + j] != 0.0f && fabsf(w[r * K + j]) > 0.0f);
+    for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    if (lane == 0) cnt[r] = c;
+}
+
+// Those entries, row by row in column order.  Warp per row.
+__global__ void masked_compact_kernel(const float* __restrict__ w, const float* __restrict__ mask, int64_t N,
+                                      int64_t K, const int32_t* __restrict__ indptr, int32_t* __restrict__ indices,
+                                      float* __restrict__ values) {
+    const int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= N) return;
+    const uint32_t lt = (1u << lane) - 1u;
+    int64_t out = indptr[r];
+    for (int64_t c0 = 0; c0 < K; c0 += 32) {
+        const int64_t c = c0 + lane;
+        const float v = c < K ? w[r * K + c] : 0.0f;
+        const bool keep = c < K && mask[r * K + c] != 0.0f && fabsf(v) > 0.0f;
+        const uint32_t b = __ballot_sync(0xffffffffu, keep);
+        if (keep) {
+            const int64_t at = out + __popc(b & lt);
+            indices[at] = static_cast<int32_t>(c);
+            values[at] = v;
+        }
+        out += __popc(b);
+    }
+}
+
 }  // namespace
 }  // namespace pfrt
 
@@ -252,6 +348,83 @@ pfrt_status pfrt_csr_from_magnitude_pruning(pfrt_ctx* ctx, int64_t N, int64_t K,
     }
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cleanup(cuda_fail(e, "magnitude pruning"));
+    cleanup(PFRT_OK);
+    return pfrt_csr_create(ctx, N, K, nnz, hip.data(), hix.data(), 32, hv.data(), out);
+}
+
+pfrt_status pfrt_csr_from_nm_pruning(pfrt_ctx* ctx, int64_t N, int64_t K, const float* w_dev, int32_t n, int32_t m,
+                                     float* mask_dev, pfrt_csr** out) {
+    pfrt_status st = enter(ctx);
+    if (st) return st;
+    if (!out || (N * K > 0 && !w_dev)) return fail(PFRT_ERR_INVALID_ARGUMENT, "N:M pruning: null argument");
+    if (N < 0 || K < 0 || N > INT32_MAX || K > INT32_MAX)
+        return fail(PFRT_ERR_INVALID_ARGUMENT, "N:M pruning: bad shape");
+    *out = nullptr;
+    // nm_sparsity.cpp:9-18 (the constructor's checks, in its order)
+    if (n > m) return fail(PFRT_ERR_INVALID_ARGUMENT, "N must be <= M in N:M sparsity");
+    if (n <= 0 || m <= 0) return fail(PFRT_ERR_INVALID_ARGUMENT, "N and M must be > 0");
+    if (m > kNmMax) return fail(PFRT_ERR_UNSUPPORTED, "N:M pruning: M above 32");
+    const int64_t total = N * K;
+    cudaStream_t s = ctx->stream;
+    float* mask = mask_dev;
+    int32_t *cnt = nullptr, *indptr = nullptr, *indices = nullptr;
+    float* values = nullptr;
+    float* own_mask = nullptr;
+    auto cleanup = [&](pfrt_status r) {
+        if (own_mask) cudaFree(own_mask);
+        if (cnt) cudaFree(cnt);
+        if (indptr) cudaFree(indptr);
+        if (indices) cudaFree(indices);
+        if (values) cudaFree(values);
+        return r;
+    };
+    cudaError_t e = cudaSuccess;
+    if (!mask && total > 0) {
+        e = cudaMalloc(&own_mask, sizeof(float) * total);
+        mask = own_mask;
+    }
+    if (e == cudaSuccess) e = cudaMalloc(&cnt, sizeof(int32_t) * std::max<int64_t>(N, 1));
+    if (e == cudaSuccess) e = cudaMalloc(&indptr, sizeof(int32_t) * (N + 1));
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "N:M pruning scratch"));
+    std::vector<int32_t> hc(static_cast<size_t>(N));
+    if (total > 0) {
+        const int64_t groups = ceil_div(total, static_cast<int64_t>(m));
+        nm_mask_kernel<<<static_cast<unsigned>(ceil_div(groups, 128)), 128, 0, s>>>(w_dev, total, n, m, mask);
+        e = cudaGetLastError();
+        const unsigned rb = static_cast<unsigned>(std::max<int64_t>(1, ceil_div(N * 32, 256)));
+        if (e == cudaSuccess) {
+            masked_rowcount_kernel<<<rb, 256, 0, s>>>(w_dev, mask, N, K, cnt);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaMemcpyAsync(hc.data(), cnt, sizeof(int32_t) * N, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return cleanup(cuda_fail(e, "nm_mask_kernel"));
+    }
+    std::vector<int32_t> hip(static_cast<size_t>(N + 1));
+    int64_t nnz = 0;
+    hip[0] = 0;
+    for (int64_t r = 0; r < N; ++r) {
+        nnz += hc[r];
+        if (nnz > INT32_MAX) return cleanup(fail(PFRT_ERR_UNSUPPORTED, "N:M pruning: more than 2^31 nonzeros"));
+        hip[r + 1] = static_cast<int32_t>(nnz);
+    }
+    std::vector<int32_t> hix(static_cast<size_t>(std::max<int64_t>(nnz, 1)));
+    std::vector<float> hv(static_cast<size_t>(std::max<int64_t>(nnz, 1)));
+    if (nnz > 0) {
+        e = cudaMalloc(&indices, sizeof(int32_t) * nnz);
+        if (e == cudaSuccess) e = cudaMalloc(&values, sizeof(float) * nnz);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(indptr, hip.data(), sizeof(int32_t) * (N + 1), cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) {
+            const unsigned rb = static_cast<unsigned>(std::max<int64_t>(1, ceil_div(N * 32, 256)));
+            masked_compact_kernel<<<rb, 256, 0, s>>>(w_dev, mask, N, K, indptr, indices, values);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaMemcpyAsync(hix.data(), indices, sizeof(int32_t) * nnz, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(hv.data(), values, sizeof(float) * nnz, cudaMemcpyDeviceToHost, s);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "N:M pruning"));
     cleanup(PFRT_OK);
     return pfrt_csr_create(ctx, N, K, nnz, hip.data(), hix.data(), 32, hv.data(), out);
 }

@@ -23,6 +23,7 @@
 #include "oracle.h"
 #include "pyflame_rt/errors.hpp"
 #include "pyflame_rt/graph.hpp"
+#include "pyflame_rt/pruning/pruning.hpp"
 #include "sparsify.hpp"
 #include "quantize_pass.hpp"
 #include "pyflame_rt/quantization/quant_ops.hpp"
@@ -378,6 +379,73 @@ int main() {
                        "mask differs (kind " + std::to_string(kind) + ", s " + std::to_string(s) + ")");
             }
         }
+    });
+
+    run_test("NMMaskMatchesReference", [&] {
+        // The pass's N:M criterion against the reference's own
+        // NMSparsityPruning::compute_mask (src/pruning/nm_sparsity.cpp), ties and NaN included.
+        std::mt19937_64 rng(77);
+        const float tie_vals[] = {0.0f, -0.0f, 1.0f, -1.0f, 2.0f, -2.0f, 0.5f};
+        for (auto nm : std::vector<std::pair<int, int>>{{2, 4}, {1, 2}, {3, 4}, {4, 8}, {5, 16}, {16, 32}}) {
+            for (int kind = 0; kind < 3; ++kind) {
+                const int64_t total = 1000 + nm.second / 2;  // a short last group
+                Tensor w({total}, DType::Float32);
+                std::normal_distribution<float> nd(0.0f, 1.0f);
+                for (int64_t i = 0; i < total; ++i) {
+                    float v = kind == 0 ? tie_vals[rng() % 7] : nd(rng);
+                    if (kind == 2 && rng() % 5 == 0) v = std::nanf("");
+                    w.data_ptr<float>()[i] = v;
+                }
+                auto mine = cuda::nm_mask(w.data_ptr<float>(), total, nm.first, nm.second);
+                pruning::NMSparsityPruning ref(static_cast<size_t>(nm.first), static_cast<size_t>(nm.second));
+                auto rm = ref.compute_mask("w", w, 0.0f);
+                EXPECT(std::memcmp(mine.data(), rm.mask.data(), 4 * total) == 0,
+                       "N:M mask differs (" + std::to_string(nm.first) + ":" + std::to_string(nm.second) +
+                           ", kind " + std::to_string(kind) + ")");
+            }
+        }
+        bool threw = false;
+        try {
+            cuda::nm_mask(nullptr, 0, 5, 4);
+        } catch (const std::invalid_argument& e) {
+            threw = std::string(e.what()) == "N must be <= M in N:M sparsity";
+        }
+        EXPECT(threw, "n > m must throw the reference's message");
+    });
+
+    run_test("SparsifyNMPrunedMatMul", [&] {
+        // 2:4 pruning of a MatMul weight [K, N] in its storage order, then SparseMatMul on
+        // the GPU, against CPUExecutor on the original graph with the reference-masked weight.
+        const int64_t M = 32, K = 512, N = 384;
+        Graph g("nm");
+        g.add_input(TensorInfo("X", sh({M, K}), DType::Float32));
+        g.add_initializer("B", randn({K, N}, 0.05f, 60));
+        g.add_node(node("mm", "MatMul", {"X", "B"}, {"Y"}));
+        g.add_output(TensorInfo("Y", sh({M, N}), DType::Float32));
+        cuda::SparsifyOptions opt;
+        opt.nm_n = 2;
+        opt.nm_m = 4;
+        cuda::SparsifyReport rep;
+        Graph sg = cuda::sparsify_matmuls(g, opt, &rep);
+        EXPECT(rep.rewritten == 1, "one node rewritten, got " + std::to_string(rep.rewritten));
+        const Tensor& B = g.get_initializer("B")->get();
+        pruning::NMSparsityPruning ref(2, 4);
+        auto rm = ref.compute_mask("B", B, 0.0f);
+        Graph pg("nm_masked");
+        pg.add_input(TensorInfo("X", sh({M, K}), DType::Float32));
+        Tensor pb({K, N}, DType::Float32);
+        for (int64_t i = 0; i < K * N; ++i) pb.data_ptr<float>()[i] = B.data_ptr<float>()[i] * rm.mask.data_ptr<float>()[i];
+        pg.add_initializer("B", pb);
+        pg.add_node(node("mm", "MatMul", {"X", "B"}, {"Y"}));
+        pg.add_output(TensorInfo("Y", sh({M, N}), DType::Float32));
+        std::unordered_map<std::string, Tensor> feeds;
+        feeds["X"] = randn({M, K}, 1.0f, 61);
+        CPUExecutor cpu(0);
+        auto r = cpu.execute(pg, feeds, {"Y"});
+        CudaBackend gpu(0);
+        auto y = gpu.execute(sg, feeds, {"Y"});
+        const double e = normwise(y[0], r[0]);
+        EXPECT(e <= 1e-5, "normwise error " + std::to_string(e));
     });
 
     run_test("SparsifyPrunedMatMulAndGemm", [&] {

@@ -88,3 +88,34 @@ def test_rejects_nan_and_empty(ctx):
     with pytest.raises(pf.PfrtError, match="empty"):
         pf.CSR.from_magnitude_pruning(ctx, torch.zeros((0, 4), device="cuda"), 0.5)
     ctx.check()
+
+
+@pytest.mark.parametrize("kind", ["normal", "ties", "zeros", "equal"])
+@pytest.mark.parametrize("n,m", [(2, 4), (1, 2), (3, 4), (4, 8), (5, 16), (16, 32), (4, 4)])
+@pytest.mark.parametrize("shape", [(64, 96), (37, 53)])
+def test_nm_mask_and_csr_match_reference(ctx, kind, n, m, shape):
+    """N:M pruning on the GPU (pfrt_csr_from_nm_pruning) vs the reference's
+    NMSparsityPruning::compute_mask (nm_sparsity.cpp:45-126) through the
+    oracle's restatement: identical mask (groups span rows at K = 53, and the
+    last group is short), identical CSR of W * mask."""
+    w = weights(kind, shape, hash((kind, n, m, shape)) % 2**32)
+    wd = torch.from_numpy(w).cuda()
+    mask = torch.full(w.shape, 7.0, dtype=torch.float32, device="cuda")
+    csr = pf.CSR.from_nm_pruning(ctx, wd, n, m, mask=mask)
+    ctx.check()
+    ref_mask = po.nm_mask(w, n, m)
+    np.testing.assert_array_equal(mask.cpu().numpy(), ref_mask)
+    ip, ix, v = po.masked_csr(w, ref_mask)
+    assert csr.nnz == ip[-1]
+    np.testing.assert_array_equal(dense_of(ctx, csr), w * ref_mask)
+
+
+def test_nm_rejects_bad_n_m(ctx):
+    wd = torch.ones((4, 8), device="cuda")
+    with pytest.raises(pf.PfrtError, match="N must be <= M"):
+        pf.CSR.from_nm_pruning(ctx, wd, 5, 4)
+    with pytest.raises(pf.PfrtError, match="N and M must be > 0"):
+        pf.CSR.from_nm_pruning(ctx, wd, 0, 4)
+    with pytest.raises(pf.PfrtError, match="above 32"):
+        pf.CSR.from_nm_pruning(ctx, wd, 2, 64)
+    ctx.check()

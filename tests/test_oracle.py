@@ -173,3 +173,23 @@ def test_magnitude_mask_empty_weight_raises():
         po.magnitude_mask(np.zeros((0, 4), np.float32), 0.5)
     with pytest.raises(RuntimeError, match="empty"):
         po.ref_magnitude_mask(np.zeros((1, 0), np.float32), 0.5)
+
+
+@pytest.mark.parametrize("n,m", [(1, 2), (2, 4), (3, 4), (2, 8), (4, 8), (5, 16), (16, 32), (3, 3)])
+@pytest.mark.parametrize("kind", ["ties", "normal", "nan", "zeros"])
+def test_nm_mask_matches_reference(n, m, kind):
+    """The restated N:M selection (ties resolved as libstdc++'s heap-based
+    std::partial_sort resolves them) equals NMSparsityPruning::compute_mask
+    compiled from src/pruning/nm_sparsity.cpp, including a short last group."""
+    rng = np.random.default_rng(n * 100 + m)
+    for total in (m * 7, m * 7 + 1, m * 5 - 1, 1):
+        if kind == "ties":
+            w = rng.choice(np.array([0.0, -0.0, 1.0, -1.0, 2.0, -2.0, 0.5], np.float32), total)
+        elif kind == "nan":
+            w = rng.standard_normal(total).astype(np.float32)
+            w[rng.random(total) < 0.2] = np.nan
+        elif kind == "zeros":
+            w = np.where(rng.random(total) < 0.6, 0.0, rng.standard_normal(total)).astype(np.float32)
+        else:
+            w = rng.standard_normal(total).astype(np.float32)
+        np.testing.assert_array_equal(po.nm_mask(w, n, m), po.ref_nm_mask(w, n, m))
