@@ -109,7 +109,6 @@ __global__ void __launch_bounds__(GemmSkCfg<BN, STAGES>::THREADS, 1)
     using G = typename Cfg::G;
     constexpr int BM = Cfg::BM;
     constexpr int HALF = Cfg::HALF;
-    constexpr int CPT = HALF / 32 / 2;  // 32-column chunks per epilogue thread in each half
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -259,20 +258,14 @@ __global__ void __launch_bounds__(GemmSkCfg<BN, STAGES>::THREADS, 1)
             // warp's 16-byte stores (and the peer's loads) cover 512
             // consecutive bytes.  Kept in L2 (.cg).
             uint4* out = xchg + static_cast<int64_t>(2 * unit + static_cast<int>(rank)) * Cfg::XGRAN;
-            {
-                // This thread's chunks (grp, grp + 2, ...) loaded together: one TMEM round trip.
-                uint32_t v[CPT][32];
-#pragma unroll
-                for (int i = 0; i < CPT; ++i)
-                    tmem_ld_32x32b_x32(tmem_base + lane_off + static_cast<uint32_t>(peer * HALF + (grp + 2 * i) * 32),
-                                       v[i]);
+#pragma unroll 1
+            for (int c = grp; c < HALF / 32; c += 2) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem_base + lane_off + static_cast<uint32_t>(peer * HALF + c * 32), v);
                 tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < CPT; ++i)
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        __stcg(out + ((grp + 2 * i) * 8 + j) * BM + rl,
-                               make_uint4(v[i][4 * j], v[i][4 * j + 1], v[i][4 * j + 2], v[i][4 * j + 3]));
+                for (int j = 0; j < 8; ++j)
+                    __stcg(out + (c * 8 + j) * BM + rl, make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
             }
             cluster_ready();
             // Each thread releases its own stores to the peer (cluster scope
@@ -283,28 +276,22 @@ __global__ void __launch_bounds__(GemmSkCfg<BN, STAGES>::THREADS, 1)
         }
         if (!bad) {
             const uint4* in = xchg + static_cast<int64_t>(2 * unit + static_cast<int>(peer)) * Cfg::XGRAN;
-            // Every load of this thread's chunks issued before any is used:
-            // one L2 round trip and one TMEM round trip instead of one per chunk.
-            uint4 p[CPT][8];
+#pragma unroll 1
+            for (int c = grp; c < HALF / 32; c += 2) {
+                uint4 p[8];
 #pragma unroll
-            for (int i = 0; i < CPT; ++i)
-#pragma unroll
-                for (int j = 0; j < 8; ++j) p[i][j] = __ldcg(in + ((grp + 2 * i) * 8 + j) * BM + rl);
-            uint32_t v[CPT][32];
-#pragma unroll
-            for (int i = 0; i < CPT; ++i)
-                tmem_ld_32x32b_x32(tmem_base + lane_off + static_cast<uint32_t>(rank * HALF + (grp + 2 * i) * 32), v[i]);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < CPT; ++i) {
+                for (int j = 0; j < 8; ++j) p[j] = __ldcg(in + (c * 8 + j) * BM + rl);
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem_base + lane_off + static_cast<uint32_t>(rank * HALF + c * 32), v);
+                tmem_ld_wait();
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    v[i][4 * j] += p[i][j].x;
-                    v[i][4 * j + 1] += p[i][j].y;
-                    v[i][4 * j + 2] += p[i][j].z;
-                    v[i][4 * j + 3] += p[i][j].w;
+                    v[4 * j] += p[j].x;
+                    v[4 * j + 1] += p[j].y;
+                    v[4 * j + 2] += p[j].z;
+                    v[4 * j + 3] += p[j].w;
                 }
-                epi.store(params, HALF, row, n_own + (grp + 2 * i) * 32, (grp + 2 * i) * 32, 0, v[i]);
+                epi.store(params, HALF, row, n_own + c * 32, c * 32, 0, v);
             }
         } else if (etid == 0) {
             stop();
