@@ -133,6 +133,31 @@ def dist_init(n_gpus):
     return world, rank, local
 
 
+def bind_gpu_local_cpus(local):
+    """Keeps this process on the CPUs that NVML reports as local to its GPU
+    (a read; only the process's own affinity is set), so pinned host buffers
+    are allocated on the GPU's NUMA node and their copies do not cross the
+    inter-socket link.  Returns the previous CPU set (to restore), or None if
+    nothing was changed (no NVML, or no overlap with the allowed CPUs)."""
+    try:
+        import pynvml
+        import torch
+        p = torch.cuda.get_device_properties(local)
+        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, ((os.cpu_count() or 64) + 63) // 64)
+        cpus = {w * 64 + b for w, word in enumerate(words) for b in range(64) if (word >> b) & 1}
+        before = os.sched_getaffinity(0)
+        near = cpus & before
+        if not near or near == before:
+            return None
+        os.sched_setaffinity(0, near)
+        return before
+    except Exception:
+        return None
+
+
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
@@ -246,12 +271,13 @@ def qlinear_setup(ctx, n_copies):
 
 
 def qlinear_e2e(ctx, q, w, steps, lanes=3):
-    """Public API with host buffers: every step copies its activations from
-    pinned host memory to the device, runs the layer (pfrt_qlinear) and reads
-    its output back to pinned host memory.  Steps alternate over `lanes`
-    independent lanes (each its own context, stream, weight copy and
-    buffers), so one step's device->host read overlaps the next step's
-    host->device copy and kernel, as in a serving loop."""
+    """Through the C ABI's host-buffer entry (pfrt_qlinear_host): every step
+    copies its activations from pinned host memory to the device, runs the
+    layer and copies its output back to pinned host memory, all enqueued by
+    one call.  Steps alternate over `lanes` independent lanes (each its own
+    context, stream, weight copy and pinned buffers), so one step's
+    device->host copy overlaps the next step's host->device copy and kernel,
+    as in a serving loop."""
     import torch
 
     import pyflamert_b200 as pf
@@ -259,20 +285,14 @@ def qlinear_e2e(ctx, q, w, steps, lanes=3):
     L = []
     for i in range(lanes):
         c = ctx if i == 0 else pf.Context(torch.cuda.current_device())
-        wl_ = w if i == 0 else pf.QWeight(c, q.w, q.w_scale)
-        L.append(dict(ctx=c, w=wl_, stream=torch.cuda.Stream(),
+        L.append(dict(ctx=c, w=w if i == 0 else pf.QWeight(c, q.w, q.w_scale), stream=torch.cuda.Stream(),
                       a_host=torch.from_numpy(q.a).pin_memory(),
-                      y_host=torch.empty((M, N), dtype=torch.int8).pin_memory(),
-                      a_dev=torch.empty((M, K), dtype=torch.uint8, device="cuda"),
-                      y_dev=torch.empty((M, N), dtype=torch.int8, device="cuda")))
+                      y_host=torch.empty((M, N), dtype=torch.int8).pin_memory()))
 
     def step(i):
         ln = L[i % lanes]
-        with torch.cuda.stream(ln["stream"]):
-            ln["a_dev"].copy_(ln["a_host"], non_blocking=True)
-            ln["w"](ln["a_dev"], q.a_scale, q.a_zp, out="int8", y_scale=q.y_scale, y=ln["y_dev"],
-                    stream=ln["stream"])
-            ln["y_host"].copy_(ln["y_dev"], non_blocking=True)
+        ln["w"].host_call(ln["a_host"], q.a_scale, q.a_zp, ln["y_host"], out="int8", y_scale=q.y_scale,
+                          stream=ln["stream"])
 
     for i in range(5 * lanes):
         step(i)
@@ -289,10 +309,9 @@ def qlinear_e2e(ctx, q, w, steps, lanes=3):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     # every lane's host buffer holds the layer's output
-    ref_dev = w(L[0]["a_dev"], q.a_scale, q.a_zp, out="int8", y_scale=q.y_scale)
-    torch.cuda.synchronize()
+    ref = w(torch.from_numpy(q.a).cuda(), q.a_scale, q.a_zp, out="int8", y_scale=q.y_scale).cpu()
     for ln in L:
-        assert torch.equal(ref_dev.cpu(), ln["y_host"])
+        assert torch.equal(ref, ln["y_host"])
     for ln in L[1:]:
         ln["ctx"].check()
         ln["w"].close()
@@ -584,6 +603,7 @@ def main():
     import pyflamert_b200 as pf
     world, rank, local = dist_init(args.gpus)
     torch.cuda.set_device(local)
+    cpus_before = bind_gpu_local_cpus(local)
     ctx = pf.Context(local)
     peaks, peak_src = measured_peaks()
     sampler = ClockSampler(local)
@@ -621,8 +641,9 @@ def main():
                                "K split between them)"},
         "e2e": {"value": world * ops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": e2e_ms, "path": "pinned host -> device, pfrt_qlinear, device -> pinned host; "
-                                                "steps alternate over 3 lanes (context, stream, buffers each)"},
+                "ms_per_step": e2e_ms, "path": "pfrt_qlinear_host (C ABI, pinned host buffers: copy in, "
+                                                "layer, copy out per call); steps alternate over 3 lanes "
+                                                "(context, stream, buffers each)"},
         "gpu_launches": args.steps,
         "clocks": clocks,
     }
@@ -698,6 +719,8 @@ def main():
             "note": "working set fits L2; launch-bound at this size",
         }
 
+    if cpus_before is not None:
+        os.sched_setaffinity(0, cpus_before)  # the CPU baseline uses every host core
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             line["cpu_baseline"] = cpu_reference_rate()

@@ -155,6 +155,20 @@ PFRT_API pfrt_status pfrt_qlinear(pfrt_ctx* ctx, const pfrt_qweight* w, int64_t 
                          int64_t lda, int a_is_u8, float a_scale, int32_t a_zp,
                          const float* bias, int relu, int out_mode, float y_scale, int32_t y_zp,
                          void* y, int64_t ldy, int32_t* acc_out, pfrt_stream stream);
+/* pfrt_qlinear with HOST activations and output: the layer as
+ * InferenceSession::run presents it (src/session.cpp:97-120, host tensors in
+ * and out).  Copies a_host [M rows, stride lda bytes] to the device, runs
+ * pfrt_qlinear, and copies the result to y_host [M rows, stride ldy
+ * elements]; bytes between rows are not touched.  Asynchronous on `stream`
+ * (all three steps in order): with pinned host buffers (pfrt_host_alloc) the
+ * copies overlap other streams' work, and y_host is valid once the stream is
+ * synchronized (pfrt_ctx_check).  The device copies are the context's own,
+ * so a context serves one such stream at a time.  bias stays a device
+ * pointer (a parameter prepared once, like the weight). */
+PFRT_API pfrt_status pfrt_qlinear_host(pfrt_ctx* ctx, const pfrt_qweight* w, int64_t M, const void* a_host,
+                                       int64_t lda, int a_is_u8, float a_scale, int32_t a_zp,
+                                       const float* bias, int relu, int out_mode, float y_scale,
+                                       int32_t y_zp, void* y_host, int64_t ldy, pfrt_stream stream);
 
 /* ------------------------------------------------------------ CSR SpMM
  * Replaces pruning::sparse_matmul (src/pruning/sparse_tensor.cpp:473-519) in

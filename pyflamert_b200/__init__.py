@@ -171,6 +171,20 @@ class QWeight:
                                   y.shape[1], _dptr(acc_out), _stream(stream)), "pfrt_qlinear")
         return y
 
+    def host_call(self, a_host, a_scale, a_zp, y_host, bias=None, relu=False, out="int8", y_scale=1.0, y_zp=0,
+                  stream=None):
+        """The layer on HOST buffers (pfrt_qlinear_host): a_host [M, K] and
+        y_host [M, N] are CPU tensors (pinned for asynchronous copies); the
+        copy in, the layer and the copy out are enqueued on `stream`, and
+        y_host holds the result once that stream is synchronized."""
+        import torch
+        M = a_host.shape[0]
+        _check(lib().pfrt_qlinear_host(self.ctx.handle, self._h, M, a_host.data_ptr(), a_host.stride(0),
+                                       int(a_host.dtype == torch.uint8), float(a_scale), int(a_zp), _dptr(bias),
+                                       int(bool(relu)), OUT_MODES[out], float(y_scale), int(y_zp),
+                                       y_host.data_ptr(), y_host.stride(0), _stream(stream)), "pfrt_qlinear_host")
+        return y_host
+
     def close(self):
         if self._h:
             lib().pfrt_qweight_destroy(self._h)

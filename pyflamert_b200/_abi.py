@@ -55,6 +55,7 @@ PROTOTYPES = {
     "pfrt_qweight_create": [_P, _I64, _I64, _P, _I32, _P, _I64, _P],
     "pfrt_qweight_destroy": [_P],
     "pfrt_qlinear": [_P, _P, _I64, _P, _I64, _INT, _F32, _I32, _P, _INT, _INT, _F32, _I32, _P, _I64, _P, _P],
+    "pfrt_qlinear_host": [_P, _P, _I64, _P, _I64, _INT, _F32, _I32, _P, _INT, _INT, _F32, _I32, _P, _I64, _P],
     "pfrt_csr_create": [_P, _I64, _I64, _I64, _P, _P, _INT, _P, _P],
     "pfrt_csr_destroy": [_P],
     "pfrt_csr_validate_host": [_I64, _I64, _I64, _P, _P, _INT],

@@ -69,6 +69,21 @@ pfrt_status scratch(pfrt_ctx* ctx, size_t bytes, void** out) {
     return PFRT_OK;
 }
 
+pfrt_status io_buffer(pfrt_ctx* ctx, size_t bytes, void** out) {
+    if (bytes == 0) bytes = 256;
+    if (bytes > ctx->io_cap) {
+        const size_t cap = align_up(bytes + bytes / 4, 1 << 20);
+        PFRT_CUDA_TRY(cudaDeviceSynchronize());
+        if (ctx->io) PFRT_CUDA_TRY(cudaFree(ctx->io));
+        ctx->io = nullptr;
+        ctx->io_cap = 0;
+        PFRT_CUDA_TRY(cudaMalloc(&ctx->io, cap));
+        ctx->io_cap = cap;
+    }
+    *out = ctx->io;
+    return PFRT_OK;
+}
+
 pfrt_status make_tmap_2d(CUtensorMap* tm, const void* base, CUtensorMapDataType dt, int elem_bytes,
                          uint64_t cols, uint64_t rows, uint64_t ld_bytes, uint32_t box_cols,
                          uint32_t box_rows) {
@@ -174,6 +189,7 @@ pfrt_status pfrt_ctx_destroy(pfrt_ctx* ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->io) cudaFree(ctx->io);
     if (ctx->d_err) cudaFree(ctx->d_err);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;

@@ -19,6 +19,8 @@ struct pfrt_ctx {
     int* d_err = nullptr;       // device error word (pfrt::DeviceError)
     void* scratch = nullptr;    // grow-only scratch arena
     size_t scratch_cap = 0;
+    void* io = nullptr;         // grow-only device copies of host-buffer calls' inputs and outputs
+    size_t io_cap = 0;
 };
 
 namespace pfrt {
@@ -48,6 +50,9 @@ cudaStream_t pick_stream(pfrt_ctx* ctx, pfrt_stream s);
 // context.  Growing it synchronizes the device.  The memory is shared by all
 // calls on the context.
 pfrt_status scratch(pfrt_ctx* ctx, size_t bytes, void** out);
+// The same for the device copies of a host-buffer call (pfrt_qlinear_host);
+// separate from the scratch arena, which the call's kernels use.
+pfrt_status io_buffer(pfrt_ctx* ctx, size_t bytes, void** out);
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }

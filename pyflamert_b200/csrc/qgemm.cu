@@ -486,4 +486,42 @@ pfrt_status pfrt_qlinear(pfrt_ctx* ctx, const pfrt_qweight* w, int64_t M, const 
     return PFRT_OK;
 }
 
+pfrt_status pfrt_qlinear_host(pfrt_ctx* ctx, const pfrt_qweight* w, int64_t M, const void* a_host, int64_t lda,
+                              int a_is_u8, float a_scale, int32_t a_zp, const float* bias, int relu, int out_mode,
+                              float y_scale, int32_t y_zp, void* y_host, int64_t ldy, pfrt_stream stream) {
+    pfrt_status st = enter(ctx);
+    if (st) return st;
+    if (!w) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_qlinear_host: null weight");
+    if (M < 0) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_qlinear: negative M");
+    if (M == 0) return PFRT_OK;
+    if (!a_host || !y_host) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_qlinear_host: null input or output");
+    if (lda < w->K || ldy < w->N) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_qlinear_host: row stride too small");
+    if (out_mode != PFRT_OUT_F32 && out_mode != PFRT_OUT_S8 && out_mode != PFRT_OUT_U8)
+        return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_qlinear_host: bad output mode");
+    const size_t esz = (out_mode == PFRT_OUT_F32) ? 4 : 1;
+    // Dense device copies (row stride K and N); the host rows keep their strides.
+    const size_t a_bytes = align_up(static_cast<size_t>(M) * w->K, 256);
+    const size_t y_bytes = static_cast<size_t>(M) * w->N * esz;
+    void* io = nullptr;
+    st = io_buffer(ctx, a_bytes + y_bytes, &io);
+    if (st) return st;
+    uint8_t* a_dev = static_cast<uint8_t*>(io);
+    uint8_t* y_dev = a_dev + a_bytes;
+    cudaStream_t s = pick_stream(ctx, stream);
+    // One linear copy for contiguous rows (a pitched copy moves row by row).
+    if (lda == w->K)
+        PFRT_CUDA_TRY(cudaMemcpyAsync(a_dev, a_host, static_cast<size_t>(M) * w->K, cudaMemcpyHostToDevice, s));
+    else
+        PFRT_CUDA_TRY(cudaMemcpy2DAsync(a_dev, w->K, a_host, lda, w->K, M, cudaMemcpyHostToDevice, s));
+    st = pfrt_qlinear(ctx, w, M, a_dev, w->K, a_is_u8, a_scale, a_zp, bias, relu, out_mode, y_scale, y_zp, y_dev,
+                      w->N, nullptr, stream);
+    if (st) return st;
+    if (ldy == w->N)
+        PFRT_CUDA_TRY(cudaMemcpyAsync(y_host, y_dev, y_bytes, cudaMemcpyDeviceToHost, s));
+    else
+        PFRT_CUDA_TRY(
+            cudaMemcpy2DAsync(y_host, ldy * esz, y_dev, w->N * esz, w->N * esz, M, cudaMemcpyDeviceToHost, s));
+    return PFRT_OK;
+}
+
 }  // extern "C"

@@ -229,3 +229,26 @@ def test_split_k_cluster_weight_zero_point(ctx, monkeypatch):
     y, acc = run(ctx, q)
     np.testing.assert_array_equal(y, oracle(q))
     np.testing.assert_array_equal(acc.astype(np.int64), exact_acc(q.a, q.a_zp, q.w, q.w_zp))
+
+
+@pytest.mark.parametrize("out", ["int8", "uint8", "f32"])
+def test_host_buffer_call(ctx, out):
+    """pfrt_qlinear_host: host activations in, host output back, async on a
+    stream; equal to the device call, with padded host rows left untouched."""
+    q = wl.qlinear_case(300, 520, 4096, seed=31, bias=True, relu=True, out=out, y_scale=4.0, y_zp=1)
+    w = pf.QWeight(ctx, q.w, q.w_scale)
+    bias = torch.from_numpy(q.bias).cuda()
+    ref = w(torch.from_numpy(q.a).cuda(), q.a_scale, q.a_zp, bias=bias, relu=True, out=out, y_scale=4.0, y_zp=1)
+    dt = {"int8": torch.int8, "uint8": torch.uint8, "f32": torch.float32}[out]
+    a_pad = torch.zeros((300, 4096 + 32), dtype=torch.uint8).pin_memory()
+    a_pad[:, :4096] = torch.from_numpy(q.a)
+    y_pad = torch.full((300, 520 + 8), 7, dtype=dt).pin_memory()
+    s = torch.cuda.Stream()
+    w.host_call(a_pad[:, :4096], q.a_scale, q.a_zp, y_pad[:, :520], bias=bias, relu=True, out=out, y_scale=4.0,
+                y_zp=1, stream=s)
+    s.synchronize()
+    ctx.check()
+    assert torch.equal(y_pad[:, :520], ref.cpu())
+    assert bool((y_pad[:, 520:] == 7).all())
+    np.testing.assert_array_equal(bits(y_pad[:, :520].numpy()), bits(oracle(q)))
+    w.close()
