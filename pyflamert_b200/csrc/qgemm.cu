@@ -255,9 +255,14 @@ pfrt_status pfrt_qweight_create(pfrt_ctx* ctx, int64_t K, int64_t N, const int8_
     if (e == cudaSuccess) e = cudaMalloc(&w->colsum, sizeof(int32_t) * w->Npad);
     if (e == cudaSuccess) e = cudaMalloc(&w->w_scale, sizeof(float) * w->Npad);
     if (e == cudaSuccess) e = cudaMalloc(&staging, static_cast<size_t>(K * N));
-    if (e == cudaSuccess) e = cudaMemcpy(staging, w_host, static_cast<size_t>(K * N), cudaMemcpyHostToDevice);
+    // On the context stream, ordered before the kernels below (a pageable
+    // cudaMemcpy may return before its DMA lands, and the context stream does
+    // not wait for the legacy stream); the stream is synchronized below.
     if (e == cudaSuccess)
-        e = cudaMemcpy(w->w_scale, scales.data(), sizeof(float) * w->Npad, cudaMemcpyHostToDevice);
+        e = cudaMemcpyAsync(staging, w_host, static_cast<size_t>(K * N), cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(w->w_scale, scales.data(), sizeof(float) * w->Npad, cudaMemcpyHostToDevice,
+                            ctx->stream);
     if (e != cudaSuccess) return cleanup(cuda_fail(e, "pfrt_qweight_create"));
 
     dim3 tb(32, 8);

@@ -1251,7 +1251,12 @@ pfrt_status pfrt_csr_create(pfrt_ctx* ctx, int64_t N, int64_t K, int64_t nnz,
     cudaError_t e = cudaMalloc(&w->indptr, sizeof(int32_t) * (N + 1));
     if (e == cudaSuccess) e = cudaMalloc(&w->indices, sizeof(int32_t) * cap);
     if (e == cudaSuccess) e = cudaMalloc(&w->values, sizeof(float) * cap);
-    if (e == cudaSuccess) e = cudaMemcpy(w->indptr, ip.data(), sizeof(int32_t) * (N + 1), cudaMemcpyHostToDevice);
+    // Every copy on the context stream, which is synchronized before the
+    // weight is returned: a pageable cudaMemcpy may return before its DMA
+    // lands, and later users may be on any stream.
+    cudaStream_t cs = ctx->stream;
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(w->indptr, ip.data(), sizeof(int32_t) * (N + 1), cudaMemcpyHostToDevice, cs);
     // Device copy in bank order (bank_order_rows); PFRT_CSR_BANK_ORDER=0
     // keeps the caller's order.
     std::vector<int32_t> ix_dev;
@@ -1264,11 +1269,11 @@ pfrt_status pfrt_csr_create(pfrt_ctx* ctx, int64_t N, int64_t K, int64_t nnz,
         bank_order_rows(ip, ix_dev, v_dev);
     }
     if (e == cudaSuccess && nnz > 0)
-        e = cudaMemcpy(w->indices, bank_order ? ix_dev.data() : ix.data(), sizeof(int32_t) * nnz,
-                       cudaMemcpyHostToDevice);
+        e = cudaMemcpyAsync(w->indices, bank_order ? ix_dev.data() : ix.data(), sizeof(int32_t) * nnz,
+                            cudaMemcpyHostToDevice, cs);
     if (e == cudaSuccess && nnz > 0)
-        e = cudaMemcpy(w->values, bank_order ? v_dev.data() : values_host, sizeof(float) * nnz,
-                       cudaMemcpyHostToDevice);
+        e = cudaMemcpyAsync(w->values, bank_order ? v_dev.data() : values_host, sizeof(float) * nnz,
+                            cudaMemcpyHostToDevice, cs);
     if (e != cudaSuccess) {
         pfrt_csr_destroy(w);
         return cuda_fail(e, "pfrt_csr_create");
@@ -1303,12 +1308,13 @@ pfrt_status pfrt_csr_create(pfrt_ctx* ctx, int64_t N, int64_t K, int64_t nnz,
             }
         e = cudaMalloc(&w->cptr, sizeof(int32_t) * (cptr.size() + 4));
         if (e == cudaSuccess) e = cudaMalloc(&w->cent, sizeof(uint2) * (cent.size() + 2));
-        if (e == cudaSuccess) e = cudaMemset(w->cptr, 0, sizeof(int32_t) * (cptr.size() + 4));
-        if (e == cudaSuccess) e = cudaMemset(w->cent, 0, sizeof(uint2) * (cent.size() + 2));
+        if (e == cudaSuccess) e = cudaMemsetAsync(w->cptr, 0, sizeof(int32_t) * (cptr.size() + 4), cs);
+        if (e == cudaSuccess) e = cudaMemsetAsync(w->cent, 0, sizeof(uint2) * (cent.size() + 2), cs);
         if (e == cudaSuccess)
-            e = cudaMemcpy(w->cptr, cptr.data(), sizeof(int32_t) * cptr.size(), cudaMemcpyHostToDevice);
+            e = cudaMemcpyAsync(w->cptr, cptr.data(), sizeof(int32_t) * cptr.size(), cudaMemcpyHostToDevice, cs);
         if (e == cudaSuccess)
-            e = cudaMemcpy(w->cent, cent.data(), sizeof(uint2) * cent.size(), cudaMemcpyHostToDevice);
+            e = cudaMemcpyAsync(w->cent, cent.data(), sizeof(uint2) * cent.size(), cudaMemcpyHostToDevice, cs);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(cs);
         w->host_cptr = std::move(cptr);
         if (e != cudaSuccess) {
             pfrt_csr_destroy(w);
