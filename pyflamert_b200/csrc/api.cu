@@ -84,21 +84,6 @@ pfrt_status io_buffer(pfrt_ctx* ctx, size_t bytes, void** out) {
     return PFRT_OK;
 }
 
-pfrt_status tile_counters(pfrt_ctx* ctx, int64_t n, int** out) {
-    if (n > ctx->tile_ctr_cap) {
-        const int64_t cap = std::max<int64_t>(n, 1024);
-        PFRT_CUDA_TRY(cudaDeviceSynchronize());
-        if (ctx->tile_ctr) PFRT_CUDA_TRY(cudaFree(ctx->tile_ctr));
-        ctx->tile_ctr = nullptr;
-        ctx->tile_ctr_cap = 0;
-        PFRT_CUDA_TRY(cudaMalloc(&ctx->tile_ctr, sizeof(int) * cap));
-        PFRT_CUDA_TRY(cudaMemset(ctx->tile_ctr, 0, sizeof(int) * cap));
-        ctx->tile_ctr_cap = cap;
-    }
-    *out = ctx->tile_ctr;
-    return PFRT_OK;
-}
-
 pfrt_status make_tmap_2d(CUtensorMap* tm, const void* base, CUtensorMapDataType dt, int elem_bytes,
                          uint64_t cols, uint64_t rows, uint64_t ld_bytes, uint32_t box_cols,
                          uint32_t box_rows) {
@@ -205,7 +190,6 @@ pfrt_status pfrt_ctx_destroy(pfrt_ctx* ctx) {
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->io) cudaFree(ctx->io);
-    if (ctx->tile_ctr) cudaFree(ctx->tile_ctr);
     if (ctx->d_err) cudaFree(ctx->d_err);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;

@@ -296,7 +296,6 @@ struct FEpi {
     int out_mode;     // kOutF32 or kOutPartial
     float* partial;   // [splits][M][N]
     int vec_ok;
-    int* tile_ctr;    // split-K reduced in the same launch: per-tile arrival counters (zero between calls), or null
 
     __device__ __forceinline__ float finalize(int row, int n, float acc) const {
         float y = __fmul_rn(alpha, acc);

@@ -158,18 +158,10 @@ pfrt_status run_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad, const CUt
     e.out_mode = kOutF32;
     e.vec_ok = ((reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (N % 4) == 0) ? 1 : 0;
     FEpi eg = e;
-    // Split K reduced in the same launch (the tile's last CTA sums the
-    // partials), unless PFRT_GEMM_FUSED_REDUCE = 0 asks for the separate
-    // reduction kernel.
-    const bool fused = splits > 1 && env_int("PFRT_GEMM_FUSED_REDUCE", 1) != 0;
     if (splits > 1) {
         eg.out_mode = kOutPartial;
         eg.partial = static_cast<float*>(scratch_tail);
         e.partial = eg.partial;
-    }
-    if (fused) {
-        pfrt_status st = tile_counters(ctx, mblk * nblk, &eg.tile_ctr);
-        if (st) return st;
     }
     GemmSched sched{};
     sched.num_m_blk = static_cast<int>(mblk);
@@ -193,7 +185,7 @@ pfrt_status run_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad, const CUt
     cfg.numAttrs = pdl_attr(attr);
     cfg.attrs = attr;
     PFRT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tmAh, tmBh, tmAl, tmBl, sched, eg, ctx->d_err));
-    if (splits > 1 && !fused) {
+    if (splits > 1) {
         const int64_t threads = M * ceil_div(N, 4);
         f_splitk_reduce_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, s>>>(e, splits);
         PFRT_CHECK_LAUNCH("f_splitk_reduce_kernel");

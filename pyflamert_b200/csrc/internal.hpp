@@ -21,8 +21,6 @@ struct pfrt_ctx {
     size_t scratch_cap = 0;
     void* io = nullptr;         // grow-only device copies of host-buffer calls' inputs and outputs
     size_t io_cap = 0;
-    int* tile_ctr = nullptr;    // grow-only per-tile counters of in-launch split-K, zero between calls
-    int64_t tile_ctr_cap = 0;
 };
 
 namespace pfrt {
@@ -55,9 +53,6 @@ pfrt_status scratch(pfrt_ctx* ctx, size_t bytes, void** out);
 // The same for the device copies of a host-buffer call (pfrt_qlinear_host);
 // separate from the scratch arena, which the call's kernels use.
 pfrt_status io_buffer(pfrt_ctx* ctx, size_t bytes, void** out);
-// At least n per-tile counters, all zero (the kernels that use them leave
-// them zero again).
-pfrt_status tile_counters(pfrt_ctx* ctx, int64_t n, int** out);
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }

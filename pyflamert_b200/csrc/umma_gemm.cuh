@@ -164,7 +164,6 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
     uint64_t* drain = tempty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);  // fused split-K: this CTA reduces
     uint8_t* params = smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES;
 
     const int warp = threadIdx.x >> 5;
@@ -393,54 +392,6 @@ __global__ void __launch_bounds__(64 + 32 * GemmCfg<KIND, BN, STAGES>::EPI_WARPS
                     epi.store(params, BN, row, n0 + cl, cl, ks, bits);
                 }
                 epi_barrier(Cfg::EPI_THREADS);  // parameters stay valid until every warp stored
-                if (epi.tile_ctr != nullptr) {
-                    // Split-K reduced in this launch: the last of the tile's
-                    // CTAs to store its partial sums all of them in split order
-                    // from zero (as f_splitk_reduce_kernel does, so the result
-                    // is the same bit for bit) and applies the epilogue.
-                    const int tile = unit / sched.splits;
-                    // Every thread makes its own partial stores visible at
-                    // device scope before the arrival is counted: a CTA
-                    // barrier orders the threads but does not publish their
-                    // stores to other SMs.
-                    __threadfence();
-                    epi_barrier(Cfg::EPI_THREADS);
-                    if (etid == 0) {
-                        const int seen = atomicAdd(epi.tile_ctr + tile, 1);
-                        *last_flag = (seen == sched.splits - 1) ? 1 : 0;
-                    }
-                    epi_barrier(Cfg::EPI_THREADS);
-                    if (*last_flag) {
-                        __threadfence();
-                        const bool vec = (epi.N % 4) == 0;
-#pragma unroll 1
-                        for (int c = 0; c < CHUNKS; ++c) {
-                            const int col0 = n0 + (half * CHUNKS + c) * 32;
-                            if (row >= epi.M || col0 >= epi.N) continue;
-                            float acc[32];
-#pragma unroll
-                            for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
-                            for (int k = 0; k < sched.splits; ++k) {
-                                const float* pk = epi.partial + (static_cast<int64_t>(k) * epi.M + row) * epi.N + col0;
-                                if (vec && col0 + 32 <= epi.N) {
-#pragma unroll
-                                    for (int j = 0; j < 32; j += 4) {
-                                        const float4 v = __ldcg(reinterpret_cast<const float4*>(pk + j));
-                                        acc[j] = __fadd_rn(acc[j], v.x);
-                                        acc[j + 1] = __fadd_rn(acc[j + 1], v.y);
-                                        acc[j + 2] = __fadd_rn(acc[j + 2], v.z);
-                                        acc[j + 3] = __fadd_rn(acc[j + 3], v.w);
-                                    }
-                                } else {
-                                    for (int j = 0; j < 32 && col0 + j < epi.N; ++j)
-                                        acc[j] = __fadd_rn(acc[j], __ldcg(pk + j));
-                                }
-                            }
-                            epi.template store_direct<32>(row, col0, acc);
-                        }
-                        if (etid == 0) epi.tile_ctr[tile] = 0;  // ready for the next call
-                    }
-                }
             } else {
                 const int slot = t & 1;
                 const uint32_t ap = static_cast<uint32_t>(t >> 1) & 1u;

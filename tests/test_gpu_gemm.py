@@ -120,22 +120,16 @@ def test_large_values_accuracy(ctx):
     assert normwise_rel(y, f64) <= FP32_TOL
 
 
-@pytest.mark.parametrize("path", ["dense", "weight"])
-@pytest.mark.parametrize("M,N,K,c_len", [(256, 1024, 1024, None), (130, 300, 1000, 7), (64, 100, 4096, "MN"),
-                                         (257, 129, 700, 0)])
-def test_split_k_reduced_in_launch(ctx, path, M, N, K, c_len, monkeypatch):
-    """Split K reduced inside the GEMM launch (the tile's last CTA sums the
-    partials in split order) gives the same bytes as the separate reduction
-    kernel, and stays within the fp32 bound of the oracle; twice in a row (the
-    per-tile counters are left at zero)."""
+@pytest.mark.parametrize("splits", ["5", "8"])
+@pytest.mark.parametrize("M,N,K,c_len", [(256, 1024, 1024, None), (130, 300, 1000, 7), (64, 100, 4096, "MN")])
+def test_fresh_weights_with_split_k(ctx, splits, M, N, K, c_len, monkeypatch):
+    """A new prepared weight per call, several calls in a row, with K split:
+    each result within the fp32 bound.  (Weight preparation once read its
+    staging copy before a pageable host-to-device copy had landed, which
+    only showed on later weights.)"""
     c = {None: None, "MN": M * N}.get(c_len, c_len)
     g = wl.gemm_case(M, N, K, seed=M + N + K, c_len=c)
-    run = gpu_dense if path == "dense" else gpu_weight
-    monkeypatch.setenv("PFRT_GEMM_SPLITS", "5")
-    fused1 = run(ctx, g)
-    fused2 = run(ctx, g)
-    monkeypatch.setenv("PFRT_GEMM_FUSED_REDUCE", "0")
-    separate = run(ctx, g)
-    np.testing.assert_array_equal(fused1.view(np.int32), separate.view(np.int32))
-    np.testing.assert_array_equal(fused2.view(np.int32), separate.view(np.int32))
-    assert normwise_rel(fused1, oracle(g)) <= FP32_TOL
+    monkeypatch.setenv("PFRT_GEMM_SPLITS", splits)
+    ref = oracle(g)
+    for _ in range(4):
+        assert normwise_rel(gpu_weight(ctx, g), ref) <= FP32_TOL
