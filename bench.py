@@ -294,20 +294,46 @@ def qlinear_e2e(ctx, q, w, steps, lanes=3):
         ln["w"].host_call(ln["a_host"], q.a_scale, q.a_zp, ln["y_host"], out="int8", y_scale=q.y_scale,
                           stream=ln["stream"])
 
-    for i in range(5 * lanes):
-        step(i)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(cur)
+    def timed(fn):
+        """(device ms per step, host enqueue us per step) of `steps` calls of
+        fn(i), the lanes' streams joined to the current stream on both sides."""
+        for i in range(5 * lanes):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        for ln in L:
+            ln["stream"].wait_stream(cur)
+        h0 = time.perf_counter()
+        for i in range(steps):
+            fn(i)
+        h1 = time.perf_counter()
+        for ln in L:
+            cur.wait_stream(ln["stream"])
+        e1.record(cur)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps, (h1 - h0) * 1e6 / steps
+
+    # The floor of this path on this host link: each direction's copies alone,
+    # in the same lanes; with both directions in flight at once (full duplex)
+    # a step cannot take less than the slower of the two.
     for ln in L:
-        ln["stream"].wait_stream(cur)
-    for i in range(steps):
-        step(i)
-    for ln in L:
-        cur.wait_stream(ln["stream"])
-    e1.record(cur)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
+        ln["a_dev"] = torch.empty_like(ln["a_host"], device="cuda")
+        ln["y_dev"] = torch.zeros_like(ln["y_host"], device="cuda")
+
+    def h2d_only(i):
+        ln = L[i % lanes]
+        with torch.cuda.stream(ln["stream"]):
+            ln["a_dev"].copy_(ln["a_host"], non_blocking=True)
+
+    def d2h_only(i):
+        ln = L[i % lanes]
+        with torch.cuda.stream(ln["stream"]):
+            ln["y_host"].copy_(ln["y_dev"], non_blocking=True)
+
+    h2d_ms, _ = timed(h2d_only)
+    d2h_ms, _ = timed(d2h_only)
+    ms, enqueue_us = timed(step)
     # every lane's host buffer holds the layer's output
     ref = w(torch.from_numpy(q.a).cuda(), q.a_scale, q.a_zp, out="int8", y_scale=q.y_scale).cpu()
     for ln in L:
@@ -316,7 +342,8 @@ def qlinear_e2e(ctx, q, w, steps, lanes=3):
         ln["ctx"].check()
         ln["w"].close()
         ln["ctx"].close()
-    return ms, M * K, M * N
+    link = {"h2d_only_ms_per_step": h2d_ms, "d2h_only_ms_per_step": d2h_ms, "enqueue_us_per_step": enqueue_us}
+    return ms, M * K, M * N, link
 
 
 def spmm_setup(ctx, n_copies):
@@ -621,8 +648,10 @@ def main():
     int8_peak = 2.0 * peaks["bf16_tflops"]
     clocks = sampler.summary(t_soak, t_end)
 
-    e2e_ms, h2d, d2h = qlinear_e2e(ctx, q, copies[0][0], max(200, args.steps))
+    e2e_ms, h2d, d2h, link = qlinear_e2e(ctx, q, copies[0][0], max(200, args.steps))
     e2e_ms = max_over_ranks(e2e_ms, world)
+    h2d_ms = max_over_ranks(link["h2d_only_ms_per_step"], world)
+    d2h_ms = max_over_ranks(link["d2h_only_ms_per_step"], world)
 
     line = {
         "metric": "int8 GEMM TOPS (config 2: u8[512,4096] x s8[4096,4096] -> s8, per-channel)",
@@ -643,7 +672,13 @@ def main():
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_ms, "path": "pfrt_qlinear_host (C ABI, pinned host buffers: copy in, "
                                                 "layer, copy out per call); steps alternate over 3 lanes "
-                                                "(context, stream, buffers each)"},
+                                                "(context, stream, buffers each)",
+                "host_link": {"h2d_gbs": h2d / (h2d_ms * 1e-3) / 1e9, "d2h_gbs": d2h / (d2h_ms * 1e-3) / 1e9,
+                              "floor_ms_per_step": max(h2d_ms, d2h_ms),
+                              "frac_of_floor": max(h2d_ms, d2h_ms) / e2e_ms,
+                              "note": "each direction's copies timed alone in the same lanes; floor = the "
+                                      "slower direction (both in flight at once)"},
+                "host_enqueue_us_per_step": link["enqueue_us_per_step"]},
         "gpu_launches": args.steps,
         "clocks": clocks,
     }

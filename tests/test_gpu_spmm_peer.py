@@ -6,8 +6,8 @@ gathered Y must match pruning::sparse_matmul (src/pruning/sparse_tensor.cpp:
 473-519) on the whole W, normwise <= 1e-5, on every rank, call after call
 (the call counter lives on the device) and inside CUDA graph replays.
 
-World 1 runs on one GPU (the rank's own buffers only); world 2
-needs two GPUs and is skipped with fewer."""
+World 1 runs on one GPU (the rank's own buffers only); worlds 2 and 4
+need that many GPUs and are skipped with fewer."""
 import os
 import socket
 
@@ -115,22 +115,24 @@ def _rank_main(rank, world, port, q):
         q.put((rank, None, repr(e)))
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_world2_two_gpus():
+@pytest.mark.parametrize("world", [2, 4])
+def test_world_n_gpus(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
-    for _ in range(2):
+    for _ in range(world):
         r, worst, err = q.get(timeout=300)
         res[r] = (worst, err)
     for p in procs:
         p.join(timeout=60)
-    for r in range(2):
+    for r in range(world):
         worst, err = res[r]
         assert err is None, err
         assert worst <= FP32_TOL
