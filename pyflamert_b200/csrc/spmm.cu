@@ -604,6 +604,10 @@ __global__ void __launch_bounds__(kSpmmThreads)
 // lane l owns MV consecutive rows of X (columns of Y), so each nonzero is one
 // broadcast read of its (column, value) and one MV-wide read of X^T[k].
 // Outputs are staged through shared memory and stored along n.
+// The local columns come from the host-side blocking of a validated CSR
+// (column - 256 * chunk, in [0, 256) by construction); the kernel masks them
+// to the tile instead of checking them, so no entry can address shared memory
+// outside the chunk's X tile.
 constexpr int kTileKT = 256;    // columns of X (rows of X^T) per chunk, = the column-blocked copy's block
 constexpr int kXtWarps = 16;    // compute warps per block
 constexpr int kXtRowsPerWarp = 8;
@@ -666,7 +670,6 @@ __global__ void __launch_bounds__((kXtWarps + 1) * 32, 1)
     for (int i = 0; i < kXtRowsPerWarp; ++i)
 #pragma unroll
         for (int v = 0; v < MV; ++v) acc[i][v] = 0.0f;
-    bool bad = false;
 
     if (warp == kXtWarps) {
         if (lane == 0) {
@@ -734,9 +737,8 @@ __global__ void __launch_bounds__((kXtWarps + 1) * 32, 1)
                         for (int u = 0; u < 4; ++u) en[u] = ents[e + u];
 #pragma unroll
                         for (int u = 0; u < 4; ++u) {
-                            const uint32_t k = en[u].x < static_cast<uint32_t>(kTileKT) ? en[u].x : 0u;
-                            bad |= en[u].x >= static_cast<uint32_t>(kTileKT);
-                            const float v = en[u].x < static_cast<uint32_t>(kTileKT) ? __uint_as_float(en[u].y) : 0.0f;
+                            const uint32_t k = en[u].x & static_cast<uint32_t>(kTileKT - 1);
+                            const float v = __uint_as_float(en[u].y);
                             if constexpr (MV == 2) {
                                 const float2 xv = reinterpret_cast<const float2*>(xs + k * MT)[lane];
                                 acc[i][0] = __fmaf_rn(v, xv.x, acc[i][0]);
@@ -748,9 +750,8 @@ __global__ void __launch_bounds__((kXtWarps + 1) * 32, 1)
                     }
                     for (; e < e1; ++e) {
                         const uint2 en = ents[e];
-                        const uint32_t k = en.x < static_cast<uint32_t>(kTileKT) ? en.x : 0u;
-                        bad |= en.x >= static_cast<uint32_t>(kTileKT);
-                        const float v = en.x < static_cast<uint32_t>(kTileKT) ? __uint_as_float(en.y) : 0.0f;
+                        const uint32_t k = en.x & static_cast<uint32_t>(kTileKT - 1);
+                        const float v = __uint_as_float(en.y);
 #pragma unroll
                         for (int q = 0; q < MV; ++q) acc[i][q] = __fmaf_rn(v, xs[k * MT + lane * MV + q], acc[i][q]);
                     }
@@ -779,7 +780,6 @@ __global__ void __launch_bounds__((kXtWarps + 1) * 32, 1)
         const int m = e / nr, i = e % nr;
         if (m0 + m < M && !*abort_flag) y[static_cast<int64_t>(m0 + m) * ldy + r0 + i] = ys[m * ld + i];
     }
-    if (bad) report_error(err, kDevBadIndex);
 }
 
 // Dense tf32 split of a CSR matrix: hi[n][k] = tf32(v), lo[n][k] = v - hi
@@ -1376,13 +1376,13 @@ pfrt_status pfrt_spmm(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* 
     // M > 8: the tiled CSR kernel (spmm_xtile_kernel) or a 3xTF32 tensor-core
     // GEMM on a dense copy of W made once (8 bytes per element of W, capped
     // at 8 GiB), whichever the cost model below expects to be faster.  Both
-    // estimates are fits to B200 measurements (8192^2 and 4096^2 at 50-99 %
-    // sparsity, M = 16..256): the tiled kernel costs ~0.9 us per 256-column
-    // chunk (the load pipeline) plus ~20 ps per nonzero and 32*MV-row tile of
-    // X (it is bound by the instructions per nonzero, not by memory); the GEMM
-    // the larger of reading the dense copy at ~5.5 TB/s and its tensor work.
-    // The dense copy wins down to ~5 % density; the tiled kernel serves
-    // sparser weights and strided X or Y.
+    // estimates are fits to B200 measurements (8192^2 and 4096^2 at 90-99 %
+    // sparsity, M = 16..256): per 32*MV-row tile of X the tiled kernel costs
+    // ~1.25 us per 256-column chunk (the load pipeline) plus ~13.3 ps per
+    // nonzero (it is bound by the instructions per nonzero, not by memory);
+    // the GEMM the larger of reading the dense copy at ~5.5 TB/s and its
+    // tensor work, plus ~12 us.  The dense copy wins down to ~6-7 % density
+    // at M <= 64; the tiled kernel serves sparser weights and strided X or Y.
     // PFRT_SPMM_TILED / PFRT_SPMM_DENSE = 0|1 override the choice.
     cudaStream_t s = pick_stream(ctx, stream);
     pfrt_csr* wm = const_cast<pfrt_csr*>(w);
@@ -1394,9 +1394,9 @@ pfrt_status pfrt_spmm(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* 
     const bool dense_ok = packed && dense_bytes <= 8.0 * (1ull << 30);
     const double mv = (M <= 32) ? 1.0 : 2.0;
     const double mtiles = std::ceil(Md / (32.0 * mv));
-    const double t_tiled = 0.9e-6 * static_cast<double>(w->nchunks) +
-                           static_cast<double>(w->nnz) * mtiles * 20.0e-12 * (148.0 / static_cast<double>(ctx->num_sms));
-    const double t_dense = std::max((dense_bytes + 8.0 * Md * Kd) / 5.5e12, 6.0 * Md * Nd * Kd / 6.0e14);
+    const double t_tiled = mtiles * (1.25e-6 * static_cast<double>(w->nchunks) + 13.3e-12 * static_cast<double>(w->nnz)) *
+                           (148.0 / static_cast<double>(ctx->num_sms));
+    const double t_dense = std::max((dense_bytes + 8.0 * Md * Kd) / 5.5e12, 6.0 * Md * Nd * Kd / 6.0e14) + 12.0e-6;
     bool use_dense = dense_ok && t_dense < t_tiled;
     if (dense_env && *dense_env) use_dense = dense_ok && *dense_env == '1';
     if (tiled_env && *tiled_env) use_dense = use_dense && *tiled_env == '0';

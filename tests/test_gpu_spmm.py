@@ -156,9 +156,10 @@ def test_small_batch_kernels(ctx, kernel, M, monkeypatch):
 @pytest.mark.parametrize("M,N,K,sparsity", [(32, 300, 700, 0.9), (130, 1000, 333, 0.5),
                                             (512, 4096, 4096, 0.9), (1024, 2048, 8192, 0.97)])
 def test_large_batch_dense_and_csr_paths(ctx, dense, M, N, K, sparsity, monkeypatch):
-    """Large batches take the tensor-core GEMM on a dense copy of W above ~2.5%
-    density; both that path and the CSR wide kernel, forced in turn, match the
-    oracle, with tails in M, N and K."""
+    """Batches above 8 rows take the tensor-core GEMM on a dense copy of W or
+    the tiled CSR kernel, by a cost model (dense above ~6-7 % density at
+    M <= 64, and at lower density as M grows); both the dense path and the
+    CSR kernels, forced in turn, match the oracle, with tails in M, N and K."""
     monkeypatch.setenv("PFRT_SPMM_DENSE", dense)
     c = wl.spmm_case(M, N, K, sparsity=sparsity, seed=M + N + K)
     y = gpu(ctx, c)
