@@ -609,7 +609,12 @@ __global__ void __launch_bounds__(kSpmmThreads)
 // to the tile instead of checking them, so no entry can address shared memory
 // outside the chunk's X tile.
 constexpr int kTileKT = 256;    // columns of X (rows of X^T) per chunk, = the column-blocked copy's block
-constexpr int kXtWarps = 16;    // compute warps per block
+// 15 compute warps + the producer: 16 warps, 4 on each of the SM's four
+// schedulers, so each thread may hold up to 128 registers (a scheduler's
+// 16 K registers over 4 warps).  With 16 compute warps the fifth warp on one
+// scheduler capped threads at 96 registers and the MV = 2 instance spilled
+// to local memory, through the L1 pipe this kernel is bound by.
+constexpr int kXtWarps = 15;    // compute warps per block
 constexpr int kXtRowsPerWarp = 8;
 constexpr int kXtRows = kXtWarps * kXtRowsPerWarp;
 constexpr int kXtEntMax = 4096; // nonzeros of one group in one chunk
@@ -1378,8 +1383,9 @@ pfrt_status pfrt_spmm(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* 
     // at 8 GiB), whichever the cost model below expects to be faster.  Both
     // estimates are fits to B200 measurements (8192^2 and 4096^2 at 90-99 %
     // sparsity, M = 16..256): per 32*MV-row tile of X the tiled kernel costs
-    // ~1.25 us per 256-column chunk (the load pipeline) plus ~13.3 ps per
-    // nonzero (it is bound by the instructions per nonzero, not by memory);
+    // ~1.25 us (MV = 1) or ~1.1 us (MV = 2) per 256-column chunk plus ~13.3
+    // or ~12.7 ps per nonzero (it is bound by the shared-memory pipe, not by
+    // DRAM);
     // the GEMM the larger of reading the dense copy at ~5.5 TB/s and its
     // tensor work, plus ~12 us.  The dense copy wins down to ~6-7 % density
     // at M <= 64; the tiled kernel serves sparser weights and strided X or Y.
@@ -1394,7 +1400,8 @@ pfrt_status pfrt_spmm(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* 
     const bool dense_ok = packed && dense_bytes <= 8.0 * (1ull << 30);
     const double mv = (M <= 32) ? 1.0 : 2.0;
     const double mtiles = std::ceil(Md / (32.0 * mv));
-    const double t_tiled = mtiles * (1.25e-6 * static_cast<double>(w->nchunks) + 13.3e-12 * static_cast<double>(w->nnz)) *
+    const double per_chunk = mv == 1.0 ? 1.25e-6 : 1.1e-6, per_nnz = mv == 1.0 ? 13.3e-12 : 12.7e-12;
+    const double t_tiled = mtiles * (per_chunk * static_cast<double>(w->nchunks) + per_nnz * static_cast<double>(w->nnz)) *
                            (148.0 / static_cast<double>(ctx->num_sms));
     const double t_dense = std::max((dense_bytes + 8.0 * Md * Kd) / 5.5e12, 6.0 * Md * Nd * Kd / 6.0e14) + 12.0e-6;
     bool use_dense = dense_ok && t_dense < t_tiled;
