@@ -16,7 +16,9 @@ copies of (activations, weights, output) that each step's working set has
 left L2 (the copies total more than twice the 126 MB L2), so every step reads
 its operands from HBM.  `e2e` is the same metric through the public API
 with host buffers: pinned-host -> device copy of the activations, the layer,
-device -> pinned-host copy of the output, every step.
+device -> pinned-host copy of the output, every step.  `e2e.host_link` times
+each direction's copies alone on the same lanes; the slower one is the least
+a step can take on that box's host link.
 
 The secondary objects report, measured the same way: the CSR SpMM (config 5,
 M=1, 90% sparse, 8192 x 8192: the HBM-bound point), the 4096^3 int8 GEMM (the
