@@ -87,6 +87,19 @@ PFRT_API pfrt_status pfrt_memcpy_h2d(pfrt_ctx* ctx, void* dst, const void* src, 
 PFRT_API pfrt_status pfrt_memcpy_d2h(pfrt_ctx* ctx, void* dst, const void* src, size_t bytes, pfrt_stream stream);
 PFRT_API pfrt_status pfrt_memcpy_d2d(pfrt_ctx* ctx, void* dst, const void* src, size_t bytes, pfrt_stream stream);
 PFRT_API pfrt_status pfrt_memset(pfrt_ctx* ctx, void* dst, int value, size_t bytes, pfrt_stream stream);
+/* Copies between PAGEABLE host memory (a host Tensor of the reference
+ * runtime, src/tensor.cpp) and the device.  They replace the per-run host
+ * copies of graph inputs and outputs that CPUExecutor::execute makes
+ * (src/backends/cpu/executor.cpp:65-74).  The bytes go through the context's
+ * ring of pinned buffers (4 x 1 MiB, allocated by the first call): several
+ * host threads copy one chunk while the DMA of the previous chunk runs.
+ * pfrt_memcpy_h2d_staged returns once src has been read (its DMAs complete
+ * in order on `stream`); pfrt_memcpy_d2h_staged returns once dst holds the
+ * bytes (it waits for the work queued before it on `stream`). */
+PFRT_API pfrt_status pfrt_memcpy_h2d_staged(pfrt_ctx* ctx, void* dst, const void* src, size_t bytes,
+                                            pfrt_stream stream);
+PFRT_API pfrt_status pfrt_memcpy_d2h_staged(pfrt_ctx* ctx, void* dst, const void* src, size_t bytes,
+                                            pfrt_stream stream);
 
 /* ------------------------------------------------------------ fp32 Gemm / MatMul
  * Replaces cpu_gemm (src/backends/cpu/ops/math.cpp:377-438) and the 2-D path
@@ -110,13 +123,16 @@ PFRT_API pfrt_status pfrt_gemm_f32(pfrt_ctx* ctx, int64_t M, int trans_a, float 
  * for callers that cannot allocate device memory while they run (for example
  * a host program whose device memory is all handed out by its own pool, or a
  * latency-bound loop that must not pay cudaMalloc's device synchronization).
- * Same arguments and result as pfrt_gemm_f32; the per-call split of A uses a
- * fixed 16 MiB device array built into the library instead of the context's
+ * Same arguments as pfrt_gemm_f32; the per-call split of A uses a fixed
+ * 16 MiB device array built into the library instead of the context's
  * scratch memory.  Limit: M * Kpad <= 2097152 (Kpad = K rounded up to 32),
- * else PFRT_ERR_UNSUPPORTED.  The first call on each device does a one-time
- * set-up (it looks up the array's device address), so make that first call
- * before any stream capture.  All calls share the array and it keeps the last
- * call's contents: calls that overlap on the GPU race on it. */
+ * else PFRT_ERR_UNSUPPORTED.  No split-K (no room for partial sums;
+ * PFRT_GEMM_SPLITS is ignored): the result agrees with pfrt_gemm_f32 within
+ * fp32 tolerance, and shapes whose tiles leave SMs idle may run slower.  The
+ * first call on each device does a one-time set-up (it looks up the array's
+ * device address), so make that first call before any stream capture.  All
+ * calls share the array and it keeps the last call's contents: calls that
+ * overlap on the GPU race on it. */
 PFRT_API pfrt_status pfrt_gemm_f32_noalloc(pfrt_ctx* ctx, int64_t M, int trans_a, float alpha,
                                            const float* a, const pfrt_fweight* b, float beta,
                                            const float* c, int64_t c_len, float* y,
@@ -183,6 +199,11 @@ PFRT_API pfrt_status pfrt_qlinear_host(pfrt_ctx* ctx, const pfrt_qweight* w, int
  * (PFRT_ERR_BAD_CSR otherwise).  The device copy uses int32 indices.
  *
  * pfrt_spmm: X device [M,K] (row stride ldx), Y device [M,N] (row stride ldy).
+ * The first call with a given M class builds state kept with the CSR (for
+ * M = 3..8 a row partition, for M > 8 row groups or a dense copy of W; each
+ * allocates device memory and synchronizes): make one call of each batch
+ * size class before capturing calls in a CUDA graph, and do not use one CSR
+ * from several threads or contexts at once.
  * pfrt_spmm_csr_f32: same on a caller-owned device CSR (int32); the kernel
  * bounds-checks every index, skips out-of-range entries and reports
  * PFRT_ERR_BAD_CSR through pfrt_ctx_check(). */
@@ -249,37 +270,80 @@ PFRT_API pfrt_status pfrt_ipc_get_handle(pfrt_ctx* ctx, const void* dev_ptr, pfr
 PFRT_API pfrt_status pfrt_ipc_open(pfrt_ctx* ctx, const pfrt_ipc_handle* handle, void** dev_ptr);
 PFRT_API pfrt_status pfrt_ipc_close(pfrt_ctx* ctx, void* dev_ptr);
 
-/* Output-channel-sharded SpMM fused with the all-gather of its output
- * (M = 1).  Rank r holds rows [r*ns, r*ns + ns) of W as its CSR w_shard
- * (ns = w_shard's N) and the whole X.  The kernel sends every output value
- * straight to every other rank as it is computed, together with the call's
- * number in one 8-byte store over NVLink (no fences), and each rank's blocks
- * unpack the values that arrive into its own gathered output y [world*ns]
- * floats.  The call ends when y is complete.  The call number lives on the
- * device (the call can sit in a CUDA graph) and the receive buffers are used
- * by its parity, so a rank can run at most one call ahead of another without
- * overwriting values not yet read.  Every rank must make the same sequence
- * of calls.
+/* Output-channel-sharded SpMM fused with the all-gather of its output.
+ * Replaces pruning::sparse_matmul (src/pruning/sparse_tensor.cpp:473-519) for
+ * a W too large to replicate: rank r holds rows [r*ns, r*ns + ns) of W as its
+ * CSR w_shard (ns = w_shard's N) and the whole X [M, K], and every rank ends
+ * with the whole Y [M, world*ns] in its own y (row stride world*ns).  The
+ * reference has no communication backend; the exchange is the all-gather its
+ * partitioner plans (src/partition/graph_partitioner.cpp:111-200).
  *
- *   y        this rank's gathered output [world*ns] floats (device);
- *   recv[p]  rank p's receive buffer [2][world*ns] uint64, mapped into this
- *            process (pfrt_ipc_open; recv[rank] is this rank's own); zeroed
- *            once before the first call;
- *   state    this rank's private [4] uint32, zeroed once.
+ * M = 1: the kernel sends every output value straight to every other rank as
+ * it is computed, together with the call's number in one 8-byte store over
+ * NVLink (no fences), and each rank's blocks unpack the values that arrive
+ * into its own y.
+ * M > 1: the rank computes its column block of Y into its own y (the kernel
+ * pfrt_spmm would pick for the shard) and the block reaches every other
+ * rank's y over NVLink: stored by the shard GEMM's epilogue as each tile is
+ * computed (the dense path, blocks of 2 MiB and more), or by a copy kernel
+ * after the SpMM.  Nothing is written into another rank's y before that
+ * rank has declared it free for this call (a rank declares it when its
+ * stream reaches the call, i.e. after everything it ran on the previous
+ * output); the call ends once every other rank has reported its block
+ * written.
  *
- * Waits on other ranks give up after about 2 s: the call then reports
- * PFRT_ERR_DEVICE_TIMEOUT through pfrt_ctx_check and the peer set must be made
- * anew (its buffers are out of step).  M != 1: PFRT_ERR_UNSUPPORTED. */
+ * The call number lives on the device (the call can sit in a CUDA graph).  A
+ * rank can run at most one call ahead of another without overwriting data
+ * not yet read.  Every rank must make the same sequence of calls with the
+ * same M; consumers of y must run on the call's stream (or after it).
+ *
+ *   y          this rank's gathered output [max_m][world*ns] floats (device);
+ *   recv[p]    rank p's M = 1 receive buffer [2][world*ns] uint64, mapped
+ *              into this process (pfrt_ipc_open; recv[rank] is this rank's
+ *              own);
+ *   state      this rank's private [4] uint32;
+ *   ns, max_m  the shard height and the rows of y (M <= max_m);
+ *   y_peer[p]  rank p's y mapped into this process (y_peer[rank] = y);
+ *   sig[p]     rank p's signal words [PFRT_PEER_SIG_WORDS] uint32, mapped
+ *              into this process (sig[rank] is this rank's own).
+ * recv, state and sig are zeroed once before the first call.  y_peer and sig
+ * are needed for M > 1 only.
+ *
+ * Waits on other ranks give up after about 2 s (PFRT_PEER_WAIT_MS overrides
+ * the limit): the call then reports PFRT_ERR_DEVICE_TIMEOUT through
+ * pfrt_ctx_check, and later calls report it at once until every rank has
+ * called pfrt_peer_reset (and the ranks have synchronized on the host).
+ * M > max_m or missing M > 1 buffers: PFRT_ERR_INVALID_ARGUMENT. */
 #define PFRT_MAX_PEERS 8
+#define PFRT_PEER_SIG_WORDS 16
 typedef struct pfrt_peer_set {
     int32_t rank;
     int32_t world;
     float* y;
     uint64_t* recv[PFRT_MAX_PEERS];
     uint32_t* state;
+    int64_t ns;
+    int64_t max_m;
+    float* y_peer[PFRT_MAX_PEERS];
+    uint32_t* sig[PFRT_MAX_PEERS];
 } pfrt_peer_set;
 PFRT_API pfrt_status pfrt_spmm_allgather(pfrt_ctx* ctx, const pfrt_csr* w_shard, int64_t M, const float* x,
                                          int64_t ldx, const pfrt_peer_set* peers, pfrt_stream stream);
+/* The all-gather alone, for an output whose column blocks the ranks have
+ * computed themselves: rank r has written columns [r*ns, r*ns + ns) of the
+ * first M rows of its own y (row stride world*ns); the call stores that block
+ * into every other rank's y and returns once every other rank's block has
+ * arrived.  Same protocol, call numbering and rules as pfrt_spmm_allgather
+ * with M > 1 (the two share one call sequence).  The C-ABI form of the NCCL
+ * all-gather of column blocks that the reference's partitioner plans as a
+ * CommOp (src/partition/graph_partitioner.cpp:111-200). */
+PFRT_API pfrt_status pfrt_peer_allgather(pfrt_ctx* ctx, int64_t M, const pfrt_peer_set* peers, pfrt_stream stream);
+/* No counterpart in the reference.  Zeroes this rank's state, its M = 1
+ * receive buffer and its signal words (asynchronously on `stream`), which
+ * clears a timeout recorded by pfrt_spmm_allgather.  Every rank of the set
+ * calls it, and the ranks synchronize their streams and each other on the
+ * host, before the next pfrt_spmm_allgather. */
+PFRT_API pfrt_status pfrt_peer_reset(pfrt_ctx* ctx, const pfrt_peer_set* peers, pfrt_stream stream);
 
 /* ------------------------------------------------------------ elementwise
  * Standalone forms of the ops the backend normally fuses into epilogues:

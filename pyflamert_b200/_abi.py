@@ -23,10 +23,15 @@ class IpcHandle(C.Structure):
     _fields_ = [("bytes", C.c_ubyte * 64)]
 
 
+PFRT_PEER_SIG_WORDS = 16
+
+
 class PeerSet(C.Structure):
     """pfrt_peer_set (include/pfrt_cuda.h)."""
     _fields_ = [("rank", C.c_int32), ("world", C.c_int32), ("y", C.c_void_p),
-                ("recv", C.c_void_p * PFRT_MAX_PEERS), ("state", C.c_void_p)]
+                ("recv", C.c_void_p * PFRT_MAX_PEERS), ("state", C.c_void_p),
+                ("ns", C.c_int64), ("max_m", C.c_int64),
+                ("y_peer", C.c_void_p * PFRT_MAX_PEERS), ("sig", C.c_void_p * PFRT_MAX_PEERS)]
 
 
 # name -> argument types; every function returns pfrt_status (int) unless listed in _RESTYPE.
@@ -47,6 +52,8 @@ PROTOTYPES = {
     "pfrt_memcpy_d2h": [_P, _P, _P, _SZ, _P],
     "pfrt_memcpy_d2d": [_P, _P, _P, _SZ, _P],
     "pfrt_memset": [_P, _P, _INT, _SZ, _P],
+    "pfrt_memcpy_h2d_staged": [_P, _P, _P, _SZ, _P],
+    "pfrt_memcpy_d2h_staged": [_P, _P, _P, _SZ, _P],
     "pfrt_fweight_create": [_P, _I64, _I64, _INT, _P, _P],
     "pfrt_fweight_destroy": [_P],
     "pfrt_gemm_f32": [_P, _I64, _INT, _F32, _P, _P, _F32, _P, _I64, _P, _P],
@@ -68,6 +75,8 @@ PROTOTYPES = {
     "pfrt_ipc_open": [_P, _P, _P],
     "pfrt_ipc_close": [_P, _P],
     "pfrt_spmm_allgather": [_P, _P, _I64, _P, _I64, _P, _P],
+    "pfrt_peer_allgather": [_P, _I64, _P, _P],
+    "pfrt_peer_reset": [_P, _P, _P],
     "pfrt_quantize_f32": [_P, _I64, _P, _F32, _I32, _INT, _P, _P],
     "pfrt_add_rowvec_f32": [_P, _I64, _I64, _P, _P, _P, _P],
     "pfrt_relu_f32": [_P, _I64, _P, _P, _P],

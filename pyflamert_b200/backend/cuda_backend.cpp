@@ -9,6 +9,8 @@
 #include "cuda_backend.hpp"
 
 #include <algorithm>
+#include <cstdlib>
+#include <exception>
 #include <chrono>
 #include <condition_variable>
 #include <cstring>
@@ -78,7 +80,27 @@ public:
                                 const std::vector<std::string>& output_names);
     CudaBackend::PrepareStats prepare(const Graph& graph);
 
+    // The two halves of execute() for a caller that holds mutex(): enqueue
+    // the inputs' copies and every node (`outs` receives the requested
+    // outputs' device tensors, `names` their names), then copy one device
+    // tensor into host memory (waits for the work before it).  check() reads
+    // the device error word.
+    std::mutex& mutex() { return mu_; }
+    void run_graph(const Graph& graph, const std::unordered_map<std::string, Tensor>& feeds,
+                   const std::vector<std::string>& output_names, std::vector<std::string>& names,
+                   std::vector<DevTensor>& outs);
+    void fetch(const DevTensor& d, void* host) {
+        if (!d.bytes()) return;
+        check(d.bytes() >= kStagedBytes ? pfrt_memcpy_d2h_staged(ctx_, host, d.ptr, d.bytes(), nullptr)
+                                        : pfrt_memcpy_d2h(ctx_, host, d.ptr, d.bytes(), nullptr),
+              nullptr);
+    }
+    void check_device() { check(pfrt_ctx_check(ctx_, nullptr), nullptr); }
+
     int device_;
+    // Host copies of at least this many bytes go through the context's pinned
+    // staging ring (pfrt_memcpy_*_staged); smaller ones are plain copies.
+    static constexpr size_t kStagedBytes = 64 * 1024;
 
 private:
     // ------------------------------------------------------------- helpers
@@ -115,15 +137,67 @@ private:
         inits_.clear();
     }
 
-    // The graph's initializers are prepared once; a different graph (or one
-    // that changed shape) drops the caches.
+    // The graph's initializers are prepared once and kept while the graph's
+    // signature holds: every node's type and inputs, and every initializer's
+    // name, data address, dtype, shape and 16 words sampled across its bytes.
+    // A graph freed and another built at the same address, an initializer
+    // replaced or reshaped, gives another signature and drops the caches; an
+    // in-place rewrite of an initializer's bytes is caught when it changes a
+    // sampled word, and invalidate() drops the caches explicitly.
+    static uint64_t mix(uint64_t h, uint64_t v) {
+        h ^= v + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+        return h * 0x100000001b3ull;
+    }
+    static uint64_t mix_str(uint64_t h, const std::string& s) {
+        for (unsigned char c : s) h = mix(h, c);
+        return mix(h, s.size());
+    }
+    static uint64_t graph_signature(const Graph& g) {
+        uint64_t h = 0xcbf29ce484222325ull;
+        for (const auto& n : g.nodes()) {
+            h = mix_str(h, n->op_type());
+            for (const auto& i : n->inputs()) h = mix_str(h, i);
+        }
+        // initializers in name order (the map's order is unspecified)
+        std::vector<const std::pair<const std::string, Tensor>*> inits;
+        for (const auto& kv : g.initializers()) inits.push_back(&kv);
+        std::sort(inits.begin(), inits.end(), [](auto* a, auto* b) { return a->first < b->first; });
+        for (const auto* kv : inits) {
+            const Tensor& t = kv->second;
+            h = mix_str(h, kv->first);
+            h = mix(h, reinterpret_cast<uintptr_t>(t.data()));
+            h = mix(h, static_cast<uint64_t>(t.dtype()));
+            for (auto d : t.shape()) h = mix(h, static_cast<uint64_t>(d));
+            const size_t bytes = static_cast<size_t>(pyflame_rt::numel(t.shape())) * dtype_size(t.dtype());
+            const auto* p = static_cast<const unsigned char*>(t.data());
+            if (p && bytes >= 8) {
+                for (size_t k = 0; k < 16; ++k) {
+                    uint64_t w;
+                    std::memcpy(&w, p + (bytes - 8) * k / 15, 8);
+                    h = mix(h, w);
+                }
+            }
+        }
+        return h;
+    }
+
     void bind_graph(const Graph& g) {
-        const size_t sig = g.num_nodes() * 1000003u + g.initializers().size();
+        const uint64_t sig = graph_signature(g);
         if (&g == graph_ && sig == graph_sig_) return;
         reset_caches();
         graph_ = &g;
         graph_sig_ = sig;
     }
+
+public:
+    void invalidate() {
+        std::lock_guard<std::mutex> lock(mu_);
+        reset_caches();
+        graph_ = nullptr;
+        graph_sig_ = 0;
+    }
+
+private:
 
     const Tensor* initializer(const Graph& g, const std::string& name) const {
         auto it = g.initializers().find(name);
@@ -192,7 +266,7 @@ private:
     pfrt_ctx* ctx_ = nullptr;
     std::mutex mu_;
     const Graph* graph_ = nullptr;
-    size_t graph_sig_ = 0;
+    uint64_t graph_sig_ = 0;
     std::unordered_map<std::string, DevBuf> inits_;
     std::unordered_map<std::string, pfrt_fweight*> fweights_;
     std::unordered_map<std::string, pfrt_qweight*> qweights_;
@@ -559,18 +633,21 @@ void CudaBackend::Impl::run_quantize(const Graph& g, const Node& n) {
 }
 
 // ----------------------------------------------------------------- execute
-std::vector<Tensor> CudaBackend::Impl::execute(const Graph& graph, const std::unordered_map<std::string, Tensor>& feeds,
-                                               const std::vector<std::string>& output_names) {
-    std::lock_guard<std::mutex> lock(mu_);
+void CudaBackend::Impl::run_graph(const Graph& graph, const std::unordered_map<std::string, Tensor>& feeds,
+                                  const std::vector<std::string>& output_names, std::vector<std::string>& names,
+                                  std::vector<DevTensor>& outs) {
     bind_graph(graph);
     vals_.clear();
-    // Inputs to the device.
+    // Inputs to the device: large ones through the pinned staging ring (the
+    // copy returns once the host bytes are read; the DMA runs in stream order).
     for (const auto& [name, t] : feeds) {
         DevTensor d;
         d.shape = t.shape();
         d.dtype = t.dtype();
         d.ptr = device_alloc("in:" + name, t.size_bytes());
-        check(pfrt_memcpy_h2d(ctx_, d.ptr, t.data(), t.size_bytes(), nullptr), nullptr);
+        check(t.size_bytes() >= kStagedBytes ? pfrt_memcpy_h2d_staged(ctx_, d.ptr, t.data(), t.size_bytes(), nullptr)
+                                             : pfrt_memcpy_h2d(ctx_, d.ptr, t.data(), t.size_bytes(), nullptr),
+              nullptr);
         vals_[name] = d;
     }
     const auto order = graph.topological_sort();
@@ -613,27 +690,41 @@ std::vector<Tensor> CudaBackend::Impl::execute(const Graph& graph, const std::un
             throw BackendError(e.what(), n.name());
         }
     }
-    // Outputs back to the host.
-    std::vector<std::string> names = output_names;
+    names = output_names;
     if (names.empty())
         for (const auto& o : graph.outputs()) names.push_back(o.name);
-    std::vector<Tensor> results;
-    results.reserve(names.size());
+    outs.clear();
     for (const auto& name : names) {
         auto it = vals_.find(name);
-        DevTensor d;
         if (it != vals_.end()) {
-            d = it->second;
+            outs.push_back(it->second);
         } else if (initializer(graph, name)) {
-            results.push_back(initializer(graph, name)->clone());
-            continue;
+            outs.push_back(DevTensor{});  // an initializer: the caller clones it
         } else {
             throw BackendError("Output tensor '" + name + "' not found");
         }
-        Tensor out(d.shape, d.dtype);
-        if (d.bytes()) check(pfrt_memcpy_d2h(ctx_, out.data(), d.ptr, d.bytes(), nullptr), nullptr);
-        results.push_back(std::move(out));
     }
+}
+
+std::vector<Tensor> CudaBackend::Impl::execute(const Graph& graph, const std::unordered_map<std::string, Tensor>& feeds,
+                                               const std::vector<std::string>& output_names) {
+    std::lock_guard<std::mutex> lock(mu_);
+    std::vector<std::string> names;
+    std::vector<DevTensor> outs;
+    run_graph(graph, feeds, output_names, names, outs);
+    // The host Tensors are allocated (and zero-filled by the Tensor
+    // constructor) while the device runs the graph.
+    std::vector<Tensor> results;
+    results.reserve(names.size());
+    for (size_t i = 0; i < names.size(); ++i) {
+        if (!outs[i].ptr && initializer(graph, names[i])) {
+            results.push_back(initializer(graph, names[i])->clone());
+            continue;
+        }
+        results.emplace_back(outs[i].shape, outs[i].dtype);
+    }
+    for (size_t i = 0; i < names.size(); ++i)
+        if (outs[i].ptr) fetch(outs[i], results[i].data());
     check(pfrt_ctx_check(ctx_, nullptr), nullptr);
     return results;
 }
@@ -808,8 +899,98 @@ CudaBackend::PrepareStats CudaBackend::Impl::prepare(const Graph& g) {
     return out;
 }
 
+// ----------------------------------------------------------------- batch split
+std::vector<std::pair<int64_t, int64_t>> batch_split_plan(const Graph& graph,
+                                                          const std::unordered_map<std::string, Tensor>& feeds,
+                                                          int parts, int64_t min_rows) {
+    std::vector<std::pair<int64_t, int64_t>> none;
+    if (parts <= 1 || graph.inputs().empty()) return none;
+    int64_t M = -1;
+    for (const auto& in : graph.inputs()) {
+        auto it = feeds.find(in.name);
+        if (it == feeds.end() || it->second.ndim() != 2) return none;
+        const int64_t m = it->second.shape()[0];
+        if (M >= 0 && m != M) return none;
+        M = m;
+    }
+    if (M < static_cast<int64_t>(parts) * std::max<int64_t>(1, min_rows)) return none;
+    auto is_init = [&](const std::string& name) { return graph.initializers().count(name) != 0; };
+    auto row_vector = [&](const std::string& name) {
+        const Tensor& t = graph.initializers().at(name);
+        return t.ndim() <= 1 || (t.ndim() == 2 && t.shape()[0] == 1);
+    };
+    for (const auto& node : graph.nodes()) {
+        const Node& n = *node;
+        const std::string& op = n.op_type();
+        const auto& in = n.inputs();
+        if (op == "Gemm") {
+            if (in.size() < 2 || n.get_attr<int64_t>("transA", 0) != 0 || is_init(in[0]) || !is_init(in[1])) return none;
+            const Tensor& B = graph.initializers().at(in[1]);
+            if (B.ndim() != 2) return none;
+            const int64_t N = n.get_attr<int64_t>("transB", 0) ? B.shape()[0] : B.shape()[1];
+            if (in.size() > 2 && !in[2].empty()) {
+                if (!is_init(in[2])) return none;
+                const int64_t c = graph.initializers().at(in[2]).num_elements();
+                if (c <= 0 || N % c != 0) return none;  // C[(m*N + n) % c] depends on n only
+            }
+        } else if (op == "MatMul" || op == "QuantizedMatMul") {
+            if (in.size() < 2 || is_init(in[0]) || !is_init(in[1])) return none;
+        } else if (op == "SparseMatMul") {
+            if (in.size() < 4 || is_init(in[0]) || !is_init(in[1]) || !is_init(in[2]) || !is_init(in[3])) return none;
+        } else if (op == "Add" || op == "FusedAddRelu") {
+            if (in.size() != 2) return none;
+            int acts = 0;
+            for (const auto& x : in) {
+                if (!is_init(x)) ++acts;
+                else if (!row_vector(x)) return none;
+            }
+            if (acts == 0) return none;
+        } else if (op == "Relu" || op == "Quantize") {
+            if (in.empty() || is_init(in[0])) return none;
+        } else {
+            return none;
+        }
+    }
+    for (const auto& o : graph.outputs())
+        if (is_init(o.name)) return none;
+    std::vector<std::pair<int64_t, int64_t>> plan;
+    for (int p = 0; p < parts; ++p) plan.emplace_back(M * p / parts, M * (p + 1) / parts);
+    return plan;
+}
+
+std::vector<int> parse_cuda_devices(const std::string& spec) {
+    std::string list;
+    if (spec == "cuda") {
+        const char* env = std::getenv("PFRT_CUDA_DEVICES");
+        if (!env || !*env) return {0};
+        list = env;
+    } else if (spec.rfind("cuda:", 0) == 0) {
+        list = spec.substr(5);
+    } else {
+        throw BackendError("not a CUDA device: '" + spec + "' (expected cuda, cuda:<n> or cuda:<n>,<m>,...)");
+    }
+    std::vector<int> out;
+    size_t pos = 0;
+    while (pos <= list.size()) {
+        const size_t comma = list.find(',', pos);
+        const std::string item = list.substr(pos, comma == std::string::npos ? std::string::npos : comma - pos);
+        if (item.empty() || item.find_first_not_of("0123456789") != std::string::npos || item.size() > 4)
+            throw BackendError("bad CUDA device list '" + list + "' in '" + spec + "'");
+        out.push_back(std::stoi(item));
+        if (comma == std::string::npos) break;
+        pos = comma + 1;
+    }
+    return out;
+}
+
 // ----------------------------------------------------------------- public
-CudaBackend::CudaBackend(int device) : impl_(std::make_unique<Impl>(device)) {}
+CudaBackend::CudaBackend(int device) : CudaBackend(std::vector<int>{device}) {}
+
+CudaBackend::CudaBackend(const std::vector<int>& devices) : devices_(devices) {
+    if (devices_.empty()) throw BackendError("cuda backend: no device given");
+    for (int d : devices_) impls_.push_back(std::make_unique<Impl>(d));
+}
+
 CudaBackend::~CudaBackend() = default;
 
 const std::string& CudaBackend::name() const {
@@ -827,13 +1008,87 @@ std::vector<std::string> CudaBackend::get_supported_ops() const { return support
 std::vector<Tensor> CudaBackend::execute(const Graph& graph, const std::unordered_map<std::string, Tensor>& input_feed,
                                          const std::vector<std::string>& output_names) {
     validate_inputs(graph, input_feed);
-    return impl_->execute(graph, input_feed, output_names);
+    const int parts = static_cast<int>(impls_.size());
+    if (parts == 1) return impls_[0]->execute(graph, input_feed, output_names);
+    int64_t min_rows = 256;
+    if (const char* v = std::getenv("PFRT_SPLIT_MIN_ROWS"); v && *v) min_rows = std::max<int64_t>(1, std::atoll(v));
+    const auto plan = batch_split_plan(graph, input_feed, parts, min_rows);
+    if (plan.empty()) return impls_[0]->execute(graph, input_feed, output_names);
+
+    std::vector<std::unique_lock<std::mutex>> locks;
+    for (auto& im : impls_) locks.emplace_back(im->mutex());
+    std::vector<std::vector<std::string>> names(parts);
+    std::vector<std::vector<DevTensor>> outs(parts);
+    std::vector<std::exception_ptr> errs(parts);
+    auto on_all = [&](auto&& fn) {
+        std::vector<std::thread> ts;
+        for (int p = 0; p < parts; ++p)
+            ts.emplace_back([&, p] {
+                try {
+                    fn(p);
+                } catch (...) {
+                    errs[p] = std::current_exception();
+                }
+            });
+        for (auto& t : ts) t.join();
+        for (auto& e : errs)
+            if (e) std::rethrow_exception(e);
+    };
+    // Each device: its rows of every input (views), the whole graph enqueued.
+    on_all([&](int p) {
+        const auto [m0, m1] = plan[p];
+        std::unordered_map<std::string, Tensor> feeds;
+        for (const auto& [name, t] : input_feed) {
+            const size_t row_bytes = t.size_bytes() / static_cast<size_t>(t.shape()[0]);
+            auto* base = static_cast<char*>(const_cast<void*>(t.data())) + static_cast<size_t>(m0) * row_bytes;
+            feeds.emplace(name, Tensor(base, {m1 - m0, t.shape()[1]}, t.dtype()));
+        }
+        impls_[p]->run_graph(graph, feeds, output_names, names[p], outs[p]);
+    });
+    // Output Tensors of the whole batch, then every device copies its rows in.
+    std::vector<Tensor> results;
+    for (size_t i = 0; i < outs[0].size(); ++i) {
+        std::vector<int64_t> shape = outs[0][i].shape;
+        if (shape.empty()) throw BackendError("batch split: scalar output '" + names[0][i] + "'");
+        int64_t rows = 0;
+        for (int p = 0; p < parts; ++p) rows += outs[p][i].shape.empty() ? 0 : outs[p][i].shape[0];
+        shape[0] = rows;
+        results.emplace_back(shape, outs[0][i].dtype);
+    }
+    on_all([&](int p) {
+        for (size_t i = 0; i < outs[p].size(); ++i) {
+            const size_t row_bytes = results[i].size_bytes() / static_cast<size_t>(std::max<int64_t>(1, results[i].shape()[0]));
+            impls_[p]->fetch(outs[p][i], static_cast<char*>(results[i].data()) + static_cast<size_t>(plan[p].first) * row_bytes);
+        }
+        impls_[p]->check_device();
+    });
+    return results;
 }
 
-int CudaBackend::device() const { return impl_->device_; }
+int CudaBackend::device() const { return devices_[0]; }
 
-CudaBackend::PrepareStats CudaBackend::prepare(const Graph& graph) { return impl_->prepare(graph); }
+const std::vector<int>& CudaBackend::devices() const { return devices_; }
+
+void CudaBackend::invalidate() {
+    for (auto& im : impls_) im->invalidate();
+}
+
+CudaBackend::PrepareStats CudaBackend::prepare(const Graph& graph) {
+    CudaBackend::PrepareStats total;
+    for (auto& im : impls_) {
+        const auto st = im->prepare(graph);
+        total.bytes = st.bytes;
+        total.seconds += st.seconds;
+        total.build_seconds += st.build_seconds;
+        total.fault_seconds += st.fault_seconds;
+    }
+    return total;
+}
 
 std::unique_ptr<Backend> make_cuda_backend(int device) { return std::make_unique<CudaBackend>(device); }
+
+std::unique_ptr<Backend> make_cuda_backend(const std::string& device_spec) {
+    return std::make_unique<CudaBackend>(parse_cuda_devices(device_spec));
+}
 
 }  // namespace pyflame_rt

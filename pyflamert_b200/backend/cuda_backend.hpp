@@ -45,6 +45,15 @@ namespace pyflame_rt {
 class CudaBackend : public Backend {
 public:
     explicit CudaBackend(int device = 0);
+    /// A backend over several GPUs of this process.  execute() splits a batch
+    /// over them by rows when the graph allows it (batch_split_plan: every
+    /// node is row-separable and each device gets at least
+    /// PFRT_SPLIT_MIN_ROWS rows, default 256): each device runs the graph on
+    /// its contiguous slice of every input (a view, no host copy) with its
+    /// own copy of the weights, and copies its rows of every output straight
+    /// into the output Tensors.  There is no collective: the rows are
+    /// independent.  Other graphs run on the first device.
+    explicit CudaBackend(const std::vector<int>& devices);
     ~CudaBackend() override;
 
     CudaBackend(const CudaBackend&) = delete;
@@ -58,7 +67,15 @@ public:
                                 const std::unordered_map<std::string, Tensor>& input_feed,
                                 const std::vector<std::string>& output_names = {}) override;
 
-    int device() const;
+    int device() const;  // the first device
+    const std::vector<int>& devices() const;
+
+    /// Drops every prepared initializer (the next execute() prepares them
+    /// again).  The caches are keyed on a signature of the graph (its nodes,
+    /// and each initializer's name, address, dtype, shape and sampled bytes),
+    /// so a different or changed graph is noticed by itself; call this after
+    /// rewriting an initializer's data in place.
+    void invalidate();
 
     /// Uploads and prepares every initializer the graph's nodes consume (the
     /// device forms of Gemm/MatMul/QuantizedMatMul weights, CSR arrays,
@@ -79,11 +96,33 @@ public:
 
 private:
     class Impl;
-    std::unique_ptr<Impl> impl_;
+    std::vector<int> devices_;
+    std::vector<std::unique_ptr<Impl>> impls_;
 };
 
-/// Factory for the session seam (InferenceSession::select_backend): a CudaBackend on
-/// the given device ordinal.
+/// Factories for the session seam (InferenceSession::select_backend): a
+/// CudaBackend on the given device ordinal, or on the devices a
+/// SessionOptions.device string names (parse_cuda_devices).
 std::unique_ptr<Backend> make_cuda_backend(int device = 0);
+std::unique_ptr<Backend> make_cuda_backend(const std::string& device_spec);
+
+/// Device ordinals of a device string: "cuda" -> the list in the environment
+/// variable PFRT_CUDA_DEVICES ("0,1,2,3") if it is set, else {0};
+/// "cuda:<n>" -> {n}; "cuda:<n>,<m>,..." -> that list.  Throws
+/// BackendError for anything else.
+std::vector<int> parse_cuda_devices(const std::string& device_spec);
+
+/// Row ranges [m0, m1) of a batch split of the feeds over `parts` devices, or
+/// an empty vector when the graph cannot be split by rows: every graph input
+/// must be fed a 2-D tensor with the same row count M >= parts * min_rows,
+/// every node must compute each output row from the same row of its
+/// activation inputs only (Gemm with transA = 0 and a C that broadcasts per
+/// row, MatMul / QuantizedMatMul / SparseMatMul on initializer weights,
+/// elementwise Add / FusedAddRelu / Relu / Quantize against same-shape
+/// activations or row-vector or scalar initializers), and no requested output
+/// may be an initializer.  Host-only (no device needed).
+std::vector<std::pair<int64_t, int64_t>> batch_split_plan(const Graph& graph,
+                                                          const std::unordered_map<std::string, Tensor>& feeds,
+                                                          int parts, int64_t min_rows);
 
 }  // namespace pyflame_rt

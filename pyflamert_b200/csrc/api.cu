@@ -188,6 +188,7 @@ pfrt_status pfrt_ctx_destroy(pfrt_ctx* ctx) {
     if (!ctx) return PFRT_OK;
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    staging_release(ctx);
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->io) cudaFree(ctx->io);
     if (ctx->d_err) cudaFree(ctx->d_err);

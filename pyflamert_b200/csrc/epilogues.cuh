@@ -286,6 +286,8 @@ struct QEpi {
     }
 };
 
+constexpr int kMaxPeerOut = 7;
+
 struct FEpi {
     int M, N;
     float alpha, beta;
@@ -296,6 +298,11 @@ struct FEpi {
     int out_mode;     // kOutF32 or kOutPartial
     float* partial;   // [splits][M][N]
     int vec_ok;
+    // Further copies of the output written by the same stores: other GPUs'
+    // outputs mapped into this process (the sharded SpMM's all-gather), same
+    // row stride and offsets as `out`.
+    int n_peer_out;
+    float* peer_out[kMaxPeerOut];
 
     __device__ __forceinline__ float finalize(int row, int n, float acc) const {
         float y = __fmul_rn(alpha, acc);
@@ -318,8 +325,8 @@ struct FEpi {
     }
 
     template <int W>
-    __device__ __forceinline__ void write(int row, int col0, const float (&y)[W]) const {
-        float* d = out + static_cast<int64_t>(row) * ldo + col0;
+    __device__ __forceinline__ void write_to(float* base, int row, int col0, const float (&y)[W]) const {
+        float* d = base + static_cast<int64_t>(row) * ldo + col0;
         if (col0 + W <= N && vec_ok) {
 #pragma unroll
             for (int j = 0; j < W; j += 4)
@@ -329,6 +336,12 @@ struct FEpi {
             for (int j = 0; j < W; ++j)
                 if (col0 + j < N) d[j] = y[j];
         }
+    }
+
+    template <int W>
+    __device__ __forceinline__ void write(int row, int col0, const float (&y)[W]) const {
+        write_to<W>(out, row, col0, y);
+        for (int i = 0; i < n_peer_out; ++i) write_to<W>(peer_out[i], row, col0, y);
     }
 
     // Final epilogue from global parameters (split-K reduction, empty K).

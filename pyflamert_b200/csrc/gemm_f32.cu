@@ -130,8 +130,9 @@ pfrt_status launch_split(const float* src, int64_t rows, int64_t K, int64_t ld, 
 // Runs the GEMM on prepared K-major hi/lo operands.
 pfrt_status run_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad, const CUtensorMap& tmAh,
                     const CUtensorMap& tmAl, const CUtensorMap& tmBh, const CUtensorMap& tmBl,
-                    float alpha, float beta, const float* c, int64_t c_len, float* y,
-                    void* scratch_tail, size_t tail_bytes, cudaStream_t s, int max_splits = 1 << 20) {
+                    float alpha, float beta, const float* c, int64_t c_len, float* y, int64_t ldy,
+                    void* scratch_tail, size_t tail_bytes, cudaStream_t s, int max_splits = 1 << 20,
+                    float* const* peer_y = nullptr, int n_peer_y = 0) {
     using Cfg = GemmCfg<KIND_TF32X3, kF32BN, kF32Stages>;
     const int64_t mblk = ceil_div(M, 128), nblk = ceil_div(N, kF32BN);
     const int64_t tiles = mblk * nblk;
@@ -154,9 +155,14 @@ pfrt_status run_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad, const CUt
     e.C = (c != nullptr && c_len > 0) ? c : nullptr;
     e.c_len = c_len;
     e.out = y;
-    e.ldo = N;
+    e.ldo = ldy;
     e.out_mode = kOutF32;
-    e.vec_ok = ((reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (N % 4) == 0) ? 1 : 0;
+    e.vec_ok = ((reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (N % 4) == 0 && (ldy % 4) == 0) ? 1 : 0;
+    e.n_peer_out = std::min(n_peer_y, kMaxPeerOut);
+    for (int i = 0; i < e.n_peer_out; ++i) {
+        e.peer_out[i] = peer_y[i];
+        if ((reinterpret_cast<uintptr_t>(peer_y[i]) & 15u) != 0) e.vec_ok = 0;
+    }
     FEpi eg = e;
     if (splits > 1) {
         eg.out_mode = kOutPartial;
@@ -289,6 +295,32 @@ pfrt_status fweight_from_device_split(pfrt_ctx* ctx, int64_t N, int64_t K, float
     return PFRT_OK;
 }
 
+pfrt_status gemm_f32_strided(pfrt_ctx* ctx, int64_t M, const float* a, int64_t lda, const pfrt_fweight* b,
+                             float* y, int64_t ldy, cudaStream_t s, float* const* peer_y, int n_peer_y) {
+    if (n_peer_y > kMaxPeerOut) return fail(PFRT_ERR_UNSUPPORTED, "Gemm: too many output copies");
+    const int64_t N = b->N, K = b->K;
+    pfrt_status st = check_common(M, N, K, a, y);
+    if (st) return st;
+    if (M == 0) return PFRT_OK;
+    if (lda < K || ldy < N) return fail(PFRT_ERR_INVALID_ARGUMENT, "Gemm: row stride too small");
+    const size_t part_bytes = align_up(sizeof(float) * M * b->Kpad, 256);
+    const size_t tail = splitk_bytes(ctx, M, N, b->Kpad);
+    void* scr = nullptr;
+    st = scratch(ctx, 2 * part_bytes + tail, &scr);
+    if (st) return st;
+    float* ahi = static_cast<float*>(scr);
+    float* alo = reinterpret_cast<float*>(static_cast<uint8_t*>(scr) + part_bytes);
+    st = launch_split(a, M, K, lda, 0, ahi, alo, b->Kpad, s);
+    if (st) return st;
+    CUtensorMap tah, tal;
+    st = make_tmap_2d(&tah, ahi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, b->Kpad, M, b->Kpad * 4, 32, 128);
+    if (st == PFRT_OK)
+        st = make_tmap_2d(&tal, alo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, b->Kpad, M, b->Kpad * 4, 32, 128);
+    if (st) return st;
+    return run_f32(ctx, M, N, b->Kpad, tah, tal, b->tm_hi, b->tm_lo, 1.0f, 0.0f, nullptr, 0, y, ldy,
+                   static_cast<uint8_t*>(scr) + 2 * part_bytes, tail, s, 1 << 20, peer_y, n_peer_y);
+}
+
 }  // namespace pfrt
 
 using namespace pfrt;
@@ -375,7 +407,7 @@ pfrt_status pfrt_gemm_f32(pfrt_ctx* ctx, int64_t M, int trans_a, float alpha, co
     if (st == PFRT_OK)
         st = make_tmap_2d(&tal, alo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, b->Kpad, M, b->Kpad * 4, 32, 128);
     if (st) return st;
-    return run_f32(ctx, M, N, b->Kpad, tah, tal, b->tm_hi, b->tm_lo, alpha, beta, c, c_len, y,
+    return run_f32(ctx, M, N, b->Kpad, tah, tal, b->tm_hi, b->tm_lo, alpha, beta, c, c_len, y, N,
                    static_cast<uint8_t*>(scr) + 2 * part_bytes, tail, s);
 }
 
@@ -413,11 +445,11 @@ pfrt_status pfrt_gemm_f32_dense(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, 
     if (!st) st = make_tmap_2d(&tbh, bhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Kpad, N, Kpad * 4, 32, kF32BN);
     if (!st) st = make_tmap_2d(&tbl, blo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Kpad, N, Kpad * 4, 32, kF32BN);
     if (st) return st;
-    return run_f32(ctx, M, N, Kpad, tah, tal, tbh, tbl, alpha, beta, c, c_len, y,
+    return run_f32(ctx, M, N, Kpad, tah, tal, tbh, tbl, alpha, beta, c, c_len, y, N,
                    base + 2 * pa + 2 * pb, tail, s);
 }
 
-// Same result as pfrt_gemm_f32, for callers that must not allocate device
+// The Gemm of pfrt_gemm_f32, for callers that must not allocate device
 // memory during a call.  The per-call split of A goes to the fixed 16 MiB
 // array above instead of the context's scratch arena, so the call makes no
 // cudaMalloc/cudaFree and no other allocation.  Limit: M * Kpad <= 2^21
@@ -425,7 +457,10 @@ pfrt_status pfrt_gemm_f32_dense(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t K, 
 // call on a device does a one-time set-up (the lookup of the array's device
 // address), so that first call should come before any stream capture.  All
 // calls share the array, so calls that overlap on the GPU (other streams,
-// other threads) race on it; split-K is not available here.
+// other threads) race on it.  K is never split across CTAs here (there is no
+// room for split-K partial sums, and PFRT_GEMM_SPLITS is ignored): the result
+// agrees with pfrt_gemm_f32 within fp32 tolerance, not bit for bit, and
+// shapes whose tiles leave SMs idle run slower than through pfrt_gemm_f32.
 pfrt_status pfrt_gemm_f32_noalloc(pfrt_ctx* ctx, int64_t M, int trans_a, float alpha, const float* a,
                                   const pfrt_fweight* b, float beta, const float* c, int64_t c_len,
                                   float* y, pfrt_stream stream) {
@@ -442,8 +477,6 @@ pfrt_status pfrt_gemm_f32_noalloc(pfrt_ctx* ctx, int64_t M, int trans_a, float a
                     "pfrt_gemm_f32_noalloc: M * Kpad = " + std::to_string(M) + " * " +
                         std::to_string(b->Kpad) + " exceeds the fixed scratch limit of " +
                         std::to_string(kNoAllocMaxElems) + " elements; use pfrt_gemm_f32");
-    if (env_int("PFRT_GEMM_SPLITS", 1) > 1)
-        return fail(PFRT_ERR_UNSUPPORTED, "pfrt_gemm_f32_noalloc: split-K (PFRT_GEMM_SPLITS) needs extra scratch");
     void* base = nullptr;
     st = noalloc_scratch(ctx->device, &base);
     if (st) return st;
@@ -460,7 +493,7 @@ pfrt_status pfrt_gemm_f32_noalloc(pfrt_ctx* ctx, int64_t M, int trans_a, float a
     if (st == PFRT_OK)
         st = make_tmap_2d(&tal, alo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, b->Kpad, M, b->Kpad * 4, 32, 128);
     if (st) return st;
-    return run_f32(ctx, M, N, b->Kpad, tah, tal, b->tm_hi, b->tm_lo, alpha, beta, c, c_len, y,
+    return run_f32(ctx, M, N, b->Kpad, tah, tal, b->tm_hi, b->tm_lo, alpha, beta, c, c_len, y, N,
                    nullptr, 0, s, /*max_splits=*/1);
 }
 

@@ -11,6 +11,10 @@
 
 #include "pfrt_cuda.h"
 
+namespace pfrt {
+struct StagingRing;  // pinned host chunks for pageable copies (staging.cu)
+}
+
 struct pfrt_ctx {
     int device = 0;
     int num_sms = 0;
@@ -21,6 +25,7 @@ struct pfrt_ctx {
     size_t scratch_cap = 0;
     void* io = nullptr;         // grow-only device copies of host-buffer calls' inputs and outputs
     size_t io_cap = 0;
+    pfrt::StagingRing* staging = nullptr;  // created by the first staged copy
 };
 
 namespace pfrt {
@@ -41,6 +46,9 @@ pfrt_status cuda_fail(cudaError_t e, const char* what);
         cudaError_t e__ = cudaGetLastError();               \
         if (e__ != cudaSuccess) return ::pfrt::cuda_fail(e__, what); \
     } while (0)
+
+// Frees the context's pinned staging ring (staging.cu), after its copies.
+void staging_release(pfrt_ctx* ctx);
 
 // Makes the context's device current for the calling thread.
 pfrt_status enter(pfrt_ctx* ctx);
@@ -74,6 +82,16 @@ pfrt_status make_tmap_2d_plain(CUtensorMap* tm, const void* base, CUtensorMapDat
 // ownership of both buffers.
 pfrt_status fweight_from_device_split(pfrt_ctx* ctx, int64_t N, int64_t K, float* hi, float* lo,
                                       pfrt_fweight** out);
+
+// Y[M, N] = A[M, K] * B^T on a prepared weight (alpha 1, beta 0, no C), with
+// row strides lda (>= K) and ldy (>= N); the context's device is current and
+// `s` the stream.  Used by the SpMM's dense path, which may write a column
+// block of a wider output.  The epilogue also stores every output value into
+// the n_peer_y (at most 7) further outputs peer_y[i], same offsets and row
+// stride (other GPUs' outputs mapped into this process).
+pfrt_status gemm_f32_strided(pfrt_ctx* ctx, int64_t M, const float* a, int64_t lda, const pfrt_fweight* b,
+                             float* y, int64_t ldy, cudaStream_t s, float* const* peer_y = nullptr,
+                             int n_peer_y = 0);
 
 // Fills `a` with the programmatic-stream-serialization launch attribute
 // (the kernel may start while the previous kernel on the stream finishes;

@@ -221,6 +221,7 @@ struct PeerArgs {
     float* y;
     uint64_t* recv[PFRT_MAX_PEERS];
     uint32_t* state;
+    uint64_t wait_ns;  // limit of each wait on another rank
 };
 
 template <int R, int THREADS, bool CHECK, bool PEER = false>
@@ -369,7 +370,7 @@ __global__ void __launch_bounds__(THREADS)
                     break;
                 }
                 if ((it & 255u) == 255u &&
-                    (ld_relaxed_gpu(pa.state + 3) != 0 || global_timer_ns() - t0 > kWaitLimitNs)) {
+                    (ld_relaxed_gpu(pa.state + 3) != 0 || global_timer_ns() - t0 > pa.wait_ns)) {
                     ok = false;
                     break;
                 }
@@ -388,6 +389,162 @@ __global__ void __launch_bounds__(THREADS)
             }
         }
     }
+}
+
+// M > 1 all-gather of the output-channel-sharded SpMM (pfrt_spmm_allgather).
+// Each rank writes its column block [rank*ns, rank*ns + ns) of Y into its own
+// gathered output y [M][ldy]; the block must also land in every other rank's
+// y.  Two ways, chosen per rank and per call:
+//   copy:  after the shard's SpMM, peer_push_kernel stores the block into
+//          every other rank's y over NVLink;
+//   fused: the shard's SpMM is the dense-path GEMM, whose epilogue stores each
+//          output tile into every rank's y as it is computed (FEpi's
+//          peer_out), so the transfer overlaps the GEMM; peer_ready_kernel runs
+//          before the GEMM and peer_push_kernel after it only signals.
+// Signal words of rank p (sig[p], mapped by every rank):
+//   [kSigReady + q]   the last call at which rank q's y was free (written
+//                     by q into every other rank's words);
+//   [kSigDone + par]  other ranks that have finished writing p's y in the
+//                     calls of parity par.
+// Call e = state[1] + 1.  "Ready": this rank declares its y free for e (its
+// stream has completed everything before this kernel, the consumers of call
+// e - 1's output included) by a release store into every other rank's words,
+// then waits until every other rank has declared its own; only then may it
+// write into their outputs.  "Done": after its copies (each block: a
+// system-scope fence, then one count on this rank's state[2]), the last
+// block adds one to every other rank's done count and waits until this
+// rank's count reaches world - 1; it resets the count (no rank can add to it
+// again before this rank's call e + 2 declares its y free) and publishes e.
+// One count per rank and call, whatever each rank's grid, so ranks may take
+// different ways.  Waits give up after wait_ns or once state[3] is set,
+// which they then set.
+constexpr int kSigReady = 0;
+constexpr int kSigDone = PFRT_MAX_PEERS;
+static_assert(kSigDone + 2 <= PFRT_PEER_SIG_WORDS, "signal words");
+constexpr int kPushThreads = 512;
+
+struct PushArgs {
+    int rank;
+    int world;
+    int64_t M, ns, ldy;
+    int vec;                         // float4 copies (ns and ldy multiples of 4)
+    int copy;                        // 0: the block is already in every output (fused)
+    int ready_done;                  // 1: peer_ready_kernel ran for this call
+    float* y[PFRT_MAX_PEERS];
+    uint32_t* sig[PFRT_MAX_PEERS];
+    uint32_t* state;
+    uint64_t wait_ns;
+};
+
+// Waits until *p reaches `target` (modulo 2^32).  Relaxed system-scope polls,
+// then one acquire fence.  False when the wait runs out or *abort is set.
+__device__ __forceinline__ bool wait_word_reached(const uint32_t* p, uint32_t target, const uint32_t* abort,
+                                                  uint64_t t0, uint64_t limit_ns) {
+    for (uint32_t it = 0;; ++it) {
+        uint32_t v;
+        asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        if (static_cast<int32_t>(v - target) >= 0) {
+            asm volatile("fence.acq_rel.sys;" ::: "memory");
+            return true;
+        }
+        if ((it & 63u) == 63u) {
+            if (ld_relaxed_gpu(abort) != 0) return false;
+            if (global_timer_ns() - t0 > limit_ns) return false;
+        }
+        __nanosleep(32);
+    }
+}
+
+// The "ready" exchange of call e by threads [0, world) of one block; returns
+// false (on every thread of the block) when a wait gave up.
+__device__ __forceinline__ bool peer_ready(const PushArgs& a, uint32_t e, bool declare, int* s_fail) {
+    const int tid = threadIdx.x;
+    const uint64_t t0 = global_timer_ns();
+    if (declare && tid < a.world && tid != a.rank) st_release_sys(a.sig[tid] + kSigReady + a.rank, e);
+    if (tid < a.world && tid != a.rank &&
+        !wait_word_reached(a.sig[a.rank] + kSigReady + tid, e, a.state + 3, t0, a.wait_ns))
+        *s_fail = 1;
+    __syncthreads();
+    return *s_fail == 0;
+}
+
+__global__ void __launch_bounds__(32) peer_ready_kernel(const PushArgs a, int* err) {
+    __shared__ int s_fail;
+    if (threadIdx.x == 0) s_fail = ld_relaxed_gpu(a.state + 3) != 0 ? 1 : 0;
+    __syncthreads();
+    const uint32_t e = ld_relaxed_gpu(a.state + 1) + 1u;
+    if (!peer_ready(a, e, true, &s_fail) && threadIdx.x == 0) {
+        atomicExch(a.state + 3, 1u);
+        report_error(err, kDevWaitTimeout);
+    }
+}
+
+__global__ void __launch_bounds__(kPushThreads) peer_push_kernel(const PushArgs a, int* err) {
+    __shared__ uint32_t s_epoch;
+    __shared__ int s_fail;
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        s_epoch = ld_relaxed_gpu(a.state + 1) + 1u;
+        s_fail = ld_relaxed_gpu(a.state + 3) != 0 ? 1 : 0;
+    }
+    __syncthreads();
+    const uint32_t e = s_epoch;
+    bool ok = s_fail == 0;
+    if (!a.ready_done) ok = peer_ready(a, e, blockIdx.x == 0, &s_fail);
+    if (ok && a.copy) {
+        const int64_t col0 = static_cast<int64_t>(a.rank) * a.ns;
+        const float* src = a.y[a.rank];
+        const int64_t stride = static_cast<int64_t>(gridDim.x) * kPushThreads;
+        if (a.vec) {
+            const int64_t q = a.ns / 4, total = a.M * q;
+            for (int64_t i = static_cast<int64_t>(blockIdx.x) * kPushThreads + tid; i < total; i += stride) {
+                const int64_t m = i / q;
+                const int64_t off = m * a.ldy + col0 + 4 * (i - m * q);
+                const float4 v = *reinterpret_cast<const float4*>(src + off);
+                for (int p = 0; p < a.world; ++p)
+                    if (p != a.rank) *reinterpret_cast<float4*>(a.y[p] + off) = v;
+            }
+        } else {
+            const int64_t total = a.M * a.ns;
+            for (int64_t i = static_cast<int64_t>(blockIdx.x) * kPushThreads + tid; i < total; i += stride) {
+                const int64_t m = i / a.ns;
+                const int64_t off = m * a.ldy + col0 + (i - m * a.ns);
+                const float v = src[off];
+                for (int p = 0; p < a.world; ++p)
+                    if (p != a.rank) a.y[p][off] = v;
+            }
+        }
+    }
+    __syncthreads();
+    if (tid != 0) return;
+    // A block that could not copy says so before it is counted, so the last
+    // block cannot report the output complete.
+    if (!ok) {
+        atomicExch(a.state + 3, 1u);
+        report_error(err, kDevWaitTimeout);
+    }
+    // The block's stores (ordered before this thread by the barrier) before
+    // its count; the last block's fence then covers every block's stores.
+    __threadfence_system();
+    if (atomicAdd(a.state + 2, 1u) != gridDim.x - 1) return;
+    __threadfence_system();
+    uint32_t* mine = a.sig[a.rank];
+    bool fine = ld_relaxed_gpu(a.state + 3) == 0;
+    if (fine) {
+        for (int p = 0; p < a.world; ++p)
+            if (p != a.rank)
+                asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.sig[p] + kSigDone + (e & 1u)) : "memory");
+        fine = wait_word_reached(mine + kSigDone + (e & 1u), static_cast<uint32_t>(a.world - 1), a.state + 3,
+                                 global_timer_ns(), a.wait_ns);
+    }
+    if (!fine) {
+        atomicExch(a.state + 3, 1u);
+        report_error(err, kDevWaitTimeout);
+    } else {
+        atomicExch(mine + kSigDone + (e & 1u), 0u);
+    }
+    a.state[2] = 0u;
+    st_release_gpu(a.state + 1, e);
 }
 
 // Streaming form of the skinny kernel, for a CSR uploaded with
@@ -1227,6 +1384,161 @@ pfrt_status run_spmm_xtile(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x
     return mv == 1 ? launch_xtile<1>(ctx, w, tmx, M, y, ldy, s) : launch_xtile<2>(ctx, w, tmx, M, y, ldy, s);
 }
 
+// The kernel choice of pfrt_spmm on an uploaded CSR (the context's device
+// current, `s` the stream).  M = 1, 2: one warp per row measured fastest;
+// M = 3..8: the streaming kernel (its register pipeline pays once each
+// nonzero feeds 4-8 rows).  M > 8: the tiled CSR kernel (spmm_xtile_kernel)
+// or a 3xTF32 tensor-core GEMM on a dense copy of W made once (8 bytes per
+// element of W, capped at 8 GiB), whichever the cost model below expects to
+// be faster.  Both estimates are fits to B200 measurements (8192^2 and
+// 4096^2 at 90-99 % sparsity, M = 16..256): per 32*MV-row tile of X the
+// tiled kernel costs ~1.25 us (MV = 1) or ~1.1 us (MV = 2) per 256-column
+// chunk plus ~13.3 or ~12.7 ps per nonzero (it is bound by the shared-memory
+// pipe, not by DRAM); the GEMM the larger of reading the dense copy at
+// ~5.5 TB/s and its tensor work, plus ~12 us.  The dense copy wins down to
+// ~6-7 % density at M <= 64; the tiled kernel serves sparser weights.
+// PFRT_SPMM_TILED / PFRT_SPMM_DENSE = 0|1 override the choice.
+// A sharded call's output: when the dense path runs and the block is large
+// enough, its GEMM stores the block into every rank's output as well (after
+// the "ready" exchange), and *fused says so.
+struct ShardOut {
+    const pfrt_peer_set* peers;
+    int64_t ns;
+    bool* fused;
+};
+pfrt_status launch_ready(pfrt_ctx* ctx, const pfrt_peer_set* peers, int64_t M, int64_t ns, cudaStream_t s);
+
+pfrt_status spmm_uploaded(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x, int64_t ldx, float* y,
+                          int64_t ldy, cudaStream_t s, const ShardOut* shard = nullptr) {
+    const char* rowwarp = std::getenv("PFRT_SPMM_ROWWARP");
+    const char* stream_env = std::getenv("PFRT_SPMM_STREAM");
+    const bool want_stream = (stream_env && *stream_env == '1') ||
+                             (M >= 3 && M <= 8 && !(rowwarp && *rowwarp == '1'));
+    if (M >= 1 && M <= 8 && want_stream) return run_spmm_stream(ctx, w, M, x, ldx, y, ldy, s);
+    if (M <= 8)
+        return run_spmm(ctx, M, w->N, w->K, w->nnz, w->indptr, w->indices, w->values, x, ldx, y, ldy, s,
+                        /*validated=*/true);
+    if (!x || !y) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: null pointer");
+    if (ldx < w->K || ldy < w->N) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: row stride too small");
+    const char* tiled_env = std::getenv("PFRT_SPMM_TILED");
+    const char* dense_env = std::getenv("PFRT_SPMM_DENSE");
+    const double Nd = static_cast<double>(w->N), Kd = static_cast<double>(w->K), Md = static_cast<double>(M);
+    const double dense_bytes = 8.0 * Nd * static_cast<double>(align_up(w->K, 32));
+    const bool dense_ok = w->N > 0 && w->K > 0 && dense_bytes <= 8.0 * (1ull << 30);
+    const double mv = (M <= 32) ? 1.0 : 2.0;
+    const double mtiles = std::ceil(Md / (32.0 * mv));
+    const double per_chunk = mv == 1.0 ? 1.25e-6 : 1.1e-6, per_nnz = mv == 1.0 ? 13.3e-12 : 12.7e-12;
+    const double t_tiled = mtiles * (per_chunk * static_cast<double>(w->nchunks) + per_nnz * static_cast<double>(w->nnz)) *
+                           (148.0 / static_cast<double>(ctx->num_sms));
+    const double t_dense = std::max((dense_bytes + 8.0 * Md * Kd) / 5.5e12, 6.0 * Md * Nd * Kd / 6.0e14) + 12.0e-6;
+    bool use_dense = dense_ok && t_dense < t_tiled;
+    if (dense_env && *dense_env) use_dense = dense_ok && *dense_env == '1';
+    if (tiled_env && *tiled_env) use_dense = use_dense && *tiled_env == '0';
+    pfrt_status st;
+    if (use_dense) {
+        st = ensure_dense(ctx, w, s);
+        if (st) return st;
+        // Sharded: the epilogue also writes every other rank's output (the
+        // all-gather overlaps the GEMM), for blocks of 2 MiB and more
+        // (PFRT_PEER_FUSE = 0|1 overrides).
+        const char* fuse_env = std::getenv("PFRT_PEER_FUSE");
+        const bool fuse = shard && shard->peers->world > 1 &&
+                          ((fuse_env && *fuse_env) ? *fuse_env == '1'
+                                                   : 4.0 * Md * static_cast<double>(shard->ns) >= 2.0 * (1 << 20));
+        if (fuse) {
+            const pfrt_peer_set* ps = shard->peers;
+            st = launch_ready(ctx, ps, M, shard->ns, s);
+            if (st) return st;
+            float* py[PFRT_MAX_PEERS];
+            int n = 0;
+            for (int p = 0; p < ps->world; ++p)
+                if (p != ps->rank) py[n++] = ps->y_peer[p] + static_cast<int64_t>(ps->rank) * shard->ns;
+            st = gemm_f32_strided(ctx, M, x, ldx, w->dense, y, ldy, s, py, n);
+            if (st == PFRT_OK) *shard->fused = true;
+            return st;
+        }
+        return gemm_f32_strided(ctx, M, x, ldx, w->dense, y, ldy, s);
+    }
+    if (!(tiled_env && *tiled_env == '0')) {
+        st = run_spmm_xtile(ctx, w, M, x, ldx, y, ldy, s);
+        if (st != PFRT_ERR_UNSUPPORTED) return st;  // else a row too dense for the tile: the wide kernel
+    }
+    return run_spmm(ctx, M, w->N, w->K, w->nnz, w->indptr, w->indices, w->values, x, ldx, y, ldy, s,
+                    /*validated=*/true);
+}
+
+uint64_t peer_wait_ns() {
+    const char* v = std::getenv("PFRT_PEER_WAIT_MS");
+    const long ms = (v && *v) ? std::atol(v) : 0;
+    return ms > 0 ? static_cast<uint64_t>(ms) * 1000000ull : kWaitLimitNs;
+}
+
+// The checks every call on a peer set makes; M > 1 also needs the mapped
+// outputs and signal words.
+pfrt_status check_peer_set(const pfrt_peer_set* peers, int64_t M, const char* who) {
+    const std::string w(who);
+    if (!peers) return fail(PFRT_ERR_INVALID_ARGUMENT, w + ": null peer set");
+    const int world = peers->world, rank = peers->rank;
+    if (world < 1 || world > PFRT_MAX_PEERS || rank < 0 || rank >= world || !peers->state)
+        return fail(PFRT_ERR_INVALID_ARGUMENT, w + ": bad rank/world or null state");
+    if (!peers->y) return fail(PFRT_ERR_INVALID_ARGUMENT, w + ": null output");
+    if (M < 1) return fail(PFRT_ERR_INVALID_ARGUMENT, w + ": M must be >= 1");
+    const int64_t max_m = peers->max_m > 0 ? peers->max_m : 1;
+    if (M > max_m)
+        return fail(PFRT_ERR_INVALID_ARGUMENT,
+                    w + ": M = " + std::to_string(M) + " exceeds the output's max_m = " + std::to_string(max_m));
+    if (M > 1 && world > 1) {
+        for (int p = 0; p < world; ++p)
+            if (!peers->y_peer[p] || !peers->sig[p])
+                return fail(PFRT_ERR_INVALID_ARGUMENT, w + ": M > 1 needs every rank's mapped output and signal words");
+        if (peers->y_peer[rank] != peers->y) return fail(PFRT_ERR_INVALID_ARGUMENT, w + ": y_peer[rank] must be y");
+    }
+    return PFRT_OK;
+}
+
+PushArgs push_args(const pfrt_peer_set* peers, int64_t M, int64_t ns) {
+    const int world = peers->world;
+    PushArgs a{};
+    a.rank = peers->rank;
+    a.world = world;
+    a.M = M;
+    a.ns = ns;
+    a.ldy = static_cast<int64_t>(world) * ns;
+    bool vec = (ns % 4) == 0;
+    for (int p = 0; p < world; ++p) {
+        a.y[p] = peers->y_peer[p];
+        a.sig[p] = peers->sig[p];
+        vec = vec && (reinterpret_cast<uintptr_t>(a.y[p]) & 15u) == 0;
+    }
+    a.vec = vec ? 1 : 0;
+    a.copy = 1;
+    a.state = peers->state;
+    a.wait_ns = peer_wait_ns();
+    return a;
+}
+
+// The "ready" exchange before a GEMM that writes into other ranks' outputs.
+pfrt_status launch_ready(pfrt_ctx* ctx, const pfrt_peer_set* peers, int64_t M, int64_t ns, cudaStream_t s) {
+    peer_ready_kernel<<<1, 32, 0, s>>>(push_args(peers, M, ns), ctx->d_err);
+    PFRT_CHECK_LAUNCH("peer_ready_kernel");
+    return PFRT_OK;
+}
+
+// After the shard's SpMM: copy the block to the other ranks (unless `fused`:
+// the GEMM's epilogue stored it there after launch_ready) and signal.
+pfrt_status launch_push(pfrt_ctx* ctx, const pfrt_peer_set* peers, int64_t M, int64_t ns, cudaStream_t s,
+                        bool fused = false) {
+    if (peers->world == 1 || ns == 0 || M == 0) return PFRT_OK;
+    PushArgs a = push_args(peers, M, ns);
+    a.copy = fused ? 0 : 1;
+    a.ready_done = fused ? 1 : 0;
+    const int64_t items = a.vec ? M * ns / 4 : M * ns;
+    const int blocks = fused ? 1 : static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(256, ceil_div(items, 4 * kPushThreads))));
+    peer_push_kernel<<<blocks, kPushThreads, 0, s>>>(a, ctx->d_err);
+    PFRT_CHECK_LAUNCH("peer_push_kernel");
+    return PFRT_OK;
+}
+
 }  // namespace
 }  // namespace pfrt
 
@@ -1367,57 +1679,7 @@ pfrt_status pfrt_spmm(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* 
     if (st) return st;
     if (!w) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: null CSR");
     if (w->ctx != ctx) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: CSR belongs to another context");
-    // M = 1, 2: one warp per row measured fastest; M = 3..8: the streaming
-    // kernel (its register pipeline pays once each nonzero feeds 4-8 rows).
-    const char* rowwarp = std::getenv("PFRT_SPMM_ROWWARP");
-    const char* stream_env = std::getenv("PFRT_SPMM_STREAM");
-    const bool want_stream = (stream_env && *stream_env == '1') ||
-                             (M >= 3 && M <= 8 && !(rowwarp && *rowwarp == '1'));
-    if (M >= 1 && M <= 8 && want_stream)
-        return run_spmm_stream(ctx, const_cast<pfrt_csr*>(w), M, x, ldx, y, ldy, pick_stream(ctx, stream));
-    if (M <= 8)
-        return run_spmm(ctx, M, w->N, w->K, w->nnz, w->indptr, w->indices, w->values, x, ldx, y, ldy,
-                        pick_stream(ctx, stream), /*validated=*/true);
-    // M > 8: the tiled CSR kernel (spmm_xtile_kernel) or a 3xTF32 tensor-core
-    // GEMM on a dense copy of W made once (8 bytes per element of W, capped
-    // at 8 GiB), whichever the cost model below expects to be faster.  Both
-    // estimates are fits to B200 measurements (8192^2 and 4096^2 at 90-99 %
-    // sparsity, M = 16..256): per 32*MV-row tile of X the tiled kernel costs
-    // ~1.25 us (MV = 1) or ~1.1 us (MV = 2) per 256-column chunk plus ~13.3
-    // or ~12.7 ps per nonzero (it is bound by the shared-memory pipe, not by
-    // DRAM);
-    // the GEMM the larger of reading the dense copy at ~5.5 TB/s and its
-    // tensor work, plus ~12 us.  The dense copy wins down to ~6-7 % density
-    // at M <= 64; the tiled kernel serves sparser weights and strided X or Y.
-    // PFRT_SPMM_TILED / PFRT_SPMM_DENSE = 0|1 override the choice.
-    cudaStream_t s = pick_stream(ctx, stream);
-    pfrt_csr* wm = const_cast<pfrt_csr*>(w);
-    const char* tiled_env = std::getenv("PFRT_SPMM_TILED");
-    const char* dense_env = std::getenv("PFRT_SPMM_DENSE");
-    const double Nd = static_cast<double>(w->N), Kd = static_cast<double>(w->K), Md = static_cast<double>(M);
-    const double dense_bytes = 8.0 * Nd * static_cast<double>(align_up(w->K, 32));
-    const bool packed = ldx == w->K && ldy == w->N && w->N > 0 && w->K > 0;
-    const bool dense_ok = packed && dense_bytes <= 8.0 * (1ull << 30);
-    const double mv = (M <= 32) ? 1.0 : 2.0;
-    const double mtiles = std::ceil(Md / (32.0 * mv));
-    const double per_chunk = mv == 1.0 ? 1.25e-6 : 1.1e-6, per_nnz = mv == 1.0 ? 13.3e-12 : 12.7e-12;
-    const double t_tiled = mtiles * (per_chunk * static_cast<double>(w->nchunks) + per_nnz * static_cast<double>(w->nnz)) *
-                           (148.0 / static_cast<double>(ctx->num_sms));
-    const double t_dense = std::max((dense_bytes + 8.0 * Md * Kd) / 5.5e12, 6.0 * Md * Nd * Kd / 6.0e14) + 12.0e-6;
-    bool use_dense = dense_ok && t_dense < t_tiled;
-    if (dense_env && *dense_env) use_dense = dense_ok && *dense_env == '1';
-    if (tiled_env && *tiled_env) use_dense = use_dense && *tiled_env == '0';
-    if (use_dense) {
-        st = ensure_dense(ctx, wm, s);
-        if (st) return st;
-        return pfrt_gemm_f32(ctx, M, 0, 1.0f, x, wm->dense, 0.0f, nullptr, 0, y, s);
-    }
-    if (!(tiled_env && *tiled_env == '0')) {
-        st = run_spmm_xtile(ctx, wm, M, x, ldx, y, ldy, s);
-        if (st != PFRT_ERR_UNSUPPORTED) return st;  // else a row too dense for the tile: the wide kernel
-    }
-    return run_spmm(ctx, M, w->N, w->K, w->nnz, w->indptr, w->indices, w->values, x, ldx, y, ldy,
-                    pick_stream(ctx, stream), /*validated=*/true);
+    return spmm_uploaded(ctx, const_cast<pfrt_csr*>(w), M, x, ldx, y, ldy, pick_stream(ctx, stream));
 }
 
 pfrt_status pfrt_spmm_allgather(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, const float* x, int64_t ldx,
@@ -1426,17 +1688,29 @@ pfrt_status pfrt_spmm_allgather(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, con
     if (st) return st;
     if (!w || !x || !peers) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: null argument");
     if (w->ctx != ctx) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: CSR belongs to another context");
-    if (M != 1) return fail(PFRT_ERR_UNSUPPORTED, "pfrt_spmm_allgather: only M = 1 is fused");
     if (ldx < w->K) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: row stride too small");
+    st = check_peer_set(peers, M, "pfrt_spmm_allgather");
+    if (st) return st;
     const int world = peers->world, rank = peers->rank;
-    if (world < 1 || world > PFRT_MAX_PEERS || rank < 0 || rank >= world || !peers->state)
-        return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: bad rank/world or null state");
-    if (!peers->y) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: null output");
+    if (peers->ns != 0 && peers->ns != w->N)
+        return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: the peer set's ns differs from the shard's rows");
+    const int64_t ns = w->N, ldy = static_cast<int64_t>(world) * ns;
+    cudaStream_t s = pick_stream(ctx, stream);
+    if (M > 1) {
+        // This rank's column block of Y, straight into its own gathered
+        // output (and, on the fused dense path, into every other rank's).
+        bool fused = false;
+        const ShardOut so{peers, ns, &fused};
+        st = spmm_uploaded(ctx, const_cast<pfrt_csr*>(w), M, x, ldx, peers->y + static_cast<int64_t>(rank) * ns, ldy, s,
+                           world > 1 ? &so : nullptr);
+        if (st) return st;
+        return launch_push(ctx, peers, M, ns, s, fused);
+    }
     for (int p = 0; p < world; ++p)
         if (!peers->recv[p]) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_spmm_allgather: null receive buffer");
     const size_t shm = sizeof(float) * static_cast<size_t>(std::max<int64_t>(w->K, 1));
     if (shm > 96 * 1024 || w->nnz > INT32_MAX - 4096)
-        return fail(PFRT_ERR_UNSUPPORTED, "pfrt_spmm_allgather: K or nnz too large for the fused kernel");
+        return fail(PFRT_ERR_UNSUPPORTED, "pfrt_spmm_allgather: K or nnz too large for the fused M = 1 kernel");
     PeerArgs pa{};
     pa.rank = rank;
     pa.world = world;
@@ -1444,7 +1718,7 @@ pfrt_status pfrt_spmm_allgather(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, con
     pa.y = peers->y;
     for (int p = 0; p < world; ++p) pa.recv[p] = peers->recv[p];
     pa.state = peers->state;
-    cudaStream_t s = pick_stream(ctx, stream);
+    pa.wait_ns = peer_wait_ns();
     auto kern = spmm_row1_kernel<4, 512, false, true>;
     PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(shm)));
     int occ = 1;
@@ -1455,6 +1729,36 @@ pfrt_status pfrt_spmm_allgather(pfrt_ctx* ctx, const pfrt_csr* w, int64_t M, con
     kern<<<blocks, 512, shm, s>>>(w->N, w->K, w->nnz, w->indptr, w->indices, w->values, x, vec_x, nullptr,
                                    ctx->d_err, pa);
     PFRT_CHECK_LAUNCH("spmm_row1_kernel<peer>");
+    return PFRT_OK;
+}
+
+pfrt_status pfrt_peer_allgather(pfrt_ctx* ctx, int64_t M, const pfrt_peer_set* peers, pfrt_stream stream) {
+    pfrt_status st = enter(ctx);
+    if (st) return st;
+    st = check_peer_set(peers, M, "pfrt_peer_allgather");
+    if (st) return st;
+    if (peers->ns <= 0) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_peer_allgather: the peer set's ns must be > 0");
+    for (int p = 0; p < peers->world && peers->world > 1; ++p)
+        if (!peers->y_peer[p] || !peers->sig[p])
+            return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_peer_allgather: needs every rank's mapped output and signal words");
+    return launch_push(ctx, peers, M, peers->ns, pick_stream(ctx, stream));
+}
+
+pfrt_status pfrt_peer_reset(pfrt_ctx* ctx, const pfrt_peer_set* peers, pfrt_stream stream) {
+    pfrt_status st = enter(ctx);
+    if (st) return st;
+    if (!peers || !peers->state) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_peer_reset: null argument");
+    const int world = peers->world, rank = peers->rank;
+    if (world < 1 || world > PFRT_MAX_PEERS || rank < 0 || rank >= world)
+        return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_peer_reset: bad rank/world");
+    cudaStream_t s = pick_stream(ctx, stream);
+    PFRT_CUDA_TRY(cudaMemsetAsync(peers->state, 0, 4 * sizeof(uint32_t), s));
+    if (peers->recv[rank]) {
+        if (peers->ns <= 0)
+            return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_peer_reset: the peer set's ns is needed to clear its receive buffer");
+        PFRT_CUDA_TRY(cudaMemsetAsync(peers->recv[rank], 0, sizeof(uint64_t) * 2 * world * peers->ns, s));
+    }
+    if (peers->sig[rank]) PFRT_CUDA_TRY(cudaMemsetAsync(peers->sig[rank], 0, sizeof(uint32_t) * PFRT_PEER_SIG_WORDS, s));
     return PFRT_OK;
 }
 

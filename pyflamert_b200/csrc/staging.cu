@@ -1,0 +1,228 @@
+// staging.cu -- copies between pageable host memory and the device through a
+// ring of pinned buffers owned by the context.
+//
+// A host Tensor of the reference runtime lives in ordinary (pageable) memory
+// (tensor.cpp allocates it), so every graph input and output crosses the
+// host link from pageable memory.  CUDA's own pageable path copies through a
+// driver buffer on one thread; here the context keeps kSlots pinned chunks of
+// kChunk bytes, the host side of each chunk is copied by a small pool of
+// threads (the caller plus kWorkers), and the DMA of one chunk runs while the
+// next chunk is copied on the host.  One event per slot says when its DMA is
+// done, so a slot is reused only after that.
+#include <algorithm>
+#include <condition_variable>
+#include <cstring>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+#include "internal.hpp"
+
+namespace pfrt {
+
+namespace {
+
+// memcpy of one buffer split over the caller and `kWorkers` threads.
+class CopyPool {
+public:
+    static constexpr int kWorkers = 3;
+
+    CopyPool() {
+        for (int i = 0; i < kWorkers; ++i) threads_.emplace_back([this, i] { work(i); });
+    }
+    ~CopyPool() {
+        {
+            std::lock_guard<std::mutex> l(m_);
+            stop_ = true;
+        }
+        cv_.notify_all();
+        for (auto& t : threads_) t.join();
+    }
+
+    void copy(void* dst, const void* src, size_t n) {
+        constexpr size_t kMinSplit = 256 * 1024;
+        if (n < kMinSplit) {
+            std::memcpy(dst, src, n);
+            return;
+        }
+        const size_t part = (n / (kWorkers + 1) + 63) & ~size_t{63};
+        {
+            std::lock_guard<std::mutex> l(m_);
+            dst_ = static_cast<char*>(dst);
+            src_ = static_cast<const char*>(src);
+            n_ = n;
+            part_ = part;
+            pending_ = kWorkers;
+            ++gen_;
+        }
+        cv_.notify_all();
+        std::memcpy(dst, src, std::min(part, n));  // the caller's share: part 0
+        std::unique_lock<std::mutex> l(m_);
+        done_cv_.wait(l, [this] { return pending_ == 0; });
+    }
+
+private:
+    void work(int i) {
+        uint64_t seen = 0;
+        for (;;) {
+            char* dst;
+            const char* src;
+            size_t n, part;
+            {
+                std::unique_lock<std::mutex> l(m_);
+                cv_.wait(l, [&] { return stop_ || gen_ != seen; });
+                if (stop_) return;
+                seen = gen_;
+                dst = dst_;
+                src = src_;
+                n = n_;
+                part = part_;
+            }
+            const size_t lo = std::min(n, part * static_cast<size_t>(i + 1));
+            const size_t hi = (i == kWorkers - 1) ? n : std::min(n, part * static_cast<size_t>(i + 2));
+            if (hi > lo) std::memcpy(dst + lo, src + lo, hi - lo);
+            {
+                std::lock_guard<std::mutex> l(m_);
+                if (--pending_ == 0) done_cv_.notify_all();
+            }
+        }
+    }
+
+    std::vector<std::thread> threads_;
+    std::mutex m_;
+    std::condition_variable cv_, done_cv_;
+    bool stop_ = false;
+    uint64_t gen_ = 0;
+    int pending_ = 0;
+    char* dst_ = nullptr;
+    const char* src_ = nullptr;
+    size_t n_ = 0, part_ = 0;
+};
+
+}  // namespace
+
+struct StagingRing {
+    static constexpr int kSlots = 4;
+    static constexpr size_t kChunk = size_t{1} << 20;
+    void* buf[kSlots] = {};
+    cudaEvent_t ev[kSlots] = {};
+    bool used[kSlots] = {};
+    int next = 0;
+    CopyPool pool;
+};
+
+void staging_release(pfrt_ctx* ctx) {
+    StagingRing* r = ctx->staging;
+    if (!r) return;
+    for (int i = 0; i < StagingRing::kSlots; ++i) {
+        if (r->ev[i]) {
+            cudaEventSynchronize(r->ev[i]);
+            cudaEventDestroy(r->ev[i]);
+        }
+        if (r->buf[i]) cudaFreeHost(r->buf[i]);
+    }
+    delete r;
+    ctx->staging = nullptr;
+}
+
+namespace {
+
+pfrt_status ring(pfrt_ctx* ctx, StagingRing** out) {
+    if (!ctx->staging) {
+        auto* r = new StagingRing();
+        cudaError_t e = cudaSuccess;
+        for (int i = 0; i < StagingRing::kSlots && e == cudaSuccess; ++i) {
+            e = cudaMallocHost(&r->buf[i], StagingRing::kChunk);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&r->ev[i], cudaEventDisableTiming);
+        }
+        ctx->staging = r;
+        if (e != cudaSuccess) {
+            staging_release(ctx);
+            return cuda_fail(e, "pinned staging buffers");
+        }
+    }
+    *out = ctx->staging;
+    return PFRT_OK;
+}
+
+// The next slot, once the DMA that last used it has completed.
+pfrt_status take_slot(StagingRing* r, int* slot) {
+    const int s = r->next;
+    r->next = (s + 1) % StagingRing::kSlots;
+    if (r->used[s]) {
+        PFRT_CUDA_TRY(cudaEventSynchronize(r->ev[s]));
+        r->used[s] = false;
+    }
+    *slot = s;
+    return PFRT_OK;
+}
+
+}  // namespace
+}  // namespace pfrt
+
+using namespace pfrt;
+
+extern "C" {
+
+pfrt_status pfrt_memcpy_h2d_staged(pfrt_ctx* ctx, void* dst, const void* src, size_t bytes, pfrt_stream stream) {
+    pfrt_status st = enter(ctx);
+    if (st) return st;
+    if (bytes == 0) return PFRT_OK;
+    if (!dst || !src) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_memcpy_h2d_staged: null pointer");
+    StagingRing* r = nullptr;
+    st = ring(ctx, &r);
+    if (st) return st;
+    cudaStream_t s = pick_stream(ctx, stream);
+    for (size_t off = 0; off < bytes; off += StagingRing::kChunk) {
+        const size_t n = std::min(StagingRing::kChunk, bytes - off);
+        int slot = 0;
+        st = take_slot(r, &slot);
+        if (st) return st;
+        r->pool.copy(r->buf[slot], static_cast<const char*>(src) + off, n);
+        PFRT_CUDA_TRY(cudaMemcpyAsync(static_cast<char*>(dst) + off, r->buf[slot], n, cudaMemcpyHostToDevice, s));
+        PFRT_CUDA_TRY(cudaEventRecord(r->ev[slot], s));
+        r->used[slot] = true;
+    }
+    return PFRT_OK;
+}
+
+pfrt_status pfrt_memcpy_d2h_staged(pfrt_ctx* ctx, void* dst, const void* src, size_t bytes, pfrt_stream stream) {
+    pfrt_status st = enter(ctx);
+    if (st) return st;
+    if (bytes == 0) return PFRT_OK;
+    if (!dst || !src) return fail(PFRT_ERR_INVALID_ARGUMENT, "pfrt_memcpy_d2h_staged: null pointer");
+    StagingRing* r = nullptr;
+    st = ring(ctx, &r);
+    if (st) return st;
+    cudaStream_t s = pick_stream(ctx, stream);
+    const size_t C = StagingRing::kChunk;
+    const size_t nch = (bytes + C - 1) / C;
+    std::vector<int> slot_of(nch, 0);
+    auto issue = [&](size_t i) -> pfrt_status {
+        pfrt_status e = take_slot(r, &slot_of[i]);
+        if (e) return e;
+        const int sl = slot_of[i];
+        const size_t n = std::min(C, bytes - i * C);
+        PFRT_CUDA_TRY(cudaMemcpyAsync(r->buf[sl], static_cast<const char*>(src) + i * C, n, cudaMemcpyDeviceToHost, s));
+        PFRT_CUDA_TRY(cudaEventRecord(r->ev[sl], s));
+        r->used[sl] = true;
+        return PFRT_OK;
+    };
+    for (size_t i = 0; i < std::min<size_t>(nch, StagingRing::kSlots); ++i) {
+        st = issue(i);
+        if (st) return st;
+    }
+    for (size_t i = 0; i < nch; ++i) {
+        const int sl = slot_of[i];
+        PFRT_CUDA_TRY(cudaEventSynchronize(r->ev[sl]));
+        r->used[sl] = false;
+        r->pool.copy(static_cast<char*>(dst) + i * C, r->buf[sl], std::min(C, bytes - i * C));
+        if (i + StagingRing::kSlots < nch) {
+            st = issue(i + StagingRing::kSlots);
+            if (st) return st;
+        }
+    }
+    return PFRT_OK;
+}
+
+}  // extern "C"

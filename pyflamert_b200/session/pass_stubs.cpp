@@ -1,10 +1,9 @@
-// ref_session_stubs.cpp -- link stand-ins for the parts of the reference
-// runtime that InferenceSession references but whose sources do not compile
-// (src/opt/constant_folding.cpp, cse.cpp, dead_code_elimination.cpp,
-// operator_fusion.cpp and src/quantization/quantizer.cpp).  TEST
-// INFRASTRUCTURE ONLY: the session tests run with OptLevel::None and no
-// quantization config, so none of these is ever called; each one raises if it
-// is.
+// pass_stubs.cpp -- the parts of the reference runtime that InferenceSession
+// references but whose sources do not compile (src/opt/constant_folding.cpp,
+// cse.cpp, dead_code_elimination.cpp, operator_fusion.cpp and
+// src/quantization/quantizer.cpp).  The session here runs graphs as saved
+// (OptLevel::None, no quantization config), so none of these is reached; each
+// raises if it is.  Linked into libpfrt_session.so and the session tests.
 #include <stdexcept>
 
 #include "pyflame_rt/opt/constant_folding.hpp"
@@ -18,7 +17,7 @@ namespace opt {
 
 namespace {
 [[noreturn]] void not_built(const char* what) {
-    throw std::runtime_error(std::string(what) + " is not built in this test harness (OptLevel::None only)");
+    throw std::runtime_error(std::string(what) + " is not available in this build (OptLevel::None only)");
 }
 }  // namespace
 
@@ -33,7 +32,7 @@ PassResult OperatorFusionPass::run(Graph&) { not_built("OperatorFusionPass"); }
 namespace quantization {
 
 Quantizer::Quantizer(const QuantConfig& config) : config_(config) {
-    throw std::runtime_error("Quantizer is not built in this test harness (no quantization config)");
+    throw std::runtime_error("Quantizer is not available in this build (no quantization config)");
 }
 Quantizer::~Quantizer() = default;
 QuantizationResult Quantizer::quantize_dynamic(const Graph&) { throw std::runtime_error("Quantizer"); }

@@ -8,8 +8,11 @@ Two schemes, as the path needs them:
 * output-column sharding of a sparse weight -- W [N, K] is split by CSR rows
   (output channels) into equal shards of ceil(N / world) rows (the last one
   padded with empty rows), every rank computes Y[:, its columns] for the full
-  batch, and one all-gather (NCCL over NVLink) assembles Y [M, N].  This is
-  for weights too large to replicate.
+  batch, and one all-gather over NVLink assembles Y [M, N] on every rank.
+  This is for weights too large to replicate.  FusedNShardSpMM is the product
+  path (the all-gather done by the library's own kernels over peer memory);
+  NShardSpMM does the same with NCCL's all_gather_into_tensor and stays as the
+  library baseline.
 
 The reference has no communication backend: its partitioner
 (src/partition/graph_partitioner.cpp:111-200) only plans CommOps and runs the
@@ -91,16 +94,19 @@ class _DeviceArray:
 
 
 class FusedNShardSpMM:
-    """Output-channel-sharded SpMM with the all-gather fused into the kernel
-    (pfrt_spmm_allgather, M = 1): each rank's kernel sends every value of its
+    """Output-channel-sharded SpMM with the all-gather fused into the call
+    (pfrt_spmm_allgather).  M = 1: each rank's kernel sends every value of its
     rows of Y to every other rank as it computes it, and unpacks the values it
-    receives into its own gathered output.  The output, the receive buffer and
-    the state live in library-allocated device memory; the ranks exchange CUDA
-    IPC handles of their receive buffers once, through the default process
-    group (any backend: only host objects travel).  All ranks must construct
-    the object together and then make the same calls."""
+    receives into its own gathered output.  M > 1 (up to `max_m`): each rank
+    computes its column block of Y into its own gathered output, and one
+    kernel stores the block into every other rank's output over NVLink.  The
+    output, the receive buffer, the signal words and the state live in
+    library-allocated device memory; the ranks exchange CUDA IPC handles of
+    their output, receive buffer and signal words once, through the default
+    process group (any backend: only host objects travel).  All ranks must
+    construct the object together and then make the same calls."""
 
-    def __init__(self, ctx, N: int, K: int, indptr, indices, values, rank: int, world: int):
+    def __init__(self, ctx, N: int, K: int, indptr, indices, values, rank: int, world: int, max_m: int = 1):
         import ctypes as C
 
         import torch.distributed as dist
@@ -108,23 +114,31 @@ class FusedNShardSpMM:
         from . import CSR, _abi, lib
         if world > _abi.PFRT_MAX_PEERS:
             raise ValueError(f"at most {_abi.PFRT_MAX_PEERS} ranks")
+        if max_m < 1:
+            raise ValueError("max_m must be >= 1")
         self.ctx, self.N, self.K, self.rank, self.world = ctx, int(N), int(K), rank, world
+        self.max_m = int(max_m)
         self.ns = -(-self.N // world)
         n0, nreal, ip, ix, v = csr_row_shard(indptr, indices, values, rank, world)
         self.local = CSR(ctx, self.ns, self.K, ip, ix, v)
         L = lib()
         self._own = []
         ptrs = {}
-        for name, nbytes in (("y", 4 * world * self.ns), ("recv", 8 * 2 * world * self.ns), ("state", 16)):
+        sizes = (("y", 4 * self.max_m * world * self.ns), ("recv", 8 * 2 * world * self.ns), ("state", 16),
+                 ("sig", 4 * _abi.PFRT_PEER_SIG_WORDS))
+        for name, nbytes in sizes:
             p = C.c_void_p()
-            _abi.check(L.pfrt_malloc(ctx.handle, nbytes, C.byref(p)), "pfrt_malloc")
+            _abi.check(L.pfrt_malloc(ctx.handle, max(nbytes, 16), C.byref(p)), "pfrt_malloc")
             self._own.append(p.value)
-            _abi.check(L.pfrt_memset(ctx.handle, p, 0, nbytes, None), "pfrt_memset")
+            _abi.check(L.pfrt_memset(ctx.handle, p, 0, max(nbytes, 16), None), "pfrt_memset")
             ptrs[name] = p.value
         _abi.check(L.pfrt_ctx_check(ctx.handle, None), "pfrt_ctx_check")  # zeroed before anyone sees them
-        h = _abi.IpcHandle()
-        _abi.check(L.pfrt_ipc_get_handle(ctx.handle, C.c_void_p(ptrs["recv"]), C.byref(h)), "pfrt_ipc_get_handle")
-        mine = bytes(h.bytes)
+        shared = ("recv", "y", "sig")
+        mine = []
+        for name in shared:
+            h = _abi.IpcHandle()
+            _abi.check(L.pfrt_ipc_get_handle(ctx.handle, C.c_void_p(ptrs[name]), C.byref(h)), "pfrt_ipc_get_handle")
+            mine.append(bytes(h.bytes))
         allh = [None] * world
         if world > 1:
             dist.all_gather_object(allh, mine)
@@ -134,37 +148,74 @@ class FusedNShardSpMM:
         ps = _abi.PeerSet()
         ps.rank, ps.world = rank, world
         ps.y = ptrs["y"]
+        ps.state = ptrs["state"]
+        ps.ns, ps.max_m = self.ns, self.max_m
         for p in range(world):
             if p == rank:
-                ps.recv[p] = ptrs["recv"]
+                ps.recv[p], ps.y_peer[p], ps.sig[p] = ptrs["recv"], ptrs["y"], ptrs["sig"]
                 continue
-            hp = _abi.IpcHandle()
-            C.memmove(hp.bytes, allh[p], 64)
-            d = C.c_void_p()
-            _abi.check(L.pfrt_ipc_open(ctx.handle, C.byref(hp), C.byref(d)), "pfrt_ipc_open")
-            self._opened.append(d.value)
-            ps.recv[p] = d.value
-        ps.state = ptrs["state"]
+            mapped = []
+            for i in range(len(shared)):
+                hp = _abi.IpcHandle()
+                C.memmove(hp.bytes, allh[p][i], 64)
+                d = C.c_void_p()
+                _abi.check(L.pfrt_ipc_open(ctx.handle, C.byref(hp), C.byref(d)), "pfrt_ipc_open")
+                self._opened.append(d.value)
+                mapped.append(d.value)
+            ps.recv[p], ps.y_peer[p], ps.sig[p] = mapped
         self.peers = ps
         self._y_ptr = ptrs["y"]
         if world > 1:
-            dist.barrier()  # every rank has mapped every other rank's receive buffer
+            dist.barrier()  # every rank has mapped every other rank's buffers
 
-    def output(self):
-        """This rank's gathered output Y [1, N] (a view of the library buffer)."""
+    def output(self, M: int = 1):
+        """This rank's gathered output Y [M, N] (a view of the library buffer)."""
         import torch
-        y = torch.as_tensor(_DeviceArray(self._y_ptr, (1, self.world * self.ns), "<f4"), device="cuda")
-        return y[:, : self.N]
+        y = torch.as_tensor(_DeviceArray(self._y_ptr, (self.max_m, self.world * self.ns), "<f4"), device="cuda")
+        return y[:M, : self.N]
 
-    def __call__(self, x, stream=None):
+    def __call__(self, x, stream=None, csr=None):
+        """Y [M, N] = X [M, K] W^T on every rank.  `csr` (optional) is another
+        upload of this rank's shard (same rows), used instead of the own one
+        (benchmarks rotate copies of the weight through the same buffers)."""
         import ctypes as C
 
         from . import _abi, _dptr, _stream, lib
-        if x.shape[0] != 1 or x.shape[1] != self.K:
-            raise ValueError("FusedNShardSpMM: X must be [1, K]")
-        _abi.check(lib().pfrt_spmm_allgather(self.ctx.handle, self.local._h, 1, _dptr(x), x.shape[1],
+        M = int(x.shape[0])
+        if x.shape[1] != self.K or M < 1 or M > self.max_m:
+            raise ValueError(f"FusedNShardSpMM: X must be [M <= {self.max_m}, {self.K}]")
+        if x.stride(1) != 1:
+            raise ValueError("FusedNShardSpMM: X rows must be contiguous")
+        w = self.local if csr is None else csr
+        _abi.check(lib().pfrt_spmm_allgather(self.ctx.handle, w._h, M, _dptr(x), x.stride(0),
                                              C.byref(self.peers), _stream(stream)), "pfrt_spmm_allgather")
-        return self.output()
+        return self.output(M)
+
+    def shard_copy(self, indptr, indices, values):
+        """Another upload of this rank's shard of the same W (a CSR object
+        for __call__'s `csr`)."""
+        from . import CSR
+        n0, nreal, ip, ix, v = csr_row_shard(indptr, indices, values, self.rank, self.world)
+        return CSR(self.ctx, self.ns, self.K, ip, ix, v)
+
+    def allgather(self, M: int, stream=None):
+        """The all-gather alone (pfrt_peer_allgather): every rank has written
+        its own column block of the first M rows of output(); afterwards every
+        rank's output holds all blocks."""
+        import ctypes as C
+
+        from . import _abi, _stream, lib
+        _abi.check(lib().pfrt_peer_allgather(self.ctx.handle, int(M), C.byref(self.peers), _stream(stream)),
+                   "pfrt_peer_allgather")
+        return self.output(M)
+
+    def reset(self, stream=None):
+        """pfrt_peer_reset: clears this rank's state after a timeout; every
+        rank calls it and the ranks synchronize before the next call."""
+        import ctypes as C
+
+        from . import _abi, _stream, lib
+        _abi.check(lib().pfrt_peer_reset(self.ctx.handle, C.byref(self.peers), _stream(stream)), "pfrt_peer_reset")
 
     def close(self):
         import ctypes as C

@@ -6,7 +6,8 @@
 // Links the reference runtime compiled from its sources (oracle/_ref) and the
 // C restatement (oracle/_build) as checkers, and the product libraries
 // libpfrt_cuda_backend.so / libpfrt_cuda.so.  Needs a B200; run by
-// tests/test_gpu_backend.py.  Prints one "PASS name" or "FAIL name: why" line
+// tests/test_gpu_backend.py.  With --cpu it runs only the host-only checks
+// (the batch-split plan and device strings; tests/test_backend_host.py).  Prints one "PASS name" or "FAIL name: why" line
 // per test and exits non-zero if any test failed.
 #include <algorithm>
 #include <cmath>
@@ -105,11 +106,156 @@ std::vector<Tensor> run(Backend& be, const Graph& g, const std::unordered_map<st
     return be.execute(g, feeds);
 }
 
+// A row-separable graph: X [M, 1024] -> Gemm(B, C[1024]) -> Y, and
+// U [M, 512] uint8 -> QuantizedMatMul (per-channel) -> Add bias -> Relu ->
+// Quantize uint8 -> Z.
+Graph split_graph(int64_t M) {
+    Graph g("split");
+    g.add_input(TensorInfo("X", sh({M, 1024}), DType::Float32));
+    g.add_input(TensorInfo("U", sh({M, 512}), DType::UInt8));
+    g.add_initializer("B", randn({1024, 768}, 1.0f / 32.0f, 21));
+    g.add_initializer("C", randn({768}, 0.1f, 22));
+    auto gm = node("gemm", "Gemm", {"X", "B", "C"}, {"Y"});
+    gm->set_attr("alpha", 1.0f);
+    gm->set_attr("beta", 1.0f);
+    g.add_node(gm);
+    g.add_initializer("W", randint<int8_t>({512, 384}, -127, 127, DType::Int8, 23));
+    g.add_initializer("bias", randn({384}, 10.0f, 24));
+    std::vector<float> scales(384);
+    std::mt19937_64 rng(25);
+    std::uniform_real_distribution<float> ud(0.005f, 0.02f);
+    for (auto& v : scales) v = ud(rng);
+    auto q = node("qmm", "QuantizedMatMul", {"U", "W"}, {"t0"});
+    q->set_attr("a_scale", 0.02f);
+    q->set_attr("a_zero_point", int64_t{128});
+    q->set_attr("b_scales", scales);
+    g.add_node(q);
+    g.add_node(node("add", "Add", {"t0", "bias"}, {"t1"}));
+    g.add_node(node("relu", "Relu", {"t1"}, {"t2"}));
+    auto qz = node("quant", "Quantize", {"t2"}, {"Z"});
+    qz->set_attr("scale", 2.0f);
+    qz->set_attr("dtype", std::string("uint8"));
+    g.add_node(qz);
+    g.add_output(TensorInfo("Y", sh({M, 768}), DType::Float32));
+    g.add_output(TensorInfo("Z", sh({M, 384}), DType::UInt8));
+    return g;
+}
+
+std::unordered_map<std::string, Tensor> split_feeds(int64_t M) {
+    std::unordered_map<std::string, Tensor> f;
+    f["X"] = randn({M, 1024}, 1.0f, 26);
+    f["U"] = randint<uint8_t>({M, 512}, 0, 255, DType::UInt8, 27);
+    return f;
+}
+
+// Host-only checks (no GPU): the batch-split plan and the device strings.
+void host_tests() {
+    run_test("BatchSplitPlanRows", [&] {
+        Graph g = split_graph(1000);
+        auto f = split_feeds(1000);
+        auto plan = batch_split_plan(g, f, 4, 64);
+        EXPECT(plan.size() == 4, "4 slices");
+        EXPECT(plan.front().first == 0 && plan.back().second == 1000, "slices cover the batch");
+        for (size_t i = 1; i < plan.size(); ++i) EXPECT(plan[i].first == plan[i - 1].second, "contiguous");
+        EXPECT(batch_split_plan(g, f, 4, 300).empty(), "too few rows per device");
+        EXPECT(batch_split_plan(g, f, 1, 1).empty(), "one device");
+    });
+    run_test("BatchSplitPlanRejects", [&] {
+        auto f = split_feeds(512);
+        {   // C of M*N elements: C[(m*N + n) % c_len] depends on the row
+            Graph g = split_graph(512);
+            Graph h("full_c");
+            h.add_input(TensorInfo("X", sh({512, 64}), DType::Float32));
+            h.add_initializer("B", randn({64, 8}, 1.0f, 1));
+            h.add_initializer("C", randn({512 * 8}, 1.0f, 2));
+            h.add_node(node("gemm", "Gemm", {"X", "B", "C"}, {"Y"}));
+            h.add_output(TensorInfo("Y", sh({512, 8}), DType::Float32));
+            std::unordered_map<std::string, Tensor> hf;
+            hf["X"] = randn({512, 64}, 1.0f, 3);
+            EXPECT(batch_split_plan(h, hf, 2, 1).empty(), "full-matrix C accepted");
+            (void)g;
+        }
+        {   // transA
+            Graph h("ta");
+            h.add_input(TensorInfo("X", sh({512, 64}), DType::Float32));
+            h.add_initializer("B", randn({512, 8}, 1.0f, 1));
+            auto n = node("gemm", "Gemm", {"X", "B"}, {"Y"});
+            n->set_attr("transA", int64_t{1});
+            h.add_node(n);
+            h.add_output(TensorInfo("Y", sh({64, 8}), DType::Float32));
+            std::unordered_map<std::string, Tensor> hf;
+            hf["X"] = randn({512, 64}, 1.0f, 3);
+            EXPECT(batch_split_plan(h, hf, 2, 1).empty(), "transA accepted");
+        }
+        {   // a runtime weight
+            Graph h("rt");
+            h.add_input(TensorInfo("X", sh({512, 64}), DType::Float32));
+            h.add_input(TensorInfo("W", sh({64, 8}), DType::Float32));
+            h.add_node(node("mm", "MatMul", {"X", "W"}, {"Y"}));
+            h.add_output(TensorInfo("Y", sh({512, 8}), DType::Float32));
+            std::unordered_map<std::string, Tensor> hf;
+            hf["X"] = randn({512, 64}, 1.0f, 3);
+            hf["W"] = randn({64, 8}, 1.0f, 4);
+            EXPECT(batch_split_plan(h, hf, 2, 1).empty(), "runtime weight accepted");
+        }
+        {   // inputs with different row counts
+            Graph g = split_graph(512);
+            auto bad = split_feeds(512);
+            bad["U"] = randint<uint8_t>({256, 512}, 0, 255, DType::UInt8, 5);
+            EXPECT(batch_split_plan(g, bad, 2, 1).empty(), "ragged inputs accepted");
+        }
+        (void)f;
+    });
+    run_test("CudaDeviceStrings", [&] {
+        unsetenv("PFRT_CUDA_DEVICES");
+        EXPECT(parse_cuda_devices("cuda") == std::vector<int>{0}, "cuda -> {0}");
+        EXPECT(parse_cuda_devices("cuda:3") == std::vector<int>{3}, "cuda:3");
+        EXPECT((parse_cuda_devices("cuda:0,1,2") == std::vector<int>{0, 1, 2}), "cuda:0,1,2");
+        setenv("PFRT_CUDA_DEVICES", "1,0", 1);
+        EXPECT((parse_cuda_devices("cuda") == std::vector<int>{1, 0}), "PFRT_CUDA_DEVICES");
+        unsetenv("PFRT_CUDA_DEVICES");
+        for (const char* bad : {"cpu", "cuda:", "cuda:x", "cuda:1,,2", "gpu:0"}) {
+            bool threw = false;
+            try {
+                parse_cuda_devices(bad);
+            } catch (const PyFlameRTError&) {
+                threw = true;
+            }
+            EXPECT(threw, std::string("accepted ") + bad);
+        }
+    });
+}
+
 }  // namespace
 
-int main() {
+int main(int argc, char** argv) {
+    host_tests();
+    if (argc > 1 && std::strcmp(argv[1], "--cpu") == 0) return g_failed ? 1 : 0;
     CudaBackend cuda(0);
     CPUExecutor cpu(0);
+
+    // Two backends' worth of devices on device 0 (CudaBackend({0, 0})): the
+    // batch split runs, with each slice on its own context; the outputs equal
+    // the single-device backend's (int8 bit for bit, fp32 within 1e-5 of the
+    // reference CPUExecutor).
+    run_test("MultiDeviceBatchSplit", [&] {
+        setenv("PFRT_SPLIT_MIN_ROWS", "64", 1);
+        CudaBackend multi(std::vector<int>{0, 0});
+        const int64_t M = 1000;
+        Graph g = split_graph(M);
+        auto f = split_feeds(M);
+        EXPECT(batch_split_plan(g, f, 2, 64).size() == 2, "plan");
+        auto y = multi.execute(g, f);
+        auto one = cuda.execute(g, f);
+        auto r = cpu.execute(g, f);
+        EXPECT(y.size() == 2 && y[0].shape() == r[0].shape() && y[1].shape() == one[1].shape(), "shapes");
+        const double e = normwise(y[0], r[0]);
+        EXPECT(e <= 1e-5, "Gemm normwise error " + std::to_string(e));
+        EXPECT(same_bytes(y[1], one[1]), "int8 chain differs from the single-device backend");
+        auto y2 = multi.execute(g, f);  // prepared weights reused on both slices
+        EXPECT(same_bytes(y[1], y2[1]), "second run differs");
+        unsetenv("PFRT_SPLIT_MIN_ROWS");
+    });
 
     // ExecutorTest.SupportedOps analogue (tests/cpp/test_executor.cpp:150-158).
     run_test("SupportedOps", [&] {

@@ -1,9 +1,9 @@
 // test_session_seam.cpp -- the drop-in check: the reference's own
-// InferenceSession (src/session.cpp), built with the two-line seam that lets
-// SessionOptions.device = "cuda" select CudaBackend (options.cpp:12-17 and
-// select_backend, session.cpp:67-95), loads a .pfm model written by the
-// reference's PyFlameFormat::save and runs it on "cuda" and on "cpu"; the
-// outputs are compared.  Graph, loader, session and run() are the reference's
+// InferenceSession (src/session.cpp), built with the seam that lets
+// SessionOptions.device = "cuda" (or "cuda:<n>") select CudaBackend
+// (options.cpp:12-17 and select_backend, session.cpp:67-95), loads a .pfm
+// model written by the reference's PyFlameFormat::save and runs it on "cuda",
+// "cuda:0" and "cpu"; the outputs are compared.  Graph, loader, session and run() are the reference's
 // code; only the backend differs.  TEST INFRASTRUCTURE; needs a B200.
 #include <cmath>
 #include <cstdio>
@@ -97,12 +97,15 @@ int main() {
         cpu_opts.optimization_level = OptLevel::None;
         SessionOptions cuda_opts = cpu_opts;
         cuda_opts.device = "cuda";
+        SessionOptions cuda0_opts = cpu_opts;
+        cuda0_opts.device = "cuda:0";  // a device ordinal in the device string
         InferenceSession cpu(path, cpu_opts);
         InferenceSession cuda(path, cuda_opts);
+        InferenceSession cuda0(path, cuda0_opts);
         const std::vector<std::string> outs = {"Y", "Yq"};
         for (int rep = 0; rep < 2; ++rep) {
             auto r = cpu.run(outs, feeds);
-            auto y = cuda.run(outs, feeds);
+            auto y = (rep == 0 ? cuda : cuda0).run(outs, feeds);
             double num = 0, den = 0;
             for (int64_t i = 0; i < r[0].num_elements(); ++i) {
                 num = std::max(num, std::fabs(static_cast<double>(y[0].data_ptr<float>()[i]) - r[0].data_ptr<float>()[i]));

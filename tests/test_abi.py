@@ -86,13 +86,33 @@ def test_struct_layouts_match_header(tmp_path):
     the ctypes mirrors the Python wrapper passes."""
     src = tmp_path / "layout.c"
     src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "pfrt_cuda.h"\n'
-                   'int main(void){printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(pfrt_peer_set),'
+                   'int main(void){printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\\n", sizeof(pfrt_peer_set),'
                    ' offsetof(pfrt_peer_set, world), offsetof(pfrt_peer_set, y),'
                    ' offsetof(pfrt_peer_set, recv), offsetof(pfrt_peer_set, state),'
+                   ' offsetof(pfrt_peer_set, ns), offsetof(pfrt_peer_set, max_m),'
+                   ' offsetof(pfrt_peer_set, y_peer), offsetof(pfrt_peer_set, sig),'
                    ' sizeof(pfrt_ipc_handle)); return 0;}\n')
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-std=c99", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
     got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
     P = _abi.PeerSet
-    assert got == [C.sizeof(P), P.world.offset, P.y.offset, P.recv.offset, P.state.offset,
-                   C.sizeof(_abi.IpcHandle)]
+    assert got == [C.sizeof(P), P.world.offset, P.y.offset, P.recv.offset, P.state.offset, P.ns.offset,
+                   P.max_m.offset, P.y_peer.offset, P.sig.offset, C.sizeof(_abi.IpcHandle)]
+
+
+@pytest.mark.parametrize("name", ["libpfrt_cuda.so", "libpfrt_cuda_backend.so", "libpfrt_session.so"])
+def test_libraries_share_the_system_libstdcxx(name):
+    """Each library links the shared libstdc++ and exports none of its
+    internals.  These libraries are loaded into processes that hold the
+    system's libstdc++ already (Python, the PyFlameRT runtime); a library with
+    its own static copy of the iostream and locale code broke std::ostringstream
+    across the library boundary (a null facet when the plugin formatted a
+    number in a Python process)."""
+    path = os.path.join(ROOT, "pyflamert_b200", "lib", name)
+    if not os.path.exists(path):
+        pytest.skip(f"{name} not built")
+    needed = subprocess.run(["readelf", "-d", path], capture_output=True, text=True, check=True).stdout
+    assert "libstdc++.so.6" in needed
+    syms = subprocess.run(["nm", "-D", "--defined-only", path], capture_output=True, text=True, check=True).stdout
+    leaked = [l for l in syms.splitlines() if "_ZNSo" in l or "codecvt" in l or "_ZNSt6locale" in l]
+    assert not leaked, leaked[:5]

@@ -52,7 +52,7 @@ def test_batch_sizes(ctx, M):
 
 
 @pytest.mark.parametrize("sparsity", [0.5, 0.7, 0.9, 0.95])
-@pytest.mark.parametrize("M", [1, 64, 1024])
+@pytest.mark.parametrize("M", [1, 64, 1024, 8192])
 def test_config5_sweep(ctx, sparsity, M):
     """Config 5 weights (8192 x 8192); the oracle checks 8 rows of the output."""
     c = wl.spmm_case(M, 8192, 8192, sparsity=sparsity, seed=50 + int(sparsity * 100))

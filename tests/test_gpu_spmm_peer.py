@@ -1,13 +1,18 @@
 """The output-channel-sharded SpMM fused with its all-gather
-(pfrt_spmm_allgather): every rank's kernel sends each value of its rows of Y
-to every other rank over NVLink, marked with the call's number, and unpacks
-the values it receives into its own gathered output.  The
-gathered Y must match pruning::sparse_matmul (src/pruning/sparse_tensor.cpp:
-473-519) on the whole W, normwise <= 1e-5, on every rank, call after call
-(the call counter lives on the device) and inside CUDA graph replays.
+(pfrt_spmm_allgather) and the all-gather alone (pfrt_peer_allgather).
+M = 1: every rank's kernel sends each value of its rows of Y to every other
+rank over NVLink, marked with the call's number, and unpacks the values it
+receives into its own gathered output.  M > 1: every rank computes its column
+block of Y into its own output and one kernel stores the block into every
+other rank's output.  The gathered Y must match pruning::sparse_matmul
+(src/pruning/sparse_tensor.cpp:473-519) on the whole W, normwise <= 1e-5, on
+every rank, call after call (the call counter lives on the device), with M
+changing between calls, and inside CUDA graph replays.
 
-World 1 runs on one GPU (the rank's own buffers only); worlds 2 and 4
-need that many GPUs and are skipped with fewer."""
+World 1 runs on one GPU (the rank's own buffers only), as does the timeout
+test (its peer is a local buffer nobody writes); worlds 2 and 4 need that
+many GPUs and are skipped with fewer."""
+import ctypes as C
 import os
 import socket
 
@@ -20,22 +25,34 @@ from tests.helpers import FP32_TOL, normwise_rel
 pytestmark = pytest.mark.gpu
 
 
-def _case(seed=5, N=3001, K=2048, sparsity=0.9):
+def _case(M=1, seed=5, N=3001, K=2048, sparsity=0.9):
     from pyflamert_b200 import workloads as wl
-    return wl.spmm_case(1, N, K, sparsity=sparsity, seed=seed)
+    return wl.spmm_case(M, N, K, sparsity=sparsity, seed=seed)
 
 
-def _check_calls(sh, c, rng, graph=True):
-    """Three eager calls with fresh X, then a captured call replayed with X
-    changed in place between replays.  Returns the worst normwise error."""
+def _ref_rows(c, X, rows):
     from oracle import pyoracle as po
+    return po.spmm_linear(c.indptr, c.indices, c.values, X[rows], c.N)
+
+
+def _sample(M):
+    return np.unique(np.r_[0:3, M // 2, M - 3:M].clip(0, M - 1))
+
+
+def _check_calls(sh, c, rng, Ms=(1,), graph=True):
+    """Eager calls with fresh X for each M in Ms (in order, twice), then a
+    captured call of the largest M replayed with X changed in place between
+    replays.  Rows of the output are sampled for M > 64.  Returns the worst
+    normwise error."""
     worst = 0.0
-    for _ in range(3):
-        X = rng.standard_normal((1, c.K)).astype(np.float32)
+    for M in list(Ms) * 2:
+        X = rng.standard_normal((M, c.K)).astype(np.float32)
         y = sh(torch.from_numpy(X).cuda()).cpu().numpy()
-        worst = max(worst, normwise_rel(y, po.spmm_linear(c.indptr, c.indices, c.values, X, c.N)))
+        rows = _sample(M) if M > 64 else np.arange(M)
+        worst = max(worst, normwise_rel(y[rows], _ref_rows(c, X, rows)))
     if graph:
-        xg = torch.zeros((1, c.K), dtype=torch.float32, device="cuda")
+        M = max(Ms)
+        xg = torch.zeros((M, c.K), dtype=torch.float32, device="cuda")
         sh(xg)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
@@ -46,13 +63,14 @@ def _check_calls(sh, c, rng, graph=True):
                 sh(xg, stream=s)
         torch.cuda.synchronize()
         for _ in range(3):
-            X = rng.standard_normal((1, c.K)).astype(np.float32)
+            X = rng.standard_normal((M, c.K)).astype(np.float32)
             xg.copy_(torch.from_numpy(X))
             torch.cuda.synchronize()
             g.replay()
             torch.cuda.synchronize()
-            y = sh.output().cpu().numpy()
-            worst = max(worst, normwise_rel(y, po.spmm_linear(c.indptr, c.indices, c.values, X, c.N)))
+            y = sh.output(M).cpu().numpy()
+            rows = _sample(M) if M > 64 else np.arange(M)
+            worst = max(worst, normwise_rel(y[rows], _ref_rows(c, X, rows)))
         del g
     return worst
 
@@ -60,25 +78,98 @@ def _check_calls(sh, c, rng, graph=True):
 def test_world1_self_gather(ctx):
     from pyflamert_b200 import sharding
     c = _case()
-    sh = sharding.FusedNShardSpMM(ctx, c.N, c.K, c.indptr, c.indices, c.values, 0, 1)
+    sh = sharding.FusedNShardSpMM(ctx, c.N, c.K, c.indptr, c.indices, c.values, 0, 1, max_m=40)
     try:
-        assert _check_calls(sh, c, np.random.default_rng(1)) <= FP32_TOL
+        assert _check_calls(sh, c, np.random.default_rng(1), Ms=(1, 5, 40)) <= FP32_TOL
         ctx.check()
     finally:
         sh.close()
 
 
-def test_world1_rejects_batches(ctx):
+@pytest.mark.parametrize("M", [1, 64, 1024, 8192])
+def test_world1_config5(ctx, M):
+    """Config 5's weight (8192 x 8192, 90 % sparse) at every batch size of its
+    sweep through the sharded entry at world 1."""
+    from pyflamert_b200 import sharding
+    c = _case(M, seed=51, N=8192, K=8192)
+    sh = sharding.FusedNShardSpMM(ctx, c.N, c.K, c.indptr, c.indices, c.values, 0, 1, max_m=M)
+    try:
+        y = sh(torch.from_numpy(c.X).cuda()).cpu().numpy()
+        ctx.check()
+        rows = _sample(M)
+        assert normwise_rel(y[rows], _ref_rows(c, c.X, rows)) <= FP32_TOL
+        assert np.isfinite(y).all()
+    finally:
+        sh.close()
+
+
+def test_world1_rejects_rows_beyond_max_m(ctx):
     import pyflamert_b200 as pf
     from pyflamert_b200 import sharding
     c = _case(N=64, K=32)
-    sh = sharding.FusedNShardSpMM(ctx, c.N, c.K, c.indptr, c.indices, c.values, 0, 1)
+    sh = sharding.FusedNShardSpMM(ctx, c.N, c.K, c.indptr, c.indices, c.values, 0, 1, max_m=2)
     try:
-        import ctypes as C
-        x = torch.zeros((2, c.K), dtype=torch.float32, device="cuda")
-        st = pf.lib().pfrt_spmm_allgather(ctx.handle, sh.local._h, 2, x.data_ptr(), c.K, C.byref(sh.peers), None)
-        assert st == 5  # PFRT_ERR_UNSUPPORTED
+        x = torch.zeros((3, c.K), dtype=torch.float32, device="cuda")
+        st = pf.lib().pfrt_spmm_allgather(ctx.handle, sh.local._h, 3, x.data_ptr(), c.K, C.byref(sh.peers),
+                                          pf._stream(None))
+        assert st == 1  # PFRT_ERR_INVALID_ARGUMENT
+        assert "max_m" in pf._abi.last_error()
     finally:
+        sh.close()
+
+
+@pytest.mark.parametrize("M", [1, 8])
+def test_timeout_reported_then_reset(ctx, M):
+    """A world-2 peer set whose rank 1 is a set of local buffers nobody writes:
+    the call's bounded wait runs out (limit shortened through
+    PFRT_PEER_WAIT_MS), pfrt_ctx_check reports PFRT_ERR_DEVICE_TIMEOUT, the
+    next call reports it at once, and after pfrt_peer_reset the same state
+    serves a world-1 call that matches the oracle.  All memory is local to
+    this GPU; every wait is bounded."""
+    import pyflamert_b200 as pf
+    from pyflamert_b200 import _abi, sharding
+    c = _case(M, seed=8, N=512, K=256)
+    sh = sharding.FusedNShardSpMM(ctx, c.N, c.K, c.indptr, c.indices, c.values, 0, 1, max_m=8)
+    ns = sh.ns
+    fake = {k: torch.zeros(n, dtype=torch.int64, device="cuda")
+            for k, n in (("recv", 2 * 2 * ns), ("y", 8 * 2 * ns), ("sig", _abi.PFRT_PEER_SIG_WORDS))}
+    mine = {k: torch.zeros(n, dtype=torch.int64, device="cuda")
+            for k, n in (("recv", 2 * 2 * ns), ("y", 8 * 2 * ns), ("sig", _abi.PFRT_PEER_SIG_WORDS))}
+    ps = _abi.PeerSet()
+    ps.rank, ps.world, ps.ns, ps.max_m = 0, 2, ns, 8
+    ps.y = mine["y"].data_ptr()
+    ps.state = sh.peers.state
+    ps.recv[0], ps.recv[1] = mine["recv"].data_ptr(), fake["recv"].data_ptr()
+    ps.y_peer[0], ps.y_peer[1] = mine["y"].data_ptr(), fake["y"].data_ptr()
+    ps.sig[0], ps.sig[1] = mine["sig"].data_ptr(), fake["sig"].data_ptr()
+    old = os.environ.get("PFRT_PEER_WAIT_MS")
+    os.environ["PFRT_PEER_WAIT_MS"] = "200"
+    try:
+        x = torch.from_numpy(c.X).cuda()
+        for _ in range(2):  # the second call gives up at once (the abort word is set)
+            st = pf.lib().pfrt_spmm_allgather(ctx.handle, sh.local._h, M, x.data_ptr(), c.K, C.byref(ps),
+                                              pf._stream(None))
+            assert st == 0
+            with pytest.raises(pf.PfrtError) as ei:
+                ctx.check()
+            assert ei.value.status == 6  # PFRT_ERR_DEVICE_TIMEOUT
+        # the kernel did reach its (fake) peer: values tagged with calls 1 and 2
+        # (M = 1, receive halves by parity), or its "free for call 2" word (M > 1)
+        if M == 1:
+            tags = fake["recv"].cpu().numpy().view(np.uint64) >> np.uint64(32)
+            assert (tags[2 * ns:3 * ns] == 1).all() and (tags[0:ns] == 2).all()
+        else:
+            assert int(fake["sig"].cpu().numpy().view(np.uint32)[0]) == 2
+        sh.reset()
+        ctx.check()
+        y = sh(x).cpu().numpy()
+        ctx.check()
+        assert normwise_rel(y, _ref_rows(c, c.X, np.arange(M))) <= FP32_TOL
+    finally:
+        if old is None:
+            os.environ.pop("PFRT_PEER_WAIT_MS", None)
+        else:
+            os.environ["PFRT_PEER_WAIT_MS"] = old
         sh.close()
 
 
@@ -99,20 +190,43 @@ def _rank_main(rank, world, port, q):
         torch.cuda.set_device(rank)
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
         import datetime
-        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
         ctx = pf.Context(rank)
+        worst = 0.0
+        # a ragged shape (the last shard padded with empty rows), every M
         c = _case(seed=9, N=4099, K=4096)
-        sh = sharding.FusedNShardSpMM(ctx, c.N, c.K, c.indptr, c.indices, c.values, rank, world)
-        worst = _check_calls(sh, c, np.random.default_rng(7))  # same X sequence on every rank
+        sh = sharding.FusedNShardSpMM(ctx, c.N, c.K, c.indptr, c.indices, c.values, rank, world, max_m=70)
+        worst = max(worst, _check_calls(sh, c, np.random.default_rng(7), Ms=(1, 3, 70)))  # same X on every rank
+        ctx.check()
+        # the all-gather alone: every rank writes its own block, then gathers
+        y = sh.output(5)
+        full = torch.arange(5 * sh.world * sh.ns, dtype=torch.float32, device="cuda").reshape(5, -1)
+        blk = slice(rank * sh.ns, (rank + 1) * sh.ns)
+        raw = torch.as_tensor(sharding._DeviceArray(sh._y_ptr, (sh.max_m, sh.world * sh.ns), "<f4"), device="cuda")
+        raw[:5, blk].copy_(full[:, blk])
+        torch.cuda.synchronize()
+        sh.allgather(5)
+        ctx.check()
+        ok_gather = bool(torch.equal(raw[:5], full))
+        sh.close()
+        # config 5's weight at every M of its sweep
+        c = _case(8192, seed=51, N=8192, K=8192)
+        sh = sharding.FusedNShardSpMM(ctx, c.N, c.K, c.indptr, c.indices, c.values, rank, world, max_m=8192)
+        for M in (1, 64, 1024, 8192):
+            X = c.X[:M]
+            yv = sh(torch.from_numpy(X).cuda()).cpu().numpy()
+            rows = _sample(M)
+            worst = max(worst, normwise_rel(yv[rows], _ref_rows(c, X, rows)))
         ctx.check()
         dist.barrier()
         sh.close()
         ctx.close()
         dist.destroy_process_group()
-        q.put((rank, worst, None))
+        q.put((rank, worst, ok_gather, None))
     except Exception as e:  # reported to the parent
-        q.put((rank, None, repr(e)))
+        q.put((rank, None, None, repr(e)))
 
 
 @pytest.mark.parametrize("world", [2, 4])
@@ -128,11 +242,12 @@ def test_world_n_gpus(world):
         p.start()
     res = {}
     for _ in range(world):
-        r, worst, err = q.get(timeout=300)
-        res[r] = (worst, err)
+        r, worst, ok_gather, err = q.get(timeout=600)
+        res[r] = (worst, ok_gather, err)
     for p in procs:
         p.join(timeout=60)
     for r in range(world):
-        worst, err = res[r]
+        worst, ok_gather, err = res[r]
         assert err is None, err
         assert worst <= FP32_TOL
+        assert ok_gather

@@ -10,8 +10,10 @@ M * Kpad <= 2**21 elements (Kpad = K rounded up to 32).
 The test calls it twice in a row through the C ABI, on different shapes so
 that contents left in the shared array by the first call would show up in
 the second, and compares each result with the allocating entry point
-pfrt_gemm_f32 within the fp32 tolerance the other tests use.  This file is
-named so that pytest collects it last."""
+pfrt_gemm_f32 and with the oracle (cpu_gemm's arithmetic, pinned to the
+reference) within the fp32 tolerance the other tests use.  A call exactly at
+the size limit must be accepted and match too.  This file is named so that
+pytest collects it last."""
 import ctypes as C
 
 import numpy as np
@@ -34,6 +36,11 @@ def _noalloc(ctx, w, a, c, alpha, beta, trans_a, M):
     return y
 
 
+def _oracle(g):
+    from oracle import pyoracle as po
+    return po.gemm(g.A, g.B, g.C, g.alpha, g.beta, g.trans_a, g.trans_b)
+
+
 def test_noalloc_matches_allocating_entry_point_twice(ctx):
     cases = [wl.gemm_case(256, 1024, 1024, seed=1),                         # config 1
              wl.gemm_case(70, 200, 333, seed=9, trans_a=1, alpha=0.5, beta=-2.0)]
@@ -45,8 +52,21 @@ def test_noalloc_matches_allocating_entry_point_twice(ctx):
         ref = w(a, c, g.alpha, g.beta, g.trans_a)
         y = _noalloc(ctx, w, a, c, g.alpha, g.beta, g.trans_a, M)
         ctx.check()
-        assert normwise_rel(y.cpu().numpy(), ref.cpu().numpy()) <= FP32_TOL
+        y = y.cpu().numpy()
+        assert normwise_rel(y, ref.cpu().numpy()) <= FP32_TOL
+        assert normwise_rel(y, _oracle(g)) <= FP32_TOL
         w.close()
+
+
+def test_noalloc_accepts_the_limit(ctx):
+    g = wl.gemm_case((1 << 21) // 64, 48, 64, seed=4)   # M * Kpad == 2**21 exactly
+    w = pf.FWeight(ctx, g.B)
+    a = torch.from_numpy(g.A).cuda()
+    c = torch.from_numpy(g.C).cuda()
+    y = _noalloc(ctx, w, a, c, g.alpha, g.beta, 0, g.A.shape[0])
+    ctx.check()
+    assert normwise_rel(y.cpu().numpy(), _oracle(g)) <= FP32_TOL
+    w.close()
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch(ctx):
