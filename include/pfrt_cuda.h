@@ -91,7 +91,7 @@ PFRT_API pfrt_status pfrt_memset(pfrt_ctx* ctx, void* dst, int value, size_t byt
  * runtime, src/tensor.cpp) and the device.  They replace the per-run host
  * copies of graph inputs and outputs that CPUExecutor::execute makes
  * (src/backends/cpu/executor.cpp:65-74).  The bytes go through the context's
- * ring of pinned buffers (4 x 1 MiB, allocated by the first call): several
+ * ring of pinned buffers (8 x 256 KiB, allocated by the first call): several
  * host threads copy one chunk while the DMA of the previous chunk runs.
  * pfrt_memcpy_h2d_staged returns once src has been read (its DMAs complete
  * in order on `stream`); pfrt_memcpy_d2h_staged returns once dst holds the

@@ -40,7 +40,7 @@ public:
     }
 
     void copy(void* dst, const void* src, size_t n) {
-        constexpr size_t kMinSplit = 256 * 1024;
+        constexpr size_t kMinSplit = 128 * 1024;
         if (n < kMinSplit) {
             std::memcpy(dst, src, n);
             return;
@@ -102,8 +102,11 @@ private:
 }  // namespace
 
 struct StagingRing {
-    static constexpr int kSlots = 4;
-    static constexpr size_t kChunk = size_t{1} << 20;
+    // 256 KiB chunks: small enough that the host copy of one chunk and the
+    // DMA of the previous one overlap within a 1-2 MiB tensor, large enough
+    // that each DMA runs at the link's rate.
+    static constexpr int kSlots = 8;
+    static constexpr size_t kChunk = size_t{256} << 10;
     void* buf[kSlots] = {};
     cudaEvent_t ev[kSlots] = {};
     bool used[kSlots] = {};

@@ -198,14 +198,37 @@ __global__ void __launch_bounds__(64 + 32 * Gemm2Cfg<BN, STAGES>::EPI_WARPS, 1)
         if (lane == 0) {
             tma_prefetch_desc(&tmA);
             tma_prefetch_desc(&tmB);
-            pdl_wait();
-            int stage = 0;
-            uint32_t phase = 0;
+            // B is a prepared weight (written once at its creation, never by a
+            // kernel): the first unit's first stages of B are requested
+            // before the dependency wait, A (which the previous kernel may
+            // write) after it.  The ring starts empty: no empty-barrier wait.
+            int npre = 0;
+            if (pair < sched.num_units) {
+                int mb0, nb0, ks0;
+                decode_unit(sched, pair, mb0, nb0, ks0);
+                npre = min(STAGES, sched.kb_total);
+                for (int i = 0; i < npre; ++i) {
+                    const uint32_t fbar = mapa_shared(smem_u32(&full[i]), 0u);
+                    if (leader) mbar_arrive_expect_tx(&full[i], 2 * Cfg::STAGE_BYTES);
+                    tma_load_2d_pair(tiles + i * Cfg::STAGE_BYTES + Cfg::A_TILE, &tmB, fbar, i * Cfg::BK,
+                                     nb0 * BN + static_cast<int>(rank) * Cfg::BH);
+                }
+                pdl_wait();
+                for (int i = 0; i < npre; ++i) {
+                    const uint32_t fbar = mapa_shared(smem_u32(&full[i]), 0u);
+                    tma_load_2d_pair(tiles + i * Cfg::STAGE_BYTES, &tmA, fbar, i * Cfg::BK,
+                                     mb0 * 2 * BM + static_cast<int>(rank) * BM);
+                }
+            } else {
+                pdl_wait();
+            }
+            int stage = npre % STAGES;
+            uint32_t phase = (npre == STAGES) ? 1u : 0u;
             bool ok = true;
             for (int unit = pair; ok && unit < sched.num_units; unit += npairs) {
                 int mb, nb, ks;
                 decode_unit(sched, unit, mb, nb, ks);
-                for (int kb = 0; kb < sched.kb_total; ++kb) {
+                for (int kb = (unit == pair) ? npre : 0; kb < sched.kb_total; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
                         ok = false;
                         break;

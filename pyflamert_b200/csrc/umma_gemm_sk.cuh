@@ -181,8 +181,24 @@ __global__ void __launch_bounds__(GemmSkCfg<BN, STAGES>::THREADS, 1)
             uint32_t issued = 0;
             uint32_t last_par[STAGES];
             bool ok = true;
-            pdl_wait();  // A and B may come from the previous kernel
-            for (int kb = kb0; kb < kb1; ++kb) {
+            // B is a prepared weight: written once when it is created, never
+            // by a kernel.  So the first stages' B tiles are requested before
+            // the dependency wait, while the previous kernel still runs; A
+            // (which that kernel may write) follows the wait.  The ring's
+            // stages start empty, so these need no empty-barrier wait.
+            const int npre = min(STAGES, kb1 - kb0);
+            for (int i = 0; i < npre; ++i) {
+                mbar_arrive_expect_tx(&full[i], G::STAGE_BYTES);
+                tma_load_2d(tiles + i * G::STAGE_BYTES + G::A_TILE, &tmB, &full[i], (kb0 + i) * G::BK, nb * BN);
+                issued |= 1u << i;
+                last_par[i] = 0u;
+            }
+            pdl_wait();  // A may come from the previous kernel
+            for (int i = 0; i < npre; ++i)
+                tma_load_2d(tiles + i * G::STAGE_BYTES, &tmA, &full[i], (kb0 + i) * G::BK, mb * BM);
+            stage = npre % STAGES;
+            phase = (npre == STAGES) ? 1u : 0u;
+            for (int kb = kb0 + npre; kb < kb1; ++kb) {
                 if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
                     ok = false;
                     break;
