@@ -10,6 +10,8 @@
 // next chunk is copied on the host.  One event per slot says when its DMA is
 // done, so a slot is reused only after that.
 #include <algorithm>
+#include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <cstring>
 #include <mutex>
@@ -22,10 +24,16 @@ namespace pfrt {
 
 namespace {
 
-// memcpy of one buffer split over the caller and `kWorkers` threads.
+// memcpy of one buffer split over the caller and `kWorkers` threads.  A copy
+// is handed over through atomics, and a worker that has just finished one
+// keeps polling for the next for up to kSpinNs before it sleeps on the
+// condition variable: the chunks of one transfer follow each other within
+// microseconds, and a futex wake-up per chunk would cost more than the copy
+// of a 256 KiB chunk.  Idle workers sleep.
 class CopyPool {
 public:
     static constexpr int kWorkers = 3;
+    static constexpr int64_t kSpinNs = 100000;
 
     CopyPool() {
         for (int i = 0; i < kWorkers; ++i) threads_.emplace_back([this, i] { work(i); });
@@ -33,7 +41,7 @@ public:
     ~CopyPool() {
         {
             std::lock_guard<std::mutex> l(m_);
-            stop_ = true;
+            stop_.store(true);
         }
         cv_.notify_all();
         for (auto& t : threads_) t.join();
@@ -46,54 +54,60 @@ public:
             return;
         }
         const size_t part = (n / (kWorkers + 1) + 63) & ~size_t{63};
+        dst_ = static_cast<char*>(dst);
+        src_ = static_cast<const char*>(src);
+        n_ = n;
+        part_ = part;
+        pending_.store(kWorkers, std::memory_order_relaxed);
         {
+            // The release publishes the job to polling workers; the lock
+            // orders it against a worker that is about to sleep.
             std::lock_guard<std::mutex> l(m_);
-            dst_ = static_cast<char*>(dst);
-            src_ = static_cast<const char*>(src);
-            n_ = n;
-            part_ = part;
-            pending_ = kWorkers;
-            ++gen_;
+            gen_.fetch_add(1, std::memory_order_release);
         }
-        cv_.notify_all();
+        if (sleepers_.load(std::memory_order_acquire) > 0) cv_.notify_all();
         std::memcpy(dst, src, std::min(part, n));  // the caller's share: part 0
-        std::unique_lock<std::mutex> l(m_);
-        done_cv_.wait(l, [this] { return pending_ == 0; });
+        while (pending_.load(std::memory_order_acquire) != 0) {
+        }
     }
 
 private:
     void work(int i) {
         uint64_t seen = 0;
         for (;;) {
-            char* dst;
-            const char* src;
-            size_t n, part;
-            {
-                std::unique_lock<std::mutex> l(m_);
-                cv_.wait(l, [&] { return stop_ || gen_ != seen; });
-                if (stop_) return;
-                seen = gen_;
-                dst = dst_;
-                src = src_;
-                n = n_;
-                part = part_;
+            uint64_t g = gen_.load(std::memory_order_acquire);
+            if (g == seen) {
+                const auto t0 = std::chrono::steady_clock::now();
+                while ((g = gen_.load(std::memory_order_acquire)) == seen && !stop_.load() &&
+                       std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0)
+                               .count() < kSpinNs) {
+                }
+                if (g == seen) {
+                    std::unique_lock<std::mutex> l(m_);
+                    sleepers_.fetch_add(1);
+                    cv_.wait(l, [&] { return stop_.load() || gen_.load(std::memory_order_acquire) != seen; });
+                    sleepers_.fetch_sub(1);
+                    if (stop_.load()) return;
+                    g = gen_.load(std::memory_order_acquire);
+                }
             }
+            if (stop_.load()) return;
+            seen = g;
+            const size_t n = n_, part = part_;
             const size_t lo = std::min(n, part * static_cast<size_t>(i + 1));
             const size_t hi = (i == kWorkers - 1) ? n : std::min(n, part * static_cast<size_t>(i + 2));
-            if (hi > lo) std::memcpy(dst + lo, src + lo, hi - lo);
-            {
-                std::lock_guard<std::mutex> l(m_);
-                if (--pending_ == 0) done_cv_.notify_all();
-            }
+            if (hi > lo) std::memcpy(dst_ + lo, src_ + lo, hi - lo);
+            pending_.fetch_sub(1, std::memory_order_release);
         }
     }
 
     std::vector<std::thread> threads_;
     std::mutex m_;
-    std::condition_variable cv_, done_cv_;
-    bool stop_ = false;
-    uint64_t gen_ = 0;
-    int pending_ = 0;
+    std::condition_variable cv_;
+    std::atomic<bool> stop_{false};
+    std::atomic<uint64_t> gen_{0};
+    std::atomic<int> pending_{0};
+    std::atomic<int> sleepers_{0};
     char* dst_ = nullptr;
     const char* src_ = nullptr;
     size_t n_ = 0, part_ = 0;
