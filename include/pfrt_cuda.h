@@ -284,9 +284,9 @@ PFRT_API pfrt_status pfrt_ipc_close(pfrt_ctx* ctx, void* dev_ptr);
  * into its own y.
  * M > 1: the rank computes its column block of Y into its own y (the kernel
  * pfrt_spmm would pick for the shard) and the block reaches every other
- * rank's y over NVLink: stored by the shard GEMM's epilogue as each tile is
- * computed (the dense path, blocks of 2 MiB and more), or by a copy kernel
- * after the SpMM.  Nothing is written into another rank's y before that
+ * rank's y over NVLink: by a copy kernel after the SpMM, or (PFRT_PEER_FUSE=1,
+ * dense path only) stored by the shard GEMM's epilogue as each tile is
+ * computed.  Nothing is written into another rank's y before that
  * rank has declared it free for this call (a rank declares it when its
  * stream reaches the call, i.e. after everything it ran on the previous
  * output); the call ends once every other rank has reported its block

@@ -4,7 +4,7 @@ M = 1: every rank's kernel sends each value of its rows of Y to every other
 rank over NVLink, marked with the call's number, and unpacks the values it
 receives into its own gathered output.  M > 1: every rank computes its column
 block of Y into its own output and one kernel stores the block into every
-other rank's output.  The gathered Y must match pruning::sparse_matmul
+other rank's output (or, opt-in, the dense path's GEMM epilogue does).  The gathered Y must match pruning::sparse_matmul
 (src/pruning/sparse_tensor.cpp:473-519) on the whole W, normwise <= 1e-5, on
 every rank, call after call (the call counter lives on the device), with M
 changing between calls, and inside CUDA graph replays.
@@ -219,6 +219,15 @@ def _rank_main(rank, world, port, q):
             yv = sh(torch.from_numpy(X).cuda()).cpu().numpy()
             rows = _sample(M)
             worst = max(worst, normwise_rel(yv[rows], _ref_rows(c, X, rows)))
+        ctx.check()
+        # the opt-in fused form: the dense path's GEMM epilogue stores the
+        # block into every rank's output (PFRT_PEER_FUSE=1 on every rank)
+        os.environ["PFRT_PEER_FUSE"] = "1"
+        X = c.X[:1024]
+        yv = sh(torch.from_numpy(X).cuda()).cpu().numpy()
+        os.environ.pop("PFRT_PEER_FUSE")
+        rows = _sample(1024)
+        worst = max(worst, normwise_rel(yv[rows], _ref_rows(c, X, rows)))
         ctx.check()
         dist.barrier()
         sh.close()
