@@ -10,7 +10,7 @@ every rank, call after call (the call counter lives on the device), with M
 changing between calls, and inside CUDA graph replays.
 
 World 1 runs on one GPU (the rank's own buffers only), as does the timeout
-test (its peer is a local buffer nobody writes); worlds 2 and 4 need that
+test (its peer is a local buffer nobody writes); worlds 2, 4 and 8 need that
 many GPUs and are skipped with fewer."""
 import ctypes as C
 import os
@@ -238,7 +238,7 @@ def _rank_main(rank, world, port, q):
         q.put((rank, None, None, repr(e)))
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_world_n_gpus(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
