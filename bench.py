@@ -765,9 +765,10 @@ def profile_target(args):
         a = torch.from_numpy(q.a).cuda()
         y = torch.empty((m, N), dtype=torch.int8, device="cuda")
         fns = [lambda: w(a, q.a_scale, q.a_zp, out="int8", y_scale=q.y_scale, y=y)]
-    elif t in ("spmm_m1", "spmm_cfg3", "spmm_mid"):
+    elif t in ("spmm_m1", "spmm_cfg3", "spmm_mid", "spmm_m64"):
         c = (wl.spmm_case(1, SPMM_N, SPMM_K, sparsity=SPMM_S, seed=3) if t == "spmm_m1"
              else wl.spmm_case(256, 4096, 4096, sparsity=0.9, seed=3) if t == "spmm_cfg3"
+             else wl.spmm_case(64, SPMM_N, SPMM_K, sparsity=SPMM_S, seed=3) if t == "spmm_m64"
              else wl.spmm_case(64, SPMM_N, SPMM_K, sparsity=0.95, seed=3))  # tiled CSR kernel
         w = pf.CSR(ctx, c.N, c.K, c.indptr, c.indices, c.values)
         x = torch.from_numpy(c.X).cuda()
@@ -796,7 +797,8 @@ def main():
     ap.add_argument("--eager", action="store_true",
                     help="plain launches without CUDA graph or soak (profiler runs; not a bench value)")
     ap.add_argument("--profile-target", default=None,
-                    choices=["qlinear", "spmm_m1", "spmm_cfg3", "spmm_mid", "gemm_cfg1", "qlinear_4096"],
+                    choices=["qlinear", "spmm_m1", "spmm_cfg3", "spmm_mid", "spmm_m64", "gemm_cfg1",
+                             "qlinear_4096"],
                     help="run only this workload, eagerly, for a profiler; prints its ms/step")
     args = ap.parse_args()
     global EAGER

@@ -344,6 +344,40 @@ struct FEpi {
         for (int i = 0; i < n_peer_out; ++i) write_to<W>(peer_out[i], row, col0, y);
     }
 
+    // The further output copies of one warp's 32 x 32 block (lane l holds row
+    // row0 + l, columns col0 .. col0 + 31; every lane of the warp calls this,
+    // rows past M included).  The block is transposed in registers first, so
+    // each store instruction writes 32 consecutive floats of one row: over
+    // NVLink, 128-byte row pieces instead of 16-byte pieces of 32 rows.
+    __device__ __forceinline__ void write_peers_rows(int row0, int col0, float (&y)[32]) const {
+        const int lane = threadIdx.x & 31;
+        // Recursive block transpose: at block size s, lanes whose bit s differs
+        // exchange the off-diagonal s x s blocks (element (r, c) takes
+        // (r ^ s, c ^ s) where bit s of r and c differ).
+#pragma unroll
+        for (int s = 16; s >= 1; s >>= 1) {
+            const bool upper = (lane & s) != 0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                if ((j & s) == 0) {
+                    const float send = upper ? y[j] : y[j + s];
+                    const float recv = __shfl_xor_sync(0xffffffffu, send, s);
+                    if (upper) y[j] = recv;
+                    else y[j + s] = recv;
+                }
+            }
+        }
+        // Now lane l holds column col0 + l of rows row0 .. row0 + 31.
+        const int col = col0 + lane;
+        if (col >= N) return;
+        for (int i = 0; i < n_peer_out; ++i) {
+            float* d = peer_out[i] + static_cast<int64_t>(row0) * ldo + col;
+#pragma unroll
+            for (int r = 0; r < 32; ++r)
+                if (row0 + r < M) d[static_cast<int64_t>(r) * ldo] = y[r];
+        }
+    }
+
     // Final epilogue from global parameters (split-K reduction, empty K).
     template <int W>
     __device__ __forceinline__ void store_direct(int row, int col0, const float (&acc)[W]) const {
@@ -356,6 +390,19 @@ struct FEpi {
 
     __device__ __forceinline__ void store(const uint8_t* p, int bn, int row, int col0, int cl, int ks,
                                           const uint32_t (&acc)[32]) const {
+        if (out_mode != kOutPartial && n_peer_out > 0) {
+            // Warp-collective: every lane, rows past M included.
+            float y[32];
+            if (row < M) {
+                compute(p, row, col0, cl, acc, y);
+                write_to<32>(out, row, col0, y);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) y[j] = 0.0f;
+            }
+            write_peers_rows(row - (threadIdx.x & 31), col0, y);
+            return;
+        }
         if (row >= M) return;
         if (out_mode == kOutPartial) {
             float* d = partial + (static_cast<int64_t>(ks) * M + row) * N + col0;
@@ -373,6 +420,12 @@ struct FEpi {
             return;
         }
         float y[32];
+        compute(p, row, col0, cl, acc, y);
+        write<32>(row, col0, y);
+    }
+
+    __device__ __forceinline__ void compute(const uint8_t* p, int row, int col0, int cl, const uint32_t (&acc)[32],
+                                            float (&y)[32]) const {
         if (C != nullptr && c_len == N) {
             const float4* cb4 = reinterpret_cast<const float4*>(p) + cl / 4;
 #pragma unroll
@@ -387,7 +440,6 @@ struct FEpi {
 #pragma unroll
             for (int j = 0; j < 32; ++j) y[j] = finalize(row, col0 + j, __uint_as_float(acc[j]));
         }
-        write<32>(row, col0, y);
     }
 };
 

@@ -295,6 +295,11 @@ pfrt_status fweight_from_device_split(pfrt_ctx* ctx, int64_t N, int64_t K, float
     return PFRT_OK;
 }
 
+pfrt_status split_tf32_kmajor(const float* src, int64_t rows, int64_t K, int64_t ld, float* hi, float* lo,
+                              int64_t Kpad, cudaStream_t s) {
+    return launch_split(src, rows, K, ld, 0, hi, lo, Kpad, s);
+}
+
 pfrt_status gemm_f32_strided(pfrt_ctx* ctx, int64_t M, const float* a, int64_t lda, const pfrt_fweight* b,
                              float* y, int64_t ldy, cudaStream_t s, float* const* peer_y, int n_peer_y) {
     if (n_peer_y > kMaxPeerOut) return fail(PFRT_ERR_UNSUPPORTED, "Gemm: too many output copies");

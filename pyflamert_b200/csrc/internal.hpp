@@ -93,6 +93,11 @@ pfrt_status gemm_f32_strided(pfrt_ctx* ctx, int64_t M, const float* a, int64_t l
                              float* y, int64_t ldy, cudaStream_t s, float* const* peer_y = nullptr,
                              int n_peer_y = 0);
 
+// hi[r, k] = tf32(src[r*ld + k]), lo = src - hi for k < K, zeros for
+// K <= k < Kpad: the K-major 3xTF32 split of a row-major operand.
+pfrt_status split_tf32_kmajor(const float* src, int64_t rows, int64_t K, int64_t ld, float* hi, float* lo,
+                              int64_t Kpad, cudaStream_t s);
+
 // Fills `a` with the programmatic-stream-serialization launch attribute
 // (the kernel may start while the previous kernel on the stream finishes;
 // it calls pdl_wait before touching that kernel's data) and returns 1, or

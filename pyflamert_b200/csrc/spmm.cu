@@ -32,6 +32,7 @@
 
 #include "common.cuh"
 #include "internal.hpp"
+#include "spmm_tc.cuh"
 
 struct pfrt_csr {
     pfrt_ctx* ctx = nullptr;
@@ -55,6 +56,14 @@ struct pfrt_csr {
     int64_t part_warps = 0;
     int32_t* part = nullptr;     // [part_warps + 1]
     std::vector<int32_t> host_indptr;
+    // Compressed form for the tensor-core kernel (spmm_tc.cuh), built on
+    // first use: 0 not built, 1 ready, -1 unusable (a column stored twice
+    // in a row).
+    int tc_state = 0;
+    int64_t tc_npad = 0;
+    uint32_t* tc_mask = nullptr;  // [kb_total][tc_npad]
+    uint32_t* tc_off = nullptr;   // [kb_total][tc_npad]
+    float2* tc_vals = nullptr;    // [nnz]
 };
 
 namespace pfrt {
@@ -1234,6 +1243,139 @@ pfrt_status ensure_dense(pfrt_ctx* ctx, pfrt_csr* w, cudaStream_t s) {
     return fweight_from_device_split(ctx, w->N, w->K, hi, lo, &w->dense);
 }
 
+// Compressed form of W for the tensor-core kernel (spmm_tc.cuh), built once
+// on the device.  A row that stores a column twice (the CSR sums them; the
+// compressed form has one slot per position) leaves the form unusable and
+// the other paths serve the weight.
+pfrt_status ensure_tcfmt(pfrt_csr* w, cudaStream_t s) {
+    if (w->tc_state != 0) return PFRT_OK;
+    const int64_t kb_total = ceil_div(std::max<int64_t>(w->K, 1), kTcBK);
+    const int64_t npad = ceil_div(std::max<int64_t>(w->N, 1), kTcWRows) * kTcWRows;
+    const size_t words = static_cast<size_t>(kb_total) * static_cast<size_t>(npad);
+    int* dup = nullptr;
+    cudaError_t e = cudaMalloc(&w->tc_mask, sizeof(uint32_t) * words);
+    if (e == cudaSuccess) e = cudaMalloc(&w->tc_off, sizeof(uint32_t) * words);
+    // 64 entries of slack: the producers prefetch up to 32 entries past the
+    // first value of the k-block they expand.
+    if (e == cudaSuccess) e = cudaMalloc(&w->tc_vals, sizeof(float2) * static_cast<size_t>(w->nnz + 64));
+    if (e == cudaSuccess) e = cudaMalloc(&dup, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemsetAsync(w->tc_mask, 0, sizeof(uint32_t) * words, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(dup, 0, sizeof(int), s);
+    const unsigned row_blocks = static_cast<unsigned>(ceil_div(std::max<int64_t>(w->N, 1) * 32, 256));
+    if (e == cudaSuccess) {
+        tc_mask_kernel<<<row_blocks, 256, 0, s>>>(w->N, npad, w->indptr, w->indices, w->tc_mask, dup);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) {
+        tc_off_kernel<<<static_cast<unsigned>(ceil_div(npad, 256)), 256, 0, s>>>(
+            w->N, npad, static_cast<int>(kb_total), w->indptr, w->nnz, w->tc_mask, w->tc_off);
+        e = cudaGetLastError();
+    }
+    int h_dup = 0;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&h_dup, dup, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess && !h_dup) {
+        tc_vals_kernel<<<row_blocks, 256, 0, s>>>(w->N, npad, w->indptr, w->indices, w->values, w->tc_mask,
+                                                  w->tc_off, w->tc_vals);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    }
+    if (dup) cudaFree(dup);
+    if (e != cudaSuccess || h_dup) {
+        cudaFree(w->tc_mask);
+        cudaFree(w->tc_off);
+        cudaFree(w->tc_vals);
+        w->tc_mask = w->tc_off = nullptr;
+        w->tc_vals = nullptr;
+        w->tc_state = -1;
+        return e != cudaSuccess ? cuda_fail(e, "SpMM compressed form") : PFRT_OK;
+    }
+    w->tc_npad = npad;
+    w->tc_state = 1;
+    return PFRT_OK;
+}
+
+// Stream-K schedule of the tensor-core kernel: the k-blocks of all units
+// split evenly over at most one CTA per SM.
+TcSched tc_schedule(const pfrt_ctx* ctx, const pfrt_csr* w, int64_t M) {
+    TcSched sc{};
+    sc.n_wtiles = static_cast<int>(ceil_div(std::max<int64_t>(w->N, 1), kTcWRows));
+    sc.n_xslabs = M <= 64 ? 1 : static_cast<int>(ceil_div(M, 128));
+    sc.kb_total = static_cast<int>(ceil_div(std::max<int64_t>(w->K, 1), kTcBK));
+    sc.total = static_cast<int64_t>(sc.n_wtiles) * sc.n_xslabs * sc.kb_total;
+    sc.per_cta = ceil_div(sc.total, static_cast<int64_t>(ctx->num_sms));
+    return sc;
+}
+
+// Expected time of the tensor-core kernel, fitted to measurements on
+// 4096^2 and 8192^2 weights: per k-block of a CTA's range 0.65 us (stacked,
+// 8 MMAs of 128 x 128 x 8) or 0.87 us (wide, 12 MMAs), plus the X split,
+// the fix-up of the shared units and the launches.
+double tc_time(const pfrt_ctx* ctx, const pfrt_csr* w, int64_t M) {
+    const TcSched sc = tc_schedule(ctx, w, M);
+    return static_cast<double>(sc.per_cta) * (M <= 64 ? 0.65e-6 : 0.87e-6) + 12.0e-6;
+}
+
+// Y = X W^T on the tensor cores from W's compressed form (spmm_tc.cuh).
+pfrt_status run_spmm_tc(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x, int64_t ldx, float* y,
+                        int64_t ldy, cudaStream_t s) {
+    pfrt_status st = ensure_tcfmt(w, s);
+    if (st) return st;
+    if (w->tc_state != 1) return PFRT_ERR_UNSUPPORTED;
+    const int64_t kpad = static_cast<int64_t>(align_up(static_cast<size_t>(w->K), kTcBK));
+    const TcSched sc = tc_schedule(ctx, w, M);
+    const int64_t grid = ceil_div(sc.total, sc.per_cta);
+    const bool stacked = M <= 64;
+    const size_t xbytes = align_up(sizeof(float) * static_cast<size_t>(M * kpad), 256);
+    const size_t pbytes = sizeof(float) * static_cast<size_t>(2 * grid * kTcTileElems);
+    void* scr = nullptr;
+    st = scratch(ctx, 2 * xbytes + pbytes, &scr);
+    if (st) return st;
+    float* xhi = static_cast<float*>(scr);
+    float* xlo = reinterpret_cast<float*>(static_cast<uint8_t*>(scr) + xbytes);
+    float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(scr) + 2 * xbytes);
+    st = split_tf32_kmajor(x, M, w->K, ldx, xhi, xlo, kpad, s);
+    if (st) return st;
+    CUtensorMap tmh, tml;
+    st = make_tmap_2d(&tmh, xhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, kpad, M, kpad * 4, kTcBK, 64);
+    if (st == PFRT_OK)
+        st = make_tmap_2d(&tml, xlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, kpad, M, kpad * 4, kTcBK, 64);
+    if (st) return st;
+    TcArgs a{};
+    a.mask = w->tc_mask;
+    a.off = w->tc_off;
+    a.vals = w->tc_vals;
+    a.npad = w->tc_npad;
+    a.M = static_cast<int>(M);
+    a.N = static_cast<int>(w->N);
+    a.y = y;
+    a.ldy = ldy;
+    a.partial = part;
+    auto kern = stacked ? spmm_tc_kernel<true> : spmm_tc_kernel<false>;
+    PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes));
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = kTcSmemBytes;
+    cfg.stream = s;
+    cfg.numAttrs = pdl_attr(attr);
+    cfg.attrs = attr;
+    PFRT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tmh, tml, sc, a, ctx->d_err));
+    if (grid > 1) {
+        cudaLaunchConfig_t rc{};
+        rc.gridDim = dim3(static_cast<unsigned>(grid - 1), static_cast<unsigned>((stacked ? 64 : 128) * kTcWRows / 1024));
+        rc.blockDim = dim3(256);
+        rc.stream = s;
+        rc.numAttrs = pdl_attr(attr);
+        rc.attrs = attr;
+        PFRT_CUDA_TRY(cudaLaunchKernelEx(&rc, tc_fixup_kernel, sc, static_cast<const float*>(part),
+                                         static_cast<int>(M), static_cast<int>(w->N), stacked ? 64 : 128, y,
+                                         ldy));
+    }
+    return PFRT_OK;
+}
+
 template <int MV, bool SMEM>
 pfrt_status launch_stream(pfrt_ctx* ctx, pfrt_csr* w, int M, const float* x, int64_t ldx, float* y,
                           int64_t ldy, size_t shm, cudaStream_t s) {
@@ -1434,7 +1576,20 @@ pfrt_status spmm_uploaded(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x,
     bool use_dense = dense_ok && t_dense < t_tiled;
     if (dense_env && *dense_env) use_dense = dense_ok && *dense_env == '1';
     if (tiled_env && *tiled_env) use_dense = use_dense && *tiled_env == '0';
+    // The tensor-core kernel on W's compressed form: the dense path's
+    // arithmetic without reading a dense copy of W.
+    const char* tc_env = std::getenv("PFRT_SPMM_TC");
+    const bool tc_ok = w->N > 0 && w->K > 0 && w->tc_state >= 0 && M <= (int64_t{1} << 30) / std::max<int64_t>(w->N, 1);
+    // PFRT_SPMM_TC = 0|1 forces it off or on; PFRT_SPMM_DENSE or
+    // PFRT_SPMM_TILED set without it chooses among the other paths only.
+    bool use_tc = tc_ok && !(dense_env && *dense_env) && !(tiled_env && *tiled_env) &&
+                  tc_time(ctx, w, M) < std::min(t_tiled, dense_ok ? t_dense : 1e30);
+    if (tc_env && *tc_env) use_tc = tc_ok && *tc_env == '1';
     pfrt_status st;
+    if (use_tc) {
+        st = run_spmm_tc(ctx, w, M, x, ldx, y, ldy, s);
+        if (st != PFRT_ERR_UNSUPPORTED) return st;  // else the form is unusable for this weight
+    }
     if (use_dense) {
         st = ensure_dense(ctx, w, s);
         if (st) return st;
@@ -1663,6 +1818,9 @@ pfrt_status pfrt_csr_destroy(pfrt_csr* w) {
     if (w->xt_part) cudaFree(w->xt_part);
     if (w->part) cudaFree(w->part);
     if (w->dense) pfrt_fweight_destroy(w->dense);
+    if (w->tc_mask) cudaFree(w->tc_mask);
+    if (w->tc_off) cudaFree(w->tc_off);
+    if (w->tc_vals) cudaFree(w->tc_vals);
     delete w;
     return PFRT_OK;
 }

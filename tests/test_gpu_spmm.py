@@ -169,6 +169,54 @@ def test_large_batch_dense_and_csr_paths(ctx, dense, M, N, K, sparsity, monkeypa
     assert normwise_rel(y, f64) <= 2 * normwise_rel(ref, f64) + 1e-6
 
 
+@pytest.mark.parametrize("M,N,K,sparsity", [(9, 300, 700, 0.9), (64, 1000, 333, 0.5), (100, 129, 4100, 0.99),
+                                            (256, 4096, 4096, 0.9), (300, 2048, 2048, 0.7)])
+def test_tensor_core_kernel(ctx, M, N, K, sparsity, monkeypatch):
+    """The tensor-core kernel on W's compressed form (W densified in TMEM),
+    forced: tails in M (slabs of 64 rows of X), N (tiles of 128 rows of W)
+    and K (k-blocks of 32), and the cost model's K split."""
+    monkeypatch.setenv("PFRT_SPMM_TC", "1")
+    c = wl.spmm_case(M, N, K, sparsity=sparsity, seed=M + N + K + 1)
+    y = gpu(ctx, c)
+    ref = oracle(c)
+    assert normwise_rel(y, ref) <= FP32_TOL
+    f64 = po.spmm_linear_f64(c.indptr, c.indices, c.values, c.X, c.N)
+    assert normwise_rel(y, f64) <= 2 * normwise_rel(ref, f64) + 1e-6
+
+
+@pytest.mark.parametrize("M,N,K", [(70, 333, 1000), (30, 100, 1000), (300, 4096, 1000), (200, 129, 4100)])
+def test_tensor_core_kernel_schedules(ctx, M, N, K, monkeypatch):
+    """The stream-K schedule over the SMs: fewer k-blocks than SMs (one
+    k-block per CTA, every unit finished by the fix-up from up to 32
+    partial tiles), CTA ranges longer than a unit (whole units in the
+    middle, partial pieces at both ends) and shorter ones; rows of W without
+    nonzeros give exact zeros."""
+    monkeypatch.setenv("PFRT_SPMM_TC", "1")
+    rng = np.random.default_rng(M + N + K)
+    counts, indptr, indices, values = _ragged_csr(rng, N, K, 120)
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    c = wl.CsrCase(N, K, indptr, indices, values, X)
+    y = gpu(ctx, c)
+    assert normwise_rel(y, oracle(c)) <= FP32_TOL
+    np.testing.assert_array_equal(y[:, counts == 0], 0.0)
+
+
+def test_tensor_core_kernel_duplicate_columns_fall_back(ctx, monkeypatch):
+    """A CSR row that stores a column twice (the reference sums both) cannot
+    use the compressed form; the call falls back to another path and still
+    matches the oracle."""
+    monkeypatch.setenv("PFRT_SPMM_TC", "1")
+    rng = np.random.default_rng(3)
+    N, K, M = 40, 96, 33
+    indptr = np.arange(0, 4 * N + 1, 4, dtype=np.int32)
+    indices = rng.integers(0, K, 4 * N).astype(np.int32)
+    indices[1] = indices[0]  # row 0 stores one column twice
+    values = rng.standard_normal(4 * N).astype(np.float32)
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    c = wl.CsrCase(N, K, indptr, indices, values, X)
+    assert normwise_rel(gpu(ctx, c), oracle(c)) <= FP32_TOL
+
+
 def test_dense_path_reuses_copy_and_keeps_empty_rows_zero(ctx, monkeypatch):
     """The dense copy is built once per CSR and reused; rows of W with no
     nonzeros still give exact zeros."""
