@@ -500,10 +500,58 @@ def spmm_point(nnz, M, ms, world, peaks):
     t_hbm = per_gpu_bytes / (peaks["hbm_gbs"] * 1e9)
     t_simt = flops / world / (FP32_SIMT_TFLOPS * 1e12)
     t = ms * 1e-3
+    # The tensor-core paths (W densified on chip, or the dense copy) do the
+    # dense product as 3xTF32: 3 x 2 M N K tf32 operations, at the tf32 rate
+    # (half the measured bf16 rate).
+    tf32_tflops = peaks["bf16_tflops"] / 2.0
+    t_tc = 6.0 * M * SPMM_N * SPMM_K / world / (tf32_tflops * 1e12)
     return {"M": M, "ms_per_step": ms, "tflops": flops / t / 1e12, "gbs": alg_bytes / t / 1e9,
             "roofline": {"bound": "hbm" if t_hbm >= t_simt else "fp32-simt",
                          "roof_ms": 1e3 * max(t_hbm, t_simt), "frac": max(t_hbm, t_simt) / t,
-                         "per": "GPU", "hbm_gbs": peaks["hbm_gbs"], "fp32_simt_tflops": FP32_SIMT_TFLOPS}}
+                         "per": "GPU", "hbm_gbs": peaks["hbm_gbs"], "fp32_simt_tflops": FP32_SIMT_TFLOPS},
+            "roofline_dense_3xtf32": {"roof_ms": 1e3 * t_tc, "frac": t_tc / t, "tf32_tflops": tf32_tflops,
+                                      "note": "the dense product on the tensor pipe, the bound of the "
+                                              "tensor-core paths"}}
+
+
+def spmm_config3(ctx, args, peaks, peak_src, sampler):
+    """Config 3 (the pruned Linear: X [256, 4096] times W^T, W 4096 x 4096 at
+    90 % sparsity) through pfrt_spmm's default path, one GPU, rotating over
+    copies of W larger than L2 together."""
+    import torch
+
+    import pyflamert_b200 as pf
+    from pyflamert_b200 import workloads as wl
+    M3, N3, K3 = 256, 4096, 4096
+    c = wl.spmm_case(M3, N3, K3, sparsity=0.9, seed=3)
+    nnz = int(c.values.size)
+    ncopies = int(min(24, max(2, math.ceil(2 * L2_BYTES / (12.0 * nnz)))))
+    ws = [pf.CSR(ctx, N3, K3, c.indptr, c.indices, c.values) for _ in range(ncopies)]
+    x = torch.from_numpy(c.X).cuda()
+    y = torch.empty((M3, N3), dtype=torch.float32, device="cuda")
+    fns = [(lambda w=w: w(x, y=y)) for w in ws]
+    for f in fns:  # builds each copy's lazily made device state
+        f()
+    torch.cuda.synchronize()
+    ms, t0, t1 = graph_time(fns, args.steps, args.warmup, 1, soak=False)
+    ctx.check()
+    for w in ws:
+        w.close()
+    flops = 2.0 * nnz * M3
+    alg_bytes = 8.0 * nnz + 4.0 * (N3 + 1) + 4.0 * M3 * K3 + 4.0 * M3 * N3
+    tf32 = peaks["bf16_tflops"] / 2.0
+    t_tc = 6.0 * M3 * N3 * K3 / (tf32 * 1e12)
+    t_hbm = alg_bytes / (peaks["hbm_gbs"] * 1e9)
+    return {"metric": "CSR SpMM us per call (config 3: X 256x4096, W 4096x4096 90% sparse)",
+            "value": ms * 1e3, "unit": "us", "higher_is_better": False, "ms_per_step": ms,
+            "useful_tflops": flops / (ms * 1e-3) / 1e12,
+            "path": "pfrt_spmm default (cost model: tensor cores on W's compressed form, the dense copy, "
+                    "or the tiled CSR kernel)",
+            "roofline": {"bound": "tensor (dense 3xTF32)", "roof_us": 1e6 * t_tc, "frac": t_tc / (ms * 1e-3),
+                         "tf32_tflops": tf32, "hbm_roof_us": 1e6 * t_hbm,
+                         "peak_source": f"bf16_tflops / 2, hbm_gbs ({peak_src} MEASURED_PEAKS.json)"},
+            "clocks": sampler.summary(t0, t1), "gpu_launches": 3 * args.steps,
+            "l2": f"{ncopies} copies of W rotated"}
 
 
 def spmm_sweep(ctx, args, world, rank, peaks, peak_src, sampler):  # noqa: C901
@@ -941,6 +989,7 @@ def main():
             }
             for obj in sc:
                 obj[0].close()
+            line["spmm_config3"] = spmm_config3(ctx, args, peaks, peak_src, sampler)
         else:
             line["spmm"] = spmm_nshard(ctx, args, world, rank, peaks, peak_src)
         line["spmm_sweep"] = spmm_sweep(ctx, args, world, rank, peaks, peak_src, sampler)

@@ -1308,12 +1308,12 @@ TcSched tc_schedule(const pfrt_ctx* ctx, const pfrt_csr* w, int64_t M) {
 }
 
 // Expected time of the tensor-core kernel, fitted to measurements on
-// 4096^2 and 8192^2 weights: per k-block of a CTA's range 0.65 us (stacked,
-// 8 MMAs of 128 x 128 x 8) or 0.87 us (wide, 12 MMAs), plus the X split,
-// the fix-up of the shared units and the launches.
+// 4096^2 and 8192^2 weights at 90 % sparsity: per k-block of a CTA's range
+// 0.59 us (stacked, 8 MMAs of 128 x 128 x 8) or 0.82 us (wide, 12 MMAs),
+// plus the X split, the fix-up of the shared units and the launches.
 double tc_time(const pfrt_ctx* ctx, const pfrt_csr* w, int64_t M) {
     const TcSched sc = tc_schedule(ctx, w, M);
-    return static_cast<double>(sc.per_cta) * (M <= 64 ? 0.65e-6 : 0.87e-6) + 12.0e-6;
+    return static_cast<double>(sc.per_cta) * (M <= 64 ? 0.59e-6 : 0.82e-6) + 12.0e-6;
 }
 
 // Y = X W^T on the tensor cores from W's compressed form (spmm_tc.cuh).
@@ -1579,11 +1579,18 @@ pfrt_status spmm_uploaded(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x,
     // The tensor-core kernel on W's compressed form: the dense path's
     // arithmetic without reading a dense copy of W.
     const char* tc_env = std::getenv("PFRT_SPMM_TC");
-    const bool tc_ok = w->N > 0 && w->K > 0 && w->tc_state >= 0 && M <= (int64_t{1} << 30) / std::max<int64_t>(w->N, 1);
-    // PFRT_SPMM_TC = 0|1 forces it off or on; PFRT_SPMM_DENSE or
+    const bool tc_ok = w->N > 0 && w->K > 0 && w->tc_state >= 0 &&
+                       M <= (int64_t{1} << 30) / std::max<int64_t>(w->N, 1);
+    // Chosen for up to 256 rows of X: above that the dense copy's Gemm was
+    // as fast or faster (8192^2 at 90 %: M = 512 362 against ~400 us,
+    // M = 1024 708 against 728 us), and once X's hi/lo split outgrows L2
+    // every W tile re-reads it from HBM (M = 8192: 7.2 ms against 5.9 ms).
+    // Within 10 % of the dense path it is still preferred: it reads 8 bytes
+    // per nonzero instead of 8 per element of W and holds no dense copy.
+    // PFRT_SPMM_TC = 0|1 forces it off or on (any M); PFRT_SPMM_DENSE or
     // PFRT_SPMM_TILED set without it chooses among the other paths only.
-    bool use_tc = tc_ok && !(dense_env && *dense_env) && !(tiled_env && *tiled_env) &&
-                  tc_time(ctx, w, M) < std::min(t_tiled, dense_ok ? t_dense : 1e30);
+    bool use_tc = tc_ok && M <= 256 && !(dense_env && *dense_env) && !(tiled_env && *tiled_env) &&
+                  tc_time(ctx, w, M) < std::min(t_tiled, dense_ok ? 1.1 * t_dense : 1e30);
     if (tc_env && *tc_env) use_tc = tc_ok && *tc_env == '1';
     pfrt_status st;
     if (use_tc) {

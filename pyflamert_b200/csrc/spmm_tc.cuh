@@ -192,26 +192,51 @@ __device__ __forceinline__ void tmem_st_wait() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// Expands one row's k-block into hi[j], lo[j] (j = 0..31): the stored values
-// in column order from p, zeros where the mask bit is clear.  Each column's
-// load is predicated on its bit (inline PTX, so no branch) and no load
-// depends on another's result: all 32 are in flight at once and the warp
-// waits for memory once per k-block, not once per stored value.
-__device__ __forceinline__ void tc_expand(uint32_t m, const float2* __restrict__ p, uint32_t (&hi)[32],
-                                          uint32_t (&lo)[32]) {
-    uint32_t idx = 0;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        float h = 0.0f, l = 0.0f;
-        asm("{\n\t.reg .pred q;\n\t"
-            "setp.ne.b32 q, %2, 0;\n\t"
-            "@q ld.global.nc.v2.f32 {%0, %1}, [%3];\n\t}"
-            : "+f"(h), "+f"(l)
-            : "r"(m & (1u << j)), "l"(p + idx));
-        idx += (m >> j) & 1u;
-        hi[j] = __float_as_uint(h);
-        lo[j] = __float_as_uint(l);
-    }
+// Expands 8 columns [8 G, 8 G + 8) of one row's k-block into hi[j], lo[j]:
+// the stored values in column order from *p (advanced past the values it
+// used), zeros where the mask bit is clear.  Hand-written PTX so that each
+// column costs a predicate, two zeroing moves, one predicated 8-byte load
+// and one predicated pointer step: no load depends on another's result, so
+// all are in flight at once, and the producers leave the SM's issue slots
+// to the MMA thread that shares their scheduler.
+template <int G>
+__device__ __forceinline__ void tc_expand8(uint32_t m, const float2*& p, uint32_t (&hi)[32], uint32_t (&lo)[32]) {
+    uint64_t a = reinterpret_cast<uint64_t>(p);
+    asm("{\n\t.reg .pred q0, q1, q2, q3, q4, q5, q6, q7;\n\t"
+        ".reg .b32 t;\n\t"
+#define PFRT_TC_COL(J, Q, H, L)                                 \
+        "and.b32 t, %17, " #J ";\n\t"                          \
+        "setp.ne.b32 " #Q ", t, 0;\n\t"                        \
+        "mov.b32 " H ", 0;\n\t"                                 \
+        "mov.b32 " L ", 0;\n\t"                                 \
+        "@" #Q " ld.global.nc.v2.b32 {" H ", " L "}, [%16];\n\t" \
+        "@" #Q " add.s64 %16, %16, 8;\n\t"
+        PFRT_TC_COL(%18, q0, "%0", "%8")
+        PFRT_TC_COL(%19, q1, "%1", "%9")
+        PFRT_TC_COL(%20, q2, "%2", "%10")
+        PFRT_TC_COL(%21, q3, "%3", "%11")
+        PFRT_TC_COL(%22, q4, "%4", "%12")
+        PFRT_TC_COL(%23, q5, "%5", "%13")
+        PFRT_TC_COL(%24, q6, "%6", "%14")
+        PFRT_TC_COL(%25, q7, "%7", "%15")
+#undef PFRT_TC_COL
+        "}"
+        : "=&r"(hi[8 * G + 0]), "=&r"(hi[8 * G + 1]), "=&r"(hi[8 * G + 2]), "=&r"(hi[8 * G + 3]),
+          "=&r"(hi[8 * G + 4]), "=&r"(hi[8 * G + 5]), "=&r"(hi[8 * G + 6]), "=&r"(hi[8 * G + 7]),
+          "=&r"(lo[8 * G + 0]), "=&r"(lo[8 * G + 1]), "=&r"(lo[8 * G + 2]), "=&r"(lo[8 * G + 3]),
+          "=&r"(lo[8 * G + 4]), "=&r"(lo[8 * G + 5]), "=&r"(lo[8 * G + 6]), "=&r"(lo[8 * G + 7]),
+          "+l"(a)
+        : "r"(m), "n"(1u << (8 * G + 0)), "n"(1u << (8 * G + 1)), "n"(1u << (8 * G + 2)),
+          "n"(1u << (8 * G + 3)), "n"(1u << (8 * G + 4)), "n"(1u << (8 * G + 5)), "n"(1u << (8 * G + 6)),
+          "n"(1u << (8 * G + 7)));
+    p = reinterpret_cast<const float2*>(a);
+}
+
+__device__ __forceinline__ void tc_expand(uint32_t m, const float2* p, uint32_t (&hi)[32], uint32_t (&lo)[32]) {
+    tc_expand8<0>(m, p, hi, lo);
+    tc_expand8<1>(m, p, hi, lo);
+    tc_expand8<2>(m, p, hi, lo);
+    tc_expand8<3>(m, p, hi, lo);
 }
 
 // Partial-tile slot of CTA b's piece of unit u: 2b for the first piece of
