@@ -183,10 +183,12 @@ pfrt_status launch_q2(pfrt_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& 
 }
 
 // The split-K cluster kernel (umma_gemm_sk.cuh): one 128 x BN tile per
-// cluster of two CTAs, each taking half of K.
+// cluster of two CTAs, each taking about half of K (tmBh: the weight's map
+// with a BN/2-row box; tail: the k-blocks in which each CTA accumulates only
+// its own half of the columns, umma_gemm_sk.cuh).
 template <int BN, int STAGES>
-pfrt_status launch_qsk2(pfrt_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmSched& s,
-                        const QEpi& e, uint4* xchg, cudaStream_t st) {
+pfrt_status launch_qsk2(pfrt_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmBh,
+                        const GemmSched& s, int tail, const QEpi& e, uint4* xchg, cudaStream_t st) {
     using Cfg = GemmSkCfg<BN, STAGES>;
     auto kern = umma_gemm_sk2_kernel<BN, STAGES, QEpi>;
     PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
@@ -202,7 +204,7 @@ pfrt_status launch_qsk2(pfrt_ctx* ctx, const CUtensorMap& tmA, const CUtensorMap
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1 + pdl_attr(attr + 1);
-    PFRT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tmA, tmB, s, e, xchg, ctx->d_err));
+    PFRT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmBh, s, tail, e, xchg, ctx->d_err));
     return PFRT_OK;
 }
 
@@ -456,7 +458,12 @@ pfrt_status pfrt_qlinear(pfrt_ctx* ctx, const pfrt_qweight* w, int64_t M, const 
         ks2.kb_per_split = kb_total;
         QEpi ek = eg;
         ek.idesc = idesc_make(2, a_is_u8 ? 0u : 1u, 1u, 128, 256);
-        st = launch_qsk2<256, 4>(ctx, tmA, w->tm_b256, ks2, ek,
+        // Early exchange: each CTA's last `tail` k-blocks cover only its own
+        // half of the columns, so the peer's half is exchanged while they run
+        // (umma_gemm_sk.cuh).  PFRT_QGEMM_SK2_TAIL overrides.
+        int tail = env_int("PFRT_QGEMM_SK2_TAIL", kb_total / 8);
+        tail = std::max(0, std::min(tail, kb_total - 2));
+        st = launch_qsk2<256, 4>(ctx, tmA, w->tm_b256, w->tm_b128, ks2, tail, ek,
                                  reinterpret_cast<uint4*>(base + pad_bytes + rs_bytes + part_bytes), s);
         if (st) return st;
         PFRT_CHECK_LAUNCH("umma_gemm_sk2_kernel<i8>");

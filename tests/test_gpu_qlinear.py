@@ -203,9 +203,9 @@ def test_pair_kernel(ctx, M, N, K, bn, monkeypatch):
 ])
 def test_split_k_cluster_kernel(ctx, M, N, K, out, relu, bias, y_zp, monkeypatch):
     """K split over a cluster of two CTAs (umma_gemm_sk.cuh): each CTA
-    accumulates half of the k-blocks of a 128 x 256 tile and the partials meet
-    through distributed shared memory.  Outputs and accumulators bit-exact and
-    equal to the one-CTA kernel's."""
+    accumulates about half of the k-blocks of a 128 x 256 tile and the
+    partials meet through an L2-resident exchange buffer.  Outputs and
+    accumulators bit-exact and equal to the one-CTA kernel's."""
     monkeypatch.setenv("PFRT_QGEMM_SK2", "1")
     q = wl.qlinear_case(M, N, K, seed=M + 5 * N + K, bias=bias, relu=relu, out=out, y_scale=6.0, y_zp=y_zp)
     y, acc = run(ctx, q)
@@ -220,6 +220,31 @@ def test_split_k_cluster_kernel(ctx, M, N, K, out, relu, bias, y_zp, monkeypatch
     y0, acc0 = run(ctx, q)
     np.testing.assert_array_equal(bits(y0), bits(y))
     np.testing.assert_array_equal(acc0, acc)
+
+
+@pytest.mark.parametrize("M,N,K,tail", [
+    (512, 4096, 4096, 1),       # config 2, odd tail: phase-1 ranges of 15 and 16 k-blocks
+    (512, 4096, 4096, 30),      # the longest tail: one phase-1 k-block per CTA
+    (512, 4096, 4096, 99),      # clipped to kb_total - 2
+    (129, 520, 1152, 3),        # 9 k-blocks, N tail inside the own half of the last tile
+    (7, 256, 4000, 7),          # K tail inside the last k-block
+    (300, 1000, 777, 2),
+])
+def test_split_k_cluster_early_exchange(ctx, M, N, K, tail, monkeypatch):
+    """The split-K cluster kernel's early exchange: each CTA's last `tail`
+    k-blocks accumulate only its own half of the columns while the other half
+    is exchanged.  Every tail gives the exact accumulators and bit-identical
+    outputs."""
+    monkeypatch.setenv("PFRT_QGEMM_SK2", "1")
+    monkeypatch.setenv("PFRT_QGEMM_SK2_TAIL", str(tail))
+    q = wl.qlinear_case(M, N, K, seed=7 * M + N + K + tail, bias=True, relu=True, out="int8", y_scale=6.0,
+                        y_zp=1)
+    y, acc = run(ctx, q)
+    ex = exact_acc(q.a, q.a_zp, q.w)
+    np.testing.assert_array_equal(acc.astype(np.int64), ex)
+    np.testing.assert_array_equal(y, po.qepilogue(ex, q.a_scale, q.w_scale, q.bias, True, "int8", 6.0, 1))
+    y1, _ = run(ctx, q, want_acc=False)
+    np.testing.assert_array_equal(y1, y)
 
 
 def test_split_k_cluster_weight_zero_point(ctx, monkeypatch):
