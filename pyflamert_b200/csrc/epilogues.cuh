@@ -57,6 +57,21 @@ __device__ __forceinline__ int32_t requant_rn(float y, float inv_scale, int32_t 
     return u8 ? min(max(q, 0), 255) : min(max(q, -128), 127);
 }
 
+// requant_rn with zp == 0 in one saturating conversion: for s < 2^31,
+// clamp((int32)trunc(s), qmin, qmax) is cvt.rzi.sat to the 8-bit type (which
+// also sends -inf and everything below qmin to qmin); s >= 2^31 and NaN, which
+// the reference's conversion turns into INT32_MIN, clamp to qmin as well.
+template <bool U8>
+__device__ __forceinline__ int32_t requant_rn_zp0(float y, float inv_scale) {
+    const float t = __fmul_rn(y, inv_scale);
+    const float p = __int_as_float(0x3EFFFFFF | (__float_as_int(t) & static_cast<int>(0x80000000u)));
+    const float s = __fadd_rn(t, p);
+    int32_t q;
+    if constexpr (U8) asm("cvt.rzi.sat.u8.f32 %0, %1;" : "=r"(q) : "f"(s));
+    else asm("cvt.rzi.sat.s8.f32 %0, %1;" : "=r"(q) : "f"(s));
+    return (s < 2147483648.0f) ? q : (U8 ? 0 : -128);
+}
+
 // Low bytes of four values packed little-endian into one word.
 __device__ __forceinline__ uint32_t pack_bytes4(int32_t a, int32_t b, int32_t c, int32_t d) {
     return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
@@ -180,8 +195,10 @@ struct QEpi {
 
     // The requantized int8/uint8 tile row (no accumulator copy, int32-exact
     // zero-point correction): the common case, specialised on the fused
-    // bias, ReLU and output type so each output costs ~15 instructions.
-    template <bool HB, bool RL, bool U8>
+    // bias, ReLU, output type and a zero output zero-point (Z0: one
+    // saturating conversion instead of truncation, offset and clamp), so each
+    // output costs ~11-15 instructions.
+    template <bool HB, bool RL, bool U8, bool Z0>
     __device__ __forceinline__ void store_q8(const uint8_t* p, int bn, int row, int col0, int cl, int32_t rterm,
                                              const uint32_t (&acc)[32]) const {
         const int4* zc4 = reinterpret_cast<const int4*>(p) + cl / 4;
@@ -208,7 +225,8 @@ struct QEpi {
                 // max(0, t) as activation.cpp:56 computes it, up to the sign of
                 // a zero result, which the integer conversion below discards.
                 if constexpr (RL) t = fmaxf(t, 0.0f);
-                q[u] = requant_rn(t, inv_y_scale, y_zp, U8);
+                if constexpr (Z0) q[u] = requant_rn_zp0<U8>(t, inv_y_scale);
+                else q[u] = requant_rn(t, inv_y_scale, y_zp, U8);
             }
             packed[v] = pack_bytes4(q[0], q[1], q[2], q[3]);
         }
@@ -220,6 +238,22 @@ struct QEpi {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
                 if (col0 + j < N) d[j] = static_cast<uint8_t>((packed[j >> 2] >> (8 * (j & 3))) & 0xFFu);
+        }
+    }
+
+    template <bool Z0>
+    __device__ __forceinline__ void store_q8_sel(const uint8_t* p, int bn, int row, int col0, int cl,
+                                                 int32_t rterm, const uint32_t (&acc)[32], bool u8) const {
+        if (bias != nullptr) {
+            if (relu) u8 ? store_q8<true, true, true, Z0>(p, bn, row, col0, cl, rterm, acc)
+                         : store_q8<true, true, false, Z0>(p, bn, row, col0, cl, rterm, acc);
+            else u8 ? store_q8<true, false, true, Z0>(p, bn, row, col0, cl, rterm, acc)
+                    : store_q8<true, false, false, Z0>(p, bn, row, col0, cl, rterm, acc);
+        } else {
+            if (relu) u8 ? store_q8<false, true, true, Z0>(p, bn, row, col0, cl, rterm, acc)
+                         : store_q8<false, true, false, Z0>(p, bn, row, col0, cl, rterm, acc);
+            else u8 ? store_q8<false, false, true, Z0>(p, bn, row, col0, cl, rterm, acc)
+                    : store_q8<false, false, false, Z0>(p, bn, row, col0, cl, rterm, acc);
         }
     }
 
@@ -236,17 +270,8 @@ struct QEpi {
         if (fast32 && out_mode != kOutF32 && acc_out == nullptr) {
             const int32_t rterm = (w_zp != 0) ? w_zp * rs - K * a_zp * w_zp : 0;
             const bool u8 = (out_mode == kOutU8);
-            if (bias != nullptr) {
-                if (relu) u8 ? store_q8<true, true, true>(p, bn, row, col0, cl, rterm, acc)
-                             : store_q8<true, true, false>(p, bn, row, col0, cl, rterm, acc);
-                else u8 ? store_q8<true, false, true>(p, bn, row, col0, cl, rterm, acc)
-                        : store_q8<true, false, false>(p, bn, row, col0, cl, rterm, acc);
-            } else {
-                if (relu) u8 ? store_q8<false, true, true>(p, bn, row, col0, cl, rterm, acc)
-                             : store_q8<false, true, false>(p, bn, row, col0, cl, rterm, acc);
-                else u8 ? store_q8<false, false, true>(p, bn, row, col0, cl, rterm, acc)
-                        : store_q8<false, false, false>(p, bn, row, col0, cl, rterm, acc);
-            }
+            if (y_zp == 0) store_q8_sel<true>(p, bn, row, col0, cl, rterm, acc, u8);
+            else store_q8_sel<false>(p, bn, row, col0, cl, rterm, acc, u8);
             return;
         }
         if (fast32) {

@@ -247,6 +247,26 @@ def test_split_k_cluster_early_exchange(ctx, M, N, K, tail, monkeypatch):
     np.testing.assert_array_equal(y1, y)
 
 
+@pytest.mark.parametrize("out", ["int8", "uint8"])
+@pytest.mark.parametrize("y_scale", [0.05, 1e-12, 1e-40])
+@pytest.mark.parametrize("relu,bias", [(False, False), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(512, 4096, 4096), (130, 300, 256)])
+def test_zero_point_zero_requant_extremes(ctx, M, N, K, relu, bias, y_scale, out):
+    """Output zero-point 0 takes a saturating 8-bit conversion in the fused
+    epilogue.  A tiny y_scale drives y / y_scale past 2^31 (the reference's
+    conversion gives INT32_MIN there, which clamps to the type's minimum), and
+    y_scale = 1e-40 makes 1 / y_scale infinite, so zero accumulators give NaN
+    and the others +-inf.  Rows of A equal to its zero-point give zero
+    accumulators.  Bit-exact against the reference arithmetic."""
+    q = wl.qlinear_case(M, N, K, seed=M + N + int(-np.log10(y_scale)), bias=bias, relu=relu, out=out,
+                        y_scale=y_scale, y_zp=0)
+    q.a[::7] = q.a_zp
+    y, acc = run(ctx, q, want_acc=False)
+    ex = exact_acc(q.a, q.a_zp, q.w)
+    np.testing.assert_array_equal(y, po.qepilogue(ex, q.a_scale, q.w_scale, q.bias, relu, out, y_scale, 0))
+    np.testing.assert_array_equal(y[:3], oracle(q, rows=3))
+
+
 def test_split_k_cluster_weight_zero_point(ctx, monkeypatch):
     monkeypatch.setenv("PFRT_QGEMM_SK2", "1")
     q = wl.qlinear_case(150, 512, 640, seed=21, a_signed=True, w_zp=-3, out="int8", y_scale=2.0, y_zp=-5)
