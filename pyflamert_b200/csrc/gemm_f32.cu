@@ -40,22 +40,39 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
     lo = __fsub_rn(x, hi);
 }
 
+constexpr int kSplitRows = 8;  // blockDim.y of split_kmajor_kernel
+
 // out_{hi,lo}[r, k] = split(src(r, k)) for k < K, 0 for K <= k < Kpad, where
 // src(r, k) = src[r*ld + k] (trans = 0) or src[k*ld + r] (trans = 1).
 // 32x32 tiles through shared memory keep both sides coalesced for trans = 1.
+// Launched with programmatic stream serialization: it waits for the previous
+// kernel (which may write src or still read hi/lo) before any access, and
+// lets the GEMM that follows start its set-up at once.
 __global__ void split_kmajor_kernel(const float* __restrict__ src, int64_t rows, int64_t K,
                                     int64_t ld, int trans, float* __restrict__ hi,
                                     float* __restrict__ lo, int64_t Kpad) {
+    pdl_wait();
+    pdl_launch_dependents();
+    // Block (32, kSplitRows): each thread's 32 / kSplitRows loads are issued
+    // together before any is used.
+    constexpr int RPT = 32 / kSplitRows;
     __shared__ float tile[32][33];
     const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32;
     const int64_t k0 = static_cast<int64_t>(blockIdx.x) * 32;
     if (trans) {
-        for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        float x[RPT];
+#pragma unroll
+        for (int t = 0; t < RPT; ++t) {
+            const int i = threadIdx.y + kSplitRows * t;
             const int64_t k = k0 + i, r = r0 + threadIdx.x;
-            tile[i][threadIdx.x] = (k < K && r < rows) ? src[k * ld + r] : 0.0f;
+            x[t] = (k < K && r < rows) ? src[k * ld + r] : 0.0f;
         }
+#pragma unroll
+        for (int t = 0; t < RPT; ++t) tile[threadIdx.y + kSplitRows * t][threadIdx.x] = x[t];
         __syncthreads();
-        for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+#pragma unroll
+        for (int t = 0; t < RPT; ++t) {
+            const int i = threadIdx.y + kSplitRows * t;
             const int64_t r = r0 + i, k = k0 + threadIdx.x;
             if (r < rows && k < Kpad) {
                 float h, l;
@@ -65,12 +82,18 @@ __global__ void split_kmajor_kernel(const float* __restrict__ src, int64_t rows,
             }
         }
     } else {
-        for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-            const int64_t r = r0 + i, k = k0 + threadIdx.x;
+        float x[RPT];
+#pragma unroll
+        for (int t = 0; t < RPT; ++t) {
+            const int64_t r = r0 + threadIdx.y + kSplitRows * t, k = k0 + threadIdx.x;
+            x[t] = (r < rows && k < K) ? src[r * ld + k] : 0.0f;
+        }
+#pragma unroll
+        for (int t = 0; t < RPT; ++t) {
+            const int64_t r = r0 + threadIdx.y + kSplitRows * t, k = k0 + threadIdx.x;
             if (r < rows && k < Kpad) {
-                const float x = (k < K) ? src[r * ld + k] : 0.0f;
                 float h, l;
-                split_tf32(x, h, l);
+                split_tf32(x[t], h, l);
                 hi[r * Kpad + k] = h;
                 lo[r * Kpad + k] = l;
             }
@@ -80,8 +103,11 @@ __global__ void split_kmajor_kernel(const float* __restrict__ src, int64_t rows,
 
 // Thread per (row, 4 columns): partials added in split order (IEEE fp32),
 // then alpha/beta/C as in the single-pass epilogue.  splits = 0 gives the
-// empty-K result beta*C.
+// empty-K result beta*C.  Launched with programmatic stream serialization:
+// nothing is read before the GEMM that wrote the partials has completed.
 __global__ void f_splitk_reduce_kernel(const FEpi e, int splits) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int quads = (e.N + 3) / 4;
     const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= static_cast<int64_t>(e.M) * quads) return;
@@ -89,15 +115,30 @@ __global__ void f_splitk_reduce_kernel(const FEpi e, int splits) {
     const int col0 = static_cast<int>(idx % quads) * 4;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     const bool vec = (e.N % 4) == 0;
-    for (int k = 0; k < splits; ++k) {
-        const float* p = e.partial + (static_cast<int64_t>(k) * e.M + row) * e.N + col0;
-        if (vec) {
-            const float4 v = *reinterpret_cast<const float4*>(p);
-            acc[0] = __fadd_rn(acc[0], v.x);
-            acc[1] = __fadd_rn(acc[1], v.y);
-            acc[2] = __fadd_rn(acc[2], v.z);
-            acc[3] = __fadd_rn(acc[3], v.w);
-        } else {
+    const int64_t plane = static_cast<int64_t>(e.M) * e.N;
+    const float* base = e.partial + static_cast<int64_t>(row) * e.N + col0;
+    if (vec) {
+        // Up to eight partials' loads in flight at once, then added in split
+        // order (the sum does not depend on how the loads are grouped).
+        constexpr int U = 8;
+        for (int k0 = 0; k0 < splits; k0 += U) {
+            float4 v[U];
+#pragma unroll
+            for (int j = 0; j < U; ++j)
+                if (k0 + j < splits) v[j] = *reinterpret_cast<const float4*>(base + (k0 + j) * plane);
+#pragma unroll
+            for (int j = 0; j < U; ++j) {
+                if (k0 + j < splits) {
+                    acc[0] = __fadd_rn(acc[0], v[j].x);
+                    acc[1] = __fadd_rn(acc[1], v[j].y);
+                    acc[2] = __fadd_rn(acc[2], v[j].z);
+                    acc[3] = __fadd_rn(acc[3], v[j].w);
+                }
+            }
+        }
+    } else {
+        for (int k = 0; k < splits; ++k) {
+            const float* p = base + k * plane;
 #pragma unroll
             for (int j = 0; j < 4; ++j)
                 if (col0 + j < e.N) acc[j] = __fadd_rn(acc[j], p[j]);
@@ -120,10 +161,14 @@ int default_splits(const pfrt_ctx* ctx, int64_t tiles, int kb_total) {
 
 pfrt_status launch_split(const float* src, int64_t rows, int64_t K, int64_t ld, int trans,
                          float* hi, float* lo, int64_t Kpad, cudaStream_t s) {
-    dim3 tb(32, 8);
-    dim3 tg(static_cast<unsigned>(ceil_div(Kpad, 32)), static_cast<unsigned>(ceil_div(rows, 32)));
-    split_kmajor_kernel<<<tg, tb, 0, s>>>(src, rows, K, ld, trans, hi, lo, Kpad);
-    PFRT_CHECK_LAUNCH("split_kmajor_kernel");
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    cfg.blockDim = dim3(32, kSplitRows);
+    cfg.gridDim = dim3(static_cast<unsigned>(ceil_div(Kpad, 32)), static_cast<unsigned>(ceil_div(rows, 32)));
+    cfg.stream = s;
+    cfg.numAttrs = pdl_attr(attr);
+    cfg.attrs = attr;
+    PFRT_CUDA_TRY(cudaLaunchKernelEx(&cfg, split_kmajor_kernel, src, rows, K, ld, trans, hi, lo, Kpad));
     return PFRT_OK;
 }
 
@@ -193,8 +238,14 @@ pfrt_status run_f32(pfrt_ctx* ctx, int64_t M, int64_t N, int64_t Kpad, const CUt
     PFRT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tmAh, tmBh, tmAl, tmBl, sched, eg, ctx->d_err));
     if (splits > 1) {
         const int64_t threads = M * ceil_div(N, 4);
-        f_splitk_reduce_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, s>>>(e, splits);
-        PFRT_CHECK_LAUNCH("f_splitk_reduce_kernel");
+        cudaLaunchConfig_t rc{};
+        cudaLaunchAttribute rattr[1];
+        rc.gridDim = dim3(static_cast<unsigned>(ceil_div(threads, 256)));
+        rc.blockDim = dim3(256);
+        rc.stream = s;
+        rc.numAttrs = pdl_attr(rattr);
+        rc.attrs = rattr;
+        PFRT_CUDA_TRY(cudaLaunchKernelEx(&rc, f_splitk_reduce_kernel, e, splits));
     }
     return PFRT_OK;
 }
