@@ -32,6 +32,7 @@
 
 #include "common.cuh"
 #include "internal.hpp"
+#include "spmm_sp.cuh"
 #include "spmm_tc.cuh"
 
 struct pfrt_csr {
@@ -64,6 +65,11 @@ struct pfrt_csr {
     uint32_t* tc_mask = nullptr;  // [kb_total][tc_npad]
     uint32_t* tc_off = nullptr;   // [kb_total][tc_npad]
     float2* tc_vals = nullptr;    // [nnz]
+    // 2:4 form for the structured-sparse kernel (spmm_sp.cuh), built on
+    // first use: 0 not checked, 1 ready, -1 not 2:4 along K.
+    int sp_state = 0;
+    int sp_tiles = 0, sp_kb = 0;
+    uint8_t* sp_wimg = nullptr;   // [sp_tiles][sp_kb] images of kSpWImg bytes
 };
 
 namespace pfrt {
@@ -1376,6 +1382,148 @@ pfrt_status run_spmm_tc(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x, i
     return PFRT_OK;
 }
 
+// 2:4 form of W for the structured-sparse kernel (spmm_sp.cuh), built once
+// on the device: a check that every aligned group of four columns of every
+// row stores at most two entries (and no column twice), then W's images from
+// a dense scratch copy that is freed again.  A weight that fails the check
+// keeps sp_state = -1 and the other paths serve it.
+pfrt_status ensure_sp(pfrt_csr* w, cudaStream_t s) {
+    if (w->sp_state != 0) return PFRT_OK;
+    w->sp_state = -1;
+    if (w->N <= 0 || w->K <= 0) return PFRT_OK;
+    const int groups = static_cast<int>(ceil_div(w->K, 4));
+    const int64_t row_bytes = 4 * static_cast<int64_t>(groups);
+    if (row_bytes > 96 * 1024) return PFRT_OK;  // one row's column marks must fit in shared memory
+    const int wpb = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(8, (96 * 1024) / row_bytes)));
+    const size_t check_smem = static_cast<size_t>(wpb) * static_cast<size_t>(row_bytes);
+    int* bad = nullptr;
+    cudaError_t e = cudaMalloc(&bad, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemsetAsync(bad, 0, sizeof(int), s);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(sp_check_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(check_smem));
+    if (e == cudaSuccess) {
+        sp_check_kernel<<<static_cast<unsigned>(ceil_div(w->N, wpb)), 32 * wpb, check_smem, s>>>(
+            w->N, groups, w->indptr, w->indices, bad);
+        e = cudaGetLastError();
+    }
+    int h_bad = 1;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&h_bad, bad, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (bad) cudaFree(bad);
+    if (e != cudaSuccess) return cuda_fail(e, "SpMM 2:4 check");
+    if (h_bad) return PFRT_OK;
+    const int tiles = static_cast<int>(ceil_div(w->N, 128));
+    const int KB = static_cast<int>(ceil_div(w->K, kSpBK));
+    const int64_t npad = static_cast<int64_t>(tiles) * 128, kpad = static_cast<int64_t>(KB) * kSpBK;
+    const size_t wd_bytes = sizeof(float) * static_cast<size_t>(npad) * static_cast<size_t>(kpad);
+    const size_t img_bytes = static_cast<size_t>(tiles) * static_cast<size_t>(KB) * kSpWImg;
+    float* wd = nullptr;
+    uint8_t* img = nullptr;
+    e = cudaMalloc(&wd, wd_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&img, img_bytes);
+    if (e == cudaSuccess) e = cudaMemsetAsync(wd, 0, wd_bytes, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(img, 0, img_bytes, s);
+    if (e == cudaSuccess) {
+        sp_scatter_kernel<<<static_cast<unsigned>(ceil_div(w->N * 32, 256)), 256, 0, s>>>(
+            w->N, kpad, w->indptr, w->indices, w->values, wd);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) {
+        const int64_t threads = static_cast<int64_t>(tiles) * KB * 128 * kSpSteps;
+        sp_pack_w_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, s>>>(tiles, KB, kpad, wd, img);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (wd) cudaFree(wd);
+    if (e != cudaSuccess) {
+        if (img) cudaFree(img);
+        return cuda_fail(e, "SpMM 2:4 form");
+    }
+    w->sp_wimg = img;
+    w->sp_tiles = tiles;
+    w->sp_kb = KB;
+    w->sp_state = 1;
+    return PFRT_OK;
+}
+
+TcSched sp_schedule(const pfrt_ctx* ctx, const pfrt_csr* w, int64_t M) {
+    TcSched sc{};
+    sc.n_wtiles = w->sp_tiles;
+    sc.n_xslabs = static_cast<int>(ceil_div(M, kSpSlab));
+    sc.kb_total = w->sp_kb;
+    sc.total = static_cast<int64_t>(sc.n_wtiles) * sc.n_xslabs * sc.kb_total;
+    sc.per_cta = ceil_div(sc.total, static_cast<int64_t>(ctx->num_sms));
+    return sc;
+}
+
+// Y = X W^T on the structured-sparse tensor cores (spmm_sp.cuh): X's bf16
+// images, the kernel, and the fix-up of units split between CTAs.
+pfrt_status run_spmm_sp(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x, int64_t ldx, float* y,
+                        int64_t ldy, cudaStream_t s) {
+    pfrt_status st = ensure_sp(w, s);
+    if (st) return st;
+    if (w->sp_state != 1) return PFRT_ERR_UNSUPPORTED;
+    const TcSched sc = sp_schedule(ctx, w, M);
+    const int64_t grid = ceil_div(sc.total, sc.per_cta);
+    const size_t xbytes = align_up(static_cast<size_t>(sc.n_xslabs) * static_cast<size_t>(sc.kb_total) * kSpXImg, 256);
+    const size_t pbytes = sizeof(float) * static_cast<size_t>(2 * grid * kTcTileElems);
+    void* scr = nullptr;
+    st = scratch(ctx, xbytes + pbytes, &scr);
+    if (st) return st;
+    uint8_t* ximg = static_cast<uint8_t*>(scr);
+    float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(scr) + xbytes);
+    cudaLaunchAttribute attr[1];
+    {
+        const int64_t threads = static_cast<int64_t>(sc.n_xslabs) * sc.kb_total * kSpSlab * 16;
+        cudaLaunchConfig_t pc{};
+        pc.gridDim = dim3(static_cast<unsigned>(ceil_div(threads, 256)));
+        pc.blockDim = dim3(256);
+        pc.stream = s;
+        pc.numAttrs = pdl_attr(attr);
+        pc.attrs = attr;
+        PFRT_CUDA_TRY(cudaLaunchKernelEx(&pc, sp_pack_x_kernel, x, M, w->K, ldx, sc.n_xslabs, sc.kb_total, ximg));
+    }
+    SpArgs a{};
+    a.wimg = w->sp_wimg;
+    a.ximg = ximg;
+    a.M = static_cast<int>(M);
+    a.N = static_cast<int>(w->N);
+    a.y = y;
+    a.ldy = ldy;
+    a.partial = part;
+    PFRT_CUDA_TRY(cudaFuncSetAttribute(spmm_sp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSpSmemBytes));
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kSpThreads);
+    cfg.dynamicSmemBytes = kSpSmemBytes;
+    cfg.stream = s;
+    cfg.numAttrs = pdl_attr(attr);
+    cfg.attrs = attr;
+    PFRT_CUDA_TRY(cudaLaunchKernelEx(&cfg, spmm_sp_kernel, sc, a, ctx->d_err));
+    if (grid > 1) {
+        cudaLaunchConfig_t rc{};
+        rc.gridDim = dim3(static_cast<unsigned>(grid - 1), static_cast<unsigned>(kSpSlab * kTcWRows / 1024));
+        rc.blockDim = dim3(256);
+        rc.stream = s;
+        rc.numAttrs = pdl_attr(attr);
+        rc.attrs = attr;
+        PFRT_CUDA_TRY(cudaLaunchKernelEx(&rc, tc_fixup_kernel, sc, static_cast<const float*>(part),
+                                         static_cast<int>(M), static_cast<int>(w->N), kSpSlab, y, ldy));
+    }
+    return PFRT_OK;
+}
+
+// Expected time of the structured-sparse kernel: per k-block of a CTA's
+// range 12 sparse MMAs (~1230 SM clocks) plus the X packing, the fix-up and
+// the launches.
+double sp_time(const pfrt_ctx* ctx, const pfrt_csr* w, int64_t M) {
+    const int64_t tiles = ceil_div(std::max<int64_t>(w->N, 1), 128), kb = ceil_div(std::max<int64_t>(w->K, 1), kSpBK);
+    const int64_t total = tiles * ceil_div(M, kSpSlab) * kb;
+    const double per_cta = std::ceil(static_cast<double>(total) / static_cast<double>(ctx->num_sms));
+    return per_cta * 0.65e-6 + 10.0e-6;
+}
+
 template <int MV, bool SMEM>
 pfrt_status launch_stream(pfrt_ctx* ctx, pfrt_csr* w, int M, const float* x, int64_t ldx, float* y,
                           int64_t ldy, size_t shm, cudaStream_t s) {
@@ -1593,6 +1741,19 @@ pfrt_status spmm_uploaded(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x,
                   tc_time(ctx, w, M) < std::min(t_tiled, dense_ok ? 1.1 * t_dense : 1e30);
     if (tc_env && *tc_env) use_tc = tc_ok && *tc_env == '1';
     pfrt_status st;
+    // The structured-sparse tensor cores, for weights with 2:4 structure
+    // along K (checked once per weight, on the first call that could use
+    // them): half the MMA work of the dense product, W read in compressed
+    // form.  PFRT_SPMM_SP = 0|1 forces it off or on (on: where W is 2:4).
+    const char* sp_env = std::getenv("PFRT_SPMM_SP");
+    const bool sp_ok = w->sp_state >= 0 && w->N > 0 && w->K > 0 && M <= (int64_t{1} << 30) / std::max<int64_t>(w->N, 1);
+    bool use_sp = sp_ok && M >= 16 && !(dense_env && *dense_env) && !(tiled_env && *tiled_env) && !(tc_env && *tc_env) &&
+                  sp_time(ctx, w, M) < std::min({t_tiled, dense_ok ? t_dense : 1e30, tc_ok ? tc_time(ctx, w, M) : 1e30});
+    if (sp_env && *sp_env) use_sp = sp_ok && *sp_env == '1';
+    if (use_sp) {
+        st = run_spmm_sp(ctx, w, M, x, ldx, y, ldy, s);
+        if (st != PFRT_ERR_UNSUPPORTED) return st;  // else W is not 2:4 along K
+    }
     if (use_tc) {
         st = run_spmm_tc(ctx, w, M, x, ldx, y, ldy, s);
         if (st != PFRT_ERR_UNSUPPORTED) return st;  // else the form is unusable for this weight
@@ -1828,6 +1989,7 @@ pfrt_status pfrt_csr_destroy(pfrt_csr* w) {
     if (w->tc_mask) cudaFree(w->tc_mask);
     if (w->tc_off) cudaFree(w->tc_off);
     if (w->tc_vals) cudaFree(w->tc_vals);
+    if (w->sp_wimg) cudaFree(w->sp_wimg);
     delete w;
     return PFRT_OK;
 }

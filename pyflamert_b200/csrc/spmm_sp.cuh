@@ -1,0 +1,526 @@
+// spmm_sp.cuh -- CSR SpMM for weights with 2:4 structure along K, on the
+// tensor cores' structured-sparse MMA (tcgen05.mma.sp, kind::f16 with bf16).
+//
+//   Y[M, N] = X[M, K] * W^T,   W [N, K] with at most two stored entries in
+//                               every aligned group of four columns of a row
+//
+// The 2:4 pattern is what NMSparsityPruning::compute_mask (n = 2, m = 4)
+// leaves in a weight stored [N, K] (SparseMatMul, Gemm with transB = 1): its
+// groups of m consecutive elements run along K.  A sparse MMA takes the 2:4
+// operand in compressed form (two values per group of four, plus a 2-bit
+// position for each) and does the work of a dense K = 32 step in the time of
+// a dense K = 16 one.
+//
+// fp32 accuracy from bf16 products: W and X are each split into three bf16
+// parts, w = w1 + w2 + w3 and x = x1 + x2 + x3 (each part the bf16 rounding
+// of what the earlier parts left), and the six products whose size is at
+// least 2^-16 of w1 x1 are summed: w1 x1, w1 x2, w1 x3, w2 x1, w2 x2, w3 x1.
+// The dropped ones (w2 x3, w3 x2, w3 x3) are at most ~2^-24 of the product.
+// As in the 3xTF32 kernels, TMEM accumulates one k-block (128 K) and the
+// epilogue adds each such partial in IEEE fp32.
+//
+// Orientation Y^T = W X^T: the MMA's A operand (M = 128 lanes) is a tile of
+// W in compressed form, its B operand X's parts stacked along N:
+//   B = [x1; x2; x3] (64 rows of X each, 192 rows)
+//   D[:,   0:192] += w1 * [x1; x2; x3]     (N = 192)
+//   D[:,   0:128] += w2 * [x1; x2]         (N = 128)
+//   D[:,   0: 64] += w3 * x1               (N = 64)
+// so D = [w1x1 + w2x1 + w3x1 | w1x2 + w2x2 | w1x3] and the epilogue adds
+// the three 64-column slices.  All three MMAs share one metadata word per
+// row: the parts of W have the same sparsity pattern.
+//
+// Prepared forms (both written in the exact shared-memory image the kernel
+// needs, so a stage is filled by plain 1-D bulk copies):
+//   W image, per (W tile t of 128 rows, k-block kb of 128 K), 57344 bytes:
+//     3 x [128 rows x 64 bf16 = 128 B, 128-byte swizzle]   parts w1, w2, w3
+//     4 x [128 lanes][4 u32] metadata, one block per K = 32 step: word 0 of
+//         each lane is the step's metadata word, words 1..3 are zero
+//   X image, per (X slab c of 64 rows, kb), 49152 bytes: for each K half
+//     (64 K), [x1 | x2 | x3] rows of 128 B, 128-byte swizzle.
+// Metadata word of TMEM lane l for one K = 32 step (8 groups of 4 columns),
+// as the hardware reads it: for 16-row blocks starting at row b, row
+// r = b + 8 h + i (h = 0, 1; i < 8) keeps its groups 0..3 in lane b + i and
+// groups 4..7 in lane b + 8 + i, group g at nibble 4 h + g % 4; a nibble is
+// (position of the first stored value) | (position of the second) << 2,
+// positions in 0..3 within the group, first < second.
+//
+// One CTA per SM, 192 threads: warps 0..3 epilogue (TMEM lane quarter =
+// warp), warp 4 loader (bulk copies), warp 5 MMA issuer and TMEM owner.
+// TMEM: two 192-column accumulators at columns 0 and 256, then one 8-column
+// slot per (stage, step) from column 448 for the metadata, each filled by a
+// tcgen05.cp of the step's metadata block (issued by the MMA thread, so it
+// is ordered before the MMAs that read it).  Every TMEM address an MMA is
+// given is aligned to 8 columns or more.  Work units and
+// their stream-K split over the CTAs, the partial tiles and their fix-up are
+// those of spmm_tc.cuh with 64-row slabs and 128-K k-blocks.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "spmm_tc.cuh"
+
+namespace pfrt {
+
+constexpr int kSpBK = 128;                            // K per k-block
+constexpr int kSpSteps = kSpBK / 32;                  // sparse MMA steps (K = 32) per k-block
+constexpr int kSpSlab = 64;                           // X rows per unit
+constexpr int kSpAPart = 128 * 128;                   // one W part: 128 rows x 128 B
+constexpr int kSpMetaBlock = 128 * 16;                // one step's metadata: [lane][4] u32
+constexpr int kSpMetaBytes = kSpSteps * kSpMetaBlock;
+constexpr int kSpWImg = 3 * kSpAPart + kSpMetaBytes;  // 57344
+constexpr int kSpXPart = kSpSlab * 128;               // one X part of one K half: 64 rows x 128 B
+constexpr int kSpXHalf = 3 * kSpXPart;                // 24576
+constexpr int kSpXImg = 2 * kSpXHalf;                 // 49152
+constexpr int kSpStageBytes = kSpWImg + kSpXImg;      // 106496 (a multiple of 1024)
+constexpr int kSpStages = 2;
+constexpr int kSpN = 3 * kSpSlab;                     // 192 accumulator columns
+constexpr uint32_t kSpAccStride = 256;                // accumulator slots at columns 0 and 256
+constexpr uint32_t kSpTmemCols = 512;
+constexpr uint32_t kSpMetaCol0 = 448;                 // metadata slot j at 448 + 8 j
+constexpr int kSpEpiWarps = 4;
+constexpr int kSpThreads = (kSpEpiWarps + 2) * 32;
+constexpr int kSpBarBytes = 256;
+constexpr int kSpSmemBytes = kSpStages * kSpStageBytes + kSpBarBytes + 1024;
+static_assert(kSpStageBytes % 1024 == 0 && kSpWImg % 1024 == 0, "1024-byte aligned swizzle atoms");
+static_assert(kSpAccStride + kSpN <= kSpMetaCol0, "accumulators below the metadata");
+static_assert(kSpMetaCol0 + 8 * kSpStages * kSpSteps <= kSpTmemCols, "TMEM columns");
+static_assert(kSpSmemBytes <= 227 * 1024, "shared memory");
+
+// Byte offset of 16-byte chunk `cb` (0..7) of row r in a 128-byte-swizzled
+// image of 128-byte rows (1024-byte atoms of 8 rows).
+__host__ __device__ constexpr int sp_swz(int r, int cb) {
+    return (r >> 3) * 1024 + (r & 7) * 128 + ((cb ^ (r & 7)) << 4);
+}
+
+// 1-D bulk copy global -> shared, completing on `bar` (16-byte aligned, size
+// a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// D[tmem] (+)= A_sparse[smem] * B[smem]^T, bf16 inputs, f32 accumulate; the
+// 2:4 metadata in TMEM at `meta`.
+__device__ __forceinline__ void umma_sp_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t meta,
+                                             uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "tcgen05.mma.sp.cta_group::1.kind::f16 [%0], %1, %2, [%3], %4, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(meta), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Shared-memory descriptor of a plain row-major [rows][16 B] array (no
+// swizzle, 8-row groups 128 bytes apart), for tcgen05.cp.
+__device__ __forceinline__ uint64_t sdesc_rows16(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>(128u >> 4) << 16;
+    d |= static_cast<uint64_t>(128u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    return d;
+}
+
+// Copies 128 rows x 16 bytes from shared memory into TMEM lanes 0..127,
+// columns taddr .. taddr + 3.
+__device__ __forceinline__ void tmem_cp_128x128b(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.128x128b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Instruction descriptor: bf16 x bf16 -> f32, M = 128, sparse, N given.
+__host__ __device__ constexpr uint32_t sp_idesc(uint32_t n) {
+    return idesc_make(1, 1, 1, 128, n) | (1u << 2);
+}
+
+__device__ __forceinline__ void bf16x3(float x, uint16_t& p1, uint16_t& p2, uint16_t& p3) {
+    const __nv_bfloat16 a = __float2bfloat16_rn(x);
+    const float r1 = __fsub_rn(x, __bfloat162float(a));
+    const __nv_bfloat16 b = __float2bfloat16_rn(r1);
+    const float r2 = __fsub_rn(r1, __bfloat162float(b));
+    const __nv_bfloat16 c = __float2bfloat16_rn(r2);
+    p1 = __bfloat16_as_ushort(a);
+    p2 = __bfloat16_as_ushort(b);
+    p3 = __bfloat16_as_ushort(c);
+}
+
+// Eligibility: one warp per row marks the row's stored columns in shared
+// memory (one byte per column, 4 * groups bytes per warp) and raises *bad
+// when a group of four columns holds more than two, or when a column is
+// stored twice (fewer marked bytes than entries: the CSR sums duplicates,
+// and the compressed form has one slot per position).  Columns come from a
+// validated CSR, so every index is below K <= 4 * groups.
+__global__ void sp_check_kernel(int64_t N, int groups, const int32_t* __restrict__ indptr,
+                                const int32_t* __restrict__ indices, int* bad) {
+    extern __shared__ uint8_t cnt_raw[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* cnt = cnt_raw + static_cast<int64_t>(warp) * groups * 4;
+    const int64_t n = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
+    if (n >= N) return;
+    for (int g = lane; g < groups * 4; g += 32) cnt[g] = 0;
+    __syncwarp();
+    const int32_t j0 = indptr[n], j1 = indptr[n + 1];
+    for (int32_t j = j0 + lane; j < j1; j += 32) cnt[indices[j]] = 1;
+    __syncwarp();
+    int over = 0;
+    for (int g = lane; g < groups; g += 32)
+        over |= (cnt[4 * g] + cnt[4 * g + 1] + cnt[4 * g + 2] + cnt[4 * g + 3]) > 2;
+    int set = 0;
+    for (int g = lane; g < groups * 4; g += 32) set += cnt[g];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) set += __shfl_xor_sync(0xffffffffu, set, o);
+    if (__any_sync(0xffffffffu, over) || (lane == 0 && set != j1 - j0)) atomicOr(bad, 1);
+}
+
+// W[n, c] into the zero-filled dense scratch (one warp per row).
+__global__ void sp_scatter_kernel(int64_t N, int64_t Kpad, const int32_t* __restrict__ indptr,
+                                  const int32_t* __restrict__ indices, const float* __restrict__ values,
+                                  float* __restrict__ wd) {
+    const int64_t n = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (n >= N) return;
+    for (int32_t j = indptr[n] + lane; j < indptr[n + 1]; j += 32) wd[n * Kpad + indices[j]] = values[j];
+}
+
+// W images from the dense scratch wd [Npad][Kpad] (zero padded): one thread
+// per (tile t, k-block kb, row r, step s) compresses 32 columns (8 groups)
+// of one row: its 16 kept values of each part, and its 8 metadata nibbles
+// (ORed into the two lanes' words; the image is zeroed first).
+__global__ void sp_pack_w_kernel(int tiles, int KB, int64_t Kpad, const float* __restrict__ wd,
+                                 uint8_t* __restrict__ img) {
+    const int64_t id = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (id >= static_cast<int64_t>(tiles) * KB * 128 * kSpSteps) return;
+    const int s = static_cast<int>(id % kSpSteps);
+    const int r = static_cast<int>((id / kSpSteps) % 128);
+    const int64_t tk = id / (kSpSteps * 128);
+    const int kb = static_cast<int>(tk % KB);
+    const int t = static_cast<int>(tk / KB);
+    const float* src = wd + (static_cast<int64_t>(t) * 128 + r) * Kpad + static_cast<int64_t>(kb) * kSpBK + 32 * s;
+    uint8_t* base = img + (static_cast<int64_t>(t) * KB + kb) * kSpWImg;
+    uint16_t v[3][16];
+    uint32_t nib_lo = 0, nib_hi = 0;  // groups 0..3 and 4..7
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+        const float4 q = *reinterpret_cast<const float4*>(src + 4 * g);
+        const float e[4] = {q.x, q.y, q.z, q.w};
+        int p0 = -1, p1 = -1;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (e[i] != 0.0f) {
+                if (p0 < 0) p0 = i;
+                else p1 = i;
+            }
+        // Empty slots take zero values at positions that keep p0 < p1.
+        if (p0 < 0) {
+            p0 = 0;
+            p1 = 1;
+        } else if (p1 < 0) {
+            if (p0 == 3) {
+                p0 = 2;
+                p1 = 3;
+            } else {
+                p1 = 3;
+            }
+        }
+        const float a = e[p0], b = e[p1];
+        bf16x3(a, v[0][2 * g], v[1][2 * g], v[2][2 * g]);
+        bf16x3(b, v[0][2 * g + 1], v[1][2 * g + 1], v[2][2 * g + 1]);
+        const uint32_t nib = static_cast<uint32_t>(p0 | (p1 << 2));
+        if (g < 4) nib_lo |= nib << (4 * g);
+        else nib_hi |= nib << (4 * (g - 4));
+    }
+#pragma unroll
+    for (int p = 0; p < 3; ++p) {
+        uint8_t* part = base + p * kSpAPart;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint4 w;
+            w.x = v[p][8 * h + 0] | (static_cast<uint32_t>(v[p][8 * h + 1]) << 16);
+            w.y = v[p][8 * h + 2] | (static_cast<uint32_t>(v[p][8 * h + 3]) << 16);
+            w.z = v[p][8 * h + 4] | (static_cast<uint32_t>(v[p][8 * h + 5]) << 16);
+            w.w = v[p][8 * h + 6] | (static_cast<uint32_t>(v[p][8 * h + 7]) << 16);
+            *reinterpret_cast<uint4*>(part + sp_swz(r, 2 * s + h)) = w;
+        }
+    }
+    uint32_t* meta = reinterpret_cast<uint32_t*>(base + 3 * kSpAPart + s * kSpMetaBlock);
+    const int b16 = r & ~15, i = r & 7, hh = (r >> 3) & 1;
+    atomicOr(meta + (b16 + i) * 4, nib_lo << (16 * hh));
+    atomicOr(meta + (b16 + 8 + i) * 4, nib_hi << (16 * hh));
+}
+
+// X images: one thread per (slab c, k-block kb, row j, 8-column piece q):
+// X[64 c + j, 128 kb + 8 q + 0..7] split into three bf16 parts, 16 bytes of
+// each part written to its swizzled place (zeros past M or K).
+__global__ void sp_pack_x_kernel(const float* __restrict__ x, int64_t M, int64_t K, int64_t ldx, int slabs, int KB,
+                                 uint8_t* __restrict__ img) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int64_t id = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (id >= static_cast<int64_t>(slabs) * KB * kSpSlab * 16) return;
+    const int q = static_cast<int>(id % 16);
+    const int j = static_cast<int>((id / 16) % kSpSlab);
+    const int64_t ck = id / (16 * kSpSlab);
+    const int kb = static_cast<int>(ck % KB);
+    const int c = static_cast<int>(ck / KB);
+    const int64_t m = static_cast<int64_t>(c) * kSpSlab + j;
+    const int64_t k0 = static_cast<int64_t>(kb) * kSpBK + 8 * q;
+    float e[8];
+    if (m < M && k0 + 8 <= K && (ldx % 4) == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+        const float4 a = *reinterpret_cast<const float4*>(x + m * ldx + k0);
+        const float4 b = *reinterpret_cast<const float4*>(x + m * ldx + k0 + 4);
+        e[0] = a.x; e[1] = a.y; e[2] = a.z; e[3] = a.w; e[4] = b.x; e[5] = b.y; e[6] = b.z; e[7] = b.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) e[i] = (m < M && k0 + i < K) ? x[m * ldx + k0 + i] : 0.0f;
+    }
+    uint16_t v[3][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) bf16x3(e[i], v[0][i], v[1][i], v[2][i]);
+    uint8_t* base = img + (static_cast<int64_t>(c) * KB + kb) * kSpXImg + (q >> 3) * kSpXHalf;
+#pragma unroll
+    for (int p = 0; p < 3; ++p) {
+        uint4 w;
+        w.x = v[p][0] | (static_cast<uint32_t>(v[p][1]) << 16);
+        w.y = v[p][2] | (static_cast<uint32_t>(v[p][3]) << 16);
+        w.z = v[p][4] | (static_cast<uint32_t>(v[p][5]) << 16);
+        w.w = v[p][6] | (static_cast<uint32_t>(v[p][7]) << 16);
+        *reinterpret_cast<uint4*>(base + p * kSpXPart + sp_swz(j, q & 7)) = w;
+    }
+}
+
+struct SpArgs {
+    const uint8_t* wimg;   // [tiles][KB] W images
+    const uint8_t* ximg;   // [slabs][KB] X images
+    int M, N;
+    float* y;              // output, row stride ldy
+    int64_t ldy;
+    float* partial;        // [2 * grid][64][128] partial tiles (tc_fixup_kernel's layout)
+};
+
+__global__ void __launch_bounds__(kSpThreads, 1)
+    spmm_sp_kernel(const TcSched sched, const SpArgs a, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSpStages * kSpStageBytes);
+    uint64_t* empty = full + kSpStages;
+    uint64_t* tfull = empty + kSpStages;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    constexpr int kEpiThreads = 32 * kSpEpiWarps;
+    constexpr int kLoadWarp = kSpEpiWarps;
+    constexpr int kMmaWarp = kSpEpiWarps + 1;
+    const int64_t KB = sched.kb_total;
+    const int64_t g0 = static_cast<int64_t>(blockIdx.x) * sched.per_cta;
+    const int64_t g1 = min(g0 + sched.per_cta, sched.total);  // this CTA's k-blocks [g0, g1)
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kSpStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], kEpiThreads);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == kMmaWarp) tmem_alloc(tmem_slot, kSpTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    if (threadIdx.x == 0) pdl_launch_dependents();
+
+    if (warp < kSpEpiWarps) {
+        const int q = warp;
+        const int nl = q * 32 + lane;  // this thread's TMEM lane = W row within the tile
+        const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+        pdl_wait();  // the partial tiles and Y may still be read by the previous kernel
+        int tc = 0;  // accumulation chunks consumed
+        for (int64_t g = g0; g < g1;) {
+            const int64_t u = g / KB;
+            const int kb_lo = static_cast<int>(g % KB);
+            const int kb_hi = static_cast<int>(KB < kb_lo + (g1 - g) ? KB : kb_lo + (g1 - g));
+            g += kb_hi - kb_lo;
+            int t, c;
+            tc_unit(sched, u, t, c);
+            float racc[kSpSlab];
+#pragma unroll
+            for (int j = 0; j < kSpSlab; ++j) racc[j] = 0.0f;
+            bool stop = false;
+            for (int kc = kb_lo; kc < kb_hi; ++kc, ++tc) {
+                const int slot = tc & 1;
+                const uint32_t ap = static_cast<uint32_t>(tc >> 1) & 1u;
+                const bool got = mbar_wait(&tfull[slot], ap, abort_flag);
+                if (epi_barrier_or(!got || *abort_flag != 0, kEpiThreads)) {
+                    stop = true;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t taddr = tmem_base + static_cast<uint32_t>(slot) * kSpAccStride + lane_off;
+                // X row j: columns j (x1 products), 64 + j (x2), 128 + j (x3).
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    uint32_t v0[16], v1[16], v2[16];
+                    tmem_ld_32x32b_x16(taddr + static_cast<uint32_t>(16 * h), v0);
+                    tmem_ld_32x32b_x16(taddr + static_cast<uint32_t>(64 + 16 * h), v1);
+                    tmem_ld_32x32b_x16(taddr + static_cast<uint32_t>(128 + 16 * h), v2);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        racc[16 * h + j] = __fadd_rn(
+                            racc[16 * h + j],
+                            __fadd_rn(__fadd_rn(__uint_as_float(v0[j]), __uint_as_float(v1[j])), __uint_as_float(v2[j])));
+                }
+                tc_fence_before();
+                mbar_arrive(&tempty[slot]);
+            }
+            if (stop) {
+                *abort_flag = 1;
+                report_error(err, kDevWaitTimeout);
+                break;
+            }
+            if (kb_lo == 0 && kb_hi == KB) {
+                const int n = t * kTcWRows + nl;
+                const int m0 = c * kSpSlab;
+                if (n < a.N) {
+                    float* dst = a.y + n;
+#pragma unroll
+                    for (int j = 0; j < kSpSlab; ++j)
+                        if (m0 + j < a.M) dst[static_cast<int64_t>(m0 + j) * a.ldy] = racc[j];
+                }
+            } else {
+                float* dst = a.partial + tc_slot(sched, blockIdx.x, u) * kTcTileElems + nl;
+#pragma unroll
+                for (int j = 0; j < kSpSlab; ++j) dst[j * kTcWRows] = racc[j];
+            }
+        }
+    } else if (warp == kLoadWarp) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued = 0;
+            uint32_t last_par[kSpStages];
+            bool ok = true;
+            TcCursor cur;
+            cur.init(sched, g0);
+            // W's images are a prepared weight (written once, never by a
+            // kernel that precedes this one): the first stages' W halves are
+            // requested before the dependency wait, X (written by the packing
+            // kernel just before) after it.
+            const int npre = static_cast<int>(g1 - g0 < kSpStages ? g1 - g0 : kSpStages);
+            TcCursor pc = cur;
+            for (int i = 0; i < npre; ++i, pc.next(sched)) {
+                uint8_t* st = smem + i * kSpStageBytes;
+                mbar_arrive_expect_tx(&full[i], kSpStageBytes);
+                const uint8_t* wsrc = a.wimg + (static_cast<int64_t>(pc.t) * KB + pc.kb) * kSpWImg;
+                bulk_load(st, wsrc, kSpWImg / 2, &full[i]);
+                bulk_load(st + kSpWImg / 2, wsrc + kSpWImg / 2, kSpWImg / 2, &full[i]);
+                issued |= 1u << i;
+                last_par[i] = 0u;
+            }
+            pdl_wait();
+            for (int i = 0; i < npre; ++i, cur.next(sched)) {
+                uint8_t* st = smem + i * kSpStageBytes + kSpWImg;
+                const uint8_t* xsrc = a.ximg + (static_cast<int64_t>(cur.c) * KB + cur.kb) * kSpXImg;
+                bulk_load(st, xsrc, kSpXImg / 2, &full[i]);
+                bulk_load(st + kSpXImg / 2, xsrc + kSpXImg / 2, kSpXImg / 2, &full[i]);
+            }
+            stage = npre % kSpStages;
+            phase = (npre == kSpStages) ? 1u : 0u;
+            for (int64_t g = g0 + npre; g < g1; ++g, cur.next(sched)) {
+                if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* st = smem + stage * kSpStageBytes;
+                mbar_arrive_expect_tx(&full[stage], kSpStageBytes);
+                const uint8_t* wsrc = a.wimg + (static_cast<int64_t>(cur.t) * KB + cur.kb) * kSpWImg;
+                const uint8_t* xsrc = a.ximg + (static_cast<int64_t>(cur.c) * KB + cur.kb) * kSpXImg;
+                bulk_load(st, wsrc, kSpWImg / 2, &full[stage]);
+                bulk_load(st + kSpWImg / 2, wsrc + kSpWImg / 2, kSpWImg / 2, &full[stage]);
+                bulk_load(st + kSpWImg, xsrc, kSpXImg / 2, &full[stage]);
+                bulk_load(st + kSpWImg + kSpXImg / 2, xsrc + kSpXImg / 2, kSpXImg / 2, &full[stage]);
+                issued |= 1u << stage;
+                last_par[stage] = phase;
+                if (++stage == kSpStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                report_error(err, kDevWaitTimeout);
+                const int zero = 0;
+                for (int s = 0; s < kSpStages; ++s)
+                    if (issued & (1u << s)) mbar_wait(&full[s], last_par[s], &zero);
+            }
+        }
+    } else {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int tc = 0;
+            for (int64_t g = g0; ok && g < g1; ++g, ++tc) {
+                const int slot = tc & 1;
+                const uint32_t ap = static_cast<uint32_t>(tc >> 1) & 1u;
+                if (!mbar_wait(&tempty[slot], ap ^ 1u, abort_flag) || !mbar_wait(&full[stage], phase, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t st = smem_u32(smem + stage * kSpStageBytes);
+                const uint32_t meta = tmem_base + kSpMetaCol0 + static_cast<uint32_t>(8 * kSpSteps * stage);
+#pragma unroll
+                for (int k = 0; k < kSpSteps; ++k)
+                    tmem_cp_128x128b(meta + 8 * k, sdesc_rows16(st + 3 * kSpAPart + k * kSpMetaBlock));
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot) * kSpAccStride;
+                const uint64_t a1 = sdesc_kmajor_sw128(st), a2 = sdesc_kmajor_sw128(st + kSpAPart),
+                               a3 = sdesc_kmajor_sw128(st + 2 * kSpAPart);
+#pragma unroll
+                for (int k = 0; k < kSpSteps; ++k) {
+                    const uint64_t ka = static_cast<uint64_t>((32 * k) >> 4);  // 16 stored bf16 per step
+                    const uint64_t db = sdesc_kmajor_sw128(st + kSpWImg + (k >> 1) * kSpXHalf) +
+                                        static_cast<uint64_t>((64 * (k & 1)) >> 4);  // 32 bf16 of X per step
+                    const uint32_t mk = meta + static_cast<uint32_t>(8 * k);
+                    umma_sp_bf16(d_tmem, a1 + ka, db, mk, sp_idesc(3 * kSpSlab), k > 0 ? 1u : 0u);
+                    umma_sp_bf16(d_tmem, a2 + ka, db, mk, sp_idesc(2 * kSpSlab), 1u);
+                    umma_sp_bf16(d_tmem, a3 + ka, db, mk, sp_idesc(kSpSlab), 1u);
+                }
+                umma_commit(&empty[stage]);
+                umma_commit(&tfull[slot]);
+                if (++stage == kSpStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                report_error(err, kDevWaitTimeout);
+            }
+            umma_commit(drain);
+            const int zero = 0;
+            mbar_wait(drain, 0, &zero);
+        }
+    }
+
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kSpTmemCols);
+    }
+}
+
+}  // namespace pfrt

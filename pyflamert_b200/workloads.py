@@ -114,6 +114,38 @@ def spmm_case(M=256, N=4096, K=4096, sparsity=0.9, seed=3) -> CsrCase:
     return CsrCase(N, K, indptr, indices, values, X)
 
 
+def structured24_case(M=256, N=4096, K=4096, seed=5, p_two=0.85, p_one=0.1) -> CsrCase:
+    """A weight W [N,K] with 2:4 structure along K, as N:M pruning (n = 2,
+    m = 4) of a [N, K] weight leaves it: every aligned group of four columns of
+    a row stores two entries (probability p_two), one (p_one) or none, at
+    uniform-random positions; values N(0, 0.02); X[M,K] ~ N(0,1).  A last
+    partial group (K % 4 != 0) follows the same rule over its columns."""
+    rng = np.random.default_rng(seed)
+    G = (K + 3) // 4
+    u = rng.random((N, G))
+    keep = np.where(u < p_two, 2, np.where(u < p_two + p_one, 1, 0))
+    width = np.full(G, 4)
+    width[-1] = K - 4 * (G - 1)
+    keep = np.minimum(keep, width[None, :])
+    keys = rng.random((N, G, 4))
+    keys[:, :, :][:, np.arange(G) == G - 1, width[-1]:] = 2.0  # past K: never chosen
+    order = np.argsort(keys, axis=2)
+    chosen = np.zeros((N, G, 4), bool)
+    for r in range(2):
+        pos = order[:, :, r]
+        sel = keep > r
+        n_idx, g_idx = np.nonzero(sel)
+        chosen[n_idx, g_idx, pos[n_idx, g_idx]] = True
+    mask = chosen.reshape(N, 4 * G)[:, :K]
+    counts = mask.sum(axis=1)
+    indptr = np.zeros(N + 1, np.int64)
+    indptr[1:] = np.cumsum(counts)
+    indices = np.nonzero(mask)[1].astype(np.int32)
+    values = (rng.standard_normal(int(indptr[-1]), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    X = np.random.default_rng(seed + 1000).standard_normal((M, K), dtype=np.float32)
+    return CsrCase(N, K, indptr.astype(np.int32), indices, values, X)
+
+
 def csr_to_dense(c: CsrCase) -> np.ndarray:
     W = np.zeros((c.N, c.K), np.float32)
     rows = np.repeat(np.arange(c.N), np.diff(c.indptr.astype(np.int64)))

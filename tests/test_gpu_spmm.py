@@ -316,3 +316,59 @@ def test_raw_api_single_row_batch_bad_index(ctx):
     np.add.at(W, (rows[keep], indices[keep]), values[keep].astype(np.float64))
     ref = (X.astype(np.float64) @ W.T)
     assert np.abs(y.cpu().numpy() - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 256, 512), (200, 300, 1000), (16, 128, 128), (1024, 512, 1024),
+                                   (130, 260, 1001), (64, 4096, 4096), (256, 4096, 4096)])
+def test_structured_sparse_kernel(ctx, M, N, K, monkeypatch):
+    """Weights with 2:4 structure along K on the structured-sparse tensor
+    cores (tcgen05.mma.sp, bf16 x3 split, spmm_sp.cuh): normwise <= 1e-5
+    against the reference's sparse_matmul, with N, K and M ragged (N not a
+    multiple of 128, K not a multiple of 128 or of 4, M not a multiple of 64),
+    groups holding two, one or no entries, and units shared between CTAs.
+    Equal, within the same tolerance, to the other paths on the same weight."""
+    c = wl.structured24_case(M, N, K, seed=M + N + K)
+    monkeypatch.setenv("PFRT_SPMM_SP", "1")
+    y = gpu(ctx, c)
+    ref = oracle(c)
+    assert normwise_rel(y, ref) <= FP32_TOL
+    monkeypatch.setenv("PFRT_SPMM_SP", "0")
+    assert normwise_rel(gpu(ctx, c), y) <= 2 * FP32_TOL
+
+
+def test_structured_sparse_from_nm_pruning(ctx, monkeypatch):
+    """The N:M pruning path end to end: a dense weight W [N, K] pruned 2:4 as
+    NMSparsityPruning(2, 4).compute_mask does (groups of four consecutive
+    weights of the row-major tensor; K % 4 == 0, so along K), kept as CSR,
+    multiplied on the structured-sparse kernel, repeatedly and with M
+    changing between calls."""
+    rng = np.random.default_rng(11)
+    N, K = 384, 768
+    W = rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.05)
+    mask = po.nm_mask(W, 2, 4)
+    indptr, indices, values = po.masked_csr(W, mask)
+    monkeypatch.setenv("PFRT_SPMM_SP", "1")
+    w = pf.CSR(ctx, N, K, indptr, indices, values)
+    for M in (64, 33, 300, 64):
+        X = rng.standard_normal((M, K), dtype=np.float32)
+        y = w(torch.from_numpy(X).cuda()).cpu().numpy()
+        ctx.check()
+        assert normwise_rel(y, po.spmm_linear(indptr, indices, values, X, N)) <= FP32_TOL
+
+
+def test_structured_sparse_ineligible_weights_fall_back(ctx, monkeypatch):
+    """A weight with three entries in some group of four, or a column stored
+    twice, is not 2:4: with the structured-sparse path forced on it still
+    gets the right result from the other paths."""
+    monkeypatch.setenv("PFRT_SPMM_SP", "1")
+    c = wl.spmm_case(96, 256, 512, sparsity=0.5, seed=4)
+    assert normwise_rel(gpu(ctx, c), oracle(c)) <= FP32_TOL
+    d = wl.structured24_case(96, 130, 256, seed=9)
+    ip = d.indptr.astype(np.int64)
+    # row 0 stores its first column twice (the CSR sums both)
+    idx = np.insert(d.indices, ip[0], d.indices[ip[0]])
+    val = np.insert(d.values, ip[0], np.float32(0.5))
+    ip = ip.copy()
+    ip[1:] += 1
+    dup = wl.CsrCase(d.N, d.K, ip.astype(np.int32), idx.astype(np.int32), val.astype(np.float32), d.X)
+    assert normwise_rel(gpu(ctx, dup), oracle(dup)) <= FP32_TOL
