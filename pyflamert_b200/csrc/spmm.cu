@@ -65,11 +65,16 @@ struct pfrt_csr {
     uint32_t* tc_mask = nullptr;  // [kb_total][tc_npad]
     uint32_t* tc_off = nullptr;   // [kb_total][tc_npad]
     float2* tc_vals = nullptr;    // [nnz]
-    // 2:4 form for the structured-sparse kernel (spmm_sp.cuh), built on
-    // first use: 0 not checked, 1 ready, -1 not 2:4 along K.
+    // Form of W for the structured-sparse kernel (spmm_sp.cuh): 0 nothing
+    // known, 2 the remainder's size counted, 1 built, -1 unusable (rows too
+    // long for the count).
     int sp_state = 0;
+    int64_t sp_over = 0;          // entries past the second of their group of four (R's size)
     int sp_tiles = 0, sp_kb = 0;
     uint8_t* sp_wimg = nullptr;   // [sp_tiles][sp_kb] images of kSpWImg bytes
+    int64_t* sp_rptr = nullptr;   // R: [N + 1], null when R is empty
+    int32_t* sp_rcol = nullptr;
+    float* sp_rval = nullptr;
 };
 
 namespace pfrt {
@@ -1382,12 +1387,11 @@ pfrt_status run_spmm_tc(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x, i
     return PFRT_OK;
 }
 
-// 2:4 form of W for the structured-sparse kernel (spmm_sp.cuh), built once
-// on the device: a check that every aligned group of four columns of every
-// row stores at most two entries (and no column twice), then W's images from
-// a dense scratch copy that is freed again.  A weight that fails the check
-// keeps sp_state = -1 and the other paths serve it.
-pfrt_status ensure_sp(pfrt_csr* w, cudaStream_t s) {
+// Size of W's remainder R for the structured-sparse kernel (spmm_sp.cuh):
+// the entries past the second of every aligned group of four columns of a
+// row, counted once on the device (the cost model needs it before any image
+// is built).
+pfrt_status ensure_sp_count(pfrt_csr* w, cudaStream_t s) {
     if (w->sp_state != 0) return PFRT_OK;
     w->sp_state = -1;
     if (w->N <= 0 || w->K <= 0) return PFRT_OK;
@@ -1395,24 +1399,35 @@ pfrt_status ensure_sp(pfrt_csr* w, cudaStream_t s) {
     const int64_t row_bytes = 4 * static_cast<int64_t>(groups);
     if (row_bytes > 96 * 1024) return PFRT_OK;  // one row's column marks must fit in shared memory
     const int wpb = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(8, (96 * 1024) / row_bytes)));
-    const size_t check_smem = static_cast<size_t>(wpb) * static_cast<size_t>(row_bytes);
-    int* bad = nullptr;
-    cudaError_t e = cudaMalloc(&bad, sizeof(int));
-    if (e == cudaSuccess) e = cudaMemsetAsync(bad, 0, sizeof(int), s);
+    const size_t smem = static_cast<size_t>(wpb) * static_cast<size_t>(row_bytes);
+    unsigned long long* over = nullptr;
+    cudaError_t e = cudaMalloc(&over, sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemsetAsync(over, 0, sizeof(unsigned long long), s);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(sp_check_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(check_smem));
+        e = cudaFuncSetAttribute(sp_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e == cudaSuccess) {
-        sp_check_kernel<<<static_cast<unsigned>(ceil_div(w->N, wpb)), 32 * wpb, check_smem, s>>>(
-            w->N, groups, w->indptr, w->indices, bad);
+        sp_count_kernel<<<static_cast<unsigned>(ceil_div(w->N, wpb)), 32 * wpb, smem, s>>>(w->N, groups, w->indptr,
+                                                                                         w->indices, over);
         e = cudaGetLastError();
     }
-    int h_bad = 1;
-    if (e == cudaSuccess) e = cudaMemcpyAsync(&h_bad, bad, sizeof(int), cudaMemcpyDeviceToHost, s);
+    unsigned long long h_over = 0;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&h_over, over, sizeof(h_over), cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-    if (bad) cudaFree(bad);
-    if (e != cudaSuccess) return cuda_fail(e, "SpMM 2:4 check");
-    if (h_bad) return PFRT_OK;
+    if (over) cudaFree(over);
+    if (e != cudaSuccess) return cuda_fail(e, "SpMM 2:4 count");
+    w->sp_over = static_cast<int64_t>(h_over);
+    w->sp_state = 2;
+    return PFRT_OK;
+}
+
+// W's structured-sparse form, built once on the device from a dense scratch
+// copy that is freed again: the 2:4 part W24 as images, the remainder R as a
+// CSR (each row's entries in column order, so the result does not depend on
+// how the build was scheduled).
+pfrt_status ensure_sp(pfrt_csr* w, cudaStream_t s) {
+    pfrt_status st = ensure_sp_count(w, s);
+    if (st) return st;
+    if (w->sp_state != 2) return PFRT_OK;
     const int tiles = static_cast<int>(ceil_div(w->N, 128));
     const int KB = static_cast<int>(ceil_div(w->K, kSpBK));
     const int64_t npad = static_cast<int64_t>(tiles) * 128, kpad = static_cast<int64_t>(KB) * kSpBK;
@@ -1420,13 +1435,17 @@ pfrt_status ensure_sp(pfrt_csr* w, cudaStream_t s) {
     const size_t img_bytes = static_cast<size_t>(tiles) * static_cast<size_t>(KB) * kSpWImg;
     float* wd = nullptr;
     uint8_t* img = nullptr;
-    e = cudaMalloc(&wd, wd_bytes);
+    int32_t* rcount = nullptr;
+    int64_t* rptr = nullptr;
+    int32_t* rcol = nullptr;
+    float* rval = nullptr;
+    const unsigned row_blocks = static_cast<unsigned>(ceil_div(w->N * 32, 256));
+    cudaError_t e = cudaMalloc(&wd, wd_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&img, img_bytes);
     if (e == cudaSuccess) e = cudaMemsetAsync(wd, 0, wd_bytes, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(img, 0, img_bytes, s);
     if (e == cudaSuccess) {
-        sp_scatter_kernel<<<static_cast<unsigned>(ceil_div(w->N * 32, 256)), 256, 0, s>>>(
-            w->N, kpad, w->indptr, w->indices, w->values, wd);
+        sp_scatter_kernel<<<row_blocks, 256, 0, s>>>(w->N, kpad, w->indptr, w->indices, w->values, wd);
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) {
@@ -1434,13 +1453,45 @@ pfrt_status ensure_sp(pfrt_csr* w, cudaStream_t s) {
         sp_pack_w_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, s>>>(tiles, KB, kpad, wd, img);
         e = cudaGetLastError();
     }
+    if (e == cudaSuccess && w->sp_over > 0) {
+        std::vector<int32_t> hcount(static_cast<size_t>(w->N));
+        std::vector<int64_t> hptr(static_cast<size_t>(w->N) + 1, 0);
+        e = cudaMalloc(&rcount, sizeof(int32_t) * hcount.size());
+        if (e == cudaSuccess) {
+            sp_remainder_kernel<false><<<row_blocks, 256, 0, s>>>(w->N, kpad, wd, rcount, nullptr, nullptr, nullptr);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(hcount.data(), rcount, sizeof(int32_t) * hcount.size(), cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        for (size_t i = 0; e == cudaSuccess && i < hcount.size(); ++i) hptr[i + 1] = hptr[i] + hcount[i];
+        const int64_t nr = hptr.back();
+        if (e == cudaSuccess && nr > 0) {
+            e = cudaMalloc(&rptr, sizeof(int64_t) * hptr.size());
+            if (e == cudaSuccess) e = cudaMalloc(&rcol, sizeof(int32_t) * static_cast<size_t>(nr));
+            if (e == cudaSuccess) e = cudaMalloc(&rval, sizeof(float) * static_cast<size_t>(nr));
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(rptr, hptr.data(), sizeof(int64_t) * hptr.size(), cudaMemcpyHostToDevice, s);
+            if (e == cudaSuccess) {
+                sp_remainder_kernel<true><<<row_blocks, 256, 0, s>>>(w->N, kpad, wd, nullptr, rptr, rcol, rval);
+                e = cudaGetLastError();
+            }
+        }
+    }
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (wd) cudaFree(wd);
+    if (rcount) cudaFree(rcount);
     if (e != cudaSuccess) {
         if (img) cudaFree(img);
-        return cuda_fail(e, "SpMM 2:4 form");
+        if (rptr) cudaFree(rptr);
+        if (rcol) cudaFree(rcol);
+        if (rval) cudaFree(rval);
+        return cuda_fail(e, "SpMM structured-sparse form");
     }
     w->sp_wimg = img;
+    w->sp_rptr = rptr;
+    w->sp_rcol = rcol;
+    w->sp_rval = rval;
     w->sp_tiles = tiles;
     w->sp_kb = KB;
     w->sp_state = 1;
@@ -1464,6 +1515,7 @@ pfrt_status run_spmm_sp(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x, i
     pfrt_status st = ensure_sp(w, s);
     if (st) return st;
     if (w->sp_state != 1) return PFRT_ERR_UNSUPPORTED;
+    if (ldx < w->K) return fail(PFRT_ERR_INVALID_ARGUMENT, "SpMM: row stride too small");
     const TcSched sc = sp_schedule(ctx, w, M);
     const int64_t grid = ceil_div(sc.total, sc.per_cta);
     const size_t xbytes = align_up(static_cast<size_t>(sc.n_xslabs) * static_cast<size_t>(sc.kb_total) * kSpXImg, 256);
@@ -1511,17 +1563,33 @@ pfrt_status run_spmm_sp(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x, i
         PFRT_CUDA_TRY(cudaLaunchKernelEx(&rc, tc_fixup_kernel, sc, static_cast<const float*>(part),
                                          static_cast<int>(M), static_cast<int>(w->N), kSpSlab, y, ldy));
     }
+    if (w->sp_rptr) {
+        const int64_t warps = M * ceil_div(w->N, 32);
+        cudaLaunchConfig_t qc{};
+        qc.gridDim = dim3(static_cast<unsigned>(ceil_div(warps * 32, 256)));
+        qc.blockDim = dim3(256);
+        qc.stream = s;
+        qc.numAttrs = pdl_attr(attr);
+        qc.attrs = attr;
+        PFRT_CUDA_TRY(cudaLaunchKernelEx(&qc, sp_remainder_add_kernel, x, ldx, M, w->N,
+                                         static_cast<const int64_t*>(w->sp_rptr), static_cast<const int32_t*>(w->sp_rcol),
+                                         static_cast<const float*>(w->sp_rval), y, ldy));
+    }
     return PFRT_OK;
 }
 
-// Expected time of the structured-sparse kernel: per k-block of a CTA's
-// range 12 sparse MMAs (~1230 SM clocks) plus the X packing, the fix-up and
-// the launches.
+// Expected time of the structured-sparse kernel, fitted to 2:4 weights of
+// 4096^2 and 8192^2 at M = 64 ... 1024 on B200: 1.4 us per k-block of a
+// CTA's range (each moves 104 KB from L2: the kernel runs at the L2 -> SM
+// rate, about twice its MMA time) plus 9 us of X packing, fix-up and
+// launches; the remainder's kernel ~3 us plus ~4 ps per (entry of R, row of
+// X) (measured at 90 % and 95 % on 8192^2, M = 64 ... 1024).
 double sp_time(const pfrt_ctx* ctx, const pfrt_csr* w, int64_t M) {
     const int64_t tiles = ceil_div(std::max<int64_t>(w->N, 1), 128), kb = ceil_div(std::max<int64_t>(w->K, 1), kSpBK);
     const int64_t total = tiles * ceil_div(M, kSpSlab) * kb;
     const double per_cta = std::ceil(static_cast<double>(total) / static_cast<double>(ctx->num_sms));
-    return per_cta * 0.65e-6 + 10.0e-6;
+    const double r_gathers = static_cast<double>(w->sp_over) * static_cast<double>(ceil_div(M, kSpSlab) * kSpSlab);
+    return per_cta * 1.4e-6 + 9.0e-6 + (w->sp_over > 0 ? 3.0e-6 + r_gathers * 4.0e-12 : 0.0);
 }
 
 template <int MV, bool SMEM>
@@ -1746,10 +1814,16 @@ pfrt_status spmm_uploaded(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x,
     // them): half the MMA work of the dense product, W read in compressed
     // form.  PFRT_SPMM_SP = 0|1 forces it off or on (on: where W is 2:4).
     const char* sp_env = std::getenv("PFRT_SPMM_SP");
-    const bool sp_ok = w->sp_state >= 0 && w->N > 0 && w->K > 0 && M <= (int64_t{1} << 30) / std::max<int64_t>(w->N, 1);
-    bool use_sp = sp_ok && M >= 16 && !(dense_env && *dense_env) && !(tiled_env && *tiled_env) && !(tc_env && *tc_env) &&
+    const bool sp_forced = sp_env && *sp_env;
+    const bool sp_free = !(dense_env && *dense_env) && !(tiled_env && *tiled_env) && !(tc_env && *tc_env);
+    if ((sp_forced ? *sp_env == '1' : (M >= 16 && sp_free)) && w->sp_state == 0) {
+        st = ensure_sp_count(w, s);
+        if (st) return st;
+    }
+    const bool sp_ok = w->sp_state > 0 && w->N > 0 && w->K > 0 && M <= (int64_t{1} << 30) / std::max<int64_t>(w->N, 1);
+    bool use_sp = sp_ok && M >= 16 && sp_free &&
                   sp_time(ctx, w, M) < std::min({t_tiled, dense_ok ? t_dense : 1e30, tc_ok ? tc_time(ctx, w, M) : 1e30});
-    if (sp_env && *sp_env) use_sp = sp_ok && *sp_env == '1';
+    if (sp_forced) use_sp = sp_ok && *sp_env == '1';
     if (use_sp) {
         st = run_spmm_sp(ctx, w, M, x, ldx, y, ldy, s);
         if (st != PFRT_ERR_UNSUPPORTED) return st;  // else W is not 2:4 along K
@@ -1990,6 +2064,9 @@ pfrt_status pfrt_csr_destroy(pfrt_csr* w) {
     if (w->tc_off) cudaFree(w->tc_off);
     if (w->tc_vals) cudaFree(w->tc_vals);
     if (w->sp_wimg) cudaFree(w->sp_wimg);
+    if (w->sp_rptr) cudaFree(w->sp_rptr);
+    if (w->sp_rcol) cudaFree(w->sp_rcol);
+    if (w->sp_rval) cudaFree(w->sp_rval);
     delete w;
     return PFRT_OK;
 }

@@ -44,6 +44,13 @@
 // (position of the first stored value) | (position of the second) << 2,
 // positions in 0..3 within the group, first < second.
 //
+// Any other sparse W: W = W24 + R, where W24 keeps the first two stored
+// entries (by column) of every group of four and R the others.  At 90 %
+// unstructured sparsity a group holds three or more entries with
+// probability ~0.4 %, so R is a few entries per row; sp_remainder_add_kernel
+// adds X R^T to Y afterwards in fp32 (R's entries of a row in column order,
+// products of X itself).
+//
 // One CTA per SM, 192 threads: warps 0..3 epilogue (TMEM lane quarter =
 // warp), warp 4 loader (bulk copies), warp 5 MMA issuer and TMEM owner.
 // TMEM: two 192-column accumulators at columns 0 and 256, then one 8-column
@@ -147,14 +154,12 @@ __device__ __forceinline__ void bf16x3(float x, uint16_t& p1, uint16_t& p2, uint
     p3 = __bfloat16_as_ushort(c);
 }
 
-// Eligibility: one warp per row marks the row's stored columns in shared
-// memory (one byte per column, 4 * groups bytes per warp) and raises *bad
-// when a group of four columns holds more than two, or when a column is
-// stored twice (fewer marked bytes than entries: the CSR sums duplicates,
-// and the compressed form has one slot per position).  Columns come from a
-// validated CSR, so every index is below K <= 4 * groups.
-__global__ void sp_check_kernel(int64_t N, int groups, const int32_t* __restrict__ indptr,
-                                const int32_t* __restrict__ indices, int* bad) {
+// Size of the remainder: one warp per row marks the row's stored columns in
+// shared memory (one byte per column, 4 * groups bytes per warp) and adds to
+// *over the entries past the second of every group of four columns.  Columns
+// come from a validated CSR, so every index is below K <= 4 * groups.
+__global__ void sp_count_kernel(int64_t N, int groups, const int32_t* __restrict__ indptr,
+                                const int32_t* __restrict__ indices, unsigned long long* over) {
     extern __shared__ uint8_t cnt_raw[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint8_t* cnt = cnt_raw + static_cast<int64_t>(warp) * groups * 4;
@@ -165,24 +170,57 @@ __global__ void sp_check_kernel(int64_t N, int groups, const int32_t* __restrict
     const int32_t j0 = indptr[n], j1 = indptr[n + 1];
     for (int32_t j = j0 + lane; j < j1; j += 32) cnt[indices[j]] = 1;
     __syncwarp();
-    int over = 0;
-    for (int g = lane; g < groups; g += 32)
-        over |= (cnt[4 * g] + cnt[4 * g + 1] + cnt[4 * g + 2] + cnt[4 * g + 3]) > 2;
-    int set = 0;
-    for (int g = lane; g < groups * 4; g += 32) set += cnt[g];
+    unsigned long long extra = 0;
+    for (int g = lane; g < groups; g += 32) {
+        const int c = cnt[4 * g] + cnt[4 * g + 1] + cnt[4 * g + 2] + cnt[4 * g + 3];
+        extra += c > 2 ? c - 2 : 0;
+    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) set += __shfl_xor_sync(0xffffffffu, set, o);
-    if (__any_sync(0xffffffffu, over) || (lane == 0 && set != j1 - j0)) atomicOr(bad, 1);
+    for (int o = 16; o > 0; o >>= 1) extra += __shfl_xor_sync(0xffffffffu, extra, o);
+    if (lane == 0 && extra) atomicAdd(over, extra);
 }
 
-// W[n, c] into the zero-filled dense scratch (one warp per row).
+// The remainder R from the dense scratch wd [npad][kpad]: one warp per row
+// walks the row 32 columns at a time (lane = column); an entry whose group
+// of four already has two earlier nonzeros belongs to R.  count: rcount[n]
+// = R's entries of row n; fill (rptr given): R's entries in column order.
+template <bool FILL>
+__global__ void sp_remainder_kernel(int64_t N, int64_t kpad, const float* __restrict__ wd,
+                                    int32_t* __restrict__ rcount, const int64_t* __restrict__ rptr,
+                                    int32_t* __restrict__ rcol, float* __restrict__ rval) {
+    const int64_t n = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (n >= N) return;
+    const float* row = wd + n * kpad;
+    int64_t at = FILL ? rptr[n] : 0;
+    int32_t total = 0;
+    for (int64_t c0 = 0; c0 < kpad; c0 += 32) {
+        const float v = row[c0 + lane];
+        const uint32_t nz = __ballot_sync(0xffffffffu, v != 0.0f);
+        const uint32_t gmask = 0xFu << (lane & ~3);
+        const uint32_t before = nz & gmask & ((1u << lane) - 1u);  // earlier nonzeros of my group
+        const bool extra = v != 0.0f && __popc(before) >= 2;
+        const uint32_t em = __ballot_sync(0xffffffffu, extra);
+        if (FILL && extra) {
+            const int64_t k = at + __popc(em & ((1u << lane) - 1u));
+            rcol[k] = static_cast<int32_t>(c0 + lane);
+            rval[k] = v;
+        }
+        at += __popc(em);
+        total += __popc(em);
+    }
+    if (!FILL && lane == 0) rcount[n] = total;
+}
+
+// W[n, c] into the zero-filled dense scratch (one warp per row; a column
+// stored twice is summed, as the CSR's product sums it).
 __global__ void sp_scatter_kernel(int64_t N, int64_t Kpad, const int32_t* __restrict__ indptr,
                                   const int32_t* __restrict__ indices, const float* __restrict__ values,
                                   float* __restrict__ wd) {
     const int64_t n = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (n >= N) return;
-    for (int32_t j = indptr[n] + lane; j < indptr[n + 1]; j += 32) wd[n * Kpad + indices[j]] = values[j];
+    for (int32_t j = indptr[n] + lane; j < indptr[n + 1]; j += 32) atomicAdd(wd + n * Kpad + indices[j], values[j]);
 }
 
 // W images from the dense scratch wd [Npad][Kpad] (zero padded): one thread
@@ -206,12 +244,12 @@ __global__ void sp_pack_w_kernel(int tiles, int KB, int64_t Kpad, const float* _
     for (int g = 0; g < 8; ++g) {
         const float4 q = *reinterpret_cast<const float4*>(src + 4 * g);
         const float e[4] = {q.x, q.y, q.z, q.w};
-        int p0 = -1, p1 = -1;
+        int p0 = -1, p1 = -1;  // the first two nonzeros; later ones are R's
 #pragma unroll
         for (int i = 0; i < 4; ++i)
             if (e[i] != 0.0f) {
                 if (p0 < 0) p0 = i;
-                else p1 = i;
+                else if (p1 < 0) p1 = i;
             }
         // Empty slots take zero values at positions that keep p0 < p1.
         if (p0 < 0) {
@@ -289,6 +327,31 @@ __global__ void sp_pack_x_kernel(const float* __restrict__ x, int64_t M, int64_t
         w.w = v[p][6] | (static_cast<uint32_t>(v[p][7]) << 16);
         *reinterpret_cast<uint4*>(base + p * kSpXPart + sp_swz(j, q & 7)) = w;
     }
+}
+
+// Y[m, n] += sum over R's entries (n, c, v) of v * X[m, c], in R's column
+// order, after the structured-sparse kernel (and its fix-up) wrote Y: one
+// warp per (X row m, 32 consecutive W rows), so Y's updates are coalesced;
+// rows without R entries are not touched.
+__global__ void sp_remainder_add_kernel(const float* __restrict__ x, int64_t ldx, int64_t M, int64_t N,
+                                        const int64_t* __restrict__ rptr, const int32_t* __restrict__ rcol,
+                                        const float* __restrict__ rval, float* __restrict__ y, int64_t ldy) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int64_t blocks = (N + 31) / 32;
+    const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (wid >= M * blocks) return;
+    const int64_t m = wid / blocks;
+    const int64_t n = (wid % blocks) * 32 + lane;
+    if (n >= N) return;
+    const int64_t e0 = rptr[n], e1 = rptr[n + 1];
+    if (e0 == e1) return;
+    const float* xr = x + m * ldx;
+    float acc = 0.0f;
+    for (int64_t e = e0; e < e1; ++e) acc = __fadd_rn(acc, __fmul_rn(rval[e], __ldg(xr + rcol[e])));
+    float* yp = y + m * ldy + n;
+    *yp = __fadd_rn(*yp, acc);
 }
 
 struct SpArgs {
@@ -391,9 +454,9 @@ __global__ void __launch_bounds__(kSpThreads, 1)
                 report_error(err, kDevWaitTimeout);
                 break;
             }
+            const int m0 = c * kSpSlab;
             if (kb_lo == 0 && kb_hi == KB) {
                 const int n = t * kTcWRows + nl;
-                const int m0 = c * kSpSlab;
                 if (n < a.N) {
                     float* dst = a.y + n;
 #pragma unroll

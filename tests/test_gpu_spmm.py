@@ -356,16 +356,24 @@ def test_structured_sparse_from_nm_pruning(ctx, monkeypatch):
         assert normwise_rel(y, po.spmm_linear(indptr, indices, values, X, N)) <= FP32_TOL
 
 
-def test_structured_sparse_ineligible_weights_fall_back(ctx, monkeypatch):
-    """A weight with three entries in some group of four, or a column stored
-    twice, is not 2:4: with the structured-sparse path forced on it still
-    gets the right result from the other paths."""
+@pytest.mark.parametrize("M,N,K,sparsity", [(96, 256, 512, 0.5), (64, 520, 1000, 0.9), (300, 4096, 4096, 0.9),
+                                            (64, 8192, 8192, 0.95), (17, 130, 259, 0.7)])
+def test_structured_sparse_with_remainder(ctx, M, N, K, sparsity, monkeypatch):
+    """Unstructured weights on the structured-sparse kernel: W = W24 + R, the
+    2:4 part on the tensor cores and the remainder R (entries past the second
+    of their group of four) added in fp32 by the epilogue, each CTA the
+    entries of its k-block range.  Normwise <= 1e-5 against the reference."""
     monkeypatch.setenv("PFRT_SPMM_SP", "1")
-    c = wl.spmm_case(96, 256, 512, sparsity=0.5, seed=4)
+    c = wl.spmm_case(M, N, K, sparsity=sparsity, seed=N + K)
     assert normwise_rel(gpu(ctx, c), oracle(c)) <= FP32_TOL
+
+
+def test_structured_sparse_duplicate_columns(ctx, monkeypatch):
+    """A column stored twice in a row is summed, as the reference's
+    sparse_matmul sums it, also on the structured-sparse kernel."""
+    monkeypatch.setenv("PFRT_SPMM_SP", "1")
     d = wl.structured24_case(96, 130, 256, seed=9)
     ip = d.indptr.astype(np.int64)
-    # row 0 stores its first column twice (the CSR sums both)
     idx = np.insert(d.indices, ip[0], d.indices[ip[0]])
     val = np.insert(d.values, ip[0], np.float32(0.5))
     ip = ip.copy()
