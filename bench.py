@@ -554,6 +554,70 @@ def spmm_config3(ctx, args, peaks, peak_src, sampler):
             "l2": f"{ncopies} copies of W rotated"}
 
 
+def spmm_structured(ctx, args, peaks, peak_src, sampler):
+    """A weight with 2:4 structure along K, as N:M pruning (n = 2, m = 4) of a
+    [N, K] weight leaves it (config 5's 8192 x 8192 shape, ~45 % of entries
+    kept), at M = 64 and 1024: pfrt_spmm's default path (the structured-sparse
+    tensor cores, spmm_sp.cuh) beside the dense copy's 3xTF32 Gemm and the
+    tensor-core kernel on W's compressed form, each forced by its switch, on
+    the same weight.  One GPU; W's forms (235 MB structured, 512 MB dense)
+    are each larger than L2."""
+    import torch
+
+    import pyflamert_b200 as pf
+    from pyflamert_b200 import workloads as wl
+    Ns = Ks = 8192
+    c = wl.structured24_case(8, Ns, Ks, seed=21)
+    nnz = int(c.values.size)
+    w = pf.CSR(ctx, Ns, Ks, c.indptr, c.indices, c.values)
+    envs = ("PFRT_SPMM_SP", "PFRT_SPMM_TC", "PFRT_SPMM_DENSE")
+    paths = {"default": {}, "dense": {"PFRT_SPMM_SP": "0", "PFRT_SPMM_DENSE": "1"},
+             "tc_compressed": {"PFRT_SPMM_SP": "0", "PFRT_SPMM_TC": "1"}}
+    tf32 = peaks["bf16_tflops"] / 2.0
+    bf16 = peaks["bf16_tflops"]
+    points = []
+    saved = {k: os.environ.get(k) for k in envs}
+    try:
+        for M in (64, 1024):
+            x = torch.randn((M, Ks), device="cuda")
+            y = torch.empty((M, Ns), dtype=torch.float32, device="cuda")
+            fns = [lambda: w(x, y=y)]
+            pt = {"M": M}
+            for name, env in paths.items():
+                for k in envs:
+                    os.environ.pop(k, None)
+                os.environ.update(env)
+                fns[0]()  # builds the path's device form of W outside the capture
+                torch.cuda.synchronize()
+                ms, t0, t1 = graph_time(fns, args.steps, args.warmup, 1, soak=False)
+                ctx.check()
+                pt[name + "_us"] = ms * 1e3
+                if name == "default":
+                    pt["clocks"] = sampler.summary(t0, t1)
+            # Roofs: the structured-sparse kernel's six bf16 products on the
+            # compressed operands are 6 x M x N x (K / 2) multiply-adds at the
+            # dense bf16 rate (a sparse K = 32 MMA takes the time of a dense
+            # K = 16 one); the dense path's are 3 tf32 products of M x N x K.
+            t_sp = 6.0 * M * Ns * Ks / (bf16 * 1e12)
+            pt["useful_tflops"] = 2.0 * nnz * M / (pt["default_us"] * 1e-6) / 1e12
+            pt["roofline"] = {"bound": "tensor (sparse bf16 x6)", "roof_us": 1e6 * t_sp,
+                              "frac": t_sp / (pt["default_us"] * 1e-6),
+                              "dense_3xtf32_roof_us": 1e6 * 6.0 * M * Ns * Ks / (tf32 * 1e12),
+                              "peak_source": f"bf16_tflops x 2 for 2:4 sparse MMAs ({peak_src} MEASURED_PEAKS.json)"}
+            points.append(pt)
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+        w.close()
+    return {"metric": "SpMM us per call, 2:4-structured weight (N:M pruning n=2 m=4), 8192 x 8192",
+            "unit": "us", "higher_is_better": False, "nnz": nnz,
+            "path": "default = structured-sparse tensor cores (tcgen05.mma.sp, bf16 x3 split)",
+            "points": points, "gpu_launches_note": "3 launches per step (X packing, kernel, fix-up)"}
+
+
 def spmm_sweep(ctx, args, world, rank, peaks, peak_src, sampler):  # noqa: C901
     """Config 5's batch sweep (M in 1, 64, 1024, 8192) on its 8192 x 8192
     weight at 90 % sparsity.  One GPU: pfrt_spmm (the kernel its cost model
@@ -813,6 +877,13 @@ def profile_target(args):
         a = torch.from_numpy(q.a).cuda()
         y = torch.empty((m, N), dtype=torch.int8, device="cuda")
         fns = [lambda: w(a, q.a_scale, q.a_zp, out="int8", y_scale=q.y_scale, y=y)]
+    elif t == "spmm_24":
+        # a 2:4 weight (8192 x 8192) at M = 64: the structured-sparse kernel
+        c = wl.structured24_case(64, 8192, 8192, seed=21)
+        w = pf.CSR(ctx, c.N, c.K, c.indptr, c.indices, c.values)
+        x = torch.from_numpy(c.X).cuda()
+        y = torch.empty((64, c.N), dtype=torch.float32, device="cuda")
+        fns = [lambda: w(x, y=y)]
     elif t in ("spmm_m1", "spmm_cfg3", "spmm_mid", "spmm_m64"):
         c = (wl.spmm_case(1, SPMM_N, SPMM_K, sparsity=SPMM_S, seed=3) if t == "spmm_m1"
              else wl.spmm_case(256, 4096, 4096, sparsity=0.9, seed=3) if t == "spmm_cfg3"
@@ -845,7 +916,7 @@ def main():
     ap.add_argument("--eager", action="store_true",
                     help="plain launches without CUDA graph or soak (profiler runs; not a bench value)")
     ap.add_argument("--profile-target", default=None,
-                    choices=["qlinear", "spmm_m1", "spmm_cfg3", "spmm_mid", "spmm_m64", "gemm_cfg1",
+                    choices=["qlinear", "spmm_m1", "spmm_cfg3", "spmm_mid", "spmm_m64", "spmm_24", "gemm_cfg1",
                              "qlinear_4096"],
                     help="run only this workload, eagerly, for a profiler; prints its ms/step")
     args = ap.parse_args()
@@ -990,6 +1061,7 @@ def main():
             for obj in sc:
                 obj[0].close()
             line["spmm_config3"] = spmm_config3(ctx, args, peaks, peak_src, sampler)
+            line["spmm_structured"] = spmm_structured(ctx, args, peaks, peak_src, sampler)
         else:
             line["spmm"] = spmm_nshard(ctx, args, world, rank, peaks, peak_src)
         line["spmm_sweep"] = spmm_sweep(ctx, args, world, rank, peaks, peak_src, sampler)

@@ -200,10 +200,13 @@ PFRT_API pfrt_status pfrt_qlinear_host(pfrt_ctx* ctx, const pfrt_qweight* w, int
  *
  * pfrt_spmm: X device [M,K] (row stride ldx), Y device [M,N] (row stride ldy).
  * The first call with a given M class builds state kept with the CSR (for
- * M = 3..8 a row partition, for M > 8 row groups or a dense copy of W; each
- * allocates device memory and synchronizes): make one call of each batch
- * size class before capturing calls in a CUDA graph, and do not use one CSR
- * from several threads or contexts at once.
+ * M = 3..8 a row partition; for M > 8 row groups, a dense copy of W, W's
+ * compressed form, or its structured-sparse form: for M >= 16 the first call
+ * counts the entries past the second of every group of four columns, and
+ * the first call that chooses the structured-sparse tensor cores builds W's
+ * 2:4 images and remainder; each allocates device memory and synchronizes):
+ * make one call of each batch size class before capturing calls in a CUDA
+ * graph, and do not use one CSR from several threads or contexts at once.
  * pfrt_spmm_csr_f32: same on a caller-owned device CSR (int32); the kernel
  * bounds-checks every index, skips out-of-range entries and reports
  * PFRT_ERR_BAD_CSR through pfrt_ctx_check(). */
