@@ -1519,12 +1519,16 @@ pfrt_status run_spmm_sp(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x, i
     const TcSched sc = sp_schedule(ctx, w, M);
     const int64_t grid = ceil_div(sc.total, sc.per_cta);
     const size_t xbytes = align_up(static_cast<size_t>(sc.n_xslabs) * static_cast<size_t>(sc.kb_total) * kSpXImg, 256);
-    const size_t pbytes = sizeof(float) * static_cast<size_t>(2 * grid * kTcTileElems);
+    const size_t pbytes = align_up(sizeof(float) * static_cast<size_t>(2 * grid * kTcTileElems), 256);
+    const int64_t mpad = ceil_div(M, kSpSlab) * kSpSlab;  // X^T's row stride for the remainder
+    const size_t tbytes = w->sp_rptr ? sizeof(float) * static_cast<size_t>(w->K) * static_cast<size_t>(mpad) : 0;
     void* scr = nullptr;
-    st = scratch(ctx, xbytes + pbytes, &scr);
+    st = scratch(ctx, xbytes + pbytes + tbytes, &scr);
     if (st) return st;
     uint8_t* ximg = static_cast<uint8_t*>(scr);
     float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(scr) + xbytes);
+    float* xt = reinterpret_cast<float*>(static_cast<uint8_t*>(scr) + xbytes + pbytes);
+
     cudaLaunchAttribute attr[1];
     {
         const int64_t threads = static_cast<int64_t>(sc.n_xslabs) * sc.kb_total * kSpSlab * 16;
@@ -1534,7 +1538,8 @@ pfrt_status run_spmm_sp(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x, i
         pc.stream = s;
         pc.numAttrs = pdl_attr(attr);
         pc.attrs = attr;
-        PFRT_CUDA_TRY(cudaLaunchKernelEx(&pc, sp_pack_x_kernel, x, M, w->K, ldx, sc.n_xslabs, sc.kb_total, ximg));
+        PFRT_CUDA_TRY(cudaLaunchKernelEx(&pc, sp_pack_x_kernel, x, M, w->K, ldx, sc.n_xslabs, sc.kb_total, ximg,
+                                         w->sp_rptr ? xt : static_cast<float*>(nullptr), mpad));
     }
     SpArgs a{};
     a.wimg = w->sp_wimg;
@@ -1564,14 +1569,13 @@ pfrt_status run_spmm_sp(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x, i
                                          static_cast<int>(M), static_cast<int>(w->N), kSpSlab, y, ldy));
     }
     if (w->sp_rptr) {
-        const int64_t warps = M * ceil_div(w->N, 32);
         cudaLaunchConfig_t qc{};
-        qc.gridDim = dim3(static_cast<unsigned>(ceil_div(warps * 32, 256)));
-        qc.blockDim = dim3(256);
+        qc.gridDim = dim3(static_cast<unsigned>(ceil_div(w->N, 32)), static_cast<unsigned>(mpad / kSpSlab));
+        qc.blockDim = dim3(1024);
         qc.stream = s;
         qc.numAttrs = pdl_attr(attr);
         qc.attrs = attr;
-        PFRT_CUDA_TRY(cudaLaunchKernelEx(&qc, sp_remainder_add_kernel, x, ldx, M, w->N,
+        PFRT_CUDA_TRY(cudaLaunchKernelEx(&qc, sp_remainder_add_kernel, static_cast<const float*>(xt), mpad, M, w->N,
                                          static_cast<const int64_t*>(w->sp_rptr), static_cast<const int32_t*>(w->sp_rcol),
                                          static_cast<const float*>(w->sp_rval), y, ldy));
     }
@@ -1582,14 +1586,14 @@ pfrt_status run_spmm_sp(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x, i
 // 4096^2 and 8192^2 at M = 64 ... 1024 on B200: 1.4 us per k-block of a
 // CTA's range (each moves 104 KB from L2: the kernel runs at the L2 -> SM
 // rate, about twice its MMA time) plus 9 us of X packing, fix-up and
-// launches; the remainder's kernel ~3 us plus ~4 ps per (entry of R, row of
-// X) (measured at 90 % and 95 % on 8192^2, M = 64 ... 1024).
+// launches; the remainder's kernel ~3 us plus ~0.5 ps per (entry of R, row
+// of X).
 double sp_time(const pfrt_ctx* ctx, const pfrt_csr* w, int64_t M) {
     const int64_t tiles = ceil_div(std::max<int64_t>(w->N, 1), 128), kb = ceil_div(std::max<int64_t>(w->K, 1), kSpBK);
     const int64_t total = tiles * ceil_div(M, kSpSlab) * kb;
     const double per_cta = std::ceil(static_cast<double>(total) / static_cast<double>(ctx->num_sms));
     const double r_gathers = static_cast<double>(w->sp_over) * static_cast<double>(ceil_div(M, kSpSlab) * kSpSlab);
-    return per_cta * 1.4e-6 + 9.0e-6 + (w->sp_over > 0 ? 3.0e-6 + r_gathers * 4.0e-12 : 0.0);
+    return per_cta * 1.4e-6 + 9.0e-6 + (w->sp_over > 0 ? 3.0e-6 + r_gathers * 5.0e-13 : 0.0);
 }
 
 template <int MV, bool SMEM>

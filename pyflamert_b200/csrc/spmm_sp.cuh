@@ -49,7 +49,7 @@
 // unstructured sparsity a group holds three or more entries with
 // probability ~0.4 %, so R is a few entries per row; sp_remainder_add_kernel
 // adds X R^T to Y afterwards in fp32 (R's entries of a row in column order,
-// products of X itself).
+// products of X itself, read from a transposed copy of X).
 //
 // One CTA per SM, 192 threads: warps 0..3 epilogue (TMEM lane quarter =
 // warp), warp 4 loader (bulk copies), warp 5 MMA issuer and TMEM owner.
@@ -289,17 +289,19 @@ __global__ void sp_pack_w_kernel(int tiles, int KB, int64_t Kpad, const float* _
     atomicOr(meta + (b16 + 8 + i) * 4, nib_hi << (16 * hh));
 }
 
-// X images: one thread per (slab c, k-block kb, row j, 8-column piece q):
-// X[64 c + j, 128 kb + 8 q + 0..7] split into three bf16 parts, 16 bytes of
-// each part written to its swizzled place (zeros past M or K).
+// X images: one thread per (slab c, k-block kb, 8-column piece q, row j),
+// rows fastest: X[64 c + j, 128 kb + 8 q + 0..7] split into three bf16
+// parts, 16 bytes of each part written to its swizzled place (zeros past M
+// or K).  With xt (the remainder's transposed X, [K][ldxt]) the thread also
+// writes its eight values there: a warp's 32 rows make 128-byte stores.
 __global__ void sp_pack_x_kernel(const float* __restrict__ x, int64_t M, int64_t K, int64_t ldx, int slabs, int KB,
-                                 uint8_t* __restrict__ img) {
+                                 uint8_t* __restrict__ img, float* __restrict__ xt, int64_t ldxt) {
     pdl_wait();
     pdl_launch_dependents();
     const int64_t id = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (id >= static_cast<int64_t>(slabs) * KB * kSpSlab * 16) return;
-    const int q = static_cast<int>(id % 16);
-    const int j = static_cast<int>((id / 16) % kSpSlab);
+    const int j = static_cast<int>(id % kSpSlab);
+    const int q = static_cast<int>((id / kSpSlab) % 16);
     const int64_t ck = id / (16 * kSpSlab);
     const int kb = static_cast<int>(ck % KB);
     const int c = static_cast<int>(ck / KB);
@@ -313,6 +315,11 @@ __global__ void sp_pack_x_kernel(const float* __restrict__ x, int64_t M, int64_t
     } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) e[i] = (m < M && k0 + i < K) ? x[m * ldx + k0 + i] : 0.0f;
+    }
+    if (xt != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (k0 + i < K) xt[(k0 + i) * ldxt + m] = e[i];
     }
     uint16_t v[3][8];
 #pragma unroll
@@ -330,28 +337,66 @@ __global__ void sp_pack_x_kernel(const float* __restrict__ x, int64_t M, int64_t
 }
 
 // Y[m, n] += sum over R's entries (n, c, v) of v * X[m, c], in R's column
-// order, after the structured-sparse kernel (and its fix-up) wrote Y: one
-// warp per (X row m, 32 consecutive W rows), so Y's updates are coalesced;
-// rows without R entries are not touched.
-__global__ void sp_remainder_add_kernel(const float* __restrict__ x, int64_t ldx, int64_t M, int64_t N,
-                                        const int64_t* __restrict__ rptr, const int32_t* __restrict__ rcol,
-                                        const float* __restrict__ rval, float* __restrict__ y, int64_t ldy) {
+// order, after the structured-sparse kernel (and its fix-up) wrote Y.  X
+// comes transposed and padded (xt [K][ldxt], ldxt a multiple of 64), so an
+// entry's 64 products read 256 contiguous bytes.  One block per (32 W rows,
+// 64 X rows), 32 warps: the block's R entries (contiguous in R) staged in
+// shared memory, one warp per W row with the lanes over the X rows, the sums
+// collected in a shared tile and added to Y row by row (coalesced).
+// W rows without R entries are not touched.
+constexpr int kSpRStage = 2048;  // R entries staged per block (more are read from global memory)
+
+__global__ void __launch_bounds__(1024) sp_remainder_add_kernel(const float* __restrict__ xt, int64_t ldxt, int64_t M,
+                                                               int64_t N, const int64_t* __restrict__ rptr,
+                                                               const int32_t* __restrict__ rcol,
+                                                               const float* __restrict__ rval, float* __restrict__ y,
+                                                               int64_t ldy) {
+    __shared__ int32_t s_col[kSpRStage];
+    __shared__ float s_val[kSpRStage];
+    __shared__ float tile[64][33];
     pdl_wait();
     pdl_launch_dependents();
-    const int64_t blocks = (N + 31) / 32;
-    const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (wid >= M * blocks) return;
-    const int64_t m = wid / blocks;
-    const int64_t n = (wid % blocks) * 32 + lane;
-    if (n >= N) return;
-    const int64_t e0 = rptr[n], e1 = rptr[n + 1];
-    if (e0 == e1) return;
-    const float* xr = x + m * ldx;
-    float acc = 0.0f;
-    for (int64_t e = e0; e < e1; ++e) acc = __fadd_rn(acc, __fmul_rn(rval[e], __ldg(xr + rcol[e])));
-    float* yp = y + m * ldy + n;
-    *yp = __fadd_rn(*yp, acc);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * 32, m0 = static_cast<int64_t>(blockIdx.y) * 64;
+    const int64_t e_begin = rptr[n0 < N ? n0 : N];
+    const int64_t e_end = rptr[n0 + 32 < N ? n0 + 32 : N];
+    const bool staged = e_end - e_begin <= kSpRStage;
+    if (staged)
+        for (int64_t i = threadIdx.x; i < e_end - e_begin; i += blockDim.x) {
+            s_col[i] = rcol[e_begin + i];
+            s_val[i] = rval[e_begin + i];
+        }
+    __syncthreads();
+    {
+        const int r = warp;
+        const int64_t n = n0 + r;
+        float a0 = 0.0f, a1 = 0.0f;
+        if (n < N) {
+            const int64_t e1 = rptr[n + 1];
+#pragma unroll 4
+            for (int64_t e = rptr[n]; e < e1; ++e) {
+                const int64_t c = staged ? s_col[e - e_begin] : rcol[e];
+                const float v = staged ? s_val[e - e_begin] : rval[e];
+                const float* xp = xt + c * ldxt + m0;
+                a0 = __fadd_rn(a0, __fmul_rn(v, __ldg(xp + lane)));
+                a1 = __fadd_rn(a1, __fmul_rn(v, __ldg(xp + 32 + lane)));
+            }
+        }
+        tile[lane][r] = a0;
+        tile[32 + lane][r] = a1;
+    }
+    __syncthreads();
+    const int64_t n = n0 + lane;
+    if (n >= N || rptr[n + 1] == rptr[n]) return;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int ml = warp * 2 + i;
+        const int64_t m = m0 + ml;
+        if (m < M) {
+            float* yp = y + m * ldy + n;
+            *yp = __fadd_rn(*yp, tile[ml][lane]);
+        }
+    }
 }
 
 struct SpArgs {
