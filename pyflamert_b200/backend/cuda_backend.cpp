@@ -9,6 +9,7 @@
 #include "cuda_backend.hpp"
 
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 #include <exception>
 #include <chrono>
@@ -519,6 +520,19 @@ void CudaBackend::Impl::run_qmatmul(const Graph& g, const Node& n, const std::ve
     if (A.dtype != DType::Int8 && A.dtype != DType::UInt8)
         fail_node(n, "QuantizedMatMul: input A must be Int8 or UInt8");
     if (Bd.dtype != DType::Int8) fail_node(n, "QuantizedMatMul: the cuda backend needs Int8 weights (input B)");
+    if (A.dtype == DType::UInt8) {
+        // The reference's CPU op reads a uint8 A as int8 (quantized_ops.cpp:143);
+        // this backend computes quantization::quantized_matmul's result, which
+        // reads it as unsigned.  Said once per process, so a user comparing
+        // device = "cuda" with "cpu" knows why uint8 graphs differ.
+        static std::once_flag told;
+        std::call_once(told, [] {
+            std::fprintf(stderr,
+                         "pyflamert_b200: QuantizedMatMul with a uint8 input A is computed as "
+                         "quantization::quantized_matmul does (unsigned); the reference CPU op reads uint8 A "
+                         "as int8, so device=\"cpu\" gives different numbers for such graphs\n");
+        });
+    }
     if (A.shape.size() < 2 || Bd.shape.size() != 2)
         fail_node(n, "QuantizedMatMul: A needs at least 2 dimensions and B exactly 2 on the cuda backend");
     const int64_t K = A.shape.back(), Kb = Bd.shape[0], N = Bd.shape[1];
