@@ -13,6 +13,7 @@
 #include <atomic>
 #include <chrono>
 #include <condition_variable>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <thread>
@@ -24,19 +25,25 @@ namespace pfrt {
 
 namespace {
 
-// memcpy of one buffer split over the caller and `kWorkers` threads.  A copy
-// is handed over through atomics, and a worker that has just finished one
-// keeps polling for the next for up to kSpinNs before it sleeps on the
-// condition variable: the chunks of one transfer follow each other within
-// microseconds, and a futex wake-up per chunk would cost more than the copy
-// of a 256 KiB chunk.  Idle workers sleep.
+// memcpy of one buffer split over the caller and `workers` threads (3 by
+// default; PFRT_COPY_WORKERS overrides, 0 copies on the caller alone).  A
+// copy is handed over through atomics, and a worker that has just finished
+// one keeps polling for the next for up to `spin` (100 us by default;
+// PFRT_COPY_SPIN_US overrides) before it sleeps on the condition variable:
+// the chunks of one transfer follow each other within microseconds, and a
+// futex wake-up per chunk would cost more than the copy of a 256 KiB chunk.
+// Idle workers sleep.
+int env_or(const char* name, int dflt) {
+    const char* v = std::getenv(name);
+    return (v && *v) ? std::atoi(v) : dflt;
+}
+
 class CopyPool {
 public:
-    static constexpr int kWorkers = 3;
-    static constexpr int64_t kSpinNs = 100000;
-
-    CopyPool() {
-        for (int i = 0; i < kWorkers; ++i) threads_.emplace_back([this, i] { work(i); });
+    CopyPool()
+        : workers_(std::max(0, std::min(env_or("PFRT_COPY_WORKERS", 3), 15))),
+          spin_ns_(static_cast<int64_t>(std::max(0, env_or("PFRT_COPY_SPIN_US", 100))) * 1000) {
+        for (int i = 0; i < workers_; ++i) threads_.emplace_back([this, i] { work(i); });
     }
     ~CopyPool() {
         {
@@ -49,16 +56,16 @@ public:
 
     void copy(void* dst, const void* src, size_t n) {
         constexpr size_t kMinSplit = 128 * 1024;
-        if (n < kMinSplit) {
+        if (n < kMinSplit || workers_ == 0) {
             std::memcpy(dst, src, n);
             return;
         }
-        const size_t part = (n / (kWorkers + 1) + 63) & ~size_t{63};
+        const size_t part = (n / (workers_ + 1) + 63) & ~size_t{63};
         dst_ = static_cast<char*>(dst);
         src_ = static_cast<const char*>(src);
         n_ = n;
         part_ = part;
-        pending_.store(kWorkers, std::memory_order_relaxed);
+        pending_.store(workers_, std::memory_order_relaxed);
         {
             // The release publishes the job to polling workers; the lock
             // orders it against a worker that is about to sleep.
@@ -80,7 +87,7 @@ private:
                 const auto t0 = std::chrono::steady_clock::now();
                 while ((g = gen_.load(std::memory_order_acquire)) == seen && !stop_.load() &&
                        std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0)
-                               .count() < kSpinNs) {
+                               .count() < spin_ns_) {
                 }
                 if (g == seen) {
                     std::unique_lock<std::mutex> l(m_);
@@ -95,12 +102,14 @@ private:
             seen = g;
             const size_t n = n_, part = part_;
             const size_t lo = std::min(n, part * static_cast<size_t>(i + 1));
-            const size_t hi = (i == kWorkers - 1) ? n : std::min(n, part * static_cast<size_t>(i + 2));
+            const size_t hi = (i == workers_ - 1) ? n : std::min(n, part * static_cast<size_t>(i + 2));
             if (hi > lo) std::memcpy(dst_ + lo, src_ + lo, hi - lo);
             pending_.fetch_sub(1, std::memory_order_release);
         }
     }
 
+    const int workers_;
+    const int64_t spin_ns_;
     std::vector<std::thread> threads_;
     std::mutex m_;
     std::condition_variable cv_;
