@@ -1587,13 +1587,18 @@ pfrt_status run_spmm_sp(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x, i
 // CTA's range (each moves 104 KB from L2: the kernel runs at the L2 -> SM
 // rate, about twice its MMA time) plus 9 us of X packing, fix-up and
 // launches; the remainder's kernel ~3 us plus ~0.5 ps per (entry of R, row
-// of X).
+// of X).  Once X's images outgrow L2 (above ~96 MB: M > ~2000 at K = 8192)
+// every W tile re-reads them from HBM (8192^2 at 90 %, M = 8192: 7.97 ms
+// against the dense path's 6.15 ms), charged at 6 TB/s.
 double sp_time(const pfrt_ctx* ctx, const pfrt_csr* w, int64_t M) {
     const int64_t tiles = ceil_div(std::max<int64_t>(w->N, 1), 128), kb = ceil_div(std::max<int64_t>(w->K, 1), kSpBK);
-    const int64_t total = tiles * ceil_div(M, kSpSlab) * kb;
+    const int64_t slabs = ceil_div(M, kSpSlab);
+    const int64_t total = tiles * slabs * kb;
     const double per_cta = std::ceil(static_cast<double>(total) / static_cast<double>(ctx->num_sms));
-    const double r_gathers = static_cast<double>(w->sp_over) * static_cast<double>(ceil_div(M, kSpSlab) * kSpSlab);
-    return per_cta * 1.4e-6 + 9.0e-6 + (w->sp_over > 0 ? 3.0e-6 + r_gathers * 5.0e-13 : 0.0);
+    const double r_gathers = static_cast<double>(w->sp_over) * static_cast<double>(slabs * kSpSlab);
+    const double x_bytes = static_cast<double>(slabs) * static_cast<double>(kb) * kSpXImg;
+    const double x_rereads = x_bytes > 96.0e6 ? static_cast<double>(tiles - 1) * x_bytes / 6.0e12 : 0.0;
+    return per_cta * 1.4e-6 + 9.0e-6 + x_rereads + (w->sp_over > 0 ? 3.0e-6 + r_gathers * 5.0e-13 : 0.0);
 }
 
 template <int MV, bool SMEM>
