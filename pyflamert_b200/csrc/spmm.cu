@@ -71,7 +71,11 @@ struct pfrt_csr {
     int sp_state = 0;
     int64_t sp_over = 0;          // entries past the second of their group of four (R's size)
     int sp_tiles = 0, sp_kb = 0;
-    uint8_t* sp_wimg = nullptr;   // [sp_tiles][sp_kb] images of kSpWImg bytes
+    uint8_t* sp_wimg = nullptr;   // image form: [sp_tiles][sp_kb] images of kSpWImg bytes
+    uint4* sp_cmeta = nullptr;    // compressed form (sparser weights): [sp_kb][128 sp_tiles] metadata,
+    uint2* sp_cocc = nullptr;     //   slot masks, value indices and bf16 x3 values (spmm_sp.cuh)
+    uint32_t* sp_coff = nullptr;
+    uint2* sp_cvals = nullptr;
     int64_t* sp_rptr = nullptr;   // R: [N + 1], null when R is empty
     int32_t* sp_rcol = nullptr;
     float* sp_rval = nullptr;
@@ -1420,6 +1424,37 @@ pfrt_status ensure_sp_count(pfrt_csr* w, cudaStream_t s) {
     return PFRT_OK;
 }
 
+// Which form of W24 the structured-sparse kernel reads.  The compressed form
+// (28 bytes per row and k-block plus 8 per kept entry) is chosen where the
+// images would not stay in L2 (over ~96 MB; a smaller weight's images are
+// re-read from L2 by every X slab, which beats expanding the compressed
+// form again: 4096^2 at 90 %, M = 256, 56 against 62 us) and a W tile's
+// values of one k-block fit the kernel's value slot with room to spare on
+// average (W24 under ~10 % dense; 90 %-sparse weights keep ~10 %, with the
+// longest runs still in the slot).  8192^2 at 90 % on B200: M = 64 59 us
+// both, M = 256 183 against 192 us, M = 1024 699 against 706 us; at 95 %
+// 55 against 56 and 172 against 186 us.  Whether every run fits is checked
+// when the form is built.  PFRT_SPMM_SP_FORM =
+// image|compressed forces one (read when the form is built; a forced
+// compressed form reads runs that do not fit from global memory, slowly).
+bool sp_form_forced(bool& cform) {
+    const char* f = std::getenv("PFRT_SPMM_SP_FORM");
+    if (!f) return false;
+    if (std::strcmp(f, "image") == 0) cform = false;
+    else if (std::strcmp(f, "compressed") == 0) cform = true;
+    else return false;
+    return true;
+}
+
+bool sp_use_cform(const pfrt_csr* w) {
+    const double tiles = static_cast<double>(ceil_div(w->N, 128)), KB = static_cast<double>(ceil_div(w->K, kSpBK));
+    const double kept = static_cast<double>(std::max<int64_t>(w->nnz - w->sp_over, 0));
+    if (kept >= 4.0e9) return false;  // 32-bit value indices
+    bool cform = false;
+    if (sp_form_forced(cform)) return cform;
+    return tiles * KB * kSpWImg > 96.0e6 && 8.0 * kept / (tiles * KB) < 0.85 * kSpVSlot;
+}
+
 // W's structured-sparse form, built once on the device from a dense scratch
 // copy that is freed again: the 2:4 part W24 as images, the remainder R as a
 // CSR (each row's entries in column order, so the result does not depend on
@@ -1432,26 +1467,89 @@ pfrt_status ensure_sp(pfrt_csr* w, cudaStream_t s) {
     const int KB = static_cast<int>(ceil_div(w->K, kSpBK));
     const int64_t npad = static_cast<int64_t>(tiles) * 128, kpad = static_cast<int64_t>(KB) * kSpBK;
     const size_t wd_bytes = sizeof(float) * static_cast<size_t>(npad) * static_cast<size_t>(kpad);
-    const size_t img_bytes = static_cast<size_t>(tiles) * static_cast<size_t>(KB) * kSpWImg;
+    bool cform = sp_use_cform(w);
+    bool cform_forced = false;
+    {
+        bool f = false;
+        cform_forced = sp_form_forced(f) && f;
+    }
+    const size_t nrk = static_cast<size_t>(npad) * static_cast<size_t>(KB);  // (k-block, row) pairs
     float* wd = nullptr;
     uint8_t* img = nullptr;
+    uint4* cmeta = nullptr;
+    uint2* cocc = nullptr;
+    uint32_t* coff = nullptr;
+    uint2* cvals = nullptr;
     int32_t* rcount = nullptr;
     int64_t* rptr = nullptr;
     int32_t* rcol = nullptr;
     float* rval = nullptr;
     const unsigned row_blocks = static_cast<unsigned>(ceil_div(w->N * 32, 256));
     cudaError_t e = cudaMalloc(&wd, wd_bytes);
-    if (e == cudaSuccess) e = cudaMalloc(&img, img_bytes);
     if (e == cudaSuccess) e = cudaMemsetAsync(wd, 0, wd_bytes, s);
-    if (e == cudaSuccess) e = cudaMemsetAsync(img, 0, img_bytes, s);
     if (e == cudaSuccess) {
         sp_scatter_kernel<<<row_blocks, 256, 0, s>>>(w->N, kpad, w->indptr, w->indices, w->values, wd);
         e = cudaGetLastError();
     }
-    if (e == cudaSuccess) {
+    if (e == cudaSuccess && cform) {
+        // Two passes over the scratch: counts (with each row's metadata and
+        // slot mask) per (k-block, row), a host scan into value indices,
+        // then the values.  A run (one W tile's values of one k-block)
+        // longer than the kernel's value slot sends the weight to the images
+        // unless the form is forced.
+        const unsigned cblocks = static_cast<unsigned>(ceil_div(static_cast<int64_t>(nrk), 256));
+        std::vector<uint32_t> hoff(nrk + 1);
+        e = cudaMalloc(&cmeta, sizeof(uint4) * nrk);
+        if (e == cudaSuccess) e = cudaMalloc(&cocc, sizeof(uint2) * nrk);
+        if (e == cudaSuccess) e = cudaMalloc(&coff, sizeof(uint32_t) * (nrk + 1));
+        if (e == cudaSuccess) {
+            sp_cform_kernel<true><<<cblocks, 256, 0, s>>>(npad, KB, kpad, wd, coff, cmeta, cocc, nullptr, nullptr);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaMemcpyAsync(hoff.data(), coff, sizeof(uint32_t) * nrk, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        uint64_t total = 0;
+        for (size_t i = 0; e == cudaSuccess && i < nrk; ++i) {
+            const uint32_t c = hoff[i];
+            hoff[i] = static_cast<uint32_t>(total);
+            total += c;
+        }
+        hoff[nrk] = static_cast<uint32_t>(total);
+        uint64_t longest = 0;
+        for (size_t r = 0; r < nrk; r += 128) {
+            const uint64_t b0 = (uint64_t{hoff[r]} * 8u) & ~uint64_t{15};
+            const uint64_t b1 = (uint64_t{hoff[r + 128]} * 8u + 15u) & ~uint64_t{15};
+            longest = std::max(longest, b1 - b0);
+        }
+        if (e == cudaSuccess && longest > static_cast<uint64_t>(kSpVSlot) && !cform_forced) {
+            cudaFree(cmeta);
+            cudaFree(cocc);
+            cudaFree(coff);
+            cmeta = nullptr;
+            cocc = nullptr;
+            coff = nullptr;
+            cform = false;
+        }
+        const size_t vbytes = ((8 * total + 15) & ~size_t{15}) + 16;  // copies end on a 16-byte boundary
+        if (e == cudaSuccess && cform) e = cudaMalloc(&cvals, vbytes);
+        if (e == cudaSuccess && cform)
+            e = cudaMemcpyAsync(coff, hoff.data(), sizeof(uint32_t) * (nrk + 1), cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess && cform) {
+            sp_cform_kernel<false><<<cblocks, 256, 0, s>>>(npad, KB, kpad, wd, nullptr, nullptr, nullptr, coff, cvals);
+            e = cudaGetLastError();
+        }
+        // hoff is read by the copy above: wait before it goes out of scope.
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    }
+    if (e == cudaSuccess && !cform) {
+        const size_t img_bytes = static_cast<size_t>(tiles) * static_cast<size_t>(KB) * kSpWImg;
+        e = cudaMalloc(&img, img_bytes);
+        if (e == cudaSuccess) e = cudaMemsetAsync(img, 0, img_bytes, s);
         const int64_t threads = static_cast<int64_t>(tiles) * KB * 128 * kSpSteps;
-        sp_pack_w_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, s>>>(tiles, KB, kpad, wd, img);
-        e = cudaGetLastError();
+        if (e == cudaSuccess) {
+            sp_pack_w_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, s>>>(tiles, KB, kpad, wd, img);
+            e = cudaGetLastError();
+        }
     }
     if (e == cudaSuccess && w->sp_over > 0) {
         std::vector<int32_t> hcount(static_cast<size_t>(w->N));
@@ -1483,12 +1581,20 @@ pfrt_status ensure_sp(pfrt_csr* w, cudaStream_t s) {
     if (rcount) cudaFree(rcount);
     if (e != cudaSuccess) {
         if (img) cudaFree(img);
+        if (cmeta) cudaFree(cmeta);
+        if (cocc) cudaFree(cocc);
+        if (coff) cudaFree(coff);
+        if (cvals) cudaFree(cvals);
         if (rptr) cudaFree(rptr);
         if (rcol) cudaFree(rcol);
         if (rval) cudaFree(rval);
         return cuda_fail(e, "SpMM structured-sparse form");
     }
     w->sp_wimg = img;
+    w->sp_cmeta = cmeta;
+    w->sp_cocc = cocc;
+    w->sp_coff = coff;
+    w->sp_cvals = cvals;
     w->sp_rptr = rptr;
     w->sp_rcol = rcol;
     w->sp_rval = rval;
@@ -1544,20 +1650,28 @@ pfrt_status run_spmm_sp(pfrt_ctx* ctx, pfrt_csr* w, int64_t M, const float* x, i
     SpArgs a{};
     a.wimg = w->sp_wimg;
     a.ximg = ximg;
+    a.cmeta = w->sp_cmeta;
+    a.cocc = w->sp_cocc;
+    a.coff = w->sp_coff;
+    a.cvals = w->sp_cvals;
+    a.npad = static_cast<int64_t>(w->sp_tiles) * kTcWRows;
     a.M = static_cast<int>(M);
     a.N = static_cast<int>(w->N);
     a.y = y;
     a.ldy = ldy;
     a.partial = part;
-    PFRT_CUDA_TRY(cudaFuncSetAttribute(spmm_sp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSpSmemBytes));
+    const bool cform = w->sp_cmeta != nullptr;
+    auto kern = cform ? spmm_sp_kernel<true> : spmm_sp_kernel<false>;
+    const int smem = cform ? kSpSmemBytesX : kSpSmemBytes;
+    PFRT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
-    cfg.blockDim = dim3(kSpThreads);
-    cfg.dynamicSmemBytes = kSpSmemBytes;
+    cfg.blockDim = dim3(cform ? kSpThreadsX : kSpThreads);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cfg.numAttrs = pdl_attr(attr);
     cfg.attrs = attr;
-    PFRT_CUDA_TRY(cudaLaunchKernelEx(&cfg, spmm_sp_kernel, sc, a, ctx->d_err));
+    PFRT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, sc, a, ctx->d_err));
     if (grid > 1) {
         cudaLaunchConfig_t rc{};
         rc.gridDim = dim3(static_cast<unsigned>(grid - 1), static_cast<unsigned>(kSpSlab * kTcWRows / 1024));
@@ -2073,6 +2187,10 @@ pfrt_status pfrt_csr_destroy(pfrt_csr* w) {
     if (w->tc_off) cudaFree(w->tc_off);
     if (w->tc_vals) cudaFree(w->tc_vals);
     if (w->sp_wimg) cudaFree(w->sp_wimg);
+    if (w->sp_cmeta) cudaFree(w->sp_cmeta);
+    if (w->sp_cocc) cudaFree(w->sp_cocc);
+    if (w->sp_coff) cudaFree(w->sp_coff);
+    if (w->sp_cvals) cudaFree(w->sp_cvals);
     if (w->sp_rptr) cudaFree(w->sp_rptr);
     if (w->sp_rcol) cudaFree(w->sp_rcol);
     if (w->sp_rval) cudaFree(w->sp_rval);

@@ -51,12 +51,18 @@
 // adds X R^T to Y afterwards in fp32 (R's entries of a row in column order,
 // products of X itself, read from a transposed copy of X).
 //
-// One CTA per SM, 192 threads: warps 0..3 epilogue (TMEM lane quarter =
-// warp), warp 4 loader (bulk copies), warp 5 MMA issuer and TMEM owner.
-// TMEM: two 192-column accumulators at columns 0 and 256, then one 8-column
-// slot per (stage, step) from column 448 for the metadata, each filled by a
+// A third form for sparser weights, the compressed form (sp_cform_kernel),
+// holds only W24's values and per row its metadata and slot mask; the
+// kernel's producer warps expand it into the same shared-memory parts.
+//
+// One CTA per SM, 192 threads (image form): warps 0..3 epilogue (TMEM lane
+// quarter = warp), warp 4 loader (bulk copies), warp 5 MMA issuer and TMEM
+// owner; the compressed form adds producer warps 6..13.  TMEM: two
+// 192-column accumulators at columns 0 and 256, then one 8-column slot per
+// (stage, step) from column 448 for the metadata, each filled by a
 // tcgen05.cp of the step's metadata block (issued by the MMA thread, so it
-// is ordered before the MMAs that read it).  Every TMEM address an MMA is
+// is ordered before the MMAs that read it) or, in the compressed form, by
+// the producers' tcgen05.st.  Every TMEM address an MMA is
 // given is aligned to 8 columns or more.  Work units and
 // their stream-K split over the CTAs, the partial tiles and their fix-up are
 // those of spmm_tc.cuh with 64-row slabs and 128-K k-blocks.
@@ -86,8 +92,16 @@ constexpr uint32_t kSpTmemCols = 512;
 constexpr uint32_t kSpMetaCol0 = 448;                 // metadata slot j at 448 + 8 j
 constexpr int kSpEpiWarps = 4;
 constexpr int kSpThreads = (kSpEpiWarps + 2) * 32;
+constexpr int kSpProdWarps = 8;  // compressed form: two producer warps per TMEM lane quarter
+constexpr int kSpThreadsX = (kSpEpiWarps + 2 + kSpProdWarps) * 32;
 constexpr int kSpBarBytes = 256;
 constexpr int kSpSmemBytes = kSpStages * kSpStageBytes + kSpBarBytes + 1024;
+// Compressed form: a stage holds the three W parts and X (no metadata
+// blocks), and two value slots take one W tile's values of one k-block each.
+constexpr int kSpStageBytesX = 3 * kSpAPart + kSpXImg;  // 98304
+constexpr int kSpVSlot = 16384;
+constexpr int kSpSmemBytesX = kSpStages * kSpStageBytesX + kSpStages * kSpVSlot + kSpBarBytes + 1024;
+static_assert(kSpStageBytesX % 1024 == 0 && kSpSmemBytesX <= 227 * 1024, "compressed-form shared memory");
 static_assert(kSpStageBytes % 1024 == 0 && kSpWImg % 1024 == 0, "1024-byte aligned swizzle atoms");
 static_assert(kSpAccStride + kSpN <= kSpMetaCol0, "accumulators below the metadata");
 static_assert(kSpMetaCol0 + 8 * kSpStages * kSpSteps <= kSpTmemCols, "TMEM columns");
@@ -399,41 +413,214 @@ __global__ void __launch_bounds__(1024) sp_remainder_add_kernel(const float* __r
     }
 }
 
+// Compressed form of W24 (for sparse weights, where W's images would be
+// mostly zeros).  Per (k-block kb, W row n): the row's metadata nibbles of
+// each K = 32 step (meta.{x,y,z,w}: groups 0..3 in bits 0..15, groups 4..7
+// in bits 16..31, the nibbles sp_pack_w_kernel writes), a 64-bit mask of the
+// row's occupied slots (bit 16 s + 2 g + j: slot j of group g of step s;
+// slots as in sp_pack_w_kernel: two values in slots 0 and 1, one value at
+// position 3 in slot 1, any other single value in slot 0) and the index of
+// the row's first value.  Values of (kb, n) pairs in [kb][n] order and,
+// within one, in slot order (= column order), each as its three bf16 parts
+// in 8 bytes (x = p1 | p2 << 16, y = p3).  A W tile's values of one k-block
+// are thus one contiguous run, which the kernel's loader brings into shared
+// memory with one bulk copy; the kernel then expands a row with shifts,
+// adds and predicated loads only.  Built from the dense scratch copy: one
+// thread per (kb, n) counts (COUNT: also the metadata and the slot mask) or
+// writes (fill) the row's W24 values of the k-block.
+template <bool COUNT>
+__global__ void sp_cform_kernel(int64_t npad, int KB, int64_t kpad, const float* __restrict__ wd,
+                                uint32_t* __restrict__ counts, uint4* __restrict__ cmeta, uint2* __restrict__ cocc,
+                                const uint32_t* __restrict__ coff, uint2* __restrict__ cvals) {
+    const int64_t id = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (id >= npad * KB) return;
+    const int64_t n = id % npad;
+    const int kb = static_cast<int>(id / npad);
+    const float* src = wd + n * kpad + static_cast<int64_t>(kb) * kSpBK;
+    uint32_t meta[4] = {0u, 0u, 0u, 0u};
+    uint32_t occ[2] = {0u, 0u};
+    const uint32_t at = COUNT ? 0u : coff[id];
+    uint32_t cnt = 0;
+#pragma unroll 4
+    for (int g = 0; g < kSpBK / 4; ++g) {
+        const float4 q = *reinterpret_cast<const float4*>(src + 4 * g);
+        const float e[4] = {q.x, q.y, q.z, q.w};
+        int p0 = -1, p1 = -1;  // the first two nonzeros of the group are W24's
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (e[i] != 0.0f) {
+                if (p0 < 0) p0 = i;
+                else if (p1 < 0) p1 = i;
+            }
+        uint32_t slots;  // bit j: slot j occupied
+        if (p0 < 0) {
+            slots = 0u;
+            p0 = 0;
+            p1 = 1;
+        } else if (p1 >= 0) {
+            slots = 3u;
+        } else if (p0 == 3) {
+            slots = 2u;
+            p0 = 2;
+            p1 = 3;
+        } else {
+            slots = 1u;
+            p1 = 3;
+        }
+        const int step = g >> 3, gg = g & 7;
+        meta[step] |= static_cast<uint32_t>(p0 | (p1 << 2)) << (gg < 4 ? 4 * gg : 16 + 4 * (gg - 4));
+        occ[step >> 1] |= slots << (16 * (step & 1) + 2 * gg);
+        if (!COUNT) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+                if (slots & (1u << j)) {
+                    uint16_t a1, a2, a3;
+                    bf16x3(e[j == 0 ? p0 : p1], a1, a2, a3);
+                    cvals[static_cast<int64_t>(at) + cnt] = make_uint2(a1 | (static_cast<uint32_t>(a2) << 16), a3);
+                    ++cnt;
+                }
+        } else {
+            cnt += __popc(slots);
+        }
+    }
+    if (COUNT) {
+        counts[id] = cnt;
+        cmeta[id] = make_uint4(meta[0], meta[1], meta[2], meta[3]);
+        cocc[id] = make_uint2(occ[0], occ[1]);
+    }
+}
+
+// One value record (the 3 bf16 parts of a W24 entry), loaded only where
+// `pred`: from shared memory at byte address `saddr` (SH) or from global
+// memory at `g`.  Zero where not loaded.
+template <bool SH>
+__device__ __forceinline__ uint2 sp_ldrec(uint32_t saddr, const uint2* g, bool pred) {
+    uint2 v = make_uint2(0u, 0u);
+    if (SH) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %3, 0;\n\t@p ld.shared.v2.u32 {%0, %1}, [%2];\n\t}"
+            : "+r"(v.x), "+r"(v.y)
+            : "r"(saddr), "r"(pred ? 1u : 0u));
+    } else if (pred) {
+        v = __ldg(g);
+    }
+    return v;
+}
+
+// Compressed form -> one W row of a stage: for each of the K = 32 steps
+// S0 .. S0 + NS - 1, the row's 16 slots of each of the three parts into the
+// swizzled W parts at `st`, and the step's metadata word into this thread's
+// TMEM lane at column `meta_col` + 8 step (rows rl and rl ^ 8 share a lane
+// word: the layout at the top of this file).  Values are record indices
+// from the row's first: shared byte address `sbase` + 8 i (SH) or
+// gbase + i.  All 16 loads of a step are issued before any is used.
+template <bool SH, int S0, int NS>
+__device__ __forceinline__ void sp_expand_row(const uint4& rmeta, const uint2& occ, uint32_t sbase,
+                                              const uint2* gbase, uint8_t* st, int rl, int h, uint32_t meta_col,
+                                              uint32_t lane_off) {
+    static_assert((S0 == 0 || S0 == 2) && S0 + NS <= kSpSteps, "steps 0.. or 2..");
+    const uint32_t rm[4] = {rmeta.x, rmeta.y, rmeta.z, rmeta.w};
+    uint32_t idx = S0 == 0 ? 0u : static_cast<uint32_t>(__popc(occ.x));  // values of the earlier steps
+#pragma unroll
+    for (int s = S0; s < S0 + NS; ++s) {
+        const uint32_t oc = (s < 2 ? occ.x : occ.y) >> (16 * (s & 1));
+        uint2 r[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const uint32_t bit = (oc >> k) & 1u;
+            r[k] = sp_ldrec<SH>(sbase + 8u * idx, gbase + idx, bit != 0u);
+            idx += bit;
+        }
+        uint32_t w1[8], w2[8], w3[8];
+#pragma unroll
+        for (int gg = 0; gg < 8; ++gg) {
+            w1[gg] = __byte_perm(r[2 * gg].x, r[2 * gg + 1].x, 0x5410);
+            w2[gg] = __byte_perm(r[2 * gg].x, r[2 * gg + 1].x, 0x7632);
+            w3[gg] = __byte_perm(r[2 * gg].y, r[2 * gg + 1].y, 0x5410);
+        }
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int off = sp_swz(rl, 2 * s + hh);
+            *reinterpret_cast<uint4*>(st + off) = make_uint4(w1[4 * hh], w1[4 * hh + 1], w1[4 * hh + 2], w1[4 * hh + 3]);
+            *reinterpret_cast<uint4*>(st + kSpAPart + off) =
+                make_uint4(w2[4 * hh], w2[4 * hh + 1], w2[4 * hh + 2], w2[4 * hh + 3]);
+            *reinterpret_cast<uint4*>(st + 2 * kSpAPart + off) =
+                make_uint4(w3[4 * hh], w3[4 * hh + 1], w3[4 * hh + 2], w3[4 * hh + 3]);
+        }
+        // lane word: rows b + i (h = 0) and b + 8 + i (h = 1) of a 16-row
+        // block give groups 0..3 to lane b + i and groups 4..7 to lane
+        // b + 8 + i, row b + 8 h + i at bits 16 h
+        const uint32_t mine = rm[s];
+        const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 8);
+        const uint32_t word = h == 0 ? ((mine & 0xFFFFu) | (other << 16)) : ((other >> 16) | (mine & 0xFFFF0000u));
+        asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(meta_col + 8u * s + lane_off),
+                     "r"(word)
+                     : "memory");
+    }
+}
+
 struct SpArgs {
-    const uint8_t* wimg;   // [tiles][KB] W images
-    const uint8_t* ximg;   // [slabs][KB] X images
+    const uint8_t* wimg;    // [tiles][KB] W images (image form)
+    const uint8_t* ximg;    // [slabs][KB] X images
+    const uint4* cmeta;     // compressed form: [KB][npad] metadata nibbles
+    const uint2* cocc;      // [KB][npad] slot masks
+    const uint32_t* coff;   // [KB * npad + 1] value indices (the last one the total)
+    const uint2* cvals;     // the 3 bf16 parts of each value
+    int64_t npad;
     int M, N;
     float* y;              // output, row stride ldy
     int64_t ldy;
     float* partial;        // [2 * grid][64][128] partial tiles (tc_fixup_kernel's layout)
 };
 
-__global__ void __launch_bounds__(kSpThreads, 1)
+// EXPAND = false: W's images come by bulk copy with their metadata (image
+// form).  EXPAND = true: the loader brings the W tile's values of the
+// k-block into a value slot (one bulk copy) and X into the stage, on
+// separate barriers, and eight producer warps (two per TMEM lane quarter,
+// one thread per W row and pair of K = 32 steps) expand the values with the
+// row's metadata and slot mask into the stage's three swizzled W parts and
+// write the metadata words into TMEM themselves.  A run of values longer
+// than a slot is read from global memory by the producers instead (slow;
+// the host only picks this form where every run fits).
+template <bool EXPAND>
+__global__ void __launch_bounds__(EXPAND ? kSpThreadsX : kSpThreads, 1)
     spmm_sp_kernel(const TcSched sched, const SpArgs a, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSpStages * kSpStageBytes);
+    constexpr int kStage = EXPAND ? kSpStageBytesX : kSpStageBytes;
+    constexpr int kXOff = EXPAND ? 3 * kSpAPart : kSpWImg;  // X's place in a stage
+    constexpr int kVBytes = EXPAND ? kSpStages * kSpVSlot : 0;
+    uint8_t* vslot = smem + kSpStages * kStage;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSpStages * kStage + kVBytes);
     uint64_t* empty = full + kSpStages;
     uint64_t* tfull = empty + kSpStages;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* vfull = drain + 1;          // compressed form: stage s's values landed
+    uint64_t* xfull = vfull + kSpStages;  // compressed form: stage s's X landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + kSpStages);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    // Value slot s: [2 s] index of its first value, [2 s + 1] byte offset of
+    // that value in the slot, or ~0 when the run is read from global memory.
+    volatile uint32_t* vinfo = tmem_slot + 2;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     constexpr int kEpiThreads = 32 * kSpEpiWarps;
     constexpr int kLoadWarp = kSpEpiWarps;
     constexpr int kMmaWarp = kSpEpiWarps + 1;
+    constexpr int kProdWarp0 = kSpEpiWarps + 2;
     const int64_t KB = sched.kb_total;
     const int64_t g0 = static_cast<int64_t>(blockIdx.x) * sched.per_cta;
     const int64_t g1 = min(g0 + sched.per_cta, sched.total);  // this CTA's k-blocks [g0, g1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSpStages; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], EXPAND ? kSpProdWarps : 1);  // the loader's copies, or each producer warp
             mbar_init(&empty[s], 1);
+            mbar_init(&vfull[s], 1);
+            mbar_init(&xfull[s], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull[i], 1);
@@ -514,7 +701,7 @@ __global__ void __launch_bounds__(kSpThreads, 1)
                 for (int j = 0; j < kSpSlab; ++j) dst[j * kTcWRows] = racc[j];
             }
         }
-    } else if (warp == kLoadWarp) {
+    } else if (warp == kLoadWarp && !EXPAND) {
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
@@ -575,7 +762,171 @@ __global__ void __launch_bounds__(kSpThreads, 1)
                     if (issued & (1u << s)) mbar_wait(&full[s], last_par[s], &zero);
             }
         }
-    } else {
+    } else if (warp == kLoadWarp) {
+        // Compressed form: values and X on their own barriers.  The values of
+        // a stage's next k-block are requested once the producers are done
+        // with the slot (full[s]), X once the MMAs are done with the stage
+        // (empty[s]), so the producers expand while X is still in flight.
+        if (lane == 0) {
+            uint32_t vissued = 0, xissued = 0, vpar[kSpStages], xpar[kSpStages];
+            bool ok = true;
+            TcCursor cur;
+            cur.init(sched, g0);
+            // The unit's run of values [vo0, vo1) (its W tile's values of the
+            // k-block), read one unit ahead; copied into value slot s when
+            // it fits, 16-byte aligned at both ends.
+            uint32_t vo0 = 0, vo1 = 0;
+            auto run_of = [&](const TcCursor& c) {
+                const int64_t r0 = static_cast<int64_t>(c.kb) * a.npad + static_cast<int64_t>(c.t) * kTcWRows;
+                vo0 = __ldg(a.coff + r0);
+                vo1 = __ldg(a.coff + r0 + kTcWRows);
+            };
+            // vinfo is written before the arrival, which publishes it to the
+            // producers.
+            auto issue_values = [&](int s, const TcCursor& c, bool fetch_next) {
+                const uint64_t b0 = (static_cast<uint64_t>(vo0) * 8u) & ~static_cast<uint64_t>(15);
+                const uint64_t b1 = (static_cast<uint64_t>(vo1) * 8u + 15u) & ~static_cast<uint64_t>(15);
+                const bool fits = vo1 > vo0 && b1 - b0 <= static_cast<uint64_t>(kSpVSlot);
+                vinfo[2 * s] = vo0;
+                vinfo[2 * s + 1] =
+                    fits ? static_cast<uint32_t>(static_cast<uint64_t>(vo0) * 8u - b0) : (vo1 > vo0 ? ~0u : 0u);
+                if (fits) {
+                    mbar_arrive_expect_tx(&vfull[s], static_cast<uint32_t>(b1 - b0));
+                    bulk_load(vslot + s * kSpVSlot, reinterpret_cast<const uint8_t*>(a.cvals) + b0,
+                              static_cast<uint32_t>(b1 - b0), &vfull[s]);
+                } else {
+                    mbar_arrive(&vfull[s]);
+                }
+                if (fetch_next) {
+                    TcCursor nx = c;
+                    nx.next(sched);
+                    run_of(nx);
+                }
+            };
+            auto issue_x = [&](int s, const TcCursor& c) {
+                uint8_t* st = smem + s * kStage + kXOff;
+                const uint8_t* xsrc = a.ximg + (static_cast<int64_t>(c.c) * KB + c.kb) * kSpXImg;
+                mbar_arrive_expect_tx(&xfull[s], kSpXImg);
+                bulk_load(st, xsrc, kSpXImg / 2, &xfull[s]);
+                bulk_load(st + kSpXImg / 2, xsrc + kSpXImg / 2, kSpXImg / 2, &xfull[s]);
+            };
+            // The compressed form is a prepared weight (written once, never
+            // by a kernel that precedes this one): the first values are
+            // requested before the dependency wait, X (written by the
+            // packing kernel just before) after it.
+            const int npre = static_cast<int>(g1 - g0 < kSpStages ? g1 - g0 : kSpStages);
+            if (npre > 0) run_of(cur);
+            TcCursor pc = cur;
+            for (int i = 0; i < npre; ++i, pc.next(sched)) {
+                issue_values(i, pc, g0 + i + 1 < g1);
+                vissued |= 1u << i;
+                vpar[i] = 0u;
+            }
+            pdl_wait();
+            for (int i = 0; i < npre; ++i, cur.next(sched)) {
+                issue_x(i, cur);
+                xissued |= 1u << i;
+                xpar[i] = 0u;
+            }
+            int stage = npre % kSpStages;
+            uint32_t phase = (npre == kSpStages) ? 1u : 0u;
+            for (int64_t g = g0 + npre; g < g1; ++g, cur.next(sched)) {
+                if (!mbar_wait(&full[stage], phase ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                issue_values(stage, cur, g + 1 < g1);
+                vissued |= 1u << stage;
+                vpar[stage] = phase;
+                if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                issue_x(stage, cur);
+                xissued |= 1u << stage;
+                xpar[stage] = phase;
+                if (++stage == kSpStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) {
+                // Copies still in flight land before the CTA exits.
+                *abort_flag = 1;
+                report_error(err, kDevWaitTimeout);
+                const int zero = 0;
+                for (int s = 0; s < kSpStages; ++s) {
+                    if (vissued & (1u << s)) mbar_wait(&vfull[s], vpar[s], &zero);
+                    if (xissued & (1u << s)) mbar_wait(&xfull[s], xpar[s], &zero);
+                }
+            }
+        }
+    } else if (EXPAND && warp >= kProdWarp0) {
+        // Producer: this thread builds W row n = 128 t + 32 q + lane of each
+        // k-block of the CTA's range into the stage's W parts and its TMEM
+        // lane's metadata words, from the row's metadata, slot mask and
+        // values in the stage's value slot: warps 6..9 the K = 32 steps 0
+        // and 1, warps 10..13 steps 2 and 3 (a warp reaches the TMEM lane
+        // quarter warp % 4).  The row's data of the next k-block is loaded
+        // while this one is built.
+        const int q = warp & 3;
+        const bool hi_steps = warp >= kProdWarp0 + 4;
+        const int rl = q * 32 + lane;
+        const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+        const int h = (rl >> 3) & 1;
+        TcCursor cur;
+        cur.init(sched, g0);
+        int stage = 0;
+        uint32_t phase = 0;
+        auto load_row = [&](const TcCursor& c, uint4& m, uint2& oc, uint32_t& o) {
+            const int64_t w = static_cast<int64_t>(c.kb) * a.npad + static_cast<int64_t>(c.t) * kTcWRows + rl;
+            m = __ldg(a.cmeta + w);
+            oc = __ldg(a.cocc + w);
+            o = __ldg(a.coff + w);
+        };
+        uint4 m_next{};
+        uint2 oc_next{};
+        uint32_t o_next = 0;
+        if (g0 < g1) load_row(cur, m_next, oc_next, o_next);
+        for (int64_t g = g0; g < g1; ++g) {
+            const uint4 mk = m_next;
+            const uint2 ock = oc_next;
+            const uint32_t o_row = o_next;
+            TcCursor nx = cur;
+            nx.next(sched);
+            if (g + 1 < g1) load_row(nx, m_next, oc_next, o_next);
+            // The stage's values have landed (vfull) and the MMAs of its
+            // previous k-block are done (empty): its W parts and TMEM
+            // metadata slots are free.
+            if (!mbar_wait(&vfull[stage], phase, abort_flag) || !mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+                *abort_flag = 1;
+                report_error(err, kDevWaitTimeout);
+                break;
+            }
+            tc_fence_after();
+            uint8_t* st = smem + stage * kStage;
+            const uint32_t run0 = vinfo[2 * stage], where = vinfo[2 * stage + 1];
+            const uint32_t meta = tmem_base + kSpMetaCol0 + static_cast<uint32_t>(8 * kSpSteps * stage);
+            const uint32_t sbase = smem_u32(vslot + stage * kSpVSlot) + where + 8u * (o_row - run0);
+            if (where != ~0u) {
+                if (hi_steps) sp_expand_row<true, 2, 2>(mk, ock, sbase, a.cvals + o_row, st, rl, h, meta, lane_off);
+                else sp_expand_row<true, 0, 2>(mk, ock, sbase, a.cvals + o_row, st, rl, h, meta, lane_off);
+            } else {
+                if (hi_steps) sp_expand_row<false, 2, 2>(mk, ock, 0u, a.cvals + o_row, st, rl, h, meta, lane_off);
+                else sp_expand_row<false, 0, 2>(mk, ock, 0u, a.cvals + o_row, st, rl, h, meta, lane_off);
+            }
+            tmem_st_wait();
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[stage]);
+            cur = nx;
+            if (++stage == kSpStages) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+    } else if (warp == kMmaWarp) {
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
@@ -584,23 +935,26 @@ __global__ void __launch_bounds__(kSpThreads, 1)
             for (int64_t g = g0; ok && g < g1; ++g, ++tc) {
                 const int slot = tc & 1;
                 const uint32_t ap = static_cast<uint32_t>(tc >> 1) & 1u;
-                if (!mbar_wait(&tempty[slot], ap ^ 1u, abort_flag) || !mbar_wait(&full[stage], phase, abort_flag)) {
+                if (!mbar_wait(&tempty[slot], ap ^ 1u, abort_flag) || !mbar_wait(&full[stage], phase, abort_flag) ||
+                    (EXPAND && !mbar_wait(&xfull[stage], phase, abort_flag))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t st = smem_u32(smem + stage * kSpStageBytes);
+                const uint32_t st = smem_u32(smem + stage * kStage);
                 const uint32_t meta = tmem_base + kSpMetaCol0 + static_cast<uint32_t>(8 * kSpSteps * stage);
+                if (!EXPAND) {
 #pragma unroll
-                for (int k = 0; k < kSpSteps; ++k)
-                    tmem_cp_128x128b(meta + 8 * k, sdesc_rows16(st + 3 * kSpAPart + k * kSpMetaBlock));
+                    for (int k = 0; k < kSpSteps; ++k)
+                        tmem_cp_128x128b(meta + 8 * k, sdesc_rows16(st + 3 * kSpAPart + k * kSpMetaBlock));
+                }
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot) * kSpAccStride;
                 const uint64_t a1 = sdesc_kmajor_sw128(st), a2 = sdesc_kmajor_sw128(st + kSpAPart),
                                a3 = sdesc_kmajor_sw128(st + 2 * kSpAPart);
 #pragma unroll
                 for (int k = 0; k < kSpSteps; ++k) {
                     const uint64_t ka = static_cast<uint64_t>((32 * k) >> 4);  // 16 stored bf16 per step
-                    const uint64_t db = sdesc_kmajor_sw128(st + kSpWImg + (k >> 1) * kSpXHalf) +
+                    const uint64_t db = sdesc_kmajor_sw128(st + kXOff + (k >> 1) * kSpXHalf) +
                                         static_cast<uint64_t>((64 * (k & 1)) >> 4);  // 32 bf16 of X per step
                     const uint32_t mk = meta + static_cast<uint32_t>(8 * k);
                     umma_sp_bf16(d_tmem, a1 + ka, db, mk, sp_idesc(3 * kSpSlab), k > 0 ? 1u : 0u);

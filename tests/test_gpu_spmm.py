@@ -361,8 +361,8 @@ def test_structured_sparse_from_nm_pruning(ctx, monkeypatch):
 def test_structured_sparse_with_remainder(ctx, M, N, K, sparsity, monkeypatch):
     """Unstructured weights on the structured-sparse kernel: W = W24 + R, the
     2:4 part on the tensor cores and the remainder R (entries past the second
-    of their group of four) added in fp32 by the epilogue, each CTA the
-    entries of its k-block range.  Normwise <= 1e-5 against the reference."""
+    of their group of four) added in fp32 by its own kernel afterwards.
+    Normwise <= 1e-5 against the reference."""
     monkeypatch.setenv("PFRT_SPMM_SP", "1")
     c = wl.spmm_case(M, N, K, sparsity=sparsity, seed=N + K)
     assert normwise_rel(gpu(ctx, c), oracle(c)) <= FP32_TOL
@@ -380,3 +380,30 @@ def test_structured_sparse_duplicate_columns(ctx, monkeypatch):
     ip[1:] += 1
     dup = wl.CsrCase(d.N, d.K, ip.astype(np.int32), idx.astype(np.int32), val.astype(np.float32), d.X)
     assert normwise_rel(gpu(ctx, dup), oracle(dup)) <= FP32_TOL
+
+
+@pytest.mark.parametrize("M,N,K,sparsity", [(64, 256, 512, None), (130, 260, 1001, None), (17, 130, 259, 0.7),
+                                            (64, 520, 1000, 0.9), (300, 4096, 4096, 0.9), (64, 8192, 8192, 0.9),
+                                            (1024, 512, 1024, 0.95), (33, 200, 640, 1.0)])
+def test_structured_sparse_forms_agree(ctx, M, N, K, sparsity, monkeypatch):
+    """The structured-sparse kernel reading W24 as prepared images and as the
+    compressed form (per row metadata, slot mask and bf16 x3 values, expanded
+    into shared memory and TMEM by the kernel's producer warps) gives the
+    same bits: both put the same operands and metadata before the same MMAs.
+    Cases: 2:4 weights (sparsity None, whose value runs overflow the
+    kernel's slot, so the producers read global memory), unstructured ones
+    with a remainder, ragged shapes, and a weight with no entries; the
+    compressed result within 1e-5 normwise of the reference."""
+    c = (wl.structured24_case(M, N, K, seed=M + N) if sparsity is None
+         else wl.spmm_case(M, N, K, sparsity=sparsity, seed=N + K))
+    monkeypatch.setenv("PFRT_SPMM_SP", "1")
+    out = {}
+    for form in ("image", "compressed"):
+        monkeypatch.setenv("PFRT_SPMM_SP_FORM", form)
+        out[form] = gpu(ctx, c)
+    ref = oracle(c)
+    if np.abs(ref).max() == 0:
+        assert not out["compressed"].any() and not out["image"].any()
+    else:
+        assert normwise_rel(out["compressed"], ref) <= FP32_TOL
+    assert np.array_equal(out["image"], out["compressed"])
