@@ -204,7 +204,9 @@ PFRT_API pfrt_status pfrt_qlinear_host(pfrt_ctx* ctx, const pfrt_qweight* w, int
  * compressed form, or its structured-sparse form: for M >= 16 the first call
  * counts the entries past the second of every group of four columns, and
  * the first call that chooses the structured-sparse tensor cores builds W's
- * 2:4 images and remainder; each allocates device memory and synchronizes):
+ * 2:4 part, as images or, for large sparse weights, as a compressed form the
+ * kernel expands on chip, and its remainder; each allocates device memory
+ * and synchronizes):
  * make one call of each batch size class before capturing calls in a CUDA
  * graph, and do not use one CSR from several threads or contexts at once.
  * pfrt_spmm_csr_f32: same on a caller-owned device CSR (int32); the kernel
