@@ -1425,18 +1425,20 @@ pfrt_status ensure_sp_count(pfrt_csr* w, cudaStream_t s) {
 }
 
 // Which form of W24 the structured-sparse kernel reads.  The compressed form
-// (28 bytes per row and k-block plus 8 per kept entry) is chosen where the
-// images would not stay in L2 (over ~96 MB; a smaller weight's images are
-// re-read from L2 by every X slab, which beats expanding the compressed
-// form again: 4096^2 at 90 %, M = 256, 56 against 62 us) and a W tile's
-// values of one k-block fit the kernel's value slot with room to spare on
-// average (W24 under ~10 % dense; 90 %-sparse weights keep ~10 %, with the
-// longest runs still in the slot).  8192^2 at 90 % on B200: M = 64 59 us
-// both, M = 256 183 against 192 us, M = 1024 699 against 706 us; at 95 %
-// 55 against 56 and 172 against 186 us.  Whether every run fits is checked
-// when the form is built.  PFRT_SPMM_SP_FORM =
-// image|compressed forces one (read when the form is built; a forced
-// compressed form reads runs that do not fit from global memory, slowly).
+// (28 bytes per row and k-block plus 8 per kept entry) is chosen where it is
+// under a quarter of the images' size (W24 under ~5 % dense: 95 %-sparse
+// weights and sparser), the images would not stay in L2 (over ~96 MB; a
+// smaller weight's images are re-read from L2 by every X slab, which beats
+// expanding the compressed form again) and a W tile's values of one k-block
+// fit the kernel's value slot on average.  Both kernels are bound by shared
+// memory bandwidth, so the compressed form's smaller HBM traffic pays only
+// where the images are mostly empty: on B200, 8192^2 at 95 %: M = 64 55
+// (compressed) against 55 us (images), M = 256 171 against 174 us; at 90 %
+// the images win (M = 64 58 against 59, M = 256 181 against 182, M = 1024
+// 676 against 715 us).  Whether every run fits is checked when the form is
+// built.  PFRT_SPMM_SP_FORM = image|compressed forces one (read when the
+// form is built; a forced compressed form reads runs that do not fit from
+// global memory, slowly).
 bool sp_form_forced(bool& cform) {
     const char* f = std::getenv("PFRT_SPMM_SP_FORM");
     if (!f) return false;
@@ -1452,7 +1454,8 @@ bool sp_use_cform(const pfrt_csr* w) {
     if (kept >= 4.0e9) return false;  // 32-bit value indices
     bool cform = false;
     if (sp_form_forced(cform)) return cform;
-    return tiles * KB * kSpWImg > 96.0e6 && 8.0 * kept / (tiles * KB) < 0.85 * kSpVSlot;
+    const double i_bytes = tiles * KB * kSpWImg, c_bytes = 28.0 * 128.0 * tiles * KB + 8.0 * kept;
+    return i_bytes > 96.0e6 && c_bytes < 0.25 * i_bytes && 8.0 * kept / (tiles * KB) < 0.85 * kSpVSlot;
 }
 
 // W's structured-sparse form, built once on the device from a dense scratch

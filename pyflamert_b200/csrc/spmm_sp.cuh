@@ -31,10 +31,9 @@
 //
 // Prepared forms (both written in the exact shared-memory image the kernel
 // needs, so a stage is filled by plain 1-D bulk copies):
-//   W image, per (W tile t of 128 rows, k-block kb of 128 K), 57344 bytes:
+//   W image, per (W tile t of 128 rows, k-block kb of 128 K), 51200 bytes:
 //     3 x [128 rows x 64 bf16 = 128 B, 128-byte swizzle]   parts w1, w2, w3
-//     4 x [128 lanes][4 u32] metadata, one block per K = 32 step: word 0 of
-//         each lane is the step's metadata word, words 1..3 are zero
+//     [128 lanes][4 u32] metadata: lane l's metadata word of each K = 32 step
 //   X image, per (X slab c of 64 rows, kb), 49152 bytes: for each K half
 //     (64 K), [x1 | x2 | x3] rows of 128 B, 128-byte swizzle.
 // Metadata word of TMEM lane l for one K = 32 step (8 groups of 4 columns),
@@ -55,14 +54,14 @@
 // holds only W24's values and per row its metadata and slot mask; the
 // kernel's producer warps expand it into the same shared-memory parts.
 //
-// One CTA per SM, 192 threads (image form): warps 0..3 epilogue (TMEM lane
-// quarter = warp), warp 4 loader (bulk copies), warp 5 MMA issuer and TMEM
-// owner; the compressed form adds producer warps 6..13.  TMEM: two
-// 192-column accumulators at columns 0 and 256, then one 8-column slot per
-// (stage, step) from column 448 for the metadata, each filled by a
-// tcgen05.cp of the step's metadata block (issued by the MMA thread, so it
-// is ordered before the MMAs that read it) or, in the compressed form, by
-// the producers' tcgen05.st.  Every TMEM address an MMA is
+// One CTA per SM: warps 0..3 epilogue (TMEM lane quarter = warp), warp 4
+// loader (bulk copies), warp 5 MMA issuer and TMEM owner, then (image form)
+// four metadata warps 6..9 or (compressed form) eight producer warps 6..13.
+// TMEM: two 192-column accumulators at columns 0 and 256, then one 8-column
+// slot per (stage, step) from column 448 for the metadata, written with
+// tcgen05.st by the warps of the lane quarter (warp % 4): the metadata
+// warps copy each lane's four words from the landed image, the producers
+// compute them.  Every TMEM address an MMA is
 // given is aligned to 8 columns or more.  Work units and
 // their stream-K split over the CTAs, the partial tiles and their fix-up are
 // those of spmm_tc.cuh with 64-row slabs and 128-K k-blocks.
@@ -78,20 +77,20 @@ constexpr int kSpBK = 128;                            // K per k-block
 constexpr int kSpSteps = kSpBK / 32;                  // sparse MMA steps (K = 32) per k-block
 constexpr int kSpSlab = 64;                           // X rows per unit
 constexpr int kSpAPart = 128 * 128;                   // one W part: 128 rows x 128 B
-constexpr int kSpMetaBlock = 128 * 16;                // one step's metadata: [lane][4] u32
-constexpr int kSpMetaBytes = kSpSteps * kSpMetaBlock;
-constexpr int kSpWImg = 3 * kSpAPart + kSpMetaBytes;  // 57344
+constexpr int kSpMetaBytes = 128 * 4 * kSpSteps;      // metadata: [lane][step] u32
+constexpr int kSpWImg = 3 * kSpAPart + kSpMetaBytes;  // 51200
 constexpr int kSpXPart = kSpSlab * 128;               // one X part of one K half: 64 rows x 128 B
 constexpr int kSpXHalf = 3 * kSpXPart;                // 24576
 constexpr int kSpXImg = 2 * kSpXHalf;                 // 49152
-constexpr int kSpStageBytes = kSpWImg + kSpXImg;      // 106496 (a multiple of 1024)
+constexpr int kSpStageBytes = kSpWImg + kSpXImg;      // 100352 (a multiple of 1024)
 constexpr int kSpStages = 2;
 constexpr int kSpN = 3 * kSpSlab;                     // 192 accumulator columns
 constexpr uint32_t kSpAccStride = 256;                // accumulator slots at columns 0 and 256
 constexpr uint32_t kSpTmemCols = 512;
 constexpr uint32_t kSpMetaCol0 = 448;                 // metadata slot j at 448 + 8 j
 constexpr int kSpEpiWarps = 4;
-constexpr int kSpThreads = (kSpEpiWarps + 2) * 32;
+constexpr int kSpMetaWarps = 4;  // image form: one metadata warp per TMEM lane quarter
+constexpr int kSpThreads = (kSpEpiWarps + 2 + kSpMetaWarps) * 32;
 constexpr int kSpProdWarps = 8;  // compressed form: two producer warps per TMEM lane quarter
 constexpr int kSpThreadsX = (kSpEpiWarps + 2 + kSpProdWarps) * 32;
 constexpr int kSpBarBytes = 256;
@@ -133,23 +132,6 @@ __device__ __forceinline__ void umma_sp_bf16(uint32_t d_tmem, uint64_t adesc, ui
         "tcgen05.mma.sp.cta_group::1.kind::f16 [%0], %1, %2, [%3], %4, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(meta), "r"(idesc), "r"(accumulate)
         : "memory");
-}
-
-// Shared-memory descriptor of a plain row-major [rows][16 B] array (no
-// swizzle, 8-row groups 128 bytes apart), for tcgen05.cp.
-__device__ __forceinline__ uint64_t sdesc_rows16(uint32_t smem_addr) {
-    uint64_t d = 0;
-    d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
-    d |= static_cast<uint64_t>(128u >> 4) << 16;
-    d |= static_cast<uint64_t>(128u >> 4) << 32;
-    d |= static_cast<uint64_t>(1u) << 46;
-    return d;
-}
-
-// Copies 128 rows x 16 bytes from shared memory into TMEM lanes 0..127,
-// columns taddr .. taddr + 3.
-__device__ __forceinline__ void tmem_cp_128x128b(uint32_t taddr, uint64_t sdesc) {
-    asm volatile("tcgen05.cp.cta_group::1.128x128b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 
 // Instruction descriptor: bf16 x bf16 -> f32, M = 128, sparse, N given.
@@ -240,7 +222,7 @@ __global__ void sp_scatter_kernel(int64_t N, int64_t Kpad, const int32_t* __rest
 // W images from the dense scratch wd [Npad][Kpad] (zero padded): one thread
 // per (tile t, k-block kb, row r, step s) compresses 32 columns (8 groups)
 // of one row: its 16 kept values of each part, and its 8 metadata nibbles
-// (ORed into the two lanes' words; the image is zeroed first).
+// (ORed into the step's words of the two lanes; the image is zeroed first).
 __global__ void sp_pack_w_kernel(int tiles, int KB, int64_t Kpad, const float* __restrict__ wd,
                                  uint8_t* __restrict__ img) {
     const int64_t id = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -297,10 +279,10 @@ __global__ void sp_pack_w_kernel(int tiles, int KB, int64_t Kpad, const float* _
             *reinterpret_cast<uint4*>(part + sp_swz(r, 2 * s + h)) = w;
         }
     }
-    uint32_t* meta = reinterpret_cast<uint32_t*>(base + 3 * kSpAPart + s * kSpMetaBlock);
+    uint32_t* meta = reinterpret_cast<uint32_t*>(base + 3 * kSpAPart);
     const int b16 = r & ~15, i = r & 7, hh = (r >> 3) & 1;
-    atomicOr(meta + (b16 + i) * 4, nib_lo << (16 * hh));
-    atomicOr(meta + (b16 + 8 + i) * 4, nib_hi << (16 * hh));
+    atomicOr(meta + (b16 + i) * kSpSteps + s, nib_lo << (16 * hh));
+    atomicOr(meta + (b16 + 8 + i) * kSpSteps + s, nib_hi << (16 * hh));
 }
 
 // X images: one thread per (slab c, k-block kb, 8-column piece q, row j),
@@ -574,7 +556,7 @@ struct SpArgs {
 };
 
 // EXPAND = false: W's images come by bulk copy with their metadata (image
-// form).  EXPAND = true: the loader brings the W tile's values of the
+// form), which four metadata warps move into TMEM.  EXPAND = true: the loader brings the W tile's values of the
 // k-block into a value slot (one bulk copy) and X into the stage, on
 // separate barriers, and eight producer warps (two per TMEM lane quarter,
 // one thread per W row and pair of K = 32 steps) expand the values with the
@@ -599,7 +581,8 @@ __global__ void __launch_bounds__(EXPAND ? kSpThreadsX : kSpThreads, 1)
     uint64_t* drain = tempty + 2;
     uint64_t* vfull = drain + 1;          // compressed form: stage s's values landed
     uint64_t* xfull = vfull + kSpStages;  // compressed form: stage s's X landed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + kSpStages);
+    uint64_t* mready = xfull + kSpStages;  // image form: stage s's metadata in TMEM
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mready + kSpStages);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     // Value slot s: [2 s] index of its first value, [2 s + 1] byte offset of
     // that value in the slot, or ~0 when the run is read from global memory.
@@ -621,6 +604,7 @@ __global__ void __launch_bounds__(EXPAND ? kSpThreadsX : kSpThreads, 1)
             mbar_init(&empty[s], 1);
             mbar_init(&vfull[s], 1);
             mbar_init(&xfull[s], 1);
+            mbar_init(&mready[s], kSpMetaWarps);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull[i], 1);
@@ -861,6 +845,42 @@ __global__ void __launch_bounds__(EXPAND ? kSpThreadsX : kSpThreads, 1)
                 }
             }
         }
+    } else if (!EXPAND && warp >= kProdWarp0) {
+        // Metadata warp (image form): once a stage's image has landed, each
+        // thread writes its TMEM lane's four step words (the image's
+        // [lane][step] block) into the stage's metadata slots; the MMA
+        // thread waits for all four warps (mready).  The slots are free: the
+        // loader requested the image after the MMAs of the stage's previous
+        // k-block were done.
+        const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        const int rl = (warp & 3) * 32 + lane;
+        int stage = 0;
+        uint32_t phase = 0;
+        for (int64_t g = g0; g < g1; ++g) {
+            if (!mbar_wait(&full[stage], phase, abort_flag)) {
+                *abort_flag = 1;
+                report_error(err, kDevWaitTimeout);
+                break;
+            }
+            tc_fence_after();
+            const uint4 mw = *reinterpret_cast<const uint4*>(smem + stage * kStage + 3 * kSpAPart + 16 * rl);
+            const uint32_t meta = tmem_base + kSpMetaCol0 + static_cast<uint32_t>(8 * kSpSteps * stage) + lane_off;
+            asm volatile(
+                "tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};\n\t"
+                "tcgen05.st.sync.aligned.32x32b.x1.b32 [%2], {%3};\n\t"
+                "tcgen05.st.sync.aligned.32x32b.x1.b32 [%4], {%5};\n\t"
+                "tcgen05.st.sync.aligned.32x32b.x1.b32 [%6], {%7};" ::"r"(meta),
+                "r"(mw.x), "r"(meta + 8u), "r"(mw.y), "r"(meta + 16u), "r"(mw.z), "r"(meta + 24u), "r"(mw.w)
+                : "memory");
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&mready[stage]);
+            if (++stage == kSpStages) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
     } else if (EXPAND && warp >= kProdWarp0) {
         // Producer: this thread builds W row n = 128 t + 32 q + lane of each
         // k-block of the CTA's range into the stage's W parts and its TMEM
@@ -936,18 +956,13 @@ __global__ void __launch_bounds__(EXPAND ? kSpThreadsX : kSpThreads, 1)
                 const int slot = tc & 1;
                 const uint32_t ap = static_cast<uint32_t>(tc >> 1) & 1u;
                 if (!mbar_wait(&tempty[slot], ap ^ 1u, abort_flag) || !mbar_wait(&full[stage], phase, abort_flag) ||
-                    (EXPAND && !mbar_wait(&xfull[stage], phase, abort_flag))) {
+                    !mbar_wait(EXPAND ? &xfull[stage] : &mready[stage], phase, abort_flag)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t st = smem_u32(smem + stage * kStage);
                 const uint32_t meta = tmem_base + kSpMetaCol0 + static_cast<uint32_t>(8 * kSpSteps * stage);
-                if (!EXPAND) {
-#pragma unroll
-                    for (int k = 0; k < kSpSteps; ++k)
-                        tmem_cp_128x128b(meta + 8 * k, sdesc_rows16(st + 3 * kSpAPart + k * kSpMetaBlock));
-                }
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot) * kSpAccStride;
                 const uint64_t a1 = sdesc_kmajor_sw128(st), a2 = sdesc_kmajor_sw128(st + kSpAPart),
                                a3 = sdesc_kmajor_sw128(st + 2 * kSpAPart);
